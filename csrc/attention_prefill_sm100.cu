@@ -1,0 +1,325 @@
+// Causal GQA prefill flash attention on tcgen05 tensor cores (head_dim 128).
+//
+// One CTA per (query tile of 128 rows, query head); tiles are launched
+// heaviest-first.  Warp roles (192 threads):
+//   warps 0..3  softmax + epilogue: thread = one query row = one TMEM lane.
+//   warp 4      TMA producer: Q (2 x 64-col swizzled panels), K/V double
+//               buffered straight out of the fused QKV activation.
+//   warp 5      MMA issuer: S = Q K^T into a double-buffered TMEM S tile,
+//               O += P V with P (bf16, swizzled K-major) written by the
+//               softmax warps into shared memory and V used as an MN-major
+//               operand; O accumulates in TMEM.
+// Online softmax with lazy rescaling: the reference max of a row only moves
+// when the new max exceeds it by more than 2^8, so O (in TMEM) is rarely
+// rescaled; exp2 arguments are bounded by 8 so p <= 256 stays exact enough.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+
+#include "common.cuh"
+#include "ops.h"
+#include "sm100.cuh"
+
+namespace kvs {
+namespace {
+
+constexpr int D = 128;
+constexpr int BQ = 128, BKV = 128;
+constexpr int PANEL = 128 * 128;          // bytes: 128 rows x 64 bf16
+constexpr int TILE = 2 * PANEL;           // 32 KB: 128 rows x 128 bf16
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + TILE;       // 2 stages
+constexpr int OFF_V = OFF_K + 2 * TILE;   // 2 stages
+constexpr int OFF_P = OFF_V + 2 * TILE;   // 2 buffers
+constexpr int OFF_BAR = OFF_P + 2 * TILE;
+constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;       // S0 | S1 | O | (unused)
+constexpr float kRescaleThreshold = 8.0f;
+
+struct AttnArgs {
+  bf16* out;
+  int64_t ldo;
+  int T, Hq, Hkv;
+  float scale_log2;
+  uint32_t* err;
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_prefill_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
+  using namespace sm100;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* q_full = bars;        // 1
+  uint64_t* k_full = bars + 1;    // 2
+  uint64_t* v_full = bars + 3;    // 2
+  uint64_t* kv_empty = bars + 5;  // 2
+  uint64_t* s_full = bars + 7;    // 2
+  uint64_t* s_empty = bars + 9;   // 2
+  uint64_t* p_full = bars + 11;   // 2
+  uint64_t* pv_done = bars + 13;  // 2
+  uint64_t* drain = bars + 15;    // 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x;
+  const int ntiles = (a.T + BQ - 1) / BQ;
+  const int qt = ntiles - 1 - int(blockIdx.y);
+  const int q0 = qt * BQ;
+  const int kvh = h / (a.Hq / a.Hkv);
+  const int nkv = qt + 1;  // causal: key tiles 0..qt
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tm);
+  }
+  if (warp == 5) tmem_alloc<kTmemCols>(tmem_slot);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS[2] = {tmem, tmem + 128};
+  const uint32_t tO = tmem + 256;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const int xq = h * D, xk = (a.Hq + kvh) * D, xv = (a.Hq + a.Hkv + kvh) * D;
+      uint32_t issued = 0, parity = 0;
+      mbar_arrive_expect_tx(q_full, TILE);
+      tma_load_2d(smem + OFF_Q, &tm, xq, q0, q_full);
+      tma_load_2d(smem + OFF_Q + PANEL, &tm, xq + 64, q0, q_full);
+      bool ok = true;
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, a.err)) { ok = false; break; }
+        const int k0 = j * BKV;
+        mbar_arrive_expect_tx(&k_full[st], TILE);
+        tma_load_2d(smem + OFF_K + st * TILE, &tm, xk, k0, &k_full[st]);
+        tma_load_2d(smem + OFF_K + st * TILE + PANEL, &tm, xk + 64, k0, &k_full[st]);
+        mbar_arrive_expect_tx(&v_full[st], TILE);
+        tma_load_2d(smem + OFF_V + st * TILE, &tm, xv, k0, &v_full[st]);
+        tma_load_2d(smem + OFF_V + st * TILE + PANEL, &tm, xv + 64, k0, &v_full[st]);
+        issued |= 1u << st;
+        parity = (parity & ~(1u << st)) | (uint32_t((j >> 1) & 1) << st);
+      }
+      // Always make sure our copies have landed before the CTA may exit.
+      mbar_wait(q_full, 0, nullptr);
+      for (int st = 0; st < 2; ++st)
+        if (issued & (1u << st)) {
+          mbar_wait(&k_full[st], (parity >> st) & 1u, nullptr);
+          mbar_wait(&v_full[st], (parity >> st) & 1u, nullptr);
+        }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_bf16(BQ, BKV, false);
+      constexpr uint32_t idesc_pv = idesc_bf16(BQ, D, true);
+      bool ok = mbar_wait(q_full, 0, a.err);
+      for (int j = 0; j <= nkv && ok; ++j) {
+        if (j < nkv) {
+          const int st = j & 1;
+          if (!mbar_wait(&k_full[st], (j >> 1) & 1, a.err) ||
+              !mbar_wait(&s_empty[st], ((j >> 1) & 1) ^ 1, a.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t qa = smem_u32(smem + OFF_Q), kb = smem_u32(smem + OFF_K + st * TILE);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * PANEL + (kk & 3) * 32;
+            umma_f16(tS[st], smem_desc_sw128(qa + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), idesc_qk,
+                     kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[st]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1, pb = jj & 1;
+          if (!mbar_wait(&p_full[pb], (jj >> 1) & 1, a.err) || !mbar_wait(&v_full[pb], (jj >> 1) & 1, a.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t pa = smem_u32(smem + OFF_P + pb * TILE), vb = smem_u32(smem + OFF_V + pb * TILE);
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk) {
+            const uint32_t aoff = (kk >> 2) * PANEL + (kk & 3) * 32;
+            umma_f16(tO, smem_desc_sw128(pa + aoff, 16, 1024), smem_desc_sw128(vb + kk * 2048, PANEL, 1024),
+                     idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&pv_done[pb]);
+          umma_commit(&kv_empty[pb]);
+        }
+      }
+      // Retire every issued MMA before TMEM can be released.
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int row = warp * 32 + lane;  // warps 0..3 own TMEM lane quarters 0..3
+    const uint32_t lane_off = uint32_t(warp * 32) << 16;
+    const int q_abs = q0 + row;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv && ok; ++j) {
+      const int sb = j & 1;
+      const bool diag = (j == qt);
+      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, a.err)) { ok = false; break; }
+      tc_fence_after();
+      // pass 1: row max
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tS[sb] + lane_off + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int col = c * 32 + e;
+          const float s = __uint_as_float(r[e]) * a.scale_log2;
+          if (!diag || col <= row) mx = fmaxf(mx, s);
+        }
+      }
+      const bool rescale = mx > m_ref + kRescaleThreshold;
+      const float m_use = rescale ? mx : m_ref;
+      // P buffer sb was last read by PV_{j-2}.
+      if (j >= 2 && !mbar_wait(&pv_done[sb], ((j - 2) >> 1) & 1, a.err)) { ok = false; break; }
+      // pass 2: probabilities -> bf16 P (128-byte swizzled, K-major over keys)
+      float rsum = 0.f;
+      uint8_t* pbase = smem + OFF_P + sb * TILE;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tS[sb] + lane_off + c * 32, r);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int col = c * 32 + 2 * e;
+          float p0 = exp2f(__uint_as_float(r[2 * e]) * a.scale_log2 - m_use);
+          float p1 = exp2f(__uint_as_float(r[2 * e + 1]) * a.scale_log2 - m_use);
+          if (diag && col > row) p0 = 0.f;
+          if (diag && col + 1 > row) p1 = 0.f;
+          rsum += p0 + p1;
+          pk[e] = pack_bf16x2(p0, p1);
+        }
+        uint8_t* panel = pbase + (c >> 1) * PANEL + row * 128;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const int chunk = (c & 1) * 4 + v;  // 16-byte chunk within the 128-byte row
+          *reinterpret_cast<uint4*>(panel + ((chunk ^ (row & 7)) << 4)) =
+              make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&s_empty[sb]);
+      if (rescale) {
+        if (j > 0) {
+          const float f = exp2f(m_ref - mx);
+          if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, a.err)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tO + lane_off + c * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * f);
+            tmem_st32(tO + lane_off + c * 32, r);
+          }
+          tmem_wait_st();
+          l *= f;
+        }
+        m_ref = mx;
+      }
+      l += rsum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[sb]);
+    }
+    if (ok) {
+      const int last = nkv - 1;
+      if (mbar_wait(&pv_done[last & 1], (last >> 1) & 1, a.err)) {
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.0f / l : 0.f;
+        bf16* orow = a.out + int64_t(q_abs) * a.ldo + int64_t(h) * D;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tO + lane_off + c * 32, r);
+          tmem_wait_ld();
+          if (q_abs < a.T) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 o;
+              o.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * inv, __uint_as_float(r[8 * v + 1]) * inv);
+              o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv);
+              o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv);
+              o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv);
+              *reinterpret_cast<uint4*>(orow + c * 32 + v * 8) = o;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc<kTmemCols>(tmem);
+  }
+}
+
+}  // namespace
+
+void flash_prefill(torch::Tensor qkv, int64_t Hq, int64_t Hkv, double scale, torch::Tensor out, torch::Tensor err) {
+  KVS_CHECK_ARG(qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 2 && qkv.stride(1) == 1,
+                "flash_prefill: qkv [T, (Hq+2Hkv)*128] bf16");
+  KVS_CHECK_ARG(qkv.size(1) == (Hq + 2 * Hkv) * D && Hq % Hkv == 0, "flash_prefill: head_dim 128 only");
+  KVS_CHECK_ARG(out.dim() == 2 && out.size(0) == qkv.size(0) && out.size(1) == Hq * D && out.stride(1) == 1 &&
+                    out.stride(0) % 8 == 0,
+                "flash_prefill: out [T, Hq*128]");
+  const int T = int(qkv.size(0));
+  if (T == 0) return;
+  AttnArgs a{};
+  a.out = reinterpret_cast<bf16*>(out.data_ptr());
+  a.ldo = out.stride(0);
+  a.T = T;
+  a.Hq = int(Hq);
+  a.Hkv = int(Hkv);
+  a.scale_log2 = float(scale) * 1.4426950408889634f;
+  a.err = reinterpret_cast<uint32_t*>(err.data_ptr<int32_t>());
+  const CUtensorMap tm =
+      make_tmap_2d_bf16(qkv.data_ptr(), uint64_t(qkv.size(1)), uint64_t(T), uint64_t(qkv.stride(0)) * 2, 64, 128);
+  static bool attr = false;
+  if (!attr) {
+    KVS_CUDA_CHECK(cudaFuncSetAttribute(flash_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    attr = true;
+  }
+  dim3 grid(int(Hq), (T + BQ - 1) / BQ);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  flash_prefill_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(tm, a);
+  KVS_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace kvs

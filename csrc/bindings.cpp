@@ -1,0 +1,41 @@
+// Python bindings of the kvserve_b200 sm_100a extension.  Every op runs on
+// the caller's current CUDA stream and does no host synchronisation, so the
+// ops can be captured in CUDA graphs.
+#include <torch/extension.h>
+
+#include "ops.h"
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "kvserve_b200 sm_100a kernels";
+  // fused KV transfer codec
+  m.def("kv_frame_geom", &kvs::kv_frame_geom);
+  m.def("kv_encode_layer", &kvs::kv_encode_layer);
+  m.def("kv_decode_layers", &kvs::kv_decode_layers);
+  // modular pipeline kernels
+  m.def("bitpack_encode", &kvs::bitpack_encode);
+  m.def("bitpack_decode", &kvs::bitpack_decode);
+  m.def("fwht_rows", &kvs::fwht_rows);
+  // peer memory
+  m.def("dev_alloc", &kvs::dev_alloc);
+  m.def("dev_free", &kvs::dev_free);
+  m.def("ipc_get_handle", [](int64_t p) { return pybind11::bytes(kvs::ipc_get_handle(p)); });
+  m.def("ipc_open_handle", [](pybind11::bytes b) { return kvs::ipc_open_handle(std::string(b)); });
+  m.def("ipc_close", &kvs::ipc_close);
+  m.def("can_access_peer", &kvs::can_access_peer);
+  m.def("tensor_from_ptr", &kvs::tensor_from_ptr);
+  m.def("fill_u32", &kvs::fill_u32);
+  m.def("read_u32", &kvs::read_u32);
+  m.def("store_release_u32", &kvs::store_release_u32);
+  m.def("wait_flag", &kvs::wait_flag);
+  // engine
+  m.def("rmsnorm", &kvs::rmsnorm);
+  m.def("rope_qkv", &kvs::rope_qkv);
+  m.def("silu_mul", &kvs::silu_mul);
+  m.def("embedding", &kvs::embedding);
+  m.def("argmax_rows", &kvs::argmax_rows);
+  m.def("gemm_bf16", &kvs::gemm_bf16);
+  m.def("gemv_bf16", &kvs::gemv_bf16);
+  m.def("flash_prefill", &kvs::flash_prefill);
+  m.def("paged_decode_splits", &kvs::paged_decode_splits);
+  m.def("paged_decode_attention", &kvs::paged_decode_attention);
+}

@@ -1,0 +1,287 @@
+// Persistent, warp-specialised bf16 GEMM on the 5th-generation tensor cores:
+//   C[M, N] = A[M, K] * B[N, K]^T  (+ R[M, N])          (fp32 accumulate)
+// A = activations (row-major, K contiguous), B = nn.Linear weight [out, in].
+//
+//   warp 0      TMA producer (one lane): 128x64 A and 256x64 B tiles with
+//               128-byte swizzle into a 4-stage shared-memory ring.
+//   warp 1      MMA issuer (one lane): tcgen05.mma M=128 N=256 K=16 into a
+//               double-buffered TMEM accumulator (2 x 256 columns).
+//   warps 2..5  epilogue: tcgen05.ld 32x32b -> bf16 -> global, overlapped
+//               with the next tile's main loop.
+// One CTA per SM, grid = min(tiles, #SMs), tiles rastered n-fastest.
+// No cluster multicast is used anywhere (this kernel may run in multi-GPU
+// processes).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "ops.h"
+#include "sm100.cuh"
+
+namespace kvs {
+
+namespace {
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;   // 16 KB
+constexpr int B_BYTES = BN * BK * 2;   // 32 KB
+constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+
+struct GemmArgs {
+  bf16* C;
+  const bf16* R;
+  int M, N, K;
+  int64_t ldc, ldr;
+  uint32_t* err;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        GemmArgs p) {
+  using namespace sm100;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * (A_BYTES + B_BYTES));
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;      // [0,2): accumulator full; [2]: abort drain
+  uint64_t* tempty = tfull + 3;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  __shared__ int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(&tfull[2], 1);
+    s_abort = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc<kTmemCols>(tmem_slot);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + BN - 1) / BN;
+  const int tiles = num_m * num_n;
+  const int kblocks = (p.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      uint32_t issued_mask = 0, issued_parity = 0;  // per stage: load issued / its phase parity
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        const int mb = tile / num_n, nb = tile % num_n;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          tma_load_2d(sA + stage * A_BYTES, &tmA, kb * BK, mb * BM, &full[stage]);
+          tma_load_2d(sB + stage * B_BYTES, &tmB, kb * BK, nb * BN, &full[stage]);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {
+        // Abort: wait (bounded) until every issued copy has landed so that no
+        // TMA write targets this CTA's shared memory after it exits.
+        s_abort = 1;
+        for (int i = 0; i < STAGES; ++i)
+          if (issued_mask & (1u << i)) mbar_wait(&full[i], (issued_parity >> i) & 1u, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = smem_desc_sw128(a0 + kk * 32, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(b0 + kk * 32, 16, 1024);
+            umma_f16(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+      if (!ok) {
+        // Abort: make sure every issued MMA has retired before TMEM is freed.
+        s_abort = 1;
+        umma_commit(&tfull[2]);
+        mbar_wait(&tfull[2], 0, nullptr);
+      }
+    }
+  } else {
+    // Epilogue warps 2..5: TMEM lane quarter = warp % 4.
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      const int mb = tile / num_n, nb = tile % num_n;
+      if (!mbar_wait(&tfull[acc], acc_phase, p.err)) break;
+      tc_fence_after();
+      const int row = mb * BM + row_in_tile;
+      const bool row_ok = row < p.M;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN + c * 32), r);
+        tmem_wait_ld();
+        const int col0 = nb * BN + c * 32;
+        if (row_ok) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const int col = col0 + v * 8;
+            if (col >= p.N) break;
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[v * 8 + e]);
+            if (p.R) {
+              const uint4 rr = *reinterpret_cast<const uint4*>(p.R + int64_t(row) * p.ldr + col);
+              const __nv_bfloat162* rh = reinterpret_cast<const __nv_bfloat162*>(&rr);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 x = __bfloat1622float2(rh[e]);
+                f[2 * e] += x.x;
+                f[2 * e + 1] += x.y;
+              }
+            }
+            uint4 o;
+            __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) oh[e] = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
+            *reinterpret_cast<uint4*>(p.C + int64_t(row) * p.ldc + col) = o;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<kTmemCols>(tmem_base);
+  }
+}
+
+using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+EncodeFn get_encode_fn() {
+  static EncodeFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    KVS_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q));
+    KVS_CHECK_ARG(q == cudaDriverEntryPointSuccess && ptr != nullptr, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<EncodeFn>(ptr);
+  }
+  return fn;
+}
+
+}  // namespace
+
+CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                              uint32_t box_inner, uint32_t box_outer) {
+  KVS_CHECK_ARG((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
+  KVS_CHECK_ARG(row_stride_bytes % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  KVS_CHECK_ARG(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+  return m;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    KVS_CUDA_CHECK(cudaGetDevice(&dev));
+    KVS_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  }
+  return n;
+}
+
+void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, c10::optional<torch::Tensor> residual,
+               torch::Tensor err) {
+  KVS_CHECK_ARG(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: CUDA tensors");
+  KVS_CHECK_ARG(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 &&
+                    c.scalar_type() == at::kBFloat16,
+                "gemm: bf16 operands");
+  KVS_CHECK_ARG(a.dim() == 2 && b.dim() == 2 && c.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1 &&
+                    c.stride(1) == 1,
+                "gemm: 2-D row-major operands");
+  const int M = int(a.size(0)), K = int(a.size(1)), N = int(b.size(0));
+  KVS_CHECK_ARG(b.size(1) == K && c.size(0) == M && c.size(1) == N, "gemm: shape mismatch");
+  KVS_CHECK_ARG(K % 8 == 0 && N % 8 == 0 && a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0 && c.stride(0) % 8 == 0,
+                "gemm: K, N and leading dims must be multiples of 8");
+  if (M == 0 || N == 0) return;
+  GemmArgs p{};
+  p.C = reinterpret_cast<bf16*>(c.data_ptr());
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = c.stride(0);
+  p.R = nullptr;
+  p.ldr = 0;
+  if (residual.has_value()) {
+    KVS_CHECK_ARG(residual->sizes() == c.sizes() && residual->stride(1) == 1 && residual->stride(0) % 8 == 0,
+                  "gemm: residual shape");
+    p.R = reinterpret_cast<const bf16*>(residual->data_ptr());
+    p.ldr = residual->stride(0);
+  }
+  p.err = reinterpret_cast<uint32_t*>(err.data_ptr<int32_t>());
+  const CUtensorMap ta = make_tmap_2d_bf16(a.data_ptr(), K, M, uint64_t(a.stride(0)) * 2, BK, BM);
+  const CUtensorMap tb = make_tmap_2d_bf16(b.data_ptr(), K, N, uint64_t(b.stride(0)) * 2, BK, BN);
+  static bool attr_set = false;
+  if (!attr_set) {
+    KVS_CUDA_CHECK(cudaFuncSetAttribute(gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        SMEM_BYTES));
+    attr_set = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = std::min(tiles, num_sms());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  gemm_bf16_tn_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(ta, tb, p);
+  KVS_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace kvs

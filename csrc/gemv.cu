@@ -1,0 +1,171 @@
+// Decode-step (small M) bf16 GEMM: y[M, N] = x[M, K] * W[N, K]^T, M <= 8.
+// Weight streaming is the whole cost, so each warp owns ROWS output rows and
+// keeps ROWS x UNROLL independent 16-byte weight loads in flight; x lives in
+// shared memory (bf16, 16-byte loads).  Used for every projection of a decode step and for
+// the LM head (where the tcgen05 tile kernel would leave SMs idle).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+
+#include "common.cuh"
+#include "ops.h"
+
+namespace kvs {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kRows = 2;  // output rows per warp
+
+__device__ __forceinline__ void load_x8(const bf16* p, float (&f)[8]) {
+  const uint4 v = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 t = __bfloat1622float2(h[e]);
+    f[2 * e] = t.x;
+    f[2 * e + 1] = t.y;
+  }
+}
+__device__ __forceinline__ float dot8(const uint4& w, const float (&x)[8], float acc) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 t = __bfloat1622float2(h[e]);
+    acc = fmaf(t.x, x[2 * e], acc);
+    acc = fmaf(t.y, x[2 * e + 1], acc);
+  }
+  return acc;
+}
+
+template <int M>
+__global__ void __launch_bounds__(kThreads) gemv_kernel(const bf16* __restrict__ x, int64_t ldx,
+                                                        const bf16* __restrict__ w, int64_t ldw,
+                                                        bf16* __restrict__ y, int64_t ldy, int N, int K) {
+  extern __shared__ uint4 xs_raw[];  // [M][K] bf16
+  bf16* xs = reinterpret_cast<bf16*>(xs_raw);
+  for (int i = threadIdx.x; i < M * K / 8; i += kThreads) {
+    const int m = i / (K / 8), k8 = i % (K / 8);
+    xs_raw[i] = *reinterpret_cast<const uint4*>(x + int64_t(m) * ldx + k8 * 8);
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = (blockIdx.x * (kThreads / 32) + warp) * kRows;
+  if (row0 >= N) return;
+  float acc[kRows][M];
+#pragma unroll
+  for (int r = 0; r < kRows; ++r)
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[r][m] = 0.f;
+  const int kvec = K / 8;
+  constexpr int U = 4;
+  int kv = lane;
+  for (; kv + 32 * (U - 1) < kvec; kv += 32 * U) {
+    uint4 wv[kRows][U];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int row = min(row0 + r, N - 1);
+        wv[r][u] = __ldcs(reinterpret_cast<const uint4*>(w + int64_t(row) * ldw) + kv + 32 * u);
+      }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int k = (kv + 32 * u) * 8;
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        float xf[8];
+        load_x8(xs + m * K + k, xf);
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) acc[r][m] = dot8(wv[r][u], xf, acc[r][m]);
+      }
+    }
+  }
+  for (; kv < kvec; kv += 32) {
+    const int k = kv * 8;
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      const int row = min(row0 + r, N - 1);
+      const uint4 wv = __ldcs(reinterpret_cast<const uint4*>(w + int64_t(row) * ldw) + kv);
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        float xf[8];
+        load_x8(xs + m * K + k, xf);
+        acc[r][m] = dot8(wv, xf, acc[r][m]);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kRows; ++r)
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      float v = acc[r][m];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      acc[r][m] = v;
+    }
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      if (row0 + r >= N) break;
+#pragma unroll
+      for (int m = 0; m < M; ++m) y[int64_t(m) * ldy + row0 + r] = rn(acc[r][m]);
+    }
+  }
+}
+
+}  // namespace
+
+void gemv_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y) {
+  KVS_CHECK_ARG(x.is_cuda() && w.is_cuda() && y.is_cuda() && x.scalar_type() == at::kBFloat16 &&
+                    w.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16,
+                "gemv: CUDA bf16");
+  KVS_CHECK_ARG(x.dim() == 2 && w.dim() == 2 && y.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1 &&
+                    y.stride(1) == 1,
+                "gemv: row-major 2-D operands");
+  const int M = int(x.size(0)), K = int(x.size(1)), N = int(w.size(0));
+  KVS_CHECK_ARG(w.size(1) == K && y.size(0) == M && y.size(1) == N, "gemv: shape mismatch");
+  KVS_CHECK_ARG(M >= 1 && M <= 8, "gemv: 1 <= M <= 8");
+  KVS_CHECK_ARG(K % 8 == 0 && w.stride(0) % 8 == 0, "gemv: K must be a multiple of 8");
+  KVS_CHECK_ARG(x.stride(0) % 8 == 0 && y.stride(0) % 8 == 0, "gemv: leading dims must be multiples of 8");
+  KVS_CHECK_ARG(size_t(K) * 2 <= 200 * 1024, "gemv: K too large");
+  // Rows of x are staged in shared memory; split M when they do not fit.
+  const int max_rows = int(std::min<size_t>(8, (200 * 1024) / (size_t(K) * 2)));
+  if (M > max_rows) {
+    for (int m0 = 0; m0 < M; m0 += max_rows) {
+      const int mm = std::min(max_rows, M - m0);
+      gemv_bf16(x.narrow(0, m0, mm), w, y.narrow(0, m0, mm));
+    }
+    return;
+  }
+  const int rows_per_cta = (kThreads / 32) * kRows;
+  const int grid = (N + rows_per_cta - 1) / rows_per_cta;
+  const size_t smem = size_t(M) * K * 2;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  auto xp = reinterpret_cast<const bf16*>(x.data_ptr());
+  auto wp = reinterpret_cast<const bf16*>(w.data_ptr());
+  auto yp = reinterpret_cast<bf16*>(y.data_ptr());
+#define KVS_GEMV_CASE(MM)                                                                                  \
+  case MM: {                                                                                               \
+    static bool set = false;                                                                               \
+    if (!set) {                                                                                            \
+      KVS_CUDA_CHECK(cudaFuncSetAttribute(gemv_kernel<MM>, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
+                                          200 * 1024));                                                    \
+      set = true;                                                                                          \
+    }                                                                                                      \
+    gemv_kernel<MM><<<grid, kThreads, smem, st>>>(xp, x.stride(0), wp, w.stride(0), yp, y.stride(0), N, K); \
+    break;                                                                                                 \
+  }
+  switch (M) {
+    KVS_GEMV_CASE(1)
+    KVS_GEMV_CASE(2)
+    KVS_GEMV_CASE(3)
+    KVS_GEMV_CASE(4)
+    KVS_GEMV_CASE(5)
+    KVS_GEMV_CASE(6)
+    KVS_GEMV_CASE(7)
+    KVS_GEMV_CASE(8)
+  }
+#undef KVS_GEMV_CASE
+  KVS_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace kvs

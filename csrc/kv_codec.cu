@@ -1,0 +1,772 @@
+// Fused KV-transfer kernels for sm_100a: the product hot path of the
+// prefill -> decode KV hand-off.
+//
+// Prefill side (per layer, per request, per TP shard):
+//   kv_kstats  : random-sign Hadamard (register FWHT) of K + per-channel
+//                min/max over all tokens (ordered-uint atomics).
+//   kv_quant   : K: sign+FWHT again, per-channel min-max quantisation,
+//                bit-pack, store;  V: sign+FWHT, per-token per-section
+//                min-max quantisation, bit-pack, store.  Stores go straight
+//                into the decode GPU's receive slot (a CUDA-IPC peer
+//                pointer over NVLink 5) or into a local slot.  The last CTA
+//                publishes the frame with a system-scope release store of
+//                the request sequence number into the peer's flag word.
+// Decode side:
+//   kv_decode  : (optionally persistent over all layers) bounded acquire-wait
+//                on the layer flag, unpack, dequantise, inverse FWHT, sign,
+//                and scatter straight into the paged KV cache blocks.
+//
+// Reference behaviour covered (re-designed, not translated):
+//   Hadamard with Rademacher signs  kvserve_v1/compression/transformer/hadamard_func.py:105-231
+//   hybrid min-max quantiser        kvserve_v1/compression/quantizer/kvserve_quantizer.py:171-294
+//   fused K/V encode + restore      kvserve_v1/compression/runtime/csrc/fused/kvs_fused.cu:126-388
+//   BitPack payload format          kvserve_v1/compression/codec/bitpack_codec.py:20-48
+//
+// Numerics of this path (own design): the transform is computed in fp32
+// (one rounding to bf16 at the end of decode), statistics in fp32, stored
+// parameters are bf16 (min, scale), symbols are clamp(rint((y-min)/scale),
+// 0, levels-1) so every symbol fits the section's bit width.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+
+#include "common.cuh"
+#include "kv_frame.h"
+#include "ops.h"
+
+namespace kvs {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxRowIters = 8;  // H*D <= 2048 for the fused path
+
+struct EncodeArgs {
+  const bf16* k;
+  const bf16* v;
+  int64_t k_tok_stride, k_head_stride;
+  int64_t v_tok_stride, v_head_stride;
+  FrameGeom g;
+  const int32_t* order;       // [H] section order -> original head
+  const uint32_t* sign_bits;  // [H_orig][D/32], bit set = negative
+  uint8_t* frame;             // frame base (local or peer)
+  uint32_t* stats;            // [2*H*D] ordered min | max (section order)
+  uint32_t* counter;          // CTA completion counter
+  uint32_t* flag;             // publish word (local or peer), may be null
+  uint32_t seq;
+  uint32_t layer;
+  int64_t* pacing;            // [1] next free time (ns) of the emulated link
+  double rate_bytes_per_ns;   // 0 = no link emulation
+  int tile_tokens;
+};
+
+struct DecodeArgs {
+  const uint8_t* frame_base;
+  int64_t frame_stride;
+  FrameGeom g;
+  const int32_t* orders;      // [L][H]
+  const uint32_t* sign_bits;  // [L][H][D/32]
+  bf16* cache;                // [L][2][nb][bs][H][D] (strided)
+  int64_t layer_stride, part_stride, block_stride, token_stride, head_stride;
+  const int32_t* block_table;
+  int block_size;
+  int tok_offset;
+  const uint32_t* flags;      // [L] or null (stream-ordered, no wait)
+  uint32_t seq;
+  int layer_begin;
+  int num_layers;
+  int num_layers_total;
+  uint64_t timeout_ns;
+  uint32_t* status;
+  int tile_tokens;
+};
+
+__device__ __forceinline__ void load8(const bf16* p, float (&v)[8], uint4& raw) {
+  raw = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// 1/sqrt(D) as an exactly rounded fp32 constant.
+template <int D>
+__device__ __forceinline__ constexpr float inv_sqrt_d() {
+  return D == 64 ? 0.125f : (D == 128 ? 0.0883883476483184405f : 0.0625f);
+}
+
+__device__ __forceinline__ uint32_t sign_byte(const uint32_t* row_bits, int lir) {
+  const int bit = lir * 8;
+  return (row_bits[bit >> 5] >> (bit & 31)) & 0xffu;
+}
+
+__device__ __forceinline__ void apply_signs(float (&v)[8], uint32_t sb) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    if ((sb >> e) & 1u) v[e] = -v[e];
+}
+
+// Natural-order (Sylvester) Walsh-Hadamard transform of a row of D = 8*LANES
+// values spread over LANES consecutive lanes (8 values per lane).
+template <int LANES>
+__device__ __forceinline__ void fwht_row(float (&v)[8], int lir) {
+#pragma unroll
+  for (int s = 1; s < 8; s <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if ((i & s) == 0) {
+        const float a = v[i], b = v[i + s];
+        v[i] = a + b;
+        v[i + s] = a - b;
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 1; m < LANES; m <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float o = __shfl_xor_sync(0xffffffffu, v[i], m);
+      v[i] = (lir & m) ? (o - v[i]) : (v[i] + o);
+    }
+  }
+}
+
+__device__ __forceinline__ void store_packed(uint8_t* dst, uint64_t acc, int bits) {
+  switch (bits) {
+    case 8: *reinterpret_cast<uint2*>(dst) = make_uint2(uint32_t(acc), uint32_t(acc >> 32)); break;
+    case 4: *reinterpret_cast<uint32_t*>(dst) = uint32_t(acc); break;
+    case 2: *reinterpret_cast<uint16_t*>(dst) = uint16_t(acc); break;
+    case 1: *dst = uint8_t(acc); break;
+    default:
+      for (int i = 0; i < bits; ++i) dst[i] = uint8_t(acc >> (8 * i));
+  }
+}
+
+__device__ __forceinline__ uint64_t load_packed(const uint8_t* src, int bits) {
+  switch (bits) {
+    case 8: {
+      uint2 u = __ldcg(reinterpret_cast<const uint2*>(src));
+      return uint64_t(u.x) | (uint64_t(u.y) << 32);
+    }
+    case 4: return __ldcg(reinterpret_cast<const unsigned int*>(src));
+    case 2: return __ldcg(reinterpret_cast<const unsigned short*>(src));
+    case 1: return __ldcg(reinterpret_cast<const unsigned char*>(src));
+    default: {
+      uint64_t acc = 0;
+      for (int i = 0; i < bits; ++i)
+        acc |= uint64_t(__ldcg(reinterpret_cast<const unsigned char*>(src + i))) << (8 * i);
+      return acc;
+    }
+  }
+}
+
+__device__ __forceinline__ uint64_t quant_pack8(const float (&y)[8], float mn, float inv,
+                                                int levels, int bits) {
+  uint64_t acc = 0;
+  const float top = float(levels - 1);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    float q = rintf((y[e] - mn) * inv);
+    q = fminf(fmaxf(q, 0.0f), top);
+    acc |= uint64_t(uint32_t(q)) << (e * bits);
+  }
+  return acc;
+}
+
+// Section of head slot j and its index inside the section.
+__device__ __forceinline__ void slot_section(const FrameGeom& g, int j, int& s, int& js, int& hs) {
+  s = j < g.n_low ? 0 : 1;
+  js = s ? j - g.n_low : j;
+  hs = s ? g.H - g.n_low : g.n_low;
+}
+
+__device__ __forceinline__ void write_bitpack_header(uint8_t* dst, int bits, uint64_t count) {
+  uint32_t w[4];
+  w[0] = kBitpackMagic;
+  w[1] = uint32_t(bits);
+  w[2] = uint32_t(count);
+  w[3] = uint32_t(count >> 32);
+  *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// ---------------------------------------------------------------------------
+// K statistics: per (section-order head slot, channel) min and max of the
+// transformed keys over every token.
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(kThreads) kv_kstats_kernel(EncodeArgs a) {
+  constexpr int LANES = D / 8, RPW = 32 / LANES;
+  constexpr int kRowsPerIter = (kThreads / 32) * RPW;
+  extern __shared__ uint32_t sstat[];  // [2*H*D]
+  const FrameGeom& g = a.g;
+  const int HD = g.H * D;
+  for (int i = threadIdx.x; i < 2 * HD; i += kThreads) sstat[i] = i < HD ? 0xffffffffu : 0u;
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lir = lane % LANES, rw = lane / LANES;
+  const float scale = inv_sqrt_d<D>();
+  const bool fixed_slot = (kRowsPerIter % g.H) == 0;
+  float mn[8], mx[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) { mn[e] = INFINITY; mx[e] = -INFINITY; }
+  const int ntiles = int(ceil_div(g.T, a.tile_tokens));
+  int my_slot = -1;
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int t0 = tile * a.tile_tokens;
+    const int t1 = min(g.T, t0 + a.tile_tokens);
+    const int nrows = (t1 - t0) * g.H;
+    for (int base = 0; base < nrows; base += kRowsPerIter) {
+      const int r = base + warp * RPW + rw;
+      const bool valid = r < nrows;
+      const int t = t0 + r / g.H, j = r % g.H;
+      float v[8];
+      if (valid) {
+        const int h = a.order[j];
+        uint4 raw;
+        load8(a.k + t * a.k_tok_stride + h * a.k_head_stride + lir * 8, v, raw);
+        apply_signs(v, sign_byte(a.sign_bits + h * (D / 32), lir));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = 0.f;
+      }
+      fwht_row<LANES>(v, lir);
+      if (!valid) continue;
+      int s, js, hs;
+      slot_section(g, j, s, js, hs);
+      if (g.bits[0][s] == kRawBits) continue;
+      if (fixed_slot) {
+        my_slot = j;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          mn[e] = fminf(mn[e], v[e] * scale);
+          mx[e] = fmaxf(mx[e], v[e] * scale);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          atomicMin(&sstat[j * D + lir * 8 + e], float_to_ordered(v[e] * scale));
+          atomicMax(&sstat[HD + j * D + lir * 8 + e], float_to_ordered(v[e] * scale));
+        }
+      }
+    }
+  }
+  if (fixed_slot && my_slot >= 0) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      atomicMin(&sstat[my_slot * D + lir * 8 + e], float_to_ordered(mn[e]));
+      atomicMax(&sstat[HD + my_slot * D + lir * 8 + e], float_to_ordered(mx[e]));
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < HD; i += kThreads) {
+    if (sstat[i] != 0xffffffffu) atomicMin(&a.stats[i], sstat[i]);
+    if (sstat[HD + i] != 0u) atomicMax(&a.stats[HD + i], sstat[HD + i]);
+  }
+}
+
+// Completion: every CTA fences its stores system-wide, the last CTA resets
+// the statistics, writes the frame header, optionally waits out the
+// emulated link time, and publishes the frame with a release store.
+__device__ void encode_signal_done(const EncodeArgs& a) {
+  __shared__ int s_last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t total = gridDim.x * gridDim.y;
+    s_last = (atomicAdd(a.counter, 1u) == total - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  const int HD = a.g.H * a.g.D;
+  for (int i = threadIdx.x; i < 2 * HD; i += blockDim.x) a.stats[i] = i < HD ? 0xffffffffu : 0u;
+  if (threadIdx.x == 0) {
+    FrameHeader h;
+    h.magic = kFrameMagic;
+    h.version = 1;
+    h.layer = a.layer;
+    h.tokens = uint32_t(a.g.T);
+    h.heads = uint32_t(a.g.H);
+    h.head_dim = uint32_t(a.g.D);
+    h.n_low = uint32_t(a.g.n_low);
+    h.seq = a.seq;
+    for (int p = 0; p < 2; ++p)
+      for (int s = 0; s < 2; ++s) {
+        h.bits[p][s] = uint8_t(a.g.bits[p][s]);
+        h.levels[p][s] = uint8_t(a.g.levels[p][s] - 1);
+      }
+    for (int i = 0; i < 6; ++i) h.reserved[i] = 0;
+    const uint4* src = reinterpret_cast<const uint4*>(&h);
+    uint4* dst = reinterpret_cast<uint4*>(a.frame);
+    for (int i = 0; i < 4; ++i) dst[i] = src[i];
+    if (a.pacing != nullptr && a.rate_bytes_per_ns > 0.0) {
+      // Emulated serial link: this frame occupies the link for
+      // frame_bytes / rate after the later of "now" and the link's free time.
+      const int64_t now = int64_t(globaltimer_ns());
+      const int64_t start = max(now, a.pacing[0]);
+      const int64_t done = start + int64_t(double(a.g.frame_bytes) / a.rate_bytes_per_ns);
+      a.pacing[0] = done;
+      const uint64_t cap = 20ull * 1000 * 1000 * 1000;  // hard bound: 20 s
+      const uint64_t t_begin = globaltimer_ns();
+      while (int64_t(globaltimer_ns()) < done && globaltimer_ns() - t_begin < cap) __nanosleep(2000);
+    }
+    *a.counter = 0;
+    __threadfence_system();
+    if (a.flag != nullptr) st_release_sys_u32(a.flag, a.seq);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
+  constexpr int LANES = D / 8, RPW = 32 / LANES;
+  constexpr int kWarps = kThreads / 32;
+  constexpr int kRowsPerIter = kWarps * RPW;
+  extern __shared__ float sparam[];  // K: min[HD], inv[HD]
+  const FrameGeom& g = a.g;
+  const int HD = g.H * D;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lir = lane % LANES, rw = lane / LANES;
+  const float scale = inv_sqrt_d<D>();
+  const int ntiles = int(ceil_div(g.T, a.tile_tokens));
+  const int part = blockIdx.y;
+
+  if (part == 0) {
+    // ---- K: per-channel parameters from the global statistics ----
+    bf16* kmin = reinterpret_cast<bf16*>(a.frame + g.k_aux);
+    bf16* kscl = kmin + HD;
+    for (int c = threadIdx.x; c < HD; c += kThreads) {
+      int s, js, hs;
+      slot_section(g, c / D, s, js, hs);
+      if (g.bits[0][s] == kRawBits) continue;
+      const float lo = ordered_to_float(a.stats[c]);
+      const float hi = ordered_to_float(a.stats[HD + c]);
+      const bf16 minb = rn(lo);
+      const bf16 sclb = rn(fmaxf(hi - to_f32(minb), 1e-5f) / float(g.levels[0][s] - 1));
+      sparam[c] = to_f32(minb);
+      sparam[HD + c] = 1.0f / to_f32(sclb);
+      if (blockIdx.x == 0) {
+        kmin[c] = minb;
+        kscl[c] = sclb;
+      }
+    }
+    if (blockIdx.x == 0 && threadIdx.x < 2) {
+      const int s = threadIdx.x;
+      if (section_heads(g, s) > 0 && g.bits[0][s] != kRawBits)
+        write_bitpack_header(a.frame + g.payload[0][s], g.bits[0][s],
+                             uint64_t(g.T) * section_heads(g, s) * D);
+    }
+    __syncthreads();
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      const int t0 = tile * a.tile_tokens;
+      const int t1 = min(g.T, t0 + a.tile_tokens);
+      const int nrows = (t1 - t0) * g.H;
+      for (int base = 0; base < nrows; base += kRowsPerIter) {
+        const int r = base + warp * RPW + rw;
+        const bool valid = r < nrows;
+        const int t = t0 + r / g.H, j = r % g.H;
+        float v[8];
+        uint4 raw = make_uint4(0, 0, 0, 0);
+        if (valid) {
+          const int h = a.order[j];
+          load8(a.k + t * a.k_tok_stride + h * a.k_head_stride + lir * 8, v, raw);
+          apply_signs(v, sign_byte(a.sign_bits + h * (D / 32), lir));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = 0.f;
+        }
+        fwht_row<LANES>(v, lir);
+        if (!valid) continue;
+        int s, js, hs;
+        slot_section(g, j, s, js, hs);
+        const int bits = g.bits[0][s];
+        const int64_t sym = (int64_t(t) * hs + js) * D + lir * 8;
+        if (bits == kRawBits) {
+          *reinterpret_cast<uint4*>(a.frame + g.payload[0][s] + sym * 2) = raw;
+          continue;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] *= scale;
+        // Per-channel parameters differ per element: quantise one by one.
+        uint64_t acc = 0;
+        const float top = float(g.levels[0][s] - 1);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int c = j * D + lir * 8 + e;
+          float q = rintf((v[e] - sparam[c]) * sparam[HD + c]);
+          q = fminf(fmaxf(q, 0.0f), top);
+          acc |= uint64_t(uint32_t(q)) << (e * bits);
+        }
+        store_packed(a.frame + g.payload[0][s] + 16 + sym * bits / 8, acc, bits);
+      }
+    }
+  } else {
+    // ---- V: one warp per token; per-token, per-section statistics ----
+    if (blockIdx.x == 0 && threadIdx.x < 2) {
+      const int s = threadIdx.x;
+      if (section_heads(g, s) > 0 && g.bits[1][s] != kRawBits)
+        write_bitpack_header(a.frame + g.payload[1][s], g.bits[1][s],
+                             uint64_t(g.T) * section_heads(g, s) * D);
+    }
+    const int iters = (g.H + RPW - 1) / RPW;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      const int t0 = tile * a.tile_tokens;
+      const int t1 = min(g.T, t0 + a.tile_tokens);
+      for (int t = t0 + warp; t < t1; t += kWarps) {
+        float v[kMaxRowIters][8];
+        uint4 raw[kMaxRowIters];
+        float smin[2] = {INFINITY, INFINITY}, smax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int i = 0; i < kMaxRowIters; ++i) {
+          if (i >= iters) break;
+          const int j = rw + RPW * i;
+          if (j < g.H) {
+            const int h = a.order[j];
+            load8(a.v + t * a.v_tok_stride + h * a.v_head_stride + lir * 8, v[i], raw[i]);
+            apply_signs(v[i], sign_byte(a.sign_bits + h * (D / 32), lir));
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
+          }
+          fwht_row<LANES>(v[i], lir);
+          if (j < g.H) {
+            const int s = j < g.n_low ? 0 : 1;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              v[i][e] *= scale;
+              smin[s] = fminf(smin[s], v[i][e]);
+              smax[s] = fmaxf(smax[s], v[i][e]);
+            }
+          }
+        }
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1) {
+#pragma unroll
+          for (int s = 0; s < 2; ++s) {
+            smin[s] = fminf(smin[s], __shfl_xor_sync(0xffffffffu, smin[s], m));
+            smax[s] = fmaxf(smax[s], __shfl_xor_sync(0xffffffffu, smax[s], m));
+          }
+        }
+        float pmin[2], pinv[2];
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+          pmin[s] = 0.f;
+          pinv[s] = 0.f;
+          if (section_heads(g, s) == 0 || g.bits[1][s] == kRawBits) continue;
+          const bf16 minb = rn(smin[s]);
+          const bf16 sclb = rn(fmaxf(smax[s] - to_f32(minb), 1e-5f) / float(g.levels[1][s] - 1));
+          pmin[s] = to_f32(minb);
+          pinv[s] = 1.0f / to_f32(sclb);
+          if (lane == 0) {
+            bf16* aux = reinterpret_cast<bf16*>(a.frame + g.v_aux[s]);
+            aux[t] = minb;
+            aux[g.T + t] = sclb;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kMaxRowIters; ++i) {
+          if (i >= iters) break;
+          const int j = rw + RPW * i;
+          if (j >= g.H) continue;
+          int s, js, hs;
+          slot_section(g, j, s, js, hs);
+          const int bits = g.bits[1][s];
+          const int64_t sym = (int64_t(t) * hs + js) * D + lir * 8;
+          if (bits == kRawBits) {
+            *reinterpret_cast<uint4*>(a.frame + g.payload[1][s] + sym * 2) = raw[i];
+            continue;
+          }
+          const uint64_t acc = quant_pack8(v[i], pmin[s], pinv[s], g.levels[1][s], bits);
+          store_packed(a.frame + g.payload[1][s] + 16 + sym * bits / 8, acc, bits);
+        }
+      }
+    }
+  }
+  encode_signal_done(a);
+}
+
+// ---------------------------------------------------------------------------
+// Decode: frame -> paged KV cache.
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(kThreads) kv_decode_kernel(DecodeArgs a) {
+  constexpr int LANES = D / 8, RPW = 32 / LANES;
+  constexpr int kRowsPerIter = (kThreads / 32) * RPW;
+  extern __shared__ float sk[];  // K params: min[HD], scale[HD]
+  __shared__ int s_ok;
+  const FrameGeom& g = a.g;
+  const int HD = g.H * D;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lir = lane % LANES, rw = lane / LANES;
+  const float scale = inv_sqrt_d<D>();
+  const int ntiles = int(ceil_div(g.T, a.tile_tokens));
+  const int part = blockIdx.y;
+
+  for (int li = 0; li < a.num_layers; ++li) {
+    const int layer = a.layer_begin + li;
+    const uint8_t* frame = a.frame_base + int64_t(li) * a.frame_stride;
+    if (threadIdx.x == 0) {
+      int ok = 1;
+      if (a.flags != nullptr && !wait_flag_geq(a.flags + layer, a.seq, a.timeout_ns)) {
+        atomicCAS(a.status, 0u, uint32_t(kStatusTimeout));
+        ok = 0;
+      }
+      if (ok) {
+        const FrameHeader* h = reinterpret_cast<const FrameHeader*>(frame);
+        const uint32_t magic = __ldcg(&h->magic), seq = __ldcg(&h->seq);
+        const uint32_t tok = __ldcg(&h->tokens), lay = __ldcg(&h->layer);
+        if (magic != kFrameMagic || seq != a.seq || tok != uint32_t(g.T) || lay != uint32_t(layer)) {
+          atomicCAS(a.status, 0u, uint32_t(kStatusBadHeader));
+          ok = 0;
+        }
+      }
+      s_ok = ok;
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    const int32_t* order = a.orders + int64_t(layer) * g.H;
+    const uint32_t* sbits = a.sign_bits + int64_t(layer) * g.H * (D / 32);
+    bf16* cache = a.cache + int64_t(layer) * a.layer_stride + int64_t(part) * a.part_stride;
+    if (part == 0) {
+      const bf16* kmin = reinterpret_cast<const bf16*>(frame + g.k_aux);
+      for (int c = threadIdx.x; c < HD; c += kThreads) {
+        int s, js, hs;
+        slot_section(g, c / D, s, js, hs);
+        if (g.bits[0][s] == kRawBits) continue;
+        const unsigned short mn = __ldcg(reinterpret_cast<const unsigned short*>(kmin + c));
+        const unsigned short sc = __ldcg(reinterpret_cast<const unsigned short*>(kmin + HD + c));
+        sk[c] = __bfloat162float(__ushort_as_bfloat16(mn));
+        sk[HD + c] = __bfloat162float(__ushort_as_bfloat16(sc));
+      }
+      __syncthreads();
+    }
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      const int t0 = tile * a.tile_tokens;
+      const int t1 = min(g.T, t0 + a.tile_tokens);
+      const int nrows = (t1 - t0) * g.H;
+      for (int base = 0; base < nrows; base += kRowsPerIter) {
+        const int r = base + warp * RPW + rw;
+        const bool valid = r < nrows;
+        const int t = t0 + r / g.H, j = r % g.H;
+        int s = 0, js = 0, hs = 1;
+        if (valid) slot_section(g, j, s, js, hs);
+        const int bits = g.bits[part][s];
+        const int64_t sym = (int64_t(t) * hs + js) * D + lir * 8;
+        const bool raw = valid && bits == kRawBits;
+        // Raw rows and invalid rows skip the transform; the shuffle below
+        // still needs every lane, so the branch is per-row uniform.
+        float v[8];
+        uint4 rawv = make_uint4(0, 0, 0, 0);
+        if (valid && !raw) {
+          const uint64_t acc = load_packed(frame + g.payload[part][s] + 16 + sym * bits / 8, bits);
+          const uint64_t mask = (1ull << bits) - 1ull;
+          if (part == 0) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int c = j * D + lir * 8 + e;
+              v[e] = sk[c] + float((acc >> (e * bits)) & mask) * sk[HD + c];
+            }
+          } else {
+            const bf16* aux = reinterpret_cast<const bf16*>(frame + g.v_aux[s]);
+            const float mn = __bfloat162float(__ushort_as_bfloat16(
+                __ldcg(reinterpret_cast<const unsigned short*>(aux + t))));
+            const float sc = __bfloat162float(__ushort_as_bfloat16(
+                __ldcg(reinterpret_cast<const unsigned short*>(aux + g.T + t))));
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = mn + float((acc >> (e * bits)) & mask) * sc;
+          }
+        } else {
+          if (raw) rawv = __ldcg(reinterpret_cast<const uint4*>(frame + g.payload[part][s] + sym * 2));
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = 0.f;
+        }
+        fwht_row<LANES>(v, lir);
+        if (!valid) continue;
+        const int h = order[j];
+        const int pos = a.tok_offset + t;
+        const int blk = a.block_table[pos / a.block_size];
+        bf16* dst = cache + int64_t(blk) * a.block_stride + int64_t(pos % a.block_size) * a.token_stride +
+                    int64_t(h) * a.head_stride + lir * 8;
+        if (raw) {
+          *reinterpret_cast<uint4*>(dst) = rawv;
+          continue;
+        }
+        const uint32_t sb = sign_byte(sbits + h * (D / 32), lir);
+        uint4 out;
+        __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float x0 = v[2 * i] * scale, x1 = v[2 * i + 1] * scale;
+          if ((sb >> (2 * i)) & 1u) x0 = -x0;
+          if ((sb >> (2 * i + 1)) & 1u) x1 = -x1;
+          o2[i] = __floats2bfloat162_rn(x0, x1);
+        }
+        *reinterpret_cast<uint4*>(dst) = out;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+FrameGeom geom_from(const std::vector<int64_t>& p) {
+  KVS_CHECK_ARG(p.size() == 12, "frame geometry needs 12 integers");
+  FrameGeom g{};
+  g.T = int32_t(p[0]);
+  g.H = int32_t(p[1]);
+  g.D = int32_t(p[2]);
+  g.n_low = int32_t(p[3]);
+  g.bits[0][0] = int32_t(p[4]);
+  g.bits[0][1] = int32_t(p[5]);
+  g.bits[1][0] = int32_t(p[6]);
+  g.bits[1][1] = int32_t(p[7]);
+  g.levels[0][0] = int32_t(p[8]);
+  g.levels[0][1] = int32_t(p[9]);
+  g.levels[1][0] = int32_t(p[10]);
+  g.levels[1][1] = int32_t(p[11]);
+  KVS_CHECK_ARG(g.T >= 0 && g.H >= 1 && g.n_low >= 0 && g.n_low <= g.H, "bad T/H/n_low");
+  KVS_CHECK_ARG(g.D == 64 || g.D == 128 || g.D == 256, "head_dim must be 64, 128 or 256");
+  KVS_CHECK_ARG(g.H * g.D <= 2048, "fused KV codec supports H*D <= 2048 per shard");
+  for (int p2 = 0; p2 < 2; ++p2)
+    for (int s = 0; s < 2; ++s) {
+      const int b = g.bits[p2][s], l = g.levels[p2][s];
+      KVS_CHECK_ARG(b == kRawBits || (b >= 1 && b <= 8), "bits must be 1..8 or 16 (raw)");
+      KVS_CHECK_ARG(b == kRawBits || (l >= 2 && l <= (1 << b)), "levels must be in [2, 2^bits]");
+    }
+  frame_geom_finalize(g);
+  return g;
+}
+
+template <typename Args>
+void launch_kstats(int D, dim3 grid, size_t smem, cudaStream_t st, const Args& a) {
+  switch (D) {
+    case 64: kv_kstats_kernel<64><<<grid, kThreads, smem, st>>>(a); break;
+    case 128: kv_kstats_kernel<128><<<grid, kThreads, smem, st>>>(a); break;
+    case 256: kv_kstats_kernel<256><<<grid, kThreads, smem, st>>>(a); break;
+  }
+}
+
+}  // namespace
+
+std::vector<int64_t> kv_frame_geom(std::vector<int64_t> params) {
+  const FrameGeom g = geom_from(params);
+  return {g.frame_bytes, g.k_aux, g.v_aux[0], g.v_aux[1], g.payload[0][0], g.payload[0][1],
+          g.payload[1][0], g.payload[1][1]};
+}
+
+void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom,
+                     torch::Tensor order, torch::Tensor sign_bits, int64_t frame_ptr,
+                     torch::Tensor stats, torch::Tensor counter, int64_t flag_ptr, int64_t seq,
+                     int64_t layer, c10::optional<torch::Tensor> pacing, double rate_bytes_per_ns,
+                     int64_t max_ctas, int64_t tile_tokens) {
+  const FrameGeom g = geom_from(geom);
+  KVS_CHECK_ARG(k.is_cuda() && v.is_cuda() && k.scalar_type() == at::kBFloat16 &&
+                    v.scalar_type() == at::kBFloat16,
+                "k/v must be CUDA bf16");
+  KVS_CHECK_ARG(k.dim() == 3 && v.dim() == 3 && k.size(0) == g.T && v.size(0) == g.T &&
+                    k.size(2) == g.D && k.stride(2) == 1 && v.stride(2) == 1,
+                "k/v must be [T, H, D] with contiguous D");
+  KVS_CHECK_ARG((reinterpret_cast<uintptr_t>(k.data_ptr()) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(v.data_ptr()) & 15) == 0 && k.stride(0) % 8 == 0 &&
+                    k.stride(1) % 8 == 0 && v.stride(0) % 8 == 0 && v.stride(1) % 8 == 0,
+                "k/v rows must be 16-byte aligned");
+  KVS_CHECK_ARG(order.scalar_type() == at::kInt && order.numel() == g.H && order.is_cuda(), "order: int32[H]");
+  KVS_CHECK_ARG(sign_bits.scalar_type() == at::kInt && sign_bits.is_cuda() &&
+                    sign_bits.numel() >= int64_t(k.size(1)) * g.D / 32,
+                "sign_bits: int32[H_orig, D/32]");
+  KVS_CHECK_ARG(stats.numel() >= 2 * g.H * g.D && counter.numel() >= 1, "stats/counter too small");
+  KVS_CHECK_ARG((frame_ptr & 255) == 0, "frame must be 256-byte aligned");
+  EncodeArgs a{};
+  a.k = reinterpret_cast<const bf16*>(k.data_ptr());
+  a.v = reinterpret_cast<const bf16*>(v.data_ptr());
+  a.k_tok_stride = k.stride(0);
+  a.k_head_stride = k.stride(1);
+  a.v_tok_stride = v.stride(0);
+  a.v_head_stride = v.stride(1);
+  a.g = g;
+  a.order = order.data_ptr<int32_t>();
+  a.sign_bits = reinterpret_cast<const uint32_t*>(sign_bits.data_ptr<int32_t>());
+  a.frame = reinterpret_cast<uint8_t*>(frame_ptr);
+  a.stats = reinterpret_cast<uint32_t*>(stats.data_ptr<int32_t>());
+  a.counter = reinterpret_cast<uint32_t*>(counter.data_ptr<int32_t>());
+  a.flag = reinterpret_cast<uint32_t*>(flag_ptr);
+  a.seq = uint32_t(seq);
+  a.layer = uint32_t(layer);
+  a.pacing = pacing.has_value() ? pacing->data_ptr<int64_t>() : nullptr;
+  a.rate_bytes_per_ns = rate_bytes_per_ns;
+  a.tile_tokens = int(tile_tokens);
+  const int ntiles = std::max<int>(1, int(ceil_div(g.T, tile_tokens)));
+  const int ctas = std::max<int>(1, std::min<int>(ntiles, int(max_ctas)));
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const size_t smem = size_t(2) * g.H * g.D * 4;
+  bool any_k_quant = false;
+  for (int s = 0; s < 2; ++s)
+    if (section_heads(g, s) > 0 && g.bits[0][s] != kRawBits) any_k_quant = true;
+  if (any_k_quant && g.T > 0) launch_kstats(g.D, dim3(ctas), smem, st, a);
+  dim3 grid(ctas, 2);
+  switch (g.D) {
+    case 64: kv_quant_kernel<64><<<grid, kThreads, smem, st>>>(a); break;
+    case 128: kv_quant_kernel<128><<<grid, kThreads, smem, st>>>(a); break;
+    case 256: kv_quant_kernel<256><<<grid, kThreads, smem, st>>>(a); break;
+  }
+  KVS_CUDA_CHECK(cudaGetLastError());
+}
+
+void kv_decode_layers(int64_t frame_base, int64_t frame_stride, std::vector<int64_t> geom,
+                      torch::Tensor orders, torch::Tensor sign_bits, torch::Tensor kv_cache,
+                      torch::Tensor block_table, int64_t tok_offset, int64_t flags_ptr, int64_t seq,
+                      int64_t layer_begin, int64_t num_layers, int64_t timeout_ns,
+                      torch::Tensor status, int64_t max_ctas, int64_t tile_tokens) {
+  const FrameGeom g = geom_from(geom);
+  KVS_CHECK_ARG(kv_cache.is_cuda() && kv_cache.scalar_type() == at::kBFloat16 && kv_cache.dim() == 6,
+                "kv_cache must be CUDA bf16 [L, 2, num_blocks, block_size, H, D]");
+  KVS_CHECK_ARG(kv_cache.size(4) == g.H && kv_cache.size(5) == g.D && kv_cache.stride(5) == 1,
+                "kv_cache head geometry mismatch");
+  const int64_t L = kv_cache.size(0);
+  KVS_CHECK_ARG(layer_begin >= 0 && num_layers >= 1 && layer_begin + num_layers <= L, "bad layer range");
+  KVS_CHECK_ARG(orders.scalar_type() == at::kInt && orders.numel() == L * g.H, "orders: int32[L, H]");
+  KVS_CHECK_ARG(sign_bits.scalar_type() == at::kInt && sign_bits.numel() == L * g.H * (g.D / 32),
+                "sign_bits: int32[L, H, D/32]");
+  KVS_CHECK_ARG(block_table.scalar_type() == at::kInt && block_table.is_cuda(), "block_table: int32");
+  const int64_t bs = kv_cache.size(3);
+  KVS_CHECK_ARG(block_table.numel() * bs >= tok_offset + g.T, "block_table too short");
+  KVS_CHECK_ARG(status.scalar_type() == at::kInt && status.numel() >= 1, "status: int32[1]");
+  KVS_CHECK_ARG((frame_base & 255) == 0 && (frame_stride & 255) == 0 && frame_stride >= g.frame_bytes,
+                "frame base/stride must be 256-byte aligned and hold one frame");
+  DecodeArgs a{};
+  a.frame_base = reinterpret_cast<const uint8_t*>(frame_base);
+  a.frame_stride = frame_stride;
+  a.g = g;
+  a.orders = orders.data_ptr<int32_t>();
+  a.sign_bits = reinterpret_cast<const uint32_t*>(sign_bits.data_ptr<int32_t>());
+  a.cache = reinterpret_cast<bf16*>(kv_cache.data_ptr());
+  a.layer_stride = kv_cache.stride(0);
+  a.part_stride = kv_cache.stride(1);
+  a.block_stride = kv_cache.stride(2);
+  a.token_stride = kv_cache.stride(3);
+  a.head_stride = kv_cache.stride(4);
+  a.block_table = block_table.data_ptr<int32_t>();
+  a.block_size = int(bs);
+  a.tok_offset = int(tok_offset);
+  a.flags = reinterpret_cast<const uint32_t*>(flags_ptr);
+  a.seq = uint32_t(seq);
+  a.layer_begin = int(layer_begin);
+  a.num_layers = int(num_layers);
+  a.num_layers_total = int(L);
+  a.timeout_ns = uint64_t(timeout_ns);
+  a.status = reinterpret_cast<uint32_t*>(status.data_ptr<int32_t>());
+  a.tile_tokens = int(tile_tokens);
+  const int ntiles = std::max<int>(1, int(ceil_div(g.T, tile_tokens)));
+  const int ctas = std::max<int>(1, std::min<int>(ntiles, int(max_ctas)));
+  dim3 grid(ctas, 2);
+  const size_t smem = size_t(2) * g.H * g.D * 4;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  switch (g.D) {
+    case 64: kv_decode_kernel<64><<<grid, kThreads, smem, st>>>(a); break;
+    case 128: kv_decode_kernel<128><<<grid, kThreads, smem, st>>>(a); break;
+    case 256: kv_decode_kernel<256><<<grid, kThreads, smem, st>>>(a); break;
+  }
+  KVS_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace kvs

@@ -1,0 +1,59 @@
+// Host entry points of the kvserve_b200 CUDA extension (bound in bindings.cpp).
+#pragma once
+#include <torch/extension.h>
+
+#include <string>
+#include <vector>
+
+namespace kvs {
+
+// ---- fused KV transfer codec (kv_codec.cu)
+std::vector<int64_t> kv_frame_geom(std::vector<int64_t> params);
+void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom, torch::Tensor order,
+                     torch::Tensor sign_bits, int64_t frame_ptr, torch::Tensor stats, torch::Tensor counter,
+                     int64_t flag_ptr, int64_t seq, int64_t layer, c10::optional<torch::Tensor> pacing,
+                     double rate_bytes_per_ns, int64_t max_ctas, int64_t tile_tokens);
+void kv_decode_layers(int64_t frame_base, int64_t frame_stride, std::vector<int64_t> geom, torch::Tensor orders,
+                      torch::Tensor sign_bits, torch::Tensor kv_cache, torch::Tensor block_table,
+                      int64_t tok_offset, int64_t flags_ptr, int64_t seq, int64_t layer_begin, int64_t num_layers,
+                      int64_t timeout_ns, torch::Tensor status, int64_t max_ctas, int64_t tile_tokens);
+
+// ---- modular pipeline kernels (bitpack.cu)
+void bitpack_encode(torch::Tensor src, torch::Tensor out, int64_t bits, torch::Tensor status);
+void bitpack_decode(torch::Tensor src, torch::Tensor out, int64_t bits, torch::Tensor status);
+void fwht_rows(torch::Tensor x, torch::Tensor y, c10::optional<torch::Tensor> signs, bool inverse);
+
+// ---- peer memory (p2p.cu)
+int64_t dev_alloc(int64_t bytes);
+void dev_free(int64_t ptr);
+std::string ipc_get_handle(int64_t ptr);
+int64_t ipc_open_handle(const std::string& handle);
+void ipc_close(int64_t ptr);
+bool can_access_peer(int64_t dev, int64_t peer);
+torch::Tensor tensor_from_ptr(int64_t ptr, std::vector<int64_t> shape, int64_t dtype_code, int64_t device);
+void fill_u32(int64_t ptr, int64_t value, int64_t count);
+void read_u32(int64_t ptr, torch::Tensor out);
+void store_release_u32(int64_t ptr, int64_t value);
+void wait_flag(int64_t flag_ptr, int64_t target, int64_t timeout_ns, torch::Tensor status);
+
+// ---- engine (engine_ops.cu, gemm_sm100.cu, gemv.cu, attention_*.cu)
+void rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> residual, torch::Tensor w, torch::Tensor out,
+             double eps);
+void rope_qkv(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t D, torch::Tensor positions,
+              torch::Tensor cos_sin, c10::optional<torch::Tensor> k_dst, c10::optional<torch::Tensor> v_dst,
+              int64_t dst_token_stride, int64_t dst_head_stride, c10::optional<torch::Tensor> slot_mapping,
+              int64_t slot_base);
+void silu_mul(torch::Tensor gate_up, torch::Tensor out);
+void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t vocab_begin);
+void argmax_rows(torch::Tensor logits, torch::Tensor out, c10::optional<torch::Tensor> out_val,
+                 int64_t index_offset);
+void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, c10::optional<torch::Tensor> residual,
+               torch::Tensor err);
+void gemv_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y);
+void flash_prefill(torch::Tensor qkv, int64_t Hq, int64_t Hkv, double scale, torch::Tensor out, torch::Tensor err);
+int64_t paged_decode_splits(int64_t batch, int64_t hkv, int64_t max_ctx);
+void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                            torch::Tensor block_tables, torch::Tensor ctx_lens, int64_t max_ctx, double scale,
+                            torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml, int64_t splits);
+
+}  // namespace kvs

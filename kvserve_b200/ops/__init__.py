@@ -1,0 +1,163 @@
+"""Python front-end of the hand-written sm_100a kernels.
+
+Every function here launches a kernel of ``kvserve_b200._C`` on the current
+CUDA stream; none of them synchronises the host.  Device-side failures
+(a bounded wait that timed out, a malformed frame) are recorded in per-device
+status words and surfaced by :func:`check_device_status`.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from ._ext import ext, available, ExtensionMissing
+
+__all__ = [
+    "ext", "available", "ExtensionMissing", "linear", "gemm", "gemv", "rmsnorm", "rope_qkv",
+    "silu_mul", "embedding", "argmax", "flash_prefill", "paged_decode_attention",
+    "device_status", "check_device_status", "STATUS_NAMES",
+]
+
+STATUS_NAMES = {0: "ok", 1: "timeout", 2: "bad header", 3: "bad symbol", 4: "bad size"}
+GEMV_MAX_M = 8
+
+_status: dict[int, torch.Tensor] = {}
+
+
+def _dev_index(device) -> int:
+    if device is None:
+        return torch.cuda.current_device()
+    if isinstance(device, int):
+        return device
+    d = torch.device(device)
+    return d.index if d.index is not None else torch.cuda.current_device()
+
+
+def device_status(device: torch.device | int | None = None) -> torch.Tensor:
+    """The int32 status word that kernels on ``device`` report failures into."""
+    idx = _dev_index(device)
+    t = _status.get(idx)
+    if t is None:
+        t = torch.zeros(4, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status[idx] = t
+    return t
+
+
+def check_device_status(device=None, reset: bool = True) -> None:
+    """Raise if any kernel on ``device`` recorded an error (synchronises)."""
+    st = device_status(device)
+    code = int(st[0].item())
+    if code != 0:
+        if reset:
+            st.zero_()
+        raise RuntimeError(f"kvserve_b200 device status: {STATUS_NAMES.get(code, code)}")
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None,
+         residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``out = a @ b.T (+ residual)`` on tcgen05 tensor cores (bf16 in/out, fp32 acc)."""
+    if out is None:
+        out = torch.empty((a.shape[0], b.shape[0]), dtype=a.dtype, device=a.device)
+    ext().gemm_bf16(a, b, out, residual, device_status(a.device))
+    return out
+
+
+def gemv(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``out = x @ w.T`` for at most 8 rows (weight-streaming kernel)."""
+    if out is None:
+        out = torch.empty((x.shape[0], w.shape[0]), dtype=x.dtype, device=x.device)
+    ext().gemv_bf16(x, w, out)
+    return out
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """nn.Linear without bias: picks the weight-streaming GEMV for decode-size
+    batches and the tcgen05 tile GEMM otherwise."""
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.shape[0] <= GEMV_MAX_M:
+        y = gemv(x2, w, out)
+    else:
+        y = gemm(x2, w, out)
+    return y.view(*x.shape[:-1], w.shape[0])
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float,
+            residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """RMSNorm; with ``residual`` the input is first added into it (in place)."""
+    if out is None:
+        out = torch.empty_like(x)
+    ext().rmsnorm(x, residual, weight, out, eps)
+    return out
+
+
+def rope_qkv(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int, head_dim: int,
+             positions: torch.Tensor, cos_sin: torch.Tensor, k_dst: Optional[torch.Tensor] = None,
+             v_dst: Optional[torch.Tensor] = None, slot_mapping: Optional[torch.Tensor] = None,
+             slot_base: int = 0) -> None:
+    """Rotary embedding on q/k of a fused QKV tensor (in place) and copy of the
+    rotated k and of v into ``k_dst``/``v_dst`` (``[slots, Hkv, D]`` views)."""
+    if k_dst is not None:
+        tok_stride, head_stride = k_dst.stride(0), k_dst.stride(1)
+    else:
+        tok_stride, head_stride = 0, 0
+    ext().rope_qkv(qkv, num_q_heads, num_kv_heads, head_dim, positions, cos_sin, k_dst, v_dst,
+                   tok_stride, head_stride, slot_mapping, slot_base)
+
+
+def silu_mul(gate_up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    inter = gate_up.shape[-1] // 2
+    if out is None:
+        out = torch.empty((*gate_up.shape[:-1], inter), dtype=gate_up.dtype, device=gate_up.device)
+    ext().silu_mul(gate_up, out)
+    return out
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor, vocab_begin: int = 0,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty((ids.numel(), table.shape[1]), dtype=table.dtype, device=table.device)
+    ext().embedding(ids, table, out, vocab_begin)
+    return out
+
+
+def argmax(logits: torch.Tensor, index_offset: int = 0, out_val: Optional[torch.Tensor] = None,
+           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    ext().argmax_rows(logits, out, out_val, index_offset)
+    return out
+
+
+def flash_prefill(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int,
+                  scale: Optional[float] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Causal GQA attention over a fused (already rotated) QKV tensor, head_dim 128."""
+    d = 128
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    if out is None:
+        out = torch.empty((qkv.shape[0], num_q_heads * d), dtype=qkv.dtype, device=qkv.device)
+    ext().flash_prefill(qkv, num_q_heads, num_kv_heads, scale, out, device_status(qkv.device))
+    return out
+
+
+def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                           block_tables: torch.Tensor, ctx_lens: torch.Tensor, max_ctx: int,
+                           scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
+                           scratch: Optional[tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
+    """Single-token GQA attention over paged K/V (``[num_blocks, block_size, Hkv, D]``)."""
+    b, hq, d = q.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    if out is None:
+        out = torch.empty_like(q)
+    splits = ext().paged_decode_splits(b, k_cache.shape[2], max_ctx)
+    if scratch is None:
+        part_o = torch.empty(b * hq * splits * d, dtype=torch.float32, device=q.device)
+        part_ml = torch.empty(b * hq * splits * 2, dtype=torch.float32, device=q.device)
+    else:
+        part_o, part_ml = scratch
+    ext().paged_decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, max_ctx, scale, out,
+                                 part_o, part_ml, splits)
+    return out
