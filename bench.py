@@ -1,0 +1,185 @@
+"""Headline benchmark: TTFT p50 and KV-transfer ms per request of a
+disaggregated prefill -> decode deployment (BASELINE.json metric).
+
+Config: Llama-3.1-8B-shaped decoder, random-init
+bf16 weights, 8192-token random prompts, 128 greedy output tokens, K 4-bit /
+V 2-bit compressed KV hand-off.  N GPUs of one node:
+
+* N = 1: prefill and decode colocated on one GPU (device-local hand-off);
+* N = 2k: k prefill ranks (TP k) -> k decode ranks (TP k): 1P1D, 2P2D, 4P4D.
+
+One step = one request end to end (prefill, layer-streamed compressed KV
+push over NVLink, decode of the last prompt token = first token, then the
+remaining greedy tokens).  Timing: CUDA events per rank after a device-side
+NCCL barrier, max over ranks; the prompt H2D copy (pinned) and the token D2H
+copy are inside every step.  Inputs (8192 x 32 layers of KV, 16 GB of
+weights) are far larger than L2, so no explicit flush is needed.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import time
+
+import torch
+
+BASELINE_METRIC = "TTFT p50 + KV-transfer ms/request (max over ranks), 1P1D–4P4D on B200"
+
+
+def _emit(obj) -> None:
+    print(json.dumps(obj), flush=True)
+
+
+def _profile(name: str):
+    from kvserve_b200.engine.transfer import TransferProfile
+    if name == "raw":
+        return TransferProfile.raw()
+    if name == "k4v2":
+        return TransferProfile(compressed=True, hybrid_ratio=0.0, split_type="head", key_levels=(16, 16),
+                               value_levels=(4, 4))
+    if os.path.exists(name):
+        with open(name) as f:
+            return TransferProfile.from_compression(json.load(f))
+    raise SystemExit(f"unknown profile {name!r}")
+
+
+def run_reference(args) -> None:
+    if int(os.environ.get("RANK", "0")) == 0:
+        from kvserve_b200.baselines.reference_arm import unavailable_reason
+        _emit({"impl": "reference", "unavailable": unavailable_reason()})
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="llama-3.1-8b")
+    ap.add_argument("--prompt-len", type=int, default=8192)
+    ap.add_argument("--max-new", type=int, default=128)
+    ap.add_argument("--profile", default="k4v2")
+    ap.add_argument("--link-gbps", type=float, default=0.0)
+    ap.add_argument("--layers", type=int, default=0, help="override layer count (smoke runs only)")
+    ap.add_argument("--no-graphs", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+
+    from kvserve_b200.models.config import get_config
+    from kvserve_b200.parallel.context import init_parallel, destroy_parallel
+    from kvserve_b200.engine.pd import PDEngine
+    from kvserve_b200.utils.clocks import ClockSampler
+    import torch.distributed as dist
+
+    ctx = init_parallel("nccl", timeout_s=300.0)
+    if ctx.world_size != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={ctx.world_size}")
+    cfg = get_config(args.model)
+    if args.layers:
+        cfg = cfg.with_layers(args.layers)
+    profile = _profile(args.profile)
+    engine = PDEngine(cfg, ctx, profile, max_prompt=args.prompt_len - 1, max_new_tokens=args.max_new,
+                      link_gbps=args.link_gbps, use_graphs=not args.no_graphs)
+    engine.warmup(prompt_len=min(512, args.prompt_len))
+
+    g = torch.Generator().manual_seed(1234)
+    prompts = [torch.randint(0, cfg.vocab, (args.prompt_len,), generator=g, dtype=torch.int32).pin_memory()
+               for _ in range(args.warmup + args.steps)]
+    for i in range(args.warmup):
+        engine.generate(prompts[i], args.max_new)
+
+    sampler = None
+    if ctx.rank == 0:
+        sampler = ClockSampler(list(range(torch.cuda.device_count())) if ctx.distributed else
+                               [torch.cuda.current_device()])
+        sampler.start()
+    if ctx.distributed:
+        dist.barrier(group=ctx.cpu_group)
+    torch.cuda.synchronize()
+    t_wall = time.perf_counter()
+    timings = []
+    for i in range(args.steps):
+        res = engine.generate(prompts[args.warmup + i], args.max_new)
+        timings.append(res.timing)
+    torch.cuda.synchronize()
+    if ctx.distributed:
+        dist.barrier(group=ctx.cpu_group)
+    wall_s = time.perf_counter() - t_wall
+    clocks = sampler.stop() if sampler else None
+
+    mine = [t.__dict__ for t in timings]
+    allt = [None] * ctx.world_size
+    if ctx.distributed:
+        dist.all_gather_object(allt, mine, group=ctx.cpu_group)
+    else:
+        allt = [mine]
+    if ctx.rank == 0:
+        def col(step, key):
+            vals = [allt[r][step][key] for r in range(len(allt))]
+            vals = [v for v in vals if not (isinstance(v, float) and math.isnan(v))]
+            return max(vals) if vals else float("nan")
+        ttft = [col(s, "first_token") for s in range(args.steps)]
+        end = [col(s, "all_done") for s in range(args.steps)]
+        prefill = [col(s, "prefill_done") for s in range(args.steps)]
+        ingest = [col(s, "ingest_done") for s in range(args.steps)]
+        kv_exposed = [max(0.0, ingest[s] - prefill[s]) for s in range(args.steps)]
+        payload = timings[0].payload_bytes if ctx.is_prefill else allt[0][0]["payload_bytes"]
+        raw = allt[0][0]["raw_bytes"]
+        tp = max(1, args.gpus // 2)
+        ttft_p50 = statistics.median(ttft)
+        decode_ms = [end[s] - ttft[s] for s in range(args.steps)]
+        launches = sum(allt[r][s]["launches"] for r in range(len(allt)) for s in range(args.steps))
+        e2e_ttft = [col(s, "first_token_host") for s in range(args.steps)]
+        e2e_req = [col(s, "request_host") for s in range(args.steps)]
+        out = {
+            "metric": BASELINE_METRIC,
+            "value": round(ttft_p50, 3),
+            "unit": "ms (TTFT p50)",
+            "n_gpus": args.gpus,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(statistics.mean(end), 3),
+            "higher_is_better": False,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (random-init weights of the named architecture, uniform-random prompt token ids)",
+            "impl": "ours",
+            "kv_transfer_ms_p50": round(statistics.median(kv_exposed), 3),
+            "prefill_ms_p50": round(statistics.median(prefill), 3),
+            "kv_ready_ms_p50": round(statistics.median(ingest), 3),
+            "decode_ms_per_token": round(statistics.median(decode_ms) / max(1, args.max_new - 1), 4),
+            "kv_payload_bytes_per_request": int(payload) * tp,
+            "kv_raw_bytes_per_request": int(raw) * tp,
+            "compression_ratio": round(raw / payload, 3) if payload else None,
+            "config": {"model": cfg.name, "layers": cfg.num_layers, "global_batch": 1,
+                       "seq_len": args.prompt_len, "max_new_tokens": args.max_new,
+                       "parallelism": "colocated-1gpu" if args.gpus == 1 else f"{tp}P{tp}D-tp{tp}",
+                       "profile": args.profile, "link_gbps": args.link_gbps or None,
+                       "l2": "inputs larger than L2 (16 GB weights, 1 GiB raw KV per request)"},
+            "e2e": {"value": round(statistics.median(e2e_ttft), 3),
+                    "unit": "ms (TTFT p50, host wall clock from PDEngine.generate() entry to the first token "
+                            "on the host; prompt H2D from pinned memory and token D2H inside every step)",
+                    "h2d_bytes_per_step": 4 * args.prompt_len, "d2h_bytes_per_step": 4 * (args.max_new + 1),
+                    "request_ms_p50": round(statistics.median(e2e_req), 3),
+                    "wall_ms_per_request": round(1e3 * wall_s / args.steps, 3)},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+        }
+        _emit(out)
+    engine.close()
+    destroy_parallel(ctx)
+
+
+if __name__ == "__main__":
+    main()

@@ -204,7 +204,43 @@ __global__ void argmax_kernel(const bf16* __restrict__ logits, int64_t row_strid
   }
 }
 
+// Per decode step bookkeeping, captured together with the step in one CUDA
+// graph: feed the sampled token back, record it, advance position / context
+// length and compute the next cache slot from the block table.
+__global__ void decode_advance_kernel(const int32_t* __restrict__ tok, int32_t* __restrict__ ids,
+                                      int32_t* __restrict__ pos, int32_t* __restrict__ ctx,
+                                      int32_t* __restrict__ slot, const int32_t* __restrict__ table,
+                                      int64_t table_stride, int block_size, int32_t* __restrict__ out_tokens,
+                                      int32_t* __restrict__ step, int max_steps, int B) {
+  const int b = threadIdx.x;
+  const int s = *step;
+  __syncthreads();
+  if (b < B) {
+    const int32_t t = tok[b];
+    ids[b] = t;
+    if (s < max_steps) out_tokens[int64_t(s) * B + b] = t;
+    const int p = pos[b] + 1;
+    pos[b] = p;
+    ctx[b] = ctx[b] + 1;
+    slot[b] = table[b * table_stride + p / block_size] * block_size + p % block_size;
+  }
+  __syncthreads();
+  if (b == 0) *step = s + 1;
+}
+
 }  // namespace
+
+void decode_advance(torch::Tensor tok, torch::Tensor ids, torch::Tensor pos, torch::Tensor ctx, torch::Tensor slot,
+                    torch::Tensor table, int64_t block_size, torch::Tensor out_tokens, torch::Tensor step) {
+  const int B = int(ids.numel());
+  KVS_CHECK_ARG(B >= 1 && B <= 1024 && table.dim() == 2, "decode_advance: batch / table");
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  decode_advance_kernel<<<1, std::max(32, B), 0, st>>>(
+      tok.data_ptr<int32_t>(), ids.data_ptr<int32_t>(), pos.data_ptr<int32_t>(), ctx.data_ptr<int32_t>(),
+      slot.data_ptr<int32_t>(), table.data_ptr<int32_t>(), table.stride(0), int(block_size),
+      out_tokens.data_ptr<int32_t>(), step.data_ptr<int32_t>(), int(out_tokens.numel() / B), B);
+  KVS_CUDA_CHECK(cudaGetLastError());
+}
 
 void rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> residual, torch::Tensor w, torch::Tensor out,
              double eps) {

@@ -32,6 +32,7 @@ constexpr uint32_t kTmemCols = 512;
 struct GemmArgs {
   bf16* C;
   const bf16* R;
+  const bf16* bias;
   int M, N, K;
   int64_t ldc, ldr;
   uint32_t* err;
@@ -167,6 +168,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             float f[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[v * 8 + e]);
+            if (p.bias) {
+              const uint4 bb = *reinterpret_cast<const uint4*>(p.bias + col);
+              const __nv_bfloat162* bh = reinterpret_cast<const __nv_bfloat162*>(&bb);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 x = __bfloat1622float2(bh[e]);
+                f[2 * e] += x.x;
+                f[2 * e + 1] += x.y;
+              }
+            }
             if (p.R) {
               const uint4 rr = *reinterpret_cast<const uint4*>(p.R + int64_t(row) * p.ldr + col);
               const __nv_bfloat162* rh = reinterpret_cast<const __nv_bfloat162*>(&rr);
@@ -241,7 +252,7 @@ static int num_sms() {
 }
 
 void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, c10::optional<torch::Tensor> residual,
-               torch::Tensor err) {
+               c10::optional<torch::Tensor> bias, torch::Tensor err) {
   KVS_CHECK_ARG(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: CUDA tensors");
   KVS_CHECK_ARG(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 &&
                     c.scalar_type() == at::kBFloat16,
@@ -267,6 +278,12 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, c10::optional<
                   "gemm: residual shape");
     p.R = reinterpret_cast<const bf16*>(residual->data_ptr());
     p.ldr = residual->stride(0);
+  }
+  p.bias = nullptr;
+  if (bias.has_value()) {
+    KVS_CHECK_ARG(bias->numel() == N && bias->is_contiguous() && bias->scalar_type() == at::kBFloat16,
+                  "gemm: bias must be contiguous bf16 [N]");
+    p.bias = reinterpret_cast<const bf16*>(bias->data_ptr());
   }
   p.err = reinterpret_cast<uint32_t*>(err.data_ptr<int32_t>());
   const CUtensorMap ta = make_tmap_2d_bf16(a.data_ptr(), K, M, uint64_t(a.stride(0)) * 2, BK, BM);

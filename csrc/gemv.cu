@@ -39,7 +39,8 @@ __device__ __forceinline__ float dot8(const uint4& w, const float (&x)[8], float
 template <int M>
 __global__ void __launch_bounds__(kThreads) gemv_kernel(const bf16* __restrict__ x, int64_t ldx,
                                                         const bf16* __restrict__ w, int64_t ldw,
-                                                        bf16* __restrict__ y, int64_t ldy, int N, int K) {
+                                                        bf16* __restrict__ y, int64_t ldy, int N, int K,
+                                                        const bf16* __restrict__ bias) {
   extern __shared__ uint4 xs_raw[];  // [M][K] bf16
   bf16* xs = reinterpret_cast<bf16*>(xs_raw);
   for (int i = threadIdx.x; i < M * K / 8; i += kThreads) {
@@ -107,14 +108,15 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const bf16* __restrict__
     for (int r = 0; r < kRows; ++r) {
       if (row0 + r >= N) break;
 #pragma unroll
-      for (int m = 0; m < M; ++m) y[int64_t(m) * ldy + row0 + r] = rn(acc[r][m]);
+      for (int m = 0; m < M; ++m)
+        y[int64_t(m) * ldy + row0 + r] = rn(acc[r][m] + (bias ? to_f32(bias[row0 + r]) : 0.f));
     }
   }
 }
 
 }  // namespace
 
-void gemv_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y) {
+void gemv_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, c10::optional<torch::Tensor> bias) {
   KVS_CHECK_ARG(x.is_cuda() && w.is_cuda() && y.is_cuda() && x.scalar_type() == at::kBFloat16 &&
                     w.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16,
                 "gemv: CUDA bf16");
@@ -132,9 +134,15 @@ void gemv_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y) {
   if (M > max_rows) {
     for (int m0 = 0; m0 < M; m0 += max_rows) {
       const int mm = std::min(max_rows, M - m0);
-      gemv_bf16(x.narrow(0, m0, mm), w, y.narrow(0, m0, mm));
+      gemv_bf16(x.narrow(0, m0, mm), w, y.narrow(0, m0, mm), bias);
     }
     return;
+  }
+  const bf16* bp = nullptr;
+  if (bias.has_value()) {
+    KVS_CHECK_ARG(bias->numel() == N && bias->is_contiguous() && bias->scalar_type() == at::kBFloat16,
+                  "gemv: bias must be contiguous bf16 [N]");
+    bp = reinterpret_cast<const bf16*>(bias->data_ptr());
   }
   const int rows_per_cta = (kThreads / 32) * kRows;
   const int grid = (N + rows_per_cta - 1) / rows_per_cta;
@@ -151,7 +159,7 @@ void gemv_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y) {
                                           200 * 1024));                                                    \
       set = true;                                                                                          \
     }                                                                                                      \
-    gemv_kernel<MM><<<grid, kThreads, smem, st>>>(xp, x.stride(0), wp, w.stride(0), yp, y.stride(0), N, K); \
+    gemv_kernel<MM><<<grid, kThreads, smem, st>>>(xp, x.stride(0), wp, w.stride(0), yp, y.stride(0), N, K, bp); \
     break;                                                                                                 \
   }
   switch (M) {

@@ -71,6 +71,7 @@ struct DecodeArgs {
   int block_size;
   int tok_offset;
   const uint32_t* flags;      // [L] or null (stream-ordered, no wait)
+  const int32_t* n_lows;      // [L] low-section head count per layer, or null
   uint32_t seq;
   int layer_begin;
   int num_layers;
@@ -494,16 +495,20 @@ __global__ void __launch_bounds__(kThreads) kv_decode_kernel(DecodeArgs a) {
   constexpr int kRowsPerIter = (kThreads / 32) * RPW;
   extern __shared__ float sk[];  // K params: min[HD], scale[HD]
   __shared__ int s_ok;
-  const FrameGeom& g = a.g;
-  const int HD = g.H * D;
+  const int HD = a.g.H * D;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int lir = lane % LANES, rw = lane / LANES;
   const float scale = inv_sqrt_d<D>();
-  const int ntiles = int(ceil_div(g.T, a.tile_tokens));
+  const int ntiles = int(ceil_div(a.g.T, a.tile_tokens));
   const int part = blockIdx.y;
 
   for (int li = 0; li < a.num_layers; ++li) {
     const int layer = a.layer_begin + li;
+    FrameGeom g = a.g;
+    if (a.n_lows != nullptr) {
+      g.n_low = a.n_lows[layer];
+      frame_geom_finalize(g);
+    }
     const uint8_t* frame = a.frame_base + int64_t(li) * a.frame_stride;
     if (threadIdx.x == 0) {
       int ok = 1;
@@ -716,7 +721,8 @@ void kv_decode_layers(int64_t frame_base, int64_t frame_stride, std::vector<int6
                       torch::Tensor orders, torch::Tensor sign_bits, torch::Tensor kv_cache,
                       torch::Tensor block_table, int64_t tok_offset, int64_t flags_ptr, int64_t seq,
                       int64_t layer_begin, int64_t num_layers, int64_t timeout_ns,
-                      torch::Tensor status, int64_t max_ctas, int64_t tile_tokens) {
+                      torch::Tensor status, int64_t max_ctas, int64_t tile_tokens,
+                      c10::optional<torch::Tensor> n_lows) {
   const FrameGeom g = geom_from(geom);
   KVS_CHECK_ARG(kv_cache.is_cuda() && kv_cache.scalar_type() == at::kBFloat16 && kv_cache.dim() == 6,
                 "kv_cache must be CUDA bf16 [L, 2, num_blocks, block_size, H, D]");
@@ -749,6 +755,12 @@ void kv_decode_layers(int64_t frame_base, int64_t frame_stride, std::vector<int6
   a.block_size = int(bs);
   a.tok_offset = int(tok_offset);
   a.flags = reinterpret_cast<const uint32_t*>(flags_ptr);
+  a.n_lows = nullptr;
+  if (n_lows.has_value()) {
+    KVS_CHECK_ARG(n_lows->scalar_type() == at::kInt && n_lows->is_cuda() && n_lows->numel() == L,
+                  "n_lows: int32[L] on the device");
+    a.n_lows = n_lows->data_ptr<int32_t>();
+  }
   a.seq = uint32_t(seq);
   a.layer_begin = int(layer_begin);
   a.num_layers = int(num_layers);

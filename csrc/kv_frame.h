@@ -87,8 +87,8 @@ KVS_HD inline bool section_is_raw(const FrameGeom& g, int p, int s) {
 }
 
 // Fills every offset of `g` from T/H/D/n_low/bits/levels.
-inline void frame_geom_finalize(FrameGeom& g) {
-  int64_t off = align_up(sizeof(FrameHeader), kFrameAlign);
+KVS_HD inline void frame_geom_finalize(FrameGeom& g) {
+  int64_t off = align_up(int64_t(sizeof(FrameHeader)), kFrameAlign);
   bool k_quant = false;
   for (int s = 0; s < 2; ++s)
     if (section_heads(g, s) > 0 && !section_is_raw(g, 0, s)) k_quant = true;

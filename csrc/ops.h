@@ -16,7 +16,8 @@ void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom
 void kv_decode_layers(int64_t frame_base, int64_t frame_stride, std::vector<int64_t> geom, torch::Tensor orders,
                       torch::Tensor sign_bits, torch::Tensor kv_cache, torch::Tensor block_table,
                       int64_t tok_offset, int64_t flags_ptr, int64_t seq, int64_t layer_begin, int64_t num_layers,
-                      int64_t timeout_ns, torch::Tensor status, int64_t max_ctas, int64_t tile_tokens);
+                      int64_t timeout_ns, torch::Tensor status, int64_t max_ctas, int64_t tile_tokens,
+                      c10::optional<torch::Tensor> n_lows);
 
 // ---- modular pipeline kernels (bitpack.cu)
 void bitpack_encode(torch::Tensor src, torch::Tensor out, int64_t bits, torch::Tensor status);
@@ -47,9 +48,11 @@ void silu_mul(torch::Tensor gate_up, torch::Tensor out);
 void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t vocab_begin);
 void argmax_rows(torch::Tensor logits, torch::Tensor out, c10::optional<torch::Tensor> out_val,
                  int64_t index_offset);
+void decode_advance(torch::Tensor tok, torch::Tensor ids, torch::Tensor pos, torch::Tensor ctx, torch::Tensor slot,
+                    torch::Tensor table, int64_t block_size, torch::Tensor out_tokens, torch::Tensor step);
 void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, c10::optional<torch::Tensor> residual,
-               torch::Tensor err);
-void gemv_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y);
+               c10::optional<torch::Tensor> bias, torch::Tensor err);
+void gemv_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, c10::optional<torch::Tensor> bias);
 void flash_prefill(torch::Tensor qkv, int64_t Hq, int64_t Hkv, double scale, torch::Tensor out, torch::Tensor err);
 int64_t paged_decode_splits(int64_t batch, int64_t hkv, int64_t max_ctx);
 void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,

@@ -1,0 +1,294 @@
+"""Standalone disaggregated prefill/decode engine (one process per GPU).
+
+Request flow (every rank calls :meth:`PDEngine.generate` with the same
+prompt, SPMD):
+
+* prefill ranks run the prompt's first ``T-1`` tokens through the model; after
+  each layer's K/V are written the fused encode kernel pushes the compressed
+  frame of that layer into the paired decode rank's receive slot (NVLink peer
+  stores) and publishes it — transfer overlaps the remaining layers;
+* decode ranks launch one persistent fused decode that waits for each layer
+  and writes the paged KV cache, then compute the last prompt token (as the
+  reference's consumer does: it claims ``prompt_len - 1`` external tokens,
+  kvserve_v1/connector/compressed_kv_connector.py:511-524) and continue with
+  greedy decode steps replayed from one CUDA graph per step.
+
+All timings are CUDA events on each rank's own streams relative to a start
+event recorded right after a device-side NCCL barrier, so per-rank times are
+aligned to within the barrier skew and the max over ranks is meaningful.
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from ..models.config import ModelConfig
+from ..models.llama import LlamaShard
+from ..parallel.context import ParallelContext
+from ..transport.p2p import FrameReceiver, FrameSender
+from .kv_cache import PagedKVCache
+from .transfer import KVTransfer, TransferProfile
+
+
+@dataclass
+class RequestTiming:
+    """Milliseconds from the request start on this rank (NaN where n/a)."""
+    prefill_done: float = float("nan")
+    encode_done: float = float("nan")
+    ingest_done: float = float("nan")
+    first_token: float = float("nan")
+    all_done: float = float("nan")
+    first_token_host: float = float("nan")   # wall ms from generate() entry to first token on the host
+    request_host: float = float("nan")       # wall ms of the whole generate() call
+    launches: int = 0                        # kernels of this package launched for the request
+    payload_bytes: int = 0
+    raw_bytes: int = 0
+
+
+@dataclass
+class GenerateResult:
+    tokens: Optional[list[int]]
+    timing: RequestTiming
+
+
+class PDEngine:
+    def __init__(self, cfg: ModelConfig, ctx: ParallelContext, profile: TransferProfile, max_prompt: int = 8192,
+                 max_new_tokens: int = 128, block_size: int = 16, seed: int = 0, link_gbps: float = 0.0,
+                 use_graphs: bool = True, ingest_timeout_s: float = 30.0, encode_ctas: int = 296):
+        self.cfg, self.ctx, self.profile = cfg, ctx, profile
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.max_prompt, self.max_new, self.block_size = max_prompt, max_new_tokens, block_size
+        self.use_graphs = use_graphs
+        self.ingest_timeout_ns = int(ingest_timeout_s * 1e9)
+        self.encode_ctas = encode_ctas
+        self.rate_bytes_per_ns = link_gbps / 8.0 if link_gbps else 0.0
+        self.model = LlamaShard(cfg, ctx.tp_rank, ctx.tp_size, self.device, seed, ctx.tp_group,
+                                max_position=max_prompt + max_new_tokens + block_size)
+        m = self.model
+        self.xfer = KVTransfer(profile, cfg.num_layers, cfg.num_kv_heads, m.hkv, m.D, ctx.tp_rank, ctx.tp_size,
+                               self.device, max_prompt, cfg.score_model_name)
+        self.compute = torch.cuda.current_stream(self.device)
+        self.seq = 0
+        self.status = ops.device_status(self.device)
+        L = cfg.num_layers
+        if ctx.is_prefill:
+            self.k_buf = torch.empty((L, max_prompt, m.hkv, m.D), dtype=torch.bfloat16, device=self.device)
+            self.v_buf = torch.empty_like(self.k_buf)
+            self.enc_stream = torch.cuda.Stream(self.device, priority=-1)
+            self.layer_events = [torch.cuda.Event() for _ in range(L)]
+            self.pacing = torch.zeros(2, dtype=torch.int64, device=self.device)
+            self.positions = torch.arange(max_prompt, dtype=torch.int32, device=self.device)
+        if ctx.is_decode:
+            self.max_blocks = (max_prompt + max_new_tokens + block_size - 1) // block_size + 1
+            # block 0 is a scratch block for graph warm-up
+            self.kv = PagedKVCache(L, self.max_blocks + 1, block_size, m.hkv, m.D, self.device)
+            self._scratch_block = self.kv.allocate(1)
+            self.ingest_stream = torch.cuda.Stream(self.device, priority=-1)
+            self._init_decode_buffers()
+        # ---- channel between paired ranks
+        self.receiver: Optional[FrameReceiver] = None
+        self.sender: Optional[FrameSender] = None
+        if ctx.is_decode:
+            self.receiver = FrameReceiver(L, self.xfer.frame_stride, 1, self.device)
+        if not ctx.distributed:
+            self.sender = FrameSender(local=self.receiver, device=self.device)
+        else:
+            local = self.receiver.handles() if ctx.role == "decode" else None
+            allh = [None] * ctx.world_size
+            dist.all_gather_object(allh, local, group=ctx.cpu_group)
+            if ctx.role == "prefill":
+                self.sender = FrameSender(handles=allh[ctx.peer_rank], device=self.device)
+            dist.barrier(group=ctx.cpu_group)
+            self._barrier_t = torch.zeros(1, dtype=torch.float32, device=self.device)
+        self._graph: Optional[torch.cuda.CUDAGraph] = None
+        torch.cuda.synchronize(self.device)
+
+    # ----------------------------------------------------------- decode state
+    def _init_decode_buffers(self) -> None:
+        dev = self.device
+        self.d_ids = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.d_pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.d_ctx = torch.ones(1, dtype=torch.int32, device=dev)
+        self.d_slot = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.d_step = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.d_table = torch.zeros((1, self.max_blocks), dtype=torch.int32, device=dev)
+        self.d_out = torch.zeros(self.max_new + 1, dtype=torch.int32, device=dev)
+        self.d_init_host = torch.zeros(5 + self.max_blocks, dtype=torch.int32).pin_memory()
+        self.d_init_dev = torch.zeros(5 + self.max_blocks, dtype=torch.int32, device=dev)
+        hq, D = self.model.hq, self.model.D
+        splits = ops.ext().paged_decode_splits(1, self.model.hkv, self.max_prompt + self.max_new)
+        self.attn_scratch = (torch.empty(hq * splits * D, dtype=torch.float32, device=dev),
+                             torch.empty(hq * splits * 2, dtype=torch.float32, device=dev))
+
+    def _decode_step(self) -> None:
+        tok = self.model.decode_step(self.d_ids, self.d_pos, self.d_slot, self.kv.cache, self.d_table, self.d_ctx,
+                                     self.max_prompt + self.max_new, attn_scratch=self.attn_scratch)
+        ops.count_launches(1)
+        ops.ext().decode_advance(tok, self.d_ids, self.d_pos, self.d_ctx, self.d_slot, self.d_table,
+                                 self.block_size, self.d_out, self.d_step)
+
+    def _load_decode_state(self, first_token_id: int, position: int, blocks: list[int]) -> None:
+        h = self.d_init_host
+        bs = self.block_size
+        h.zero_()
+        h[0] = first_token_id
+        h[1] = position
+        h[2] = position + 1
+        h[3] = blocks[position // bs] * bs + position % bs
+        h[4] = 0
+        h[5:5 + len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
+        self.d_init_dev.copy_(h, non_blocking=True)
+        d = self.d_init_dev
+        self.d_ids.copy_(d[0:1])
+        self.d_pos.copy_(d[1:2])
+        self.d_ctx.copy_(d[2:3])
+        self.d_slot.copy_(d[3:4])
+        self.d_step.copy_(d[4:5])
+        self.d_table[0].copy_(d[5:])
+
+    def _ensure_graph(self) -> None:
+        if not self.use_graphs or self._graph is not None:
+            return
+        # warm up on the scratch block, then capture one step
+        self._load_decode_state(0, 0, self._scratch_block * self.max_blocks)
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(self.compute)
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._load_decode_state(0, 0, self._scratch_block * self.max_blocks)
+                self._decode_step()
+        self.compute.wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        self._load_decode_state(0, 0, self._scratch_block * self.max_blocks)
+        torch.cuda.synchronize(self.device)
+        c0 = ops.launches()
+        with torch.cuda.graph(g, stream=s):
+            self._decode_step()
+        torch.cuda.synchronize(self.device)
+        self._graph_launches = ops.launches() - c0
+        self._graph = g
+
+    def warmup(self, prompt_len: int = 256) -> None:
+        """Compile-free warm-up: runs one short request through every path."""
+        if self.ctx.is_decode:
+            self._ensure_graph()
+        ids = torch.randint(0, self.cfg.vocab, (prompt_len,), dtype=torch.int32)
+        self.generate(ids, 2)
+
+    # --------------------------------------------------------------- request
+    def _barrier(self) -> None:
+        if self.ctx.distributed:
+            dist.all_reduce(self._barrier_t, group=self.ctx.world_group)
+
+    def generate(self, prompt_ids: torch.Tensor, max_new_tokens: Optional[int] = None,
+                 return_tokens: bool = True) -> GenerateResult:
+        """Serve one request.  ``prompt_ids`` is a host int32 tensor (pinned
+        preferably); the prompt is copied to the device inside the request."""
+        t_host0 = time.perf_counter()
+        ctx, m = self.ctx, self.model
+        n_new = self.max_new if max_new_tokens is None else max_new_tokens
+        if n_new < 1 or n_new > self.max_new:
+            raise ValueError(f"max_new_tokens must be in [1, {self.max_new}]")
+        T = int(prompt_ids.numel())
+        if T < 2 or T - 1 > self.max_prompt:
+            raise ValueError(f"prompt length must be in [2, {self.max_prompt + 1}]")
+        Tx = T - 1
+        self.seq += 1
+        seq = self.seq
+        ev = {k: torch.cuda.Event(enable_timing=True) for k in ("start", "prefill", "encode", "ingest", "first", "end")}
+        self._barrier()
+        c_launch0 = ops.launches()
+        replays = 0
+        ev["start"].record(self.compute)
+        ids = prompt_ids.to(self.device, non_blocking=True)
+        timing = RequestTiming(payload_bytes=self.xfer.payload_bytes(Tx), raw_bytes=self.xfer.raw_bytes(Tx))
+        blocks = None
+        if ctx.is_decode:
+            blocks = self.kv.allocate(T + n_new)
+            table = self.kv.block_table(blocks, self.max_blocks)
+            if ctx.distributed:
+                self.ingest_stream.wait_stream(self.compute)
+                with torch.cuda.stream(self.ingest_stream):
+                    self.xfer.ingest_all(Tx, self.receiver.slot_base(0), self.receiver.frame_stride,
+                                         self.receiver.flags_base(0), self.kv.cache, table, self.status, seq,
+                                         self.ingest_timeout_ns)
+                    ev["ingest"].record(self.ingest_stream)
+        if ctx.is_prefill:
+            enc = self.enc_stream
+            enc.wait_stream(self.compute)
+
+            def hook(l: int) -> None:
+                self.layer_events[l].record(self.compute)
+                enc.wait_event(self.layer_events[l])
+                with torch.cuda.stream(enc):
+                    flag = self.sender.flag_ptr(0, l) if ctx.distributed else 0
+                    self.xfer.encode(l, self.k_buf[l, :Tx], self.v_buf[l, :Tx], self.sender.frame_ptr(0, l), flag,
+                                     seq, self.pacing, self.rate_bytes_per_ns, self.encode_ctas)
+                    if not ctx.distributed:
+                        self.xfer.ingest_layer(l, Tx, self.sender.frame_ptr(0, l), self.kv.cache, table,
+                                               self.status, seq)
+
+            m.prefill(ids[:Tx], self.positions[:Tx], self.k_buf, self.v_buf, layer_hook=hook)
+            ev["prefill"].record(self.compute)
+            ev["encode"].record(enc)
+            if not ctx.distributed:
+                ev["ingest"].record(enc)
+        tokens = None
+        if ctx.is_decode:
+            self.compute.wait_event(ev["ingest"])
+            self._ensure_graph()
+            self._load_decode_state(0, T - 1, blocks)
+            self.d_ids.copy_(ids[T - 1:T])
+            first_host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+            for i in range(n_new):
+                if self._graph is not None:
+                    self._graph.replay()
+                    replays += 1
+                else:
+                    self._decode_step()
+                if i == 0:
+                    ev["first"].record(self.compute)
+                    # stream the first token to the host (what a server returns first)
+                    first_host.copy_(self.d_out[0:1], non_blocking=True)
+                    ev_fh = torch.cuda.Event()
+                    ev_fh.record(self.compute)
+                    ev_fh.synchronize()
+                    timing.first_token_host = 1e3 * (time.perf_counter() - t_host0)
+            out_host = torch.empty(n_new, dtype=torch.int32, pin_memory=True)
+            out_host.copy_(self.d_out[:n_new], non_blocking=True)
+            ev["end"].record(self.compute)
+            torch.cuda.synchronize(self.device)
+            tokens = out_host.tolist() if return_tokens else None
+            self.kv.release(blocks)
+        else:
+            ev["end"].record(self.compute)
+            torch.cuda.synchronize(self.device)
+        st = int(self.status[0].item())
+        if st != 0:
+            self.status.zero_()
+            raise RuntimeError(f"KV hand-off failed on rank {ctx.rank}: {ops.STATUS_NAMES.get(st, st)}")
+        timing.launches = ops.launches() - c_launch0 + replays * getattr(self, "_graph_launches", 0)
+        timing.request_host = 1e3 * (time.perf_counter() - t_host0)
+        e = lambda k: ev["start"].elapsed_time(ev[k])  # noqa: E731
+        if ctx.is_prefill:
+            timing.prefill_done = e("prefill")
+            timing.encode_done = e("encode")
+        if ctx.is_decode:
+            timing.ingest_done = e("ingest")
+            timing.first_token = e("first")
+            timing.all_done = e("end")
+        return GenerateResult(tokens, timing)
+
+    def close(self) -> None:
+        self._graph = None
+        if self.sender is not None:
+            self.sender.close()
+        if self.receiver is not None:
+            torch.cuda.synchronize(self.device)
+            self.receiver.close()

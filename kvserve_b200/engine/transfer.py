@@ -1,0 +1,149 @@
+"""Layer-streamed KV hand-off of the PD engine (the product hot path).
+
+``TransferProfile`` is the fused-path view of a compression profile (the
+same ``configs/compression`` JSON the modular pipeline uses): per-section
+levels for K and V, the head split and the Hadamard seed — or ``raw`` for an
+uncompressed bf16 hand-off through the same frame machinery.
+
+``KVTransfer`` owns, for one prefill->decode channel, the per-layer head
+orders / section sizes / sign bits and issues the fused kernels:
+
+* prefill rank: ``encode(layer)`` right after layer ``l``'s K/V are written,
+  on a side stream, so the push of layer ``l`` overlaps layers ``l+1..``;
+* decode rank: ``ingest_all`` launches one persistent fused decode over all
+  layers that waits (bounded) on each layer's publish flag; in a colocated
+  deployment ``ingest_layer`` is stream-ordered right after the encode.
+
+The reference sends every layer after the whole prefill
+(kvserve_v1/connector/compressed_kv_connector.py:393-497, layer-wise
+``wait_for_layer_load`` is a no-op at :374-375); streaming is this design's.
+"""
+from __future__ import annotations
+
+import copy
+from dataclasses import dataclass, field
+from typing import Any, Optional
+
+import torch
+
+from ..compression.heads import (get_scores, low_precision_mask, pack_sign_bits, rademacher_signs,
+                                 section_orders, tp_slice_mask)
+from ..ops import kv_codec as kc
+
+DEFAULT_SEED = 3237919422
+
+
+@dataclass(frozen=True)
+class TransferProfile:
+    compressed: bool = True
+    seed: int = DEFAULT_SEED
+    hybrid_ratio: float = 0.8
+    split_type: str = "head"
+    key_levels: tuple = (6, 12)     # (low section, high section)
+    value_levels: tuple = (4, 8)
+    score_model: Optional[str] = None
+    score_path: Optional[str] = None
+
+    @classmethod
+    def raw(cls) -> "TransferProfile":
+        return cls(compressed=False)
+
+    @classmethod
+    def from_compression(cls, spec: Any, model_name: Optional[str] = None) -> "TransferProfile":
+        """From ``kv_connector_extra_config["compression"]``: ``None`` (raw),
+        ``"default"`` or a custom pipeline dict."""
+        if spec is None:
+            return cls.raw()
+        if spec == "default":
+            from ..compression.manager import get_default_compression_config
+            spec = get_default_compression_config()
+        if not isinstance(spec, dict):
+            raise TypeError("compression spec must be None, 'default' or a dict")
+        if not spec.get("enabled", True) or "quantizer" not in spec.get("pipeline", ["quantizer"]):
+            return cls.raw()
+        qc = spec.get("quantizer_config") or {}
+        tc = spec.get("transformer_config") or {}
+        seed = qc.get("base_seed", qc.get("seed", tc.get("seed", DEFAULT_SEED)))
+        return cls(compressed=True, seed=int(seed), hybrid_ratio=float(qc.get("hybrid_ratio", 0.8)),
+                   split_type=qc.get("split_type", "head"),
+                   key_levels=(int(qc.get("low_key_max_value", 6)), int(qc.get("high_key_max_value", 12))),
+                   value_levels=(int(qc.get("low_value_max_value", 4)), int(qc.get("high_value_max_value", 8))),
+                   score_model=qc.get("model_name") or model_name, score_path=qc.get("score_path"))
+
+    def to_compression(self) -> Optional[dict]:
+        if not self.compressed:
+            return None
+        return {"enabled": True, "pipeline": ["quantizer", "codec"],
+                "quantizer_config": {"impl": "tilelang_fused", "base_seed": self.seed,
+                                     "hybrid_ratio": self.hybrid_ratio, "split_type": self.split_type,
+                                     "low_key_max_value": self.key_levels[0], "high_key_max_value": self.key_levels[1],
+                                     "low_value_max_value": self.value_levels[0],
+                                     "high_value_max_value": self.value_levels[1],
+                                     "model_name": self.score_model, "axis_key": "channel", "axis_value": "token"},
+                "codec_config": {"codec_type": "bitpack", "bitpack_bits": 8}}
+
+
+class KVTransfer:
+    def __init__(self, profile: TransferProfile, num_layers: int, num_kv_heads_total: int, local_heads: int,
+                 head_dim: int, tp_rank: int, tp_size: int, device, max_tokens: int,
+                 score_model_name: Optional[str] = None):
+        self.profile = profile
+        self.L, self.H, self.D = num_layers, local_heads, head_dim
+        self.device = torch.device(device)
+        if profile.compressed:
+            scores = get_scores(profile.score_model or score_model_name, num_layers, num_kv_heads_total,
+                                profile.score_path)
+            if scores.shape != (num_layers, num_kv_heads_total):
+                scores = get_scores(None, num_layers, num_kv_heads_total)
+            mask = low_precision_mask(scores, profile.hybrid_ratio, profile.split_type)
+            mask = tp_slice_mask(mask, local_heads, tp_rank, tp_size)
+        else:
+            mask = torch.zeros((num_layers, local_heads), dtype=torch.bool)
+        orders, n_lows = section_orders(mask)
+        self.orders_cpu, self.n_lows_cpu = orders, n_lows
+        self.orders = orders.to(self.device)
+        self.n_lows = n_lows.to(self.device)
+        signs = torch.stack([rademacher_signs(profile.seed, l, local_heads, head_dim) for l in range(num_layers)])
+        self.sign_bits = pack_sign_bits(signs).to(self.device)   # [L, H, D/32]
+        self.max_tokens = max_tokens
+        self.frame_stride = max(kc.frame_layout(self.spec(l, max_tokens)).frame_bytes for l in range(num_layers))
+        self._state: Optional[kc.EncoderState] = None
+
+    def spec(self, layer: int, T: int) -> kc.FrameSpec:
+        n_low = int(self.n_lows_cpu[layer])
+        p = self.profile
+        return kc.spec_from_profile(T, self.H, self.D, n_low, p.key_levels, p.value_levels, raw=not p.compressed)
+
+    def max_spec(self, T: int) -> kc.FrameSpec:
+        """The spec of the largest frame (used as the decode kernel's base geometry)."""
+        best = max(range(self.L), key=lambda l: kc.frame_layout(self.spec(l, T)).frame_bytes)
+        return self.spec(best, T)
+
+    def payload_bytes(self, T: int) -> int:
+        return sum(kc.frame_layout(self.spec(l, T)).frame_bytes for l in range(self.L))
+
+    def raw_bytes(self, T: int) -> int:
+        return 2 * self.L * T * self.H * self.D * 2
+
+    # ------------------------------------------------------------ prefill
+    def encode(self, layer: int, k: torch.Tensor, v: torch.Tensor, frame_ptr: int, flag_ptr: int, seq: int,
+               pacing: Optional[torch.Tensor] = None, rate_bytes_per_ns: float = 0.0, max_ctas: int = 296) -> None:
+        if self._state is None:
+            self._state = kc.EncoderState(self.device)
+        kc.encode_layer(k, v, self.spec(layer, k.shape[0]), self.orders[layer], self.sign_bits[layer], frame_ptr,
+                        self._state, flag_ptr=flag_ptr, seq=seq, layer=layer, pacing=pacing,
+                        rate_bytes_per_ns=rate_bytes_per_ns, max_ctas=max_ctas)
+
+    # ------------------------------------------------------------- decode
+    def ingest_layer(self, layer: int, T: int, frame_ptr: int, kv_cache: torch.Tensor, block_table: torch.Tensor,
+                     status: torch.Tensor, seq: int, tok_offset: int = 0) -> None:
+        spec = self.spec(layer, T)
+        kc.decode_layers(frame_ptr, kc.frame_layout(spec).frame_bytes, spec, self.orders, self.sign_bits, kv_cache,
+                         block_table, status, tok_offset=tok_offset, seq=seq, layer_begin=layer, num_layers=1)
+
+    def ingest_all(self, T: int, slot_base: int, frame_stride: int, flags_ptr: int, kv_cache: torch.Tensor,
+                   block_table: torch.Tensor, status: torch.Tensor, seq: int, timeout_ns: int,
+                   tok_offset: int = 0, max_ctas: int = 64) -> None:
+        kc.decode_layers(slot_base, frame_stride, self.max_spec(T), self.orders, self.sign_bits, kv_cache,
+                         block_table, status, tok_offset=tok_offset, flags_ptr=flags_ptr, seq=seq, layer_begin=0,
+                         num_layers=self.L, timeout_ns=timeout_ns, max_ctas=max_ctas, n_lows=self.n_lows)

@@ -25,6 +25,27 @@ GEMV_MAX_M = 8
 
 _status: dict[int, torch.Tensor] = {}
 
+_DTYPE_CODES = {torch.uint8: 0, torch.int8: 1, torch.int16: 2, torch.int32: 3, torch.int64: 4,
+                torch.float16: 5, torch.float32: 6, torch.float64: 7, torch.bool: 11, torch.bfloat16: 15}
+
+
+_launches = [0]
+
+
+def count_launches(n: int = 1) -> None:
+    """Book-keeping of kernel launches issued through this package (eager
+    calls; CUDA-graph replays are accounted by their owners)."""
+    _launches[0] += n
+
+
+def launches() -> int:
+    return _launches[0]
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    """c10::ScalarType code of ``dtype`` (for tensors wrapped around raw pointers)."""
+    return _DTYPE_CODES[dtype]
+
 
 def _dev_index(device) -> int:
     if device is None:
@@ -56,30 +77,34 @@ def check_device_status(device=None, reset: bool = True) -> None:
 
 
 def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None,
-         residual: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """``out = a @ b.T (+ residual)`` on tcgen05 tensor cores (bf16 in/out, fp32 acc)."""
+         residual: Optional[torch.Tensor] = None, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``out = a @ b.T (+ bias) (+ residual)`` on tcgen05 tensor cores (bf16 in/out, fp32 acc)."""
     if out is None:
         out = torch.empty((a.shape[0], b.shape[0]), dtype=a.dtype, device=a.device)
-    ext().gemm_bf16(a, b, out, residual, device_status(a.device))
+    count_launches(1)
+    ext().gemm_bf16(a, b, out, residual, bias, device_status(a.device))
     return out
 
 
-def gemv(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """``out = x @ w.T`` for at most 8 rows (weight-streaming kernel)."""
+def gemv(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+         bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``out = x @ w.T (+ bias)`` for at most 8 rows (weight-streaming kernel)."""
     if out is None:
         out = torch.empty((x.shape[0], w.shape[0]), dtype=x.dtype, device=x.device)
-    ext().gemv_bf16(x, w, out)
+    count_launches(1)
+    ext().gemv_bf16(x, w, out, bias)
     return out
 
 
-def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """nn.Linear without bias: picks the weight-streaming GEMV for decode-size
-    batches and the tcgen05 tile GEMM otherwise."""
+def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+           bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """nn.Linear: the weight-streaming GEMV for decode-size batches, the
+    tcgen05 tile GEMM otherwise."""
     x2 = x.reshape(-1, x.shape[-1])
     if x2.shape[0] <= GEMV_MAX_M:
-        y = gemv(x2, w, out)
+        y = gemv(x2, w, out, bias)
     else:
-        y = gemm(x2, w, out)
+        y = gemm(x2, w, out, bias=bias)
     return y.view(*x.shape[:-1], w.shape[0])
 
 
@@ -88,6 +113,7 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float,
     """RMSNorm; with ``residual`` the input is first added into it (in place)."""
     if out is None:
         out = torch.empty_like(x)
+    count_launches(1)
     ext().rmsnorm(x, residual, weight, out, eps)
     return out
 
@@ -102,6 +128,7 @@ def rope_qkv(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int, head_dim: i
         tok_stride, head_stride = k_dst.stride(0), k_dst.stride(1)
     else:
         tok_stride, head_stride = 0, 0
+    count_launches(1)
     ext().rope_qkv(qkv, num_q_heads, num_kv_heads, head_dim, positions, cos_sin, k_dst, v_dst,
                    tok_stride, head_stride, slot_mapping, slot_base)
 
@@ -110,6 +137,7 @@ def silu_mul(gate_up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch
     inter = gate_up.shape[-1] // 2
     if out is None:
         out = torch.empty((*gate_up.shape[:-1], inter), dtype=gate_up.dtype, device=gate_up.device)
+    count_launches(1)
     ext().silu_mul(gate_up, out)
     return out
 
@@ -118,6 +146,7 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, vocab_begin: int = 0,
               out: Optional[torch.Tensor] = None) -> torch.Tensor:
     if out is None:
         out = torch.empty((ids.numel(), table.shape[1]), dtype=table.dtype, device=table.device)
+    count_launches(1)
     ext().embedding(ids, table, out, vocab_begin)
     return out
 
@@ -126,6 +155,7 @@ def argmax(logits: torch.Tensor, index_offset: int = 0, out_val: Optional[torch.
            out: Optional[torch.Tensor] = None) -> torch.Tensor:
     if out is None:
         out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    count_launches(1)
     ext().argmax_rows(logits, out, out_val, index_offset)
     return out
 
@@ -138,6 +168,7 @@ def flash_prefill(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int,
         scale = 1.0 / math.sqrt(d)
     if out is None:
         out = torch.empty((qkv.shape[0], num_q_heads * d), dtype=qkv.dtype, device=qkv.device)
+    count_launches(1)
     ext().flash_prefill(qkv, num_q_heads, num_kv_heads, scale, out, device_status(qkv.device))
     return out
 
@@ -158,6 +189,7 @@ def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torc
         part_ml = torch.empty(b * hq * splits * 2, dtype=torch.float32, device=q.device)
     else:
         part_o, part_ml = scratch
+    count_launches(2 if splits > 1 else 1)
     ext().paged_decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, max_ctx, scale, out,
                                  part_o, part_ml, splits)
     return out

@@ -305,6 +305,8 @@ def encode_layer(k: torch.Tensor, v: torch.Tensor, spec: FrameSpec, order: torch
                  rate_bytes_per_ns: float = 0.0, max_ctas: int = 296, tile_tokens: int = 32) -> None:
     """Launch the fused encode of one layer into ``frame_ptr`` (local or peer)."""
     from ._ext import ext
+    from . import count_launches
+    count_launches(2 if any(spec.section_heads(s) and spec.bits[0][s] != RAW_BITS for s in range(2)) else 1)
     state.prepare(spec.H * spec.D)
     ext().kv_encode_layer(k, v, spec.params(), order, sign_bits, int(frame_ptr), state.stats, state.counter,
                           int(flag_ptr), int(seq), int(layer), pacing, float(rate_bytes_per_ns), int(max_ctas),
@@ -315,12 +317,16 @@ def decode_layers(frame_base: int, frame_stride: int, spec: FrameSpec, orders: t
                   sign_bits: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tensor,
                   status: torch.Tensor, tok_offset: int = 0, flags_ptr: int = 0, seq: int = 1,
                   layer_begin: int = 0, num_layers: int = 1, timeout_ns: int = 5_000_000_000,
-                  max_ctas: int = 148, tile_tokens: int = 32) -> None:
+                  max_ctas: int = 148, tile_tokens: int = 32, n_lows: Optional[torch.Tensor] = None) -> None:
     """Launch the fused decode of ``num_layers`` consecutive frames into the
     paged cache ``kv_cache`` ``[L, 2, num_blocks, block_size, H, D]``.  With
     ``flags_ptr`` the kernel waits (bounded by ``timeout_ns``) for each
-    layer's publish flag to reach ``seq``."""
+    layer's publish flag to reach ``seq``.  ``n_lows`` (int32 [L] on the
+    device) gives each layer's low-section head count when it varies; the
+    frame stride must then hold the largest frame."""
     from ._ext import ext
+    from . import count_launches
+    count_launches(1)
     ext().kv_decode_layers(int(frame_base), int(frame_stride), spec.params(), orders, sign_bits, kv_cache,
                            block_table, int(tok_offset), int(flags_ptr), int(seq), int(layer_begin),
-                           int(num_layers), int(timeout_ns), status, int(max_ctas), int(tile_tokens))
+                           int(num_layers), int(timeout_ns), status, int(max_ctas), int(tile_tokens), n_lows)
