@@ -1,0 +1,139 @@
+"""Connector logic on CPU with a fake transport (no vLLM engine, no GPU)."""
+from collections import defaultdict, deque
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+
+class FakeTransport:
+    def __init__(self, arrivals):
+        self.arrivals = deque(arrivals)  # (transfer_id, (names, payload)) delivered one per drain
+        self.released = []
+        self.expected = []
+        self.stats = []
+        self.device = torch.device("cpu")
+        self.sent = []
+
+    def drain_received(self):
+        if not self.arrivals:
+            return {}
+        nxt = self.arrivals.popleft()
+        if nxt is None:
+            return {}
+        tid, item = nxt
+        return {tid: [item]}
+
+    def set_expected_requests(self, ids):
+        self.expected.append(list(ids))
+
+    def payload_nbytes(self, p):
+        from kvserve_b200.transport.nccl_transport import payload_nbytes
+        return payload_nbytes(p)
+
+    def release_received(self, tid, n):
+        self.released.append((tid, n))
+
+    def record_stat(self, row):
+        self.stats.append(row)
+
+    def send(self, tid, names, t):
+        self.sent.append(("raw", tid, names, t))
+
+    def send_bundle(self, tid, names, meta, body, aux):
+        self.sent.append(("bundle", tid, names, meta, body, aux))
+
+    def wait_for_sent(self):
+        pass
+
+
+def _bare(is_producer, transport, compression=None):
+    from kvserve_b200.connector.compressed_kv_connector import CompressedKVConnector
+    c = CompressedKVConnector.__new__(CompressedKVConnector)
+    c.is_producer = is_producer
+    c._transport = transport
+    c._worker_received_kv = defaultdict(deque)
+    c._layer_buffers = {}
+    c._compression_cfg = compression
+    c._compressor = None
+    c._num_kv_heads, c._head_size, c._num_layers = 4, 128, 2
+    c._model_name, c._tp_rank, c._tp_size = "synthetic", 0, 1
+    c._async_send = False
+    c._block_size = 16
+    c._request_transfer_ids = {}
+    c._requests_need_load = {}
+    c.chunked_prefill = {}
+    return c
+
+
+def _meta(*tids):
+    from kvserve_b200.connector.compressed_kv_connector import CompressedKVConnectorMetadata
+    m = CompressedKVConnectorMetadata()
+    for t in tids:
+        m.add_request("req-" + t, t, list(range(20)), [0, 1], 16)
+    return m
+
+
+def test_consumer_consumes_out_of_order_and_releases_credit(monkeypatch):
+    # "b" (scheduled second) arrives first and must not wait behind "a"
+    tr = FakeTransport([None, ("b", (["l0"], torch.zeros(1, 2, 2, 16, 4, 128))), None,
+                        ("a", (["l0"], torch.ones(1, 2, 2, 16, 4, 128)))])
+    c = _bare(False, tr)
+    c._get_connector_metadata = lambda: _meta("a", "b")
+    injected = []
+    c.inject = lambda fc, names, stacked, req: injected.append((req.transfer_id, float(stacked.sum())))
+    c.start_load_kv(SimpleNamespace())
+    assert [i[0] for i in injected] == ["b", "a"]
+    assert [r[0] for r in tr.released] == ["b", "a"] and all(n > 0 for _, n in tr.released)
+    assert tr.expected[0] == ["a", "b"] and tr.expected[-1] == []
+
+
+def test_consumer_fails_fast_on_failure_sentinel():
+    tr = FakeTransport([("a", ([], None))])
+    c = _bare(False, tr)
+    c._get_connector_metadata = lambda: _meta("a")
+    c.inject = lambda *a: None
+    with pytest.raises(RuntimeError, match="transport failed"):
+        c.start_load_kv(SimpleNamespace())
+
+
+def test_consumer_times_out(monkeypatch):
+    import kvserve_b200.connector.compressed_kv_connector as mod
+    monkeypatch.setattr(mod, "LOAD_TIMEOUT_S", 0.1)
+    tr = FakeTransport([])
+    c = _bare(False, tr)
+    c._get_connector_metadata = lambda: _meta("x")
+    with pytest.raises(TimeoutError):
+        c.start_load_kv(SimpleNamespace())
+    assert any(s.get("kind") == "timeout" for s in tr.stats)
+
+
+def test_producer_compressed_bundle_round_trip():
+    from test_compression_cpu import CFG0, synthetic_kv
+    tr = FakeTransport([])
+    prod = _bare(True, tr, compression=CFG0)
+    kv = synthetic_kv()  # [L, 2, 1, 256, 4, 128]
+    stacked = kv.view(2, 2, 16, 16, 4, 128)
+    prod.send_stacked("req-1", "t-1", ["l0", "l1"], stacked)
+    kind, tid, names, meta, body, aux = tr.sent[0]
+    assert kind == "bundle" and names[0] == "__compressed__"
+    cons = _bare(False, FakeTransport([("t-1", (names, {"__bundle__": True, "meta": meta, "body_chunks": body,
+                                                        "aux_tensors": aux}))]), compression=CFG0)
+    cons._get_connector_metadata = lambda: _meta("t-1")
+    got = []
+    cons.inject = lambda fc, n, s, req: got.append((n, s))
+    cons.start_load_kv(SimpleNamespace())
+    names_out, restored = got[0]
+    assert names_out == ["l0", "l1"] and restored.shape == stacked.shape
+    assert ((restored.float() - stacked.float()).norm() / stacked.float().norm()) < 0.2
+
+
+def test_scheduler_claims_prompt_minus_one():
+    c = _bare(False, FakeTransport([]))
+    req = SimpleNamespace(prompt_token_ids=list(range(100)), request_id="r", kv_transfer_params={"transfer_id": "T"})
+    assert c.get_num_new_matched_tokens(req, 0) == (99, False)
+    assert c.get_num_new_matched_tokens(req, 99) == (0, False)
+    c.update_state_after_alloc(req, SimpleNamespace(get_block_ids=lambda: [[3, 4]]), 99)
+    assert c._resolve_transfer_id("r") == "T" and "r" in c._requests_need_load
+    p = _bare(True, FakeTransport([]))
+    assert p.get_num_new_matched_tokens(req, 0) == (0, False)
