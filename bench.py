@@ -36,6 +36,11 @@ def _emit(obj) -> None:
     print(json.dumps(obj), flush=True)
 
 
+def _log(msg: str) -> None:
+    if os.environ.get("KVS_BENCH_VERBOSE"):
+        print(f"[bench r{os.environ.get('RANK', '0')} {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
 def _profile(name: str):
     from kvserve_b200.engine.transfer import TransferProfile
     if name == "raw":
@@ -74,6 +79,9 @@ def main() -> None:
         return
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    if os.environ.get("KVS_BENCH_DUMP_AFTER"):
+        import faulthandler
+        faulthandler.dump_traceback_later(float(os.environ["KVS_BENCH_DUMP_AFTER"]), repeat=True)
 
     from kvserve_b200.models.config import get_config
     from kvserve_b200.parallel.context import init_parallel, destroy_parallel
@@ -90,13 +98,16 @@ def main() -> None:
     profile = _profile(args.profile)
     engine = PDEngine(cfg, ctx, profile, max_prompt=args.prompt_len - 1, max_new_tokens=args.max_new,
                       link_gbps=args.link_gbps, use_graphs=not args.no_graphs)
+    _log("engine built")
     engine.warmup(prompt_len=min(512, args.prompt_len))
+    _log("engine warm")
 
     g = torch.Generator().manual_seed(1234)
     prompts = [torch.randint(0, cfg.vocab, (args.prompt_len,), generator=g, dtype=torch.int32).pin_memory()
                for _ in range(args.warmup + args.steps)]
     for i in range(args.warmup):
         engine.generate(prompts[i], args.max_new)
+        _log(f"warmup step {i} done")
 
     sampler = None
     if ctx.rank == 0:

@@ -15,6 +15,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bitpack_encode", &kvs::bitpack_encode);
   m.def("bitpack_decode", &kvs::bitpack_decode);
   m.def("fwht_rows", &kvs::fwht_rows);
+  // lossless codec
+  m.def("rze_max_encoded_bytes", &kvs::rze_max_encoded_bytes);
+  m.def("rze_scratch_bytes", &kvs::rze_scratch_bytes);
+  m.def("rze_encode", &kvs::rze_encode);
+  m.def("rze_decode", &kvs::rze_decode);
   // peer memory
   m.def("dev_alloc", &kvs::dev_alloc);
   m.def("dev_free", &kvs::dev_free);

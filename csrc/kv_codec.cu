@@ -57,7 +57,21 @@ struct EncodeArgs {
   int64_t* pacing;            // [1] next free time (ns) of the emulated link
   double rate_bytes_per_ns;   // 0 = no link emulation
   int tile_tokens;
+  int part_mask;              // bit 0: encode K, bit 1: encode V
+  const int32_t* block_table; // paged source: token t lives in block block_table[t / block_size]
+  int block_size;
+  int64_t k_block_stride, v_block_stride;
 };
+
+// Address of row (token t, head h) of a K or V source that is either a
+// contiguous [T, H, D] view or a paged cache read through a block table.
+__device__ __forceinline__ const bf16* src_row(const bf16* base, int t, int h, int64_t tok_stride,
+                                               int64_t head_stride, const int32_t* table, int bs,
+                                               int64_t block_stride) {
+  if (table != nullptr)
+    return base + int64_t(table[t / bs]) * block_stride + int64_t(t % bs) * tok_stride + int64_t(h) * head_stride;
+  return base + int64_t(t) * tok_stride + int64_t(h) * head_stride;
+}
 
 struct DecodeArgs {
   const uint8_t* frame_base;
@@ -72,6 +86,8 @@ struct DecodeArgs {
   int tok_offset;
   const uint32_t* flags;      // [L] or null (stream-ordered, no wait)
   const int32_t* n_lows;      // [L] low-section head count per layer, or null
+  const int64_t* layer_ptrs;  // [L][2] K/V base address per layer, or null (use cache + strides)
+  int part_mask;              // bit 0: decode K, bit 1: decode V
   uint32_t seq;
   int layer_begin;
   int num_layers;
@@ -207,7 +223,7 @@ __global__ void __launch_bounds__(kThreads) kv_kstats_kernel(EncodeArgs a) {
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int lir = lane % LANES, rw = lane / LANES;
-  const float scale = inv_sqrt_d<D>();
+  const float scale = a.g.transform ? inv_sqrt_d<D>() : 1.0f;
   const bool fixed_slot = (kRowsPerIter % g.H) == 0;
   float mn[8], mx[8];
 #pragma unroll
@@ -226,13 +242,14 @@ __global__ void __launch_bounds__(kThreads) kv_kstats_kernel(EncodeArgs a) {
       if (valid) {
         const int h = a.order[j];
         uint4 raw;
-        load8(a.k + t * a.k_tok_stride + h * a.k_head_stride + lir * 8, v, raw);
-        apply_signs(v, sign_byte(a.sign_bits + h * (D / 32), lir));
+        load8(src_row(a.k, t, h, a.k_tok_stride, a.k_head_stride, a.block_table, a.block_size, a.k_block_stride) +
+                  lir * 8, v, raw);
+        if (a.g.transform) apply_signs(v, sign_byte(a.sign_bits + h * (D / 32), lir));
       } else {
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] = 0.f;
       }
-      fwht_row<LANES>(v, lir);
+      if (g.transform) fwht_row<LANES>(v, lir);
       if (!valid) continue;
       int s, js, hs;
       slot_section(g, j, s, js, hs);
@@ -297,7 +314,8 @@ __device__ void encode_signal_done(const EncodeArgs& a) {
         h.bits[p][s] = uint8_t(a.g.bits[p][s]);
         h.levels[p][s] = uint8_t(a.g.levels[p][s] - 1);
       }
-    for (int i = 0; i < 6; ++i) h.reserved[i] = 0;
+    h.transform = uint32_t(a.g.transform);
+    for (int i = 0; i < 5; ++i) h.reserved[i] = 0;
     const uint4* src = reinterpret_cast<const uint4*>(&h);
     uint4* dst = reinterpret_cast<uint4*>(a.frame);
     for (int i = 0; i < 4; ++i) dst[i] = src[i];
@@ -328,9 +346,9 @@ __global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
   const int HD = g.H * D;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int lir = lane % LANES, rw = lane / LANES;
-  const float scale = inv_sqrt_d<D>();
+  const float scale = a.g.transform ? inv_sqrt_d<D>() : 1.0f;
   const int ntiles = int(ceil_div(g.T, a.tile_tokens));
-  const int part = blockIdx.y;
+  const int part = a.part_mask == 2 ? 1 : int(blockIdx.y);
 
   if (part == 0) {
     // ---- K: per-channel parameters from the global statistics ----
@@ -370,13 +388,14 @@ __global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
         uint4 raw = make_uint4(0, 0, 0, 0);
         if (valid) {
           const int h = a.order[j];
-          load8(a.k + t * a.k_tok_stride + h * a.k_head_stride + lir * 8, v, raw);
-          apply_signs(v, sign_byte(a.sign_bits + h * (D / 32), lir));
+          load8(src_row(a.k, t, h, a.k_tok_stride, a.k_head_stride, a.block_table, a.block_size,
+                        a.k_block_stride) + lir * 8, v, raw);
+          if (a.g.transform) apply_signs(v, sign_byte(a.sign_bits + h * (D / 32), lir));
         } else {
 #pragma unroll
           for (int e = 0; e < 8; ++e) v[e] = 0.f;
         }
-        fwht_row<LANES>(v, lir);
+        if (g.transform) fwht_row<LANES>(v, lir);
         if (!valid) continue;
         int s, js, hs;
         slot_section(g, j, s, js, hs);
@@ -423,13 +442,14 @@ __global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
           const int j = rw + RPW * i;
           if (j < g.H) {
             const int h = a.order[j];
-            load8(a.v + t * a.v_tok_stride + h * a.v_head_stride + lir * 8, v[i], raw[i]);
-            apply_signs(v[i], sign_byte(a.sign_bits + h * (D / 32), lir));
+            load8(src_row(a.v, t, h, a.v_tok_stride, a.v_head_stride, a.block_table, a.block_size,
+                          a.v_block_stride) + lir * 8, v[i], raw[i]);
+            if (a.g.transform) apply_signs(v[i], sign_byte(a.sign_bits + h * (D / 32), lir));
           } else {
 #pragma unroll
             for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
           }
-          fwht_row<LANES>(v[i], lir);
+          if (g.transform) fwht_row<LANES>(v[i], lir);
           if (j < g.H) {
             const int s = j < g.n_low ? 0 : 1;
 #pragma unroll
@@ -498,9 +518,9 @@ __global__ void __launch_bounds__(kThreads) kv_decode_kernel(DecodeArgs a) {
   const int HD = a.g.H * D;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int lir = lane % LANES, rw = lane / LANES;
-  const float scale = inv_sqrt_d<D>();
+  const float scale = a.g.transform ? inv_sqrt_d<D>() : 1.0f;
   const int ntiles = int(ceil_div(a.g.T, a.tile_tokens));
-  const int part = blockIdx.y;
+  const int part = a.part_mask == 2 ? 1 : int(blockIdx.y);
 
   for (int li = 0; li < a.num_layers; ++li) {
     const int layer = a.layer_begin + li;
@@ -532,7 +552,9 @@ __global__ void __launch_bounds__(kThreads) kv_decode_kernel(DecodeArgs a) {
     asm volatile("fence.acq_rel.sys;" ::: "memory");
     const int32_t* order = a.orders + int64_t(layer) * g.H;
     const uint32_t* sbits = a.sign_bits + int64_t(layer) * g.H * (D / 32);
-    bf16* cache = a.cache + int64_t(layer) * a.layer_stride + int64_t(part) * a.part_stride;
+    bf16* cache = a.layer_ptrs != nullptr
+                      ? reinterpret_cast<bf16*>(a.layer_ptrs[2 * layer + part])
+                      : a.cache + int64_t(layer) * a.layer_stride + int64_t(part) * a.part_stride;
     if (part == 0) {
       const bf16* kmin = reinterpret_cast<const bf16*>(frame + g.k_aux);
       for (int c = threadIdx.x; c < HD; c += kThreads) {
@@ -586,7 +608,7 @@ __global__ void __launch_bounds__(kThreads) kv_decode_kernel(DecodeArgs a) {
 #pragma unroll
           for (int e = 0; e < 8; ++e) v[e] = 0.f;
         }
-        fwht_row<LANES>(v, lir);
+        if (g.transform) fwht_row<LANES>(v, lir);
         if (!valid) continue;
         const int h = order[j];
         const int pos = a.tok_offset + t;
@@ -597,7 +619,7 @@ __global__ void __launch_bounds__(kThreads) kv_decode_kernel(DecodeArgs a) {
           *reinterpret_cast<uint4*>(dst) = rawv;
           continue;
         }
-        const uint32_t sb = sign_byte(sbits + h * (D / 32), lir);
+        const uint32_t sb = g.transform ? sign_byte(sbits + h * (D / 32), lir) : 0u;
         uint4 out;
         __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&out);
 #pragma unroll
@@ -615,7 +637,7 @@ __global__ void __launch_bounds__(kThreads) kv_decode_kernel(DecodeArgs a) {
 }
 
 FrameGeom geom_from(const std::vector<int64_t>& p) {
-  KVS_CHECK_ARG(p.size() == 12, "frame geometry needs 12 integers");
+  KVS_CHECK_ARG(p.size() == 12 || p.size() == 13, "frame geometry needs 12 or 13 integers");
   FrameGeom g{};
   g.T = int32_t(p[0]);
   g.H = int32_t(p[1]);
@@ -629,6 +651,7 @@ FrameGeom geom_from(const std::vector<int64_t>& p) {
   g.levels[0][1] = int32_t(p[9]);
   g.levels[1][0] = int32_t(p[10]);
   g.levels[1][1] = int32_t(p[11]);
+  g.transform = p.size() == 13 ? int32_t(p[12] != 0) : 1;
   KVS_CHECK_ARG(g.T >= 0 && g.H >= 1 && g.n_low >= 0 && g.n_low <= g.H, "bad T/H/n_low");
   KVS_CHECK_ARG(g.D == 64 || g.D == 128 || g.D == 256, "head_dim must be 64, 128 or 256");
   KVS_CHECK_ARG(g.H * g.D <= 2048, "fused KV codec supports H*D <= 2048 per shard");
@@ -663,31 +686,56 @@ void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom
                      torch::Tensor order, torch::Tensor sign_bits, int64_t frame_ptr,
                      torch::Tensor stats, torch::Tensor counter, int64_t flag_ptr, int64_t seq,
                      int64_t layer, c10::optional<torch::Tensor> pacing, double rate_bytes_per_ns,
-                     int64_t max_ctas, int64_t tile_tokens) {
+                     int64_t max_ctas, int64_t tile_tokens, int64_t part_mask,
+                     c10::optional<torch::Tensor> block_table, bool hnd) {
   const FrameGeom g = geom_from(geom);
+  KVS_CHECK_ARG(part_mask >= 1 && part_mask <= 3, "part_mask must be 1 (K), 2 (V) or 3");
   KVS_CHECK_ARG(k.is_cuda() && v.is_cuda() && k.scalar_type() == at::kBFloat16 &&
                     v.scalar_type() == at::kBFloat16,
                 "k/v must be CUDA bf16");
-  KVS_CHECK_ARG(k.dim() == 3 && v.dim() == 3 && k.size(0) == g.T && v.size(0) == g.T &&
-                    k.size(2) == g.D && k.stride(2) == 1 && v.stride(2) == 1,
-                "k/v must be [T, H, D] with contiguous D");
+  EncodeArgs a{};
+  int64_t src_heads;
+  if (block_table.has_value()) {
+    // paged source: [num_blocks, block_size, H, D] (NHD) or [num_blocks, H, block_size, D] (HND)
+    KVS_CHECK_ARG(k.dim() == 4 && v.dim() == 4 && k.size(3) == g.D && k.stride(3) == 1 && v.stride(3) == 1 &&
+                      k.sizes() == v.sizes(),
+                  "paged k/v must be 4-D with contiguous D");
+    KVS_CHECK_ARG(block_table->scalar_type() == at::kInt && block_table->is_cuda(), "block_table: int32 CUDA");
+    const int tok_dim = hnd ? 2 : 1, head_dim = hnd ? 1 : 2;
+    a.block_table = block_table->data_ptr<int32_t>();
+    a.block_size = int(k.size(tok_dim));
+    KVS_CHECK_ARG(block_table->numel() * a.block_size >= g.T, "block_table too short for T tokens");
+    a.k_block_stride = k.stride(0);
+    a.v_block_stride = v.stride(0);
+    a.k_tok_stride = k.stride(tok_dim);
+    a.k_head_stride = k.stride(head_dim);
+    a.v_tok_stride = v.stride(tok_dim);
+    a.v_head_stride = v.stride(head_dim);
+    src_heads = k.size(head_dim);
+  } else {
+    KVS_CHECK_ARG(k.dim() == 3 && v.dim() == 3 && k.size(0) == g.T && v.size(0) == g.T &&
+                      k.size(2) == g.D && k.stride(2) == 1 && v.stride(2) == 1,
+                  "k/v must be [T, H, D] with contiguous D");
+    a.k_tok_stride = k.stride(0);
+    a.k_head_stride = k.stride(1);
+    a.v_tok_stride = v.stride(0);
+    a.v_head_stride = v.stride(1);
+    src_heads = k.size(1);
+  }
   KVS_CHECK_ARG((reinterpret_cast<uintptr_t>(k.data_ptr()) & 15) == 0 &&
-                    (reinterpret_cast<uintptr_t>(v.data_ptr()) & 15) == 0 && k.stride(0) % 8 == 0 &&
-                    k.stride(1) % 8 == 0 && v.stride(0) % 8 == 0 && v.stride(1) % 8 == 0,
+                    (reinterpret_cast<uintptr_t>(v.data_ptr()) & 15) == 0 && a.k_tok_stride % 8 == 0 &&
+                    a.k_head_stride % 8 == 0 && a.v_tok_stride % 8 == 0 && a.v_head_stride % 8 == 0 &&
+                    a.k_block_stride % 8 == 0 && a.v_block_stride % 8 == 0,
                 "k/v rows must be 16-byte aligned");
   KVS_CHECK_ARG(order.scalar_type() == at::kInt && order.numel() == g.H && order.is_cuda(), "order: int32[H]");
+  KVS_CHECK_ARG(src_heads >= g.H, "source has fewer heads than the frame");
   KVS_CHECK_ARG(sign_bits.scalar_type() == at::kInt && sign_bits.is_cuda() &&
-                    sign_bits.numel() >= int64_t(k.size(1)) * g.D / 32,
+                    sign_bits.numel() >= src_heads * g.D / 32,
                 "sign_bits: int32[H_orig, D/32]");
   KVS_CHECK_ARG(stats.numel() >= 2 * g.H * g.D && counter.numel() >= 1, "stats/counter too small");
   KVS_CHECK_ARG((frame_ptr & 255) == 0, "frame must be 256-byte aligned");
-  EncodeArgs a{};
   a.k = reinterpret_cast<const bf16*>(k.data_ptr());
   a.v = reinterpret_cast<const bf16*>(v.data_ptr());
-  a.k_tok_stride = k.stride(0);
-  a.k_head_stride = k.stride(1);
-  a.v_tok_stride = v.stride(0);
-  a.v_head_stride = v.stride(1);
   a.g = g;
   a.order = order.data_ptr<int32_t>();
   a.sign_bits = reinterpret_cast<const uint32_t*>(sign_bits.data_ptr<int32_t>());
@@ -700,6 +748,7 @@ void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom
   a.pacing = pacing.has_value() ? pacing->data_ptr<int64_t>() : nullptr;
   a.rate_bytes_per_ns = rate_bytes_per_ns;
   a.tile_tokens = int(tile_tokens);
+  a.part_mask = int(part_mask);
   const int ntiles = std::max<int>(1, int(ceil_div(g.T, tile_tokens)));
   const int ctas = std::max<int>(1, std::min<int>(ntiles, int(max_ctas)));
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
@@ -707,8 +756,8 @@ void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom
   bool any_k_quant = false;
   for (int s = 0; s < 2; ++s)
     if (section_heads(g, s) > 0 && g.bits[0][s] != kRawBits) any_k_quant = true;
-  if (any_k_quant && g.T > 0) launch_kstats(g.D, dim3(ctas), smem, st, a);
-  dim3 grid(ctas, 2);
+  if (any_k_quant && g.T > 0 && (a.part_mask & 1)) launch_kstats(g.D, dim3(ctas), smem, st, a);
+  dim3 grid(ctas, a.part_mask == 3 ? 2 : 1);
   switch (g.D) {
     case 64: kv_quant_kernel<64><<<grid, kThreads, smem, st>>>(a); break;
     case 128: kv_quant_kernel<128><<<grid, kThreads, smem, st>>>(a); break;
@@ -722,35 +771,57 @@ void kv_decode_layers(int64_t frame_base, int64_t frame_stride, std::vector<int6
                       torch::Tensor block_table, int64_t tok_offset, int64_t flags_ptr, int64_t seq,
                       int64_t layer_begin, int64_t num_layers, int64_t timeout_ns,
                       torch::Tensor status, int64_t max_ctas, int64_t tile_tokens,
-                      c10::optional<torch::Tensor> n_lows) {
+                      c10::optional<torch::Tensor> n_lows, int64_t part_mask,
+                      c10::optional<torch::Tensor> layer_ptrs, bool hnd) {
   const FrameGeom g = geom_from(geom);
-  KVS_CHECK_ARG(kv_cache.is_cuda() && kv_cache.scalar_type() == at::kBFloat16 && kv_cache.dim() == 6,
-                "kv_cache must be CUDA bf16 [L, 2, num_blocks, block_size, H, D]");
-  KVS_CHECK_ARG(kv_cache.size(4) == g.H && kv_cache.size(5) == g.D && kv_cache.stride(5) == 1,
-                "kv_cache head geometry mismatch");
-  const int64_t L = kv_cache.size(0);
+  KVS_CHECK_ARG(part_mask >= 1 && part_mask <= 3, "part_mask must be 1 (K), 2 (V) or 3");
+  KVS_CHECK_ARG(kv_cache.is_cuda() && kv_cache.scalar_type() == at::kBFloat16, "kv_cache must be CUDA bf16");
+  DecodeArgs a{};
+  int64_t L, bs;
+  if (layer_ptrs.has_value()) {
+    // per-layer K/V tensors; kv_cache is one of them as a layout template:
+    // [num_blocks, block_size, H, D] (NHD) or [num_blocks, H, block_size, D] (HND)
+    KVS_CHECK_ARG(kv_cache.dim() == 4 && kv_cache.size(3) == g.D && kv_cache.stride(3) == 1,
+                  "layout template must be a 4-D per-layer cache view");
+    KVS_CHECK_ARG(layer_ptrs->scalar_type() == at::kLong && layer_ptrs->is_cuda() && layer_ptrs->dim() == 2 &&
+                      layer_ptrs->size(1) == 2,
+                  "layer_ptrs: int64 [L, 2] on the device");
+    L = layer_ptrs->size(0);
+    const int tok_dim = hnd ? 2 : 1, head_dim = hnd ? 1 : 2;
+    KVS_CHECK_ARG(kv_cache.size(head_dim) == g.H, "kv_cache head geometry mismatch");
+    bs = kv_cache.size(tok_dim);
+    a.layer_ptrs = layer_ptrs->data_ptr<int64_t>();
+    a.block_stride = kv_cache.stride(0);
+    a.token_stride = kv_cache.stride(tok_dim);
+    a.head_stride = kv_cache.stride(head_dim);
+  } else {
+    KVS_CHECK_ARG(kv_cache.dim() == 6, "kv_cache must be [L, 2, num_blocks, block_size, H, D]");
+    KVS_CHECK_ARG(kv_cache.size(4) == g.H && kv_cache.size(5) == g.D && kv_cache.stride(5) == 1,
+                  "kv_cache head geometry mismatch");
+    L = kv_cache.size(0);
+    bs = kv_cache.size(3);
+    a.layer_stride = kv_cache.stride(0);
+    a.part_stride = kv_cache.stride(1);
+    a.block_stride = kv_cache.stride(2);
+    a.token_stride = kv_cache.stride(3);
+    a.head_stride = kv_cache.stride(4);
+  }
   KVS_CHECK_ARG(layer_begin >= 0 && num_layers >= 1 && layer_begin + num_layers <= L, "bad layer range");
   KVS_CHECK_ARG(orders.scalar_type() == at::kInt && orders.numel() == L * g.H, "orders: int32[L, H]");
   KVS_CHECK_ARG(sign_bits.scalar_type() == at::kInt && sign_bits.numel() == L * g.H * (g.D / 32),
                 "sign_bits: int32[L, H, D/32]");
   KVS_CHECK_ARG(block_table.scalar_type() == at::kInt && block_table.is_cuda(), "block_table: int32");
-  const int64_t bs = kv_cache.size(3);
   KVS_CHECK_ARG(block_table.numel() * bs >= tok_offset + g.T, "block_table too short");
   KVS_CHECK_ARG(status.scalar_type() == at::kInt && status.numel() >= 1, "status: int32[1]");
   KVS_CHECK_ARG((frame_base & 255) == 0 && (frame_stride & 255) == 0 && frame_stride >= g.frame_bytes,
                 "frame base/stride must be 256-byte aligned and hold one frame");
-  DecodeArgs a{};
   a.frame_base = reinterpret_cast<const uint8_t*>(frame_base);
   a.frame_stride = frame_stride;
   a.g = g;
   a.orders = orders.data_ptr<int32_t>();
   a.sign_bits = reinterpret_cast<const uint32_t*>(sign_bits.data_ptr<int32_t>());
   a.cache = reinterpret_cast<bf16*>(kv_cache.data_ptr());
-  a.layer_stride = kv_cache.stride(0);
-  a.part_stride = kv_cache.stride(1);
-  a.block_stride = kv_cache.stride(2);
-  a.token_stride = kv_cache.stride(3);
-  a.head_stride = kv_cache.stride(4);
+  a.part_mask = int(part_mask);
   a.block_table = block_table.data_ptr<int32_t>();
   a.block_size = int(bs);
   a.tok_offset = int(tok_offset);
@@ -770,7 +841,7 @@ void kv_decode_layers(int64_t frame_base, int64_t frame_stride, std::vector<int6
   a.tile_tokens = int(tile_tokens);
   const int ntiles = std::max<int>(1, int(ceil_div(g.T, tile_tokens)));
   const int ctas = std::max<int>(1, std::min<int>(ntiles, int(max_ctas)));
-  dim3 grid(ctas, 2);
+  dim3 grid(ctas, a.part_mask == 3 ? 2 : 1);
   const size_t smem = size_t(2) * g.H * g.D * 4;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   switch (g.D) {

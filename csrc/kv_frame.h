@@ -49,7 +49,8 @@ struct FrameHeader {
   uint32_t seq;
   uint8_t bits[2][2];
   uint8_t levels[2][2];
-  uint32_t reserved[6];
+  uint32_t transform;
+  uint32_t reserved[5];
 };
 static_assert(sizeof(FrameHeader) == 64, "frame header is 64 bytes");
 
@@ -60,6 +61,7 @@ struct FrameGeom {
   int32_t n_low;           // heads in section 0
   int32_t bits[2][2];      // [part][section]; 16 = raw bf16
   int32_t levels[2][2];    // quantisation levels (symbols 0..levels-1)
+  int32_t transform;       // 1: random-sign Hadamard before quantisation, 0: none
   int64_t k_aux;           // offset of K min/scale
   int64_t v_aux[2];        // offset of V min/scale per section
   int64_t payload[2][2];   // offset of the BitPack block per [part][section]

@@ -12,17 +12,25 @@ std::vector<int64_t> kv_frame_geom(std::vector<int64_t> params);
 void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom, torch::Tensor order,
                      torch::Tensor sign_bits, int64_t frame_ptr, torch::Tensor stats, torch::Tensor counter,
                      int64_t flag_ptr, int64_t seq, int64_t layer, c10::optional<torch::Tensor> pacing,
-                     double rate_bytes_per_ns, int64_t max_ctas, int64_t tile_tokens);
+                     double rate_bytes_per_ns, int64_t max_ctas, int64_t tile_tokens, int64_t part_mask,
+                     c10::optional<torch::Tensor> block_table, bool hnd);
 void kv_decode_layers(int64_t frame_base, int64_t frame_stride, std::vector<int64_t> geom, torch::Tensor orders,
                       torch::Tensor sign_bits, torch::Tensor kv_cache, torch::Tensor block_table,
                       int64_t tok_offset, int64_t flags_ptr, int64_t seq, int64_t layer_begin, int64_t num_layers,
                       int64_t timeout_ns, torch::Tensor status, int64_t max_ctas, int64_t tile_tokens,
-                      c10::optional<torch::Tensor> n_lows);
+                      c10::optional<torch::Tensor> n_lows, int64_t part_mask,
+                      c10::optional<torch::Tensor> layer_ptrs, bool hnd);
 
 // ---- modular pipeline kernels (bitpack.cu)
 void bitpack_encode(torch::Tensor src, torch::Tensor out, int64_t bits, torch::Tensor status);
 void bitpack_decode(torch::Tensor src, torch::Tensor out, int64_t bits, torch::Tensor status);
 void fwht_rows(torch::Tensor x, torch::Tensor y, c10::optional<torch::Tensor> signs, bool inverse);
+
+// ---- lossless codec (lossless.cu)
+int64_t rze_max_encoded_bytes(int64_t n, int64_t chunk);
+int64_t rze_scratch_bytes(int64_t n, int64_t chunk);
+void rze_encode(torch::Tensor src, torch::Tensor out, torch::Tensor scratch, torch::Tensor out_total, int64_t chunk);
+void rze_decode(torch::Tensor src, torch::Tensor out, torch::Tensor scratch, int64_t chunk);
 
 // ---- peer memory (p2p.cu)
 int64_t dev_alloc(int64_t bytes);

@@ -50,17 +50,18 @@ class FrameSpec:
     n_low: int
     bits: tuple = ((4, 4), (4, 4))
     levels: tuple = ((16, 16), (16, 16))
+    transform: bool = True
 
     def params(self) -> list[int]:
         return [self.T, self.H, self.D, self.n_low,
                 self.bits[0][0], self.bits[0][1], self.bits[1][0], self.bits[1][1],
-                self.levels[0][0], self.levels[0][1], self.levels[1][0], self.levels[1][1]]
+                self.levels[0][0], self.levels[0][1], self.levels[1][0], self.levels[1][1], int(self.transform)]
 
     def section_heads(self, s: int) -> int:
         return self.n_low if s == 0 else self.H - self.n_low
 
     def with_tokens(self, T: int) -> "FrameSpec":
-        return FrameSpec(T, self.H, self.D, self.n_low, self.bits, self.levels)
+        return FrameSpec(T, self.H, self.D, self.n_low, self.bits, self.levels, self.transform)
 
 
 @dataclass(frozen=True)
@@ -173,11 +174,14 @@ def cpu_encode_frame(k: torch.Tensor, v: torch.Tensor, spec: FrameSpec, order: t
     buf = bytearray(lay.frame_bytes)
     hdr = np.zeros(16, dtype=np.uint32)
     hdr[:8] = [FRAME_MAGIC, 1, layer, T, H, D, spec.n_low, seq]
+    hdr[10] = int(spec.transform)
     hb = bytearray(hdr.tobytes())
     hb[32:36] = bytes([spec.bits[0][0], spec.bits[0][1], spec.bits[1][0], spec.bits[1][1]])
     hb[36:40] = bytes([spec.levels[0][0] - 1, spec.levels[0][1] - 1, spec.levels[1][0] - 1, spec.levels[1][1] - 1])
     buf[0:64] = hb
-    Hm = hadamard_matrix(D) / math.sqrt(D)
+    Hm = hadamard_matrix(D) / math.sqrt(D) if spec.transform else torch.eye(D)
+    if not spec.transform:
+        signs = torch.ones_like(signs)
     order_l = [int(x) for x in order.tolist()]
     sec_heads = [order_l[:spec.n_low], order_l[spec.n_low:]]
     for p, x in enumerate((k, v)):
@@ -230,7 +234,9 @@ def cpu_decode_frame(buf: bytes, spec: FrameSpec, order: torch.Tensor, signs: to
     """Reference decoder -> (k, v) bf16 ``[T, H, D]`` in original head order."""
     T, H, D = spec.T, spec.H, spec.D
     lay = frame_layout(spec)
-    Hm = hadamard_matrix(D) / math.sqrt(D)
+    Hm = hadamard_matrix(D) / math.sqrt(D) if spec.transform else torch.eye(D)
+    if not spec.transform:
+        signs = torch.ones_like(signs)
     order_l = [int(x) for x in order.tolist()]
     sec_heads = [order_l[:spec.n_low], order_l[spec.n_low:]]
     outs = []
@@ -302,22 +308,30 @@ class EncoderState:
 def encode_layer(k: torch.Tensor, v: torch.Tensor, spec: FrameSpec, order: torch.Tensor,
                  sign_bits: torch.Tensor, frame_ptr: int, state: EncoderState, flag_ptr: int = 0,
                  seq: int = 1, layer: int = 0, pacing: Optional[torch.Tensor] = None,
-                 rate_bytes_per_ns: float = 0.0, max_ctas: int = 296, tile_tokens: int = 32) -> None:
-    """Launch the fused encode of one layer into ``frame_ptr`` (local or peer)."""
+                 rate_bytes_per_ns: float = 0.0, max_ctas: int = 296, tile_tokens: int = 32,
+                 part_mask: int = 3, block_table: Optional[torch.Tensor] = None, hnd: bool = False) -> None:
+    """Launch the fused encode of one layer into ``frame_ptr`` (local or peer).
+
+    ``k``/``v`` are ``[T, H, D]`` views, or — with ``block_table`` — paged
+    per-layer caches ``[num_blocks, block_size, H, D]`` (``hnd``: ``[num_blocks,
+    H, block_size, D]``) read through the block table (fused gather).
+    ``part_mask`` selects K (1), V (2) or both (3)."""
     from ._ext import ext
     from . import count_launches
-    count_launches(2 if any(spec.section_heads(s) and spec.bits[0][s] != RAW_BITS for s in range(2)) else 1)
+    count_launches(2 if (part_mask & 1) and any(spec.section_heads(s) and spec.bits[0][s] != RAW_BITS
+                                                for s in range(2)) else 1)
     state.prepare(spec.H * spec.D)
     ext().kv_encode_layer(k, v, spec.params(), order, sign_bits, int(frame_ptr), state.stats, state.counter,
                           int(flag_ptr), int(seq), int(layer), pacing, float(rate_bytes_per_ns), int(max_ctas),
-                          int(tile_tokens))
+                          int(tile_tokens), int(part_mask), block_table, bool(hnd))
 
 
 def decode_layers(frame_base: int, frame_stride: int, spec: FrameSpec, orders: torch.Tensor,
                   sign_bits: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tensor,
                   status: torch.Tensor, tok_offset: int = 0, flags_ptr: int = 0, seq: int = 1,
                   layer_begin: int = 0, num_layers: int = 1, timeout_ns: int = 5_000_000_000,
-                  max_ctas: int = 148, tile_tokens: int = 32, n_lows: Optional[torch.Tensor] = None) -> None:
+                  max_ctas: int = 148, tile_tokens: int = 32, n_lows: Optional[torch.Tensor] = None,
+                  part_mask: int = 3, layer_ptrs: Optional[torch.Tensor] = None, hnd: bool = False) -> None:
     """Launch the fused decode of ``num_layers`` consecutive frames into the
     paged cache ``kv_cache`` ``[L, 2, num_blocks, block_size, H, D]``.  With
     ``flags_ptr`` the kernel waits (bounded by ``timeout_ns``) for each
@@ -329,4 +343,5 @@ def decode_layers(frame_base: int, frame_stride: int, spec: FrameSpec, orders: t
     count_launches(1)
     ext().kv_decode_layers(int(frame_base), int(frame_stride), spec.params(), orders, sign_bits, kv_cache,
                            block_table, int(tok_offset), int(flags_ptr), int(seq), int(layer_begin),
-                           int(num_layers), int(timeout_ns), status, int(max_ctas), int(tile_tokens), n_lows)
+                           int(num_layers), int(timeout_ns), status, int(max_ctas), int(tile_tokens), n_lows,
+                           int(part_mask), layer_ptrs, bool(hnd))

@@ -299,3 +299,20 @@ def test_decode_wait_times_out_without_fault():
     assert int(st[0].item()) == 1
     # the context is still usable
     assert float(torch.ones(4, device="cuda").sum().item()) == 4.0
+
+
+@pytest.mark.parametrize("n", [5, 16384, 100000, 3 * 16384 + 17])
+def test_lossless_gpu_matches_cpu_bytes(n):
+    from kvserve_b200.compression.codec.lossless import encode_bytes, decode_bytes
+    from kvserve_b200.ops.lossless import gpu_encode, gpu_decode
+    g = torch.Generator().manual_seed(n)
+    x = torch.randint(0, 16, (n,), generator=g, dtype=torch.uint8)
+    x[: n // 4] = 0
+    if n > 50000:
+        x[50000:60000] = torch.randint(0, 256, (10000,), generator=g, dtype=torch.uint8)  # incompressible chunk
+    enc = gpu_encode(x.cuda())
+    ref = encode_bytes(x.numpy())
+    assert bytes(enc.cpu().numpy().tobytes()) == ref
+    back = gpu_decode(enc)
+    assert torch.equal(back.cpu(), x)
+    assert torch.equal(torch.from_numpy(decode_bytes(ref)), x)
