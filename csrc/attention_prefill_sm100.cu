@@ -19,6 +19,8 @@
 #include "ops.h"
 #include "sm100.cuh"
 
+#include <cstdlib>
+
 namespace kvs {
 namespace {
 
@@ -183,7 +185,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < nkv && ok; ++j) {
       const int sb = j & 1;
       const bool diag = (j == qt);
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, a.err)) { ok = false; break; }
+      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, a.err)) ok = false;
+      if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
       tc_fence_after();
       // pass 1: row max
       float mx = -INFINITY;
@@ -202,7 +205,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool rescale = mx > m_ref + kRescaleThreshold;
       const float m_use = rescale ? mx : m_ref;
       // P buffer sb was last read by PV_{j-2}.
-      if (j >= 2 && !mbar_wait(&pv_done[sb], ((j - 2) >> 1) & 1, a.err)) { ok = false; break; }
+      if (j >= 2 && !mbar_wait(&pv_done[sb], ((j - 2) >> 1) & 1, a.err)) ok = false;
+      if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
       // pass 2: probabilities -> bf16 P (128-byte swizzled, K-major over keys)
       float rsum = 0.f;
       uint8_t* pbase = smem + OFF_P + sb * TILE;
@@ -232,25 +236,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&s_empty[sb]);
-      if (rescale) {
-        if (j > 0) {
-          const float f = exp2f(m_ref - mx);
-          if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, a.err)) { ok = false; break; }
-          tc_fence_after();
+      // tcgen05.ld/st are warp-collective (.sync.aligned): the O rescale must
+      // be taken by the whole warp; rows that do not need it use factor 1.
+      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+        const float f = rescale ? exp2f(m_ref - mx) : 1.0f;
+        if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, a.err)) ok = false;
+        if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
+        tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tO + lane_off + c * 32, r);
-            tmem_wait_ld();
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tO + lane_off + c * 32, r);
+          tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * f);
-            tmem_st32(tO + lane_off + c * 32, r);
-          }
-          tmem_wait_st();
-          l *= f;
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * f);
+          tmem_st32(tO + lane_off + c * 32, r);
         }
-        m_ref = mx;
+        tmem_wait_st();
+        l *= f;
       }
+      if (rescale) m_ref = mx;
       l += rsum;
       fence_proxy_async_smem();
       tc_fence_before();
@@ -258,7 +263,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (ok) {
       const int last = nkv - 1;
-      if (mbar_wait(&pv_done[last & 1], (last >> 1) & 1, a.err)) {
+      const bool done = mbar_wait(&pv_done[last & 1], (last >> 1) & 1, a.err);
+      if (__all_sync(0xffffffffu, done)) {
         tc_fence_after();
         const float inv = l > 0.f ? 1.0f / l : 0.f;
         bf16* orow = a.out + int64_t(q_abs) * a.ldo + int64_t(h) * D;
@@ -290,6 +296,217 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Variant 2: two CTAs per SM.  P is written back into the S columns of TMEM
+// (bf16 pairs) and consumed by the PV MMA straight from tensor memory, so a
+// CTA needs only Q + one K + one V tile of shared memory (96 KB) and 256 TMEM
+// columns; the second resident CTA's softmax overlaps this CTA's MMAs.
+// ---------------------------------------------------------------------------
+namespace v2 {
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = TILE;
+constexpr int OFF_V = 2 * TILE;
+constexpr int OFF_BAR = 3 * TILE;
+constexpr int SMEM_BYTES = OFF_BAR + 128 + 1024;
+constexpr uint32_t kTmemCols = 256;  // S/P | O
+}  // namespace v2
+
+__global__ void __launch_bounds__(kThreads, 2)
+    flash_prefill_v2_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
+  using namespace sm100;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + v2::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = bars + 2;
+  uint64_t* k_empty = bars + 3;
+  uint64_t* v_empty = bars + 4;
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* pv_done = bars + 7;
+  uint64_t* drain = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x;
+  const int ntiles = (a.T + BQ - 1) / BQ;
+  const int qt = ntiles - 1 - int(blockIdx.y);
+  const int q0 = qt * BQ;
+  const int kvh = h / (a.Hq / a.Hkv);
+  const int nkv = qt + 1;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 8; ++i) mbar_init(&bars[i], (i == 6) ? 128 : 1);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tm);
+  }
+  if (warp == 5) tmem_alloc<v2::kTmemCols>(tmem_slot);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + 128;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      const int xq = h * D, xk = (a.Hq + kvh) * D, xv = (a.Hq + a.Hkv + kvh) * D;
+      mbar_arrive_expect_tx(q_full, TILE);
+      tma_load_2d(smem + v2::OFF_Q, &tm, xq, q0, q_full);
+      tma_load_2d(smem + v2::OFF_Q + PANEL, &tm, xq + 64, q0, q_full);
+      int kdone = -1, vdone = -1;
+      for (int j = 0; j < nkv; ++j) {
+        const int k0 = j * BKV;
+        if (!mbar_wait(k_empty, (j & 1) ^ 1, a.err)) break;
+        mbar_arrive_expect_tx(k_full, TILE);
+        tma_load_2d(smem + v2::OFF_K, &tm, xk, k0, k_full);
+        tma_load_2d(smem + v2::OFF_K + PANEL, &tm, xk + 64, k0, k_full);
+        kdone = j;
+        if (!mbar_wait(v_empty, (j & 1) ^ 1, a.err)) break;
+        mbar_arrive_expect_tx(v_full, TILE);
+        tma_load_2d(smem + v2::OFF_V, &tm, xv, k0, v_full);
+        tma_load_2d(smem + v2::OFF_V + PANEL, &tm, xv + 64, k0, v_full);
+        vdone = j;
+      }
+      // make sure every issued copy has landed before the CTA can exit
+      mbar_wait(q_full, 0, nullptr);
+      if (kdone >= 0) mbar_wait(k_full, kdone & 1, nullptr);
+      if (vdone >= 0) mbar_wait(v_full, vdone & 1, nullptr);
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_bf16(BQ, BKV, false);
+      constexpr uint32_t idesc_pv = idesc_bf16(BQ, D, true);
+      bool ok = mbar_wait(q_full, 0, a.err);
+      const uint32_t qa = smem_u32(smem + v2::OFF_Q), kb = smem_u32(smem + v2::OFF_K);
+      const uint32_t vb = smem_u32(smem + v2::OFF_V);
+      for (int j = 0; j < nkv && ok; ++j) {
+        // S_j = Q K_j^T (overwrites P_{j-1}: PV_{j-1} was issued before, the
+        // tensor pipe executes in order)
+        if (!mbar_wait(k_full, j & 1, a.err)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * PANEL + (kk & 3) * 32;
+          umma_f16(tS, smem_desc_sw128(qa + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), idesc_qk,
+                   kk > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full);
+        umma_commit(k_empty);
+        // O += P_j V_j with P_j read from TMEM
+        if (!mbar_wait(p_full, j & 1, a.err) || !mbar_wait(v_full, j & 1, a.err)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk)
+          umma_f16_ta(tO, tS + kk * 8, smem_desc_sw128(vb + kk * 2048, PANEL, 1024), idesc_pv,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(pv_done);
+        umma_commit(v_empty);
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr);
+    }
+  } else {
+    const int row = warp * 32 + lane;
+    const uint32_t lane_off = uint32_t(warp * 32) << 16;
+    const int q_abs = q0 + row;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      const bool diag = (j == qt);
+      // s_full_j also implies PV_{j-1} has retired (committed after it).
+      if (!mbar_wait(s_full, j & 1, a.err)) ok = false;
+      if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
+      tc_fence_after();
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tS + lane_off + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float sv = __uint_as_float(r[e]) * a.scale_log2;
+          if (!diag || c * 32 + e <= row) mx = fmaxf(mx, sv);
+        }
+      }
+      const bool rescale = mx > m_ref + kRescaleThreshold;
+      const float m_use = rescale ? mx : m_ref;
+      float rsum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tS + lane_off + c * 32, r);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int col = c * 32 + 2 * e;
+          float p0 = exp2f(__uint_as_float(r[2 * e]) * a.scale_log2 - m_use);
+          float p1 = exp2f(__uint_as_float(r[2 * e + 1]) * a.scale_log2 - m_use);
+          if (diag && col > row) p0 = 0.f;
+          if (diag && col + 1 > row) p1 = 0.f;
+          rsum += p0 + p1;
+          pk[e] = pack_bf16x2(p0, p1);
+        }
+        // P chunk c (keys 32c..32c+31) -> columns [16c, 16c+16): only columns
+        // of S chunks already read are overwritten.
+        tmem_st16(tS + lane_off + c * 16, pk);
+      }
+      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+        const float f = rescale ? exp2f(m_ref - mx) : 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tO + lane_off + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * f);
+          tmem_st32(tO + lane_off + c * 32, r);
+        }
+        l *= f;
+      }
+      tmem_wait_st();
+      if (rescale) m_ref = mx;
+      l += rsum;
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok) {
+      const bool done = mbar_wait(pv_done, (nkv - 1) & 1, a.err);
+      if (__all_sync(0xffffffffu, done)) {
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.0f / l : 0.f;
+        bf16* orow = a.out + int64_t(q_abs) * a.ldo + int64_t(h) * D;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tO + lane_off + c * 32, r);
+          tmem_wait_ld();
+          if (q_abs < a.T) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 o;
+              o.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * inv, __uint_as_float(r[8 * v + 1]) * inv);
+              o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv);
+              o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv);
+              o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv);
+              *reinterpret_cast<uint4*>(orow + c * 32 + v * 8) = o;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc<v2::kTmemCols>(tmem);
+  }
+}
+
 }  // namespace
 
 void flash_prefill(torch::Tensor qkv, int64_t Hq, int64_t Hkv, double scale, torch::Tensor out, torch::Tensor err) {
@@ -314,11 +531,20 @@ void flash_prefill(torch::Tensor qkv, int64_t Hq, int64_t Hkv, double scale, tor
   static bool attr = false;
   if (!attr) {
     KVS_CUDA_CHECK(cudaFuncSetAttribute(flash_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    KVS_CUDA_CHECK(cudaFuncSetAttribute(flash_prefill_v2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        v2::SMEM_BYTES));
     attr = true;
   }
   dim3 grid(int(Hq), (T + BQ - 1) / BQ);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  flash_prefill_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(tm, a);
+  static const int variant = [] {
+    const char* e = std::getenv("KVS_ATTN_VARIANT");
+    return e ? std::atoi(e) : 2;
+  }();
+  if (variant == 1)
+    flash_prefill_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(tm, a);
+  else
+    flash_prefill_v2_kernel<<<grid, kThreads, v2::SMEM_BYTES, st>>>(tm, a);
   KVS_CUDA_CHECK(cudaGetLastError());
 }
 

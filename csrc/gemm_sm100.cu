@@ -150,7 +150,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
       const int mb = tile / num_n, nb = tile % num_n;
-      if (!mbar_wait(&tfull[acc], acc_phase, p.err)) break;
+      // tcgen05.ld is warp-collective: leave the loop as a whole warp.
+      const bool ready = mbar_wait(&tfull[acc], acc_phase, p.err);
+      if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
       const int row = mb * BM + row_in_tile;
       const bool row_ok = row < p.M;

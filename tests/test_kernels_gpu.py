@@ -316,3 +316,14 @@ def test_lossless_gpu_matches_cpu_bytes(n):
     back = gpu_decode(enc)
     assert torch.equal(back.cpu(), x)
     assert torch.equal(torch.from_numpy(decode_bytes(ref)), x)
+
+
+@pytest.mark.parametrize("T", [255, 511, 1023, 4095])
+def test_flash_prefill_partial_tiles_llama_heads(T):
+    """Prompt lengths T-1 of power-of-two prompts (the engine's prefill sizes)."""
+    ops = _ops()
+    torch.manual_seed(T)
+    qkv = torch.randn(T, (32 + 16) * 128, device="cuda", dtype=torch.bfloat16) * 2.0
+    o = ops.flash_prefill(qkv, 32, 8)
+    ops.check_device_status()
+    assert _rel_err(o, _ref_causal(qkv, 32, 8)) < 2e-2
