@@ -23,6 +23,7 @@ SOURCES = [
     "gemv.cu",
     "attention_prefill_sm100.cu",
     "attention_decode.cu",
+    "paged_decode_noalloc.cu",
     "p2p.cu",
 ]
 
