@@ -55,9 +55,11 @@ def _profile(name: str):
 
 
 def run_reference(args) -> None:
-    if int(os.environ.get("RANK", "0")) == 0:
-        from kvserve_b200.baselines.reference_arm import unavailable_reason
-        _emit({"impl": "reference", "unavailable": unavailable_reason()})
+    """The unmodified reference (baseline/_ref) through its own public API:
+    vLLM V1 producer/consumer engines with its CompressedKVConnector."""
+    from kvserve_b200.baselines.reference_arm import run
+    args.metric = BASELINE_METRIC
+    run(args, _emit)
 
 
 def main() -> None:
@@ -73,6 +75,8 @@ def main() -> None:
     ap.add_argument("--link-gbps", type=float, default=0.0)
     ap.add_argument("--layers", type=int, default=0, help="override layer count (smoke runs only)")
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--ref-eager", action="store_true",
+                    help="reference arm: run vLLM with enforce_eager=True (the reference's own PD tests do)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -187,9 +187,14 @@ class PDEngine:
             dist.all_reduce(self._barrier_t, group=self.ctx.world_group)
 
     def generate(self, prompt_ids: torch.Tensor, max_new_tokens: Optional[int] = None,
-                 return_tokens: bool = True) -> GenerateResult:
+                 return_tokens: bool = True, sync: bool = True) -> GenerateResult:
         """Serve one request.  ``prompt_ids`` is a host int32 tensor (pinned
-        preferably); the prompt is copied to the device inside the request."""
+        preferably); the prompt is copied to the device inside the request.
+
+        ``sync`` aligns all ranks on a host collective before the request so
+        per-request device timings share a start; with ``sync=False`` a decode
+        rank relies on the per-layer frame flags alone (a prefill rank that
+        never publishes then surfaces as a device-side timeout status)."""
         t_host0 = time.perf_counter()
         ctx, m = self.ctx, self.model
         n_new = self.max_new if max_new_tokens is None else max_new_tokens
@@ -202,7 +207,8 @@ class PDEngine:
         self.seq += 1
         seq = self.seq
         ev = {k: torch.cuda.Event(enable_timing=True) for k in ("start", "prefill", "encode", "ingest", "first", "end")}
-        self._barrier()
+        if sync:
+            self._barrier()
         c_launch0 = ops.launches()
         replays = 0
         ev["start"].record(self.compute)
