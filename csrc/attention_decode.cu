@@ -15,7 +15,7 @@
 namespace kvs {
 
 int64_t paged_decode_splits(int64_t batch, int64_t hkv, int64_t max_ctx) {
-  const int64_t want = std::max<int64_t>(1, (2 * kNumSMs) / std::max<int64_t>(1, batch * hkv));
+  const int64_t want = std::max<int64_t>(1, (3 * kNumSMs) / std::max<int64_t>(1, batch * hkv));
   const int64_t by_len = std::max<int64_t>(1, max_ctx / 128);
   return std::min<int64_t>(std::min<int64_t>(want, by_len), 64);
 }

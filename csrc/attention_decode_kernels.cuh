@@ -10,6 +10,24 @@ namespace {
 constexpr int kThreads = 128;
 constexpr int kMaxGroup = 8;  // query heads per KV head
 
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ float fast_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// One CTA = one (split, kv head, sequence).  A token row of K or V (D bf16)
+// is spread over D/8 lanes (16 bytes each); every row group handles U
+// consecutive tokens per step and issues all 2U of its 16-byte loads before
+// using any of them (16 KB per CTA in flight, 3 CTAs per SM).  The U scores of a
+// step share one online-softmax update per query head.
 template <int D, int G>
 __global__ void __launch_bounds__(kThreads) paged_decode_kernel(
     const bf16* __restrict__ q, int64_t q_tok_stride, const bf16* __restrict__ kc, const bf16* __restrict__ vc,
@@ -18,8 +36,10 @@ __global__ void __launch_bounds__(kThreads) paged_decode_kernel(
     float scale_log2, float* __restrict__ part_o, float* __restrict__ part_ml, bf16* __restrict__ out,
     int64_t out_tok_stride) {
   constexpr int LANES = D / 8;          // lanes per token row
-  constexpr int TPW = 32 / LANES;       // tokens per warp step
+  constexpr int TPW = 32 / LANES;       // row groups per warp
   constexpr int kGroups = (kThreads / 32) * TPW;
+  constexpr int U = G >= 8 ? 2 : (G >= 4 ? 4 : 8);  // tokens per row group per step
+  constexpr int STEP = kGroups * U;
   __shared__ float s_m[kGroups][G], s_l[kGroups][G];
   __shared__ float s_o[kGroups][G][D];
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -51,50 +71,82 @@ __global__ void __launch_bounds__(kThreads) paged_decode_kernel(
     for (int e = 0; e < 8; ++e) o[g][e] = 0.f;
   }
   const int32_t* bt = block_tables + int64_t(b) * bt_stride;
-  for (int t0 = t_begin; t0 < t_end; t0 += (kThreads / 32) * TPW) {
-    const int t = t0 + warp * TPW + sub;
-    const bool valid = t < t_end;
-    float kf[8], vf[8];
-    if (valid) {
-      const int blk = bt[t / block_size];
-      const int64_t off = int64_t(blk) * blk_stride + int64_t(t % block_size) * tok_stride +
-                          int64_t(kvh) * head_stride + lir * 8;
-      const uint4 kr = *reinterpret_cast<const uint4*>(kc + off);
-      const uint4 vr = *reinterpret_cast<const uint4*>(vc + off);
-      const __nv_bfloat162* kh = reinterpret_cast<const __nv_bfloat162*>(&kr);
-      const __nv_bfloat162* vh = reinterpret_cast<const __nv_bfloat162*>(&vr);
+  const int64_t head_off = int64_t(kvh) * head_stride + lir * 8;
+  for (int t0 = t_begin; t0 < t_end; t0 += STEP) {
+    const int tg = t0 + grp * U;
+    uint4 kr[U], vr[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = tg + u;
+      if (t < t_end) {
+        const int64_t off = int64_t(bt[t / block_size]) * blk_stride + int64_t(t % block_size) * tok_stride +
+                            head_off;
+        kr[u] = ld_stream16(kc + off);
+        vr[u] = ld_stream16(vc + off);
+      } else {
+        kr[u] = make_uint4(0, 0, 0, 0);
+        vr[u] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    float s[U][G];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float kf[8];
+      const __nv_bfloat162* kh = reinterpret_cast<const __nv_bfloat162*>(&kr[u]);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 a = __bfloat1622float2(kh[e]);
-        const float2 c = __bfloat1622float2(vh[e]);
         kf[2 * e] = a.x;
         kf[2 * e + 1] = a.y;
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float acc = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc = fmaf(qf[g][e], kf[e], acc);
+        s[u][g] = acc;
+      }
+    }
+#pragma unroll
+    for (int mm = 1; mm < LANES; mm <<= 1)
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int g = 0; g < G; ++g) s[u][g] += __shfl_xor_sync(0xffffffffu, s[u][g], mm);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float mx = m[g];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (tg + u < t_end) mx = fmaxf(mx, s[u][g]);
+      // no valid token seen yet (mx = -inf): nothing to rescale
+      const float alpha = (mx == -INFINITY) ? 1.0f : fast_ex2(m[g] - mx);
+      l[g] *= alpha;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[g][e] *= alpha;
+      m[g] = mx;
+#pragma unroll
+      for (int u = 0; u < U; ++u) s[u][g] = (tg + u < t_end) ? fast_ex2(s[u][g] - mx) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const __nv_bfloat162* vh = reinterpret_cast<const __nv_bfloat162*>(&vr[u]);
+      float vf[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 c = __bfloat1622float2(vh[e]);
         vf[2 * e] = c.x;
         vf[2 * e + 1] = c.y;
       }
-    } else {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) kf[e] = vf[e] = 0.f;
-    }
+      for (int g = 0; g < G; ++g) {
+        l[g] += s[u][g];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float s = 0.f;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) s = fmaf(qf[g][e], kf[e], s);
-#pragma unroll
-      for (int mm = 1; mm < LANES; mm <<= 1) s += __shfl_xor_sync(0xffffffffu, s, mm);
-      if (valid) {
-        const float mn = fmaxf(m[g], s);
-        const float alpha = exp2f(m[g] - mn);
-        const float p = exp2f(s - mn);
-        l[g] = l[g] * alpha + p;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o[g][e] = o[g][e] * alpha + p * vf[e];
-        m[g] = mn;
+        for (int e = 0; e < 8; ++e) o[g][e] = fmaf(s[u][g], vf[e], o[g][e]);
       }
     }
   }
-  // Merge the per-half-warp states of the CTA.
+  // Merge the per-row-group states of the CTA.
   if (lir == 0) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -114,7 +166,7 @@ __global__ void __launch_bounds__(kThreads) paged_decode_kernel(
     float lsum = 0.f, acc = 0.f;
     if (mx != -INFINITY) {
       for (int k = 0; k < kGroups; ++k) {
-        const float w = exp2f(s_m[k][g] - mx);
+        const float w = fast_ex2(s_m[k][g] - mx);
         lsum += s_l[k][g] * w;
         acc += s_o[k][g][d] * w;
       }

@@ -134,16 +134,21 @@ __global__ void rope_qkv_kernel(bf16* __restrict__ qkv, int64_t qkv_stride, int 
   }
 }
 
+// out[r, c] = silu(gate[r, c]) * up[r, c].  blk == 0: gate = gu[:, :inter],
+// up = gu[:, inter:]; blk > 0: gate/up interleaved in blocks of blk columns
+// (the layout the fused GEMM epilogue consumes).
 __global__ void silu_mul_kernel(const bf16* __restrict__ gu, bf16* __restrict__ out, int64_t rows,
-                                int inter) {
+                                int inter, int blk) {
   const int64_t groups = rows * (inter / 8);
   for (int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; g < groups;
        g += int64_t(gridDim.x) * blockDim.x) {
     const int64_t r = g / (inter / 8);
     const int c = int(g % (inter / 8)) * 8;
     float a[8], b[8], o[8];
-    unpack8(*reinterpret_cast<const uint4*>(gu + r * 2 * inter + c), a);
-    unpack8(*reinterpret_cast<const uint4*>(gu + r * 2 * inter + inter + c), b);
+    const int gc = blk ? (c / blk) * 2 * blk + c % blk : c;
+    const int uc = blk ? gc + blk : inter + c;
+    unpack8(*reinterpret_cast<const uint4*>(gu + r * 2 * inter + gc), a);
+    unpack8(*reinterpret_cast<const uint4*>(gu + r * 2 * inter + uc), b);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const float sg = a[e] / (1.0f + __expf(-a[e]));
@@ -288,17 +293,18 @@ void rope_qkv(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t D, torch::Tens
   KVS_CUDA_CHECK(cudaGetLastError());
 }
 
-void silu_mul(torch::Tensor gate_up, torch::Tensor out) {
+void silu_mul(torch::Tensor gate_up, torch::Tensor out, int64_t blk) {
   const int inter = int(out.size(-1));
   KVS_CHECK_ARG(gate_up.size(-1) == 2 * inter && inter % 8 == 0 && gate_up.is_contiguous() && out.is_contiguous(),
                 "silu_mul: shapes");
+  KVS_CHECK_ARG(blk == 0 || (blk % 8 == 0 && inter % blk == 0), "silu_mul: interleave block");
   const int64_t rows = out.numel() / inter;
   if (rows == 0) return;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int64_t groups = rows * (inter / 8);
   const int grid = int(std::min<int64_t>(ceil_div(groups, 256), 148 * 16));
   silu_mul_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const bf16*>(gate_up.data_ptr()),
-                                        reinterpret_cast<bf16*>(out.data_ptr()), rows, inter);
+                                        reinterpret_cast<bf16*>(out.data_ptr()), rows, inter, int(blk));
   KVS_CUDA_CHECK(cudaGetLastError());
 }
 

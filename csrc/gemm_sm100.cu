@@ -8,7 +8,11 @@
 //               double-buffered TMEM accumulator (2 x 256 columns).
 //   warps 2..5  epilogue: tcgen05.ld 32x32b -> bf16 -> global, overlapped
 //               with the next tile's main loop.
-// One CTA per SM, grid = min(tiles, #SMs), tiles rastered n-fastest.
+// One CTA per SM, grid = min(tiles, #SMs).  Tiles are rastered in groups of
+// kGroupM row blocks (m fastest inside a group), so the ~148 tiles in flight
+// share 16 A row blocks and ~9 B column blocks: a weight much larger than L2
+// (e.g. the 235 MB gate/up projection) is streamed num_m / 16 times instead
+// of num_m times.
 // No cluster multicast is used anywhere (this kernel may run in multi-GPU
 // processes).
 #include <torch/extension.h>
@@ -29,11 +33,24 @@ constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + 1024 /*align*/ + 256 /
 constexpr int kThreads = 192;
 constexpr uint32_t kTmemCols = 512;
 
+constexpr int kGroupM = 16;
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = kGroupM * num_n;
+  const int group = tile / per_group;
+  const int first_m = group * kGroupM;
+  const int gm = min(num_m - first_m, kGroupM);
+  const int r = tile - group * per_group;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
 struct GemmArgs {
   bf16* C;
   const bf16* R;
   const bf16* bias;
   int M, N, K;
+  int act;  // 1: C[:, n] = silu(gate) * up, gate/up rows of B interleaved in blocks of BN/2
   int64_t ldc, ldr;
   uint32_t* err;
 };
@@ -86,7 +103,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       uint32_t issued_mask = 0, issued_parity = 0;  // per stage: load issued / its phase parity
       for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-        const int mb = tile / num_n, nb = tile % num_n;
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
@@ -149,13 +167,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-      const int mb = tile / num_n, nb = tile % num_n;
+      int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
       // tcgen05.ld is warp-collective: leave the loop as a whole warp.
       const bool ready = mbar_wait(&tfull[acc], acc_phase, p.err);
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after();
       const int row = mb * BM + row_in_tile;
       const bool row_ok = row < p.M;
+      if (p.act) {
+        // gate in accumulator columns [0, 128), up in [128, 256) of the same
+        // 128 output features; output columns nb*128 + [0, 128).
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t g[32], u[32];
+          const uint32_t t0 = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN + c * 32);
+          tmem_ld32(t0, g);
+          tmem_ld32(t0 + BN / 2, u);
+          tmem_wait_ld();
+          const int col0 = nb * (BN / 2) + c * 32;
+          if (row_ok) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const int col = col0 + v * 8;
+              if (col >= p.N / 2) break;
+              uint4 o;
+              __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float g0 = __uint_as_float(g[v * 8 + 2 * e]), g1 = __uint_as_float(g[v * 8 + 2 * e + 1]);
+                const float u0 = __uint_as_float(u[v * 8 + 2 * e]), u1 = __uint_as_float(u[v * 8 + 2 * e + 1]);
+                oh[e] = __floats2bfloat162_rn(g0 / (1.0f + __expf(-g0)) * u0, g1 / (1.0f + __expf(-g1)) * u1);
+              }
+              *reinterpret_cast<uint4*>(p.C + int64_t(row) * p.ldc + col) = o;
+            }
+          }
+        }
+      } else {
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -197,6 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             *reinterpret_cast<uint4*>(p.C + int64_t(row) * p.ldc + col) = o;
           }
         }
+      }
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -253,6 +302,49 @@ static int num_sms() {
   return n;
 }
 
+namespace {
+void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, GemmArgs& p) {
+  const int M = p.M, N = p.N, K = p.K;
+  const CUtensorMap ta = make_tmap_2d_bf16(a.data_ptr(), K, M, uint64_t(a.stride(0)) * 2, BK, BM);
+  const CUtensorMap tb = make_tmap_2d_bf16(b.data_ptr(), K, N, uint64_t(b.stride(0)) * 2, BK, BN);
+  static bool attr_set = false;
+  if (!attr_set) {
+    KVS_CUDA_CHECK(cudaFuncSetAttribute(gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        SMEM_BYTES));
+    attr_set = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = std::min(tiles, num_sms());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  gemm_bf16_tn_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(ta, tb, p);
+  KVS_CUDA_CHECK(cudaGetLastError());
+}
+}  // namespace
+
+void gemm_silu_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor err) {
+  KVS_CHECK_ARG(a.is_cuda() && b.is_cuda() && c.is_cuda() && a.scalar_type() == at::kBFloat16 &&
+                    b.scalar_type() == at::kBFloat16 && c.scalar_type() == at::kBFloat16,
+                "gemm_silu: bf16 CUDA operands");
+  KVS_CHECK_ARG(a.dim() == 2 && b.dim() == 2 && c.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1 &&
+                    c.stride(1) == 1,
+                "gemm_silu: 2-D row-major operands");
+  const int M = int(a.size(0)), K = int(a.size(1)), N = int(b.size(0));
+  KVS_CHECK_ARG(b.size(1) == K && c.size(0) == M && 2 * c.size(1) == N && N % BN == 0,
+                "gemm_silu: b [2I, K] (gate/up interleaved in 128-row blocks), c [M, I], I % 128 == 0");
+  KVS_CHECK_ARG(K % 8 == 0 && a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0 && c.stride(0) % 8 == 0,
+                "gemm_silu: K and leading dims must be multiples of 8");
+  if (M == 0) return;
+  GemmArgs p{};
+  p.C = reinterpret_cast<bf16*>(c.data_ptr());
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = c.stride(0);
+  p.act = 1;
+  p.err = reinterpret_cast<uint32_t*>(err.data_ptr<int32_t>());
+  launch_gemm(a, b, p);
+}
+
 void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, c10::optional<torch::Tensor> residual,
                c10::optional<torch::Tensor> bias, torch::Tensor err) {
   KVS_CHECK_ARG(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: CUDA tensors");
@@ -288,19 +380,7 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, c10::optional<
     p.bias = reinterpret_cast<const bf16*>(bias->data_ptr());
   }
   p.err = reinterpret_cast<uint32_t*>(err.data_ptr<int32_t>());
-  const CUtensorMap ta = make_tmap_2d_bf16(a.data_ptr(), K, M, uint64_t(a.stride(0)) * 2, BK, BM);
-  const CUtensorMap tb = make_tmap_2d_bf16(b.data_ptr(), K, N, uint64_t(b.stride(0)) * 2, BK, BN);
-  static bool attr_set = false;
-  if (!attr_set) {
-    KVS_CUDA_CHECK(cudaFuncSetAttribute(gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        SMEM_BYTES));
-    attr_set = true;
-  }
-  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const int grid = std::min(tiles, num_sms());
-  cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  gemm_bf16_tn_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(ta, tb, p);
-  KVS_CUDA_CHECK(cudaGetLastError());
+  launch_gemm(a, b, p);
 }
 
 }  // namespace kvs

@@ -52,12 +52,13 @@ void rope_qkv(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t D, torch::Tens
               torch::Tensor cos_sin, c10::optional<torch::Tensor> k_dst, c10::optional<torch::Tensor> v_dst,
               int64_t dst_token_stride, int64_t dst_head_stride, c10::optional<torch::Tensor> slot_mapping,
               int64_t slot_base);
-void silu_mul(torch::Tensor gate_up, torch::Tensor out);
+void silu_mul(torch::Tensor gate_up, torch::Tensor out, int64_t blk);
 void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t vocab_begin);
 void argmax_rows(torch::Tensor logits, torch::Tensor out, c10::optional<torch::Tensor> out_val,
                  int64_t index_offset);
 void decode_advance(torch::Tensor tok, torch::Tensor ids, torch::Tensor pos, torch::Tensor ctx, torch::Tensor slot,
                     torch::Tensor table, int64_t block_size, torch::Tensor out_tokens, torch::Tensor step);
+void gemm_silu_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor err);
 void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, c10::optional<torch::Tensor> residual,
                c10::optional<torch::Tensor> bias, torch::Tensor err);
 void gemv_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, c10::optional<torch::Tensor> bias);

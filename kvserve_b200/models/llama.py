@@ -65,6 +65,7 @@ class LlamaShard:
             self.hkv = 1
             self.kv_head_offset = tp_rank * cfg.num_kv_heads // tp_size
         self.inter = cfg.intermediate // tp_size
+        self.gu_block = ops.GATE_UP_BLOCK if self.inter % ops.GATE_UP_BLOCK == 0 else 0
         self.vocab_local = cfg.vocab // tp_size
         self.vocab_begin = tp_rank * self.vocab_local
         self.D = cfg.head_dim
@@ -79,6 +80,8 @@ class LlamaShard:
                 qkv=self._rand((qkv_rows, cfg.hidden), l, "qkv"),
                 qkv_bias=self._rand((qkv_rows,), l, "qkv_bias") if cfg.qkv_bias else None,
                 o=self._rand((cfg.hidden, self.hq * self.D), l, "o"),
+                # [2I, K], gate/up rows interleaved in blocks of ops.GATE_UP_BLOCK
+                # (the fused SiLU GEMM layout) when I allows it
                 gate_up=self._rand((2 * self.inter, cfg.hidden), l, "gate_up"),
                 down=self._rand((cfg.hidden, self.inter), l, "down"),
                 in_norm=torch.ones(cfg.hidden, dtype=torch.bfloat16, device=dev),
@@ -111,8 +114,10 @@ class LlamaShard:
         return ops.linear(h, lw.qkv, bias=lw.qkv_bias)
 
     def _mlp(self, h: torch.Tensor, lw: LayerWeights) -> torch.Tensor:
-        gu = ops.linear(h, lw.gate_up)
-        a = ops.silu_mul(gu)
+        if self.gu_block and h.shape[0] > ops.GEMV_MAX_M:
+            a = ops.gemm_silu(h, lw.gate_up)
+        else:
+            a = ops.silu_mul(ops.linear(h, lw.gate_up), block=self.gu_block)
         d = ops.linear(a, lw.down)
         self._all_reduce(d)
         return d

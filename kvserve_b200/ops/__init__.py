@@ -16,7 +16,7 @@ from ._ext import ext, available, ExtensionMissing
 
 __all__ = [
     "ext", "available", "ExtensionMissing", "linear", "gemm", "gemv", "rmsnorm", "rope_qkv",
-    "silu_mul", "embedding", "argmax", "flash_prefill", "paged_decode_attention",
+    "silu_mul", "gemm_silu", "interleave_gate_up", "GATE_UP_BLOCK", "embedding", "argmax", "flash_prefill", "paged_decode_attention",
     "device_status", "check_device_status", "STATUS_NAMES",
 ]
 
@@ -133,12 +133,39 @@ def rope_qkv(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int, head_dim: i
                    tok_stride, head_stride, slot_mapping, slot_base)
 
 
-def silu_mul(gate_up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+def silu_mul(gate_up: torch.Tensor, out: Optional[torch.Tensor] = None, block: int = 0) -> torch.Tensor:
+    """``silu(gate) * up``.  ``block == 0``: ``gate_up = [gate | up]``;
+    ``block > 0``: gate and up columns interleaved in blocks of ``block``
+    (the layout of :func:`interleave_gate_up`)."""
     inter = gate_up.shape[-1] // 2
     if out is None:
         out = torch.empty((*gate_up.shape[:-1], inter), dtype=gate_up.dtype, device=gate_up.device)
     count_launches(1)
-    ext().silu_mul(gate_up, out)
+    ext().silu_mul(gate_up, out, int(block))
+    return out
+
+
+GATE_UP_BLOCK = 128
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, block: int = GATE_UP_BLOCK) -> torch.Tensor:
+    """Stack ``gate``/``up`` weights ``[I, K]`` as ``[2I, K]`` with rows
+    interleaved in blocks of ``block`` (gate block b, then up block b), the
+    operand layout of :func:`gemm_silu`."""
+    I, K = gate.shape
+    if I % block:
+        raise ValueError("intermediate size must be a multiple of the interleave block")
+    return torch.stack([gate.view(I // block, block, K), up.view(I // block, block, K)], 1).reshape(2 * I, K)
+
+
+def gemm_silu(a: torch.Tensor, w_gate_up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``silu(a @ gate^T) * (a @ up^T)`` in one tcgen05 GEMM whose epilogue
+    applies the activation; ``w_gate_up`` is ``[2I, K]`` in the
+    :func:`interleave_gate_up` layout."""
+    if out is None:
+        out = torch.empty((a.shape[0], w_gate_up.shape[0] // 2), dtype=a.dtype, device=a.device)
+    count_launches(1)
+    ext().gemm_silu_bf16(a, w_gate_up, out, device_status(a.device))
     return out
 
 

@@ -20,7 +20,7 @@ def _rel_err(a, b):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 520, 136), (1024, 1024, 1024), (8192, 4096, 512),
-                                   (17, 4096, 4096), (2048, 6144, 4096)])
+                                   (17, 4096, 4096), (2048, 6144, 4096), (2200, 1280, 256)])
 def test_gemm_tcgen05(M, N, K):
     ops = _ops()
     torch.manual_seed(0)
@@ -30,6 +30,23 @@ def test_gemm_tcgen05(M, N, K):
     ops.check_device_status()
     ref = a.float() @ b.float().T
     assert _rel_err(c, ref) < 1e-2
+
+
+@pytest.mark.parametrize("M,I,K", [(9, 256, 128), (300, 1024, 512), (4096, 3584, 4096)])
+def test_gemm_silu_fused_epilogue(M, I, K):
+    ops = _ops()
+    torch.manual_seed(1)
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    g = torch.randn(I, K, device="cuda", dtype=torch.bfloat16) / math.sqrt(K)
+    u = torch.randn(I, K, device="cuda", dtype=torch.bfloat16) / math.sqrt(K)
+    w = ops.interleave_gate_up(g, u)
+    y = ops.gemm_silu(a, w)
+    ops.check_device_status()
+    ref = torch.nn.functional.silu(a.float() @ g.float().T) * (a.float() @ u.float().T)
+    assert _rel_err(y, ref) < 1e-2
+    # the unfused path on the same interleaved layout (decode-size batches)
+    y2 = ops.silu_mul(ops.gemm(a, w), block=ops.GATE_UP_BLOCK)
+    assert _rel_err(y2, ref) < 1e-2
 
 
 def test_gemm_residual():
