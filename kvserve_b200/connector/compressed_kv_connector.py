@@ -145,6 +145,28 @@ class CompressedKVConnector(KVConnectorBase_V1):
             self._tp_size = get_tensor_model_parallel_world_size()
             self._transport = self._build_transport(cfg, local_rank, self._tp_rank, self._data_plane)
 
+    # ---- connector-owned memory, planned before KV sizing -----------------
+    @classmethod
+    def build_worker_memory_plan(cls, vllm_config, kv_cache_specs):
+        """Plan this connector's GPU memory before the KV cache is sized
+        (called by patched workers; stock vLLM can use
+        :func:`~kvserve_b200.connector.memory_plan.adjusted_utilization`)."""
+        from .memory_plan import plan_worker_memory
+        extra = vllm_config.kv_transfer_config.kv_connector_extra_config or {}
+        tp_size = int(getattr(vllm_config.parallel_config, "tensor_parallel_size", 1) or 1)
+        tp_rank = 0
+        try:
+            from vllm.distributed.parallel_state import get_tensor_model_parallel_rank
+            tp_rank = get_tensor_model_parallel_rank()
+        except Exception:
+            pass
+        return plan_worker_memory(extra, kv_cache_specs, tp_rank, tp_size)
+
+    def initialize_worker_memory(self, memory_plan) -> None:
+        """Allocate exactly the planned memory after the KV cache exists."""
+        from .memory_plan import WorkerMemory
+        self._worker_memory = WorkerMemory(memory_plan)
+
     @classmethod
     def get_required_kvcache_layout(cls, vllm_config) -> Optional[str]:
         if vllm_config.model_config is None or vllm_config.model_config.use_mla:

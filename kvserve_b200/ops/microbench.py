@@ -82,8 +82,9 @@ def case_gemm(a, pk):
     # gate/up projection with the SiLU-mul epilogue (output [M, N/2])
     M, I, K = 8192, 14336, 4096
     A = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
-    W = interleave_gate_up(torch.randn(I, K, device="cuda", dtype=torch.bfloat16),
-                           torch.randn(I, K, device="cuda", dtype=torch.bfloat16))
+    # unit-variance pre-activations, as after an RMSNorm-ed input
+    W = interleave_gate_up(torch.randn(I, K, device="cuda", dtype=torch.bfloat16) / math.sqrt(K),
+                           torch.randn(I, K, device="cuda", dtype=torch.bfloat16) / math.sqrt(K))
     Y = torch.empty(M, I, device="cuda", dtype=torch.bfloat16)
     t = time_ms([lambda: gemm_silu(A, W, Y)], a.iters, a.once)
     res[f"gemm_silu_{M}x{2 * I}x{K}"] = {"ms": round(t, 4), "tflops": round(2 * M * 2 * I * K / t / 1e9, 1),

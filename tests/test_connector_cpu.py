@@ -137,3 +137,23 @@ def test_scheduler_claims_prompt_minus_one():
     assert c._resolve_transfer_id("r") == "T" and "r" in c._requests_need_load
     p = _bare(True, FakeTransport([]))
     assert p.get_num_new_matched_tokens(req, 0) == (0, False)
+
+
+def test_worker_memory_plan_matches_runtime_plan():
+    from types import SimpleNamespace
+
+    import torch
+    from kvserve_b200.compression.runtime import CompressionConfig, build_memory_plan
+    from kvserve_b200.connector.memory_plan import (KVConnectorWorkerMemoryPlan, adjusted_utilization,
+                                                    cache_specs_from_vllm, layer_index_of, plan_worker_memory)
+    specs = {f"model.layers.{i}.self_attn.attn": SimpleNamespace(block_size=16, num_kv_heads=8, head_size=128,
+                                                                  dtype=torch.bfloat16) for i in range(4)}
+    assert layer_index_of("model.layers.12.self_attn.attn") == 12
+    assert plan_worker_memory({}, specs) == KVConnectorWorkerMemoryPlan()
+    extra = {"compression": {"enable-compression-pipeline": True, "slot_count": 3}}
+    plan = plan_worker_memory(extra, specs)
+    ref = build_memory_plan(CompressionConfig.from_extra_config(extra), cache_specs_from_vllm(specs))
+    assert plan.reserved_bytes == ref.reserved_bytes > 0
+    assert plan.connector_data.slot_bytes == ref.slot_bytes
+    u = adjusted_utilization(100 * 2 ** 30, 0.9, plan)
+    assert abs(u * 100 * 2 ** 30 - (0.9 * 100 * 2 ** 30 - plan.reserved_bytes)) < 1.0

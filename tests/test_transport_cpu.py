@@ -91,3 +91,46 @@ def test_credit_retry_then_delivery():
     res, ok = _run(capacity=100, faults="refuse_credit:2")
     assert ok
     assert set(res) == {"r0", "r1", "r2", "b0"}
+
+
+def test_zmq_transport_roundtrip_without_pickle():
+    import socket
+    import time
+    from kvserve_b200.transport.zmq_transport import ZmqTransport
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    rx = ZmqTransport(False, "127.0.0.1", port)
+    tx = ZmqTransport(True, "127.0.0.1", port)
+    try:
+        kv = torch.randn(3, 2, 7, 32).to(torch.bfloat16)
+        tx.send("req-a", ["l0", "l1", "l2"], kv)
+        tx.send("req-b", ["l0"], torch.arange(10, dtype=torch.int32))
+        got = {}
+        for _ in range(100):
+            got.update(rx.drain_received())
+            if len(got) == 2:
+                break
+            time.sleep(0.02)
+        assert got["req-a"][0] == ["l0", "l1", "l2"] and torch.equal(got["req-a"][1], kv)
+        assert torch.equal(got["req-b"][1], torch.arange(10, dtype=torch.int32))
+        assert rx.drain_received() == {}
+    finally:
+        tx.close()
+        rx.close()
+
+
+def test_logger_levels(capsys):
+    from kvserve_b200.utils import logger
+    old = logger.get_log_level()
+    try:
+        logger.set_log_level(logger.LogLevel.WARNING)
+        logger.log_info("quiet")
+        logger.log_warning("loud")
+        logger.set_log_level(logger.LogLevel.ERROR)
+        logger.log_error("always")
+        err = capsys.readouterr().err
+        assert "loud" in err and "always" in err and "quiet" not in err
+    finally:
+        logger.set_log_level(old)
