@@ -27,3 +27,44 @@ def test_search_and_library_feed_the_controller(tmp_path):
     assert prof is not None
     assert (tmp_path / "cr_cache.csv").exists()
     json.loads((tmp_path / "tolerance_5_results.json").read_text())
+
+
+def test_cache_simulators_trade_ratio_for_error():
+    import torch
+    from kvserve_b200.offline_search.cache_sim import CacheGenSim, DuoAttentionSim, KIVISim, KVServeSim
+    from kvserve_b200.offline_search.search import synthetic_kv
+    kv = synthetic_kv(layers=2, tokens=256, heads=4)
+    err = lambda r: ((r.float() - kv.float()).norm() / kv.float().norm()).item()  # noqa: E731
+    r2, cr2 = KIVISim(bits=2, group=32, residual=64)(kv)
+    r4, cr4 = KIVISim(bits=4, group=32, residual=64)(kv)
+    assert cr2 > cr4 > 2.0 and err(r4) < err(r2) < 0.5
+    rc, crc = CacheGenSim()(kv)
+    assert crc > 2.0 and err(rc) < 0.5
+    rd, crd = DuoAttentionSim(sparsity=0.5, sink=16, recent=32)(kv)
+    assert 1.3 < crd < 2.0 and torch.equal(rd[:, :, :, -32:], kv[:, :, :, -32:])
+    cfg = {"enabled": True, "pipeline": ["transformer", "quantizer"],
+           "transformer_config": {"transform_type": "hadamard"},
+           "quantizer_config": {"hybrid_ratio": 0.0, "high_key_max_value": 16, "high_value_max_value": 16,
+                                "low_key_max_value": 16, "low_value_max_value": 16, "axis_key": "channel",
+                                "axis_value": "token", "split_type": "head"}}
+    rk, crk = KVServeSim(cfg, 4, 128, num_layers=2)(kv)
+    assert crk > 1.5 and err(rk) < 0.2
+
+
+def test_simulated_hf_cache_degrades_prefill_kv():
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from kvserve_b200.offline_search.cache_sim import KIVISim, simulated_cache
+    torch.manual_seed(0)
+    cfg = LlamaConfig(vocab_size=128, hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, head_dim=16, max_position_embeddings=256)
+    model = LlamaForCausalLM(cfg).eval()
+    ids = torch.randint(0, 128, (1, 96))
+    with torch.no_grad():
+        ref = model(ids, use_cache=True).past_key_values
+        cache = simulated_cache(KIVISim(bits=2, group=16, residual=32), 2)
+        model(ids, past_key_values=cache, use_cache=True)
+    assert set(cache.ratios) == {0, 1} and all(r > 1.5 for r in cache.ratios.values())
+    k_ref = ref.layers[0].keys if hasattr(ref, "layers") else ref.key_cache[0]
+    k_sim = cache.layers[0].keys if hasattr(cache, "layers") else cache.key_cache[0]
+    assert k_ref.shape == k_sim.shape and not torch.equal(k_ref, k_sim)
