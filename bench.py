@@ -75,8 +75,9 @@ def main() -> None:
     ap.add_argument("--link-gbps", type=float, default=0.0)
     ap.add_argument("--layers", type=int, default=0, help="override layer count (smoke runs only)")
     ap.add_argument("--no-graphs", action="store_true")
-    ap.add_argument("--ref-eager", action="store_true",
-                    help="reference arm: run vLLM with enforce_eager=True (the reference's own PD tests do)")
+    ap.add_argument("--ref-cuda-graphs", action="store_true",
+                    help="reference arm: let vLLM capture CUDA graphs (default eager, as the reference's own PD "
+                         "tests run; capture fails with its connector's per-layer save hook)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -197,7 +197,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int e = 0; e < 4; ++e) {
                 const float g0 = __uint_as_float(g[v * 8 + 2 * e]), g1 = __uint_as_float(g[v * 8 + 2 * e + 1]);
                 const float u0 = __uint_as_float(u[v * 8 + 2 * e]), u1 = __uint_as_float(u[v * 8 + 2 * e + 1]);
-                oh[e] = __floats2bfloat162_rn(g0 / (1.0f + __expf(-g0)) * u0, g1 / (1.0f + __expf(-g1)) * u1);
+                // silu(g) = g / (1 + e^-g); the exponent argument is capped so the
+                // divisor stays finite and the fast division applies
+                const float d0 = 1.0f + __expf(fminf(-g0, 80.0f)), d1 = 1.0f + __expf(fminf(-g1, 80.0f));
+                oh[e] = __floats2bfloat162_rn(__fdividef(g0, d0) * u0, __fdividef(g1, d1) * u1);
               }
               *reinterpret_cast<uint4*>(p.C + int64_t(row) * p.ldc + col) = o;
             }

@@ -39,6 +39,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kMaxRowIters = 8;  // H*D <= 2048 for the fused path
+constexpr int kRowUnroll = 4;    // rows per row group whose loads are issued together
 
 struct EncodeArgs {
   const bf16* k;
@@ -234,38 +235,50 @@ __global__ void __launch_bounds__(kThreads) kv_kstats_kernel(EncodeArgs a) {
     const int t0 = tile * a.tile_tokens;
     const int t1 = min(g.T, t0 + a.tile_tokens);
     const int nrows = (t1 - t0) * g.H;
-    for (int base = 0; base < nrows; base += kRowsPerIter) {
-      const int r = base + warp * RPW + rw;
-      const bool valid = r < nrows;
-      const int t = t0 + r / g.H, j = r % g.H;
-      float v[8];
-      if (valid) {
-        const int h = a.order[j];
-        uint4 raw;
-        load8(src_row(a.k, t, h, a.k_tok_stride, a.k_head_stride, a.block_table, a.block_size, a.k_block_stride) +
-                  lir * 8, v, raw);
-        if (a.g.transform) apply_signs(v, sign_byte(a.sign_bits + h * (D / 32), lir));
-      } else {
+    for (int base = 0; base < nrows; base += kRowsPerIter * kRowUnroll) {
+      // all kRowUnroll loads of this row group are issued before any use
+      float v[kRowUnroll][8];
+      int jr[kRowUnroll];
+      bool valid[kRowUnroll];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = 0.f;
-      }
-      if (g.transform) fwht_row<LANES>(v, lir);
-      if (!valid) continue;
-      int s, js, hs;
-      slot_section(g, j, s, js, hs);
-      if (g.bits[0][s] == kRawBits) continue;
-      if (fixed_slot) {
-        my_slot = j;
+      for (int i = 0; i < kRowUnroll; ++i) {
+        const int r = base + i * kRowsPerIter + warp * RPW + rw;
+        valid[i] = r < nrows;
+        const int t = t0 + r / g.H;
+        jr[i] = r % g.H;
+        if (valid[i]) {
+          uint4 raw;
+          load8(src_row(a.k, t, a.order[jr[i]], a.k_tok_stride, a.k_head_stride, a.block_table, a.block_size,
+                        a.k_block_stride) + lir * 8, v[i], raw);
+        } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          mn[e] = fminf(mn[e], v[e] * scale);
-          mx[e] = fmaxf(mx[e], v[e] * scale);
+          for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
         }
-      } else {
+      }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          atomicMin(&sstat[j * D + lir * 8 + e], float_to_ordered(v[e] * scale));
-          atomicMax(&sstat[HD + j * D + lir * 8 + e], float_to_ordered(v[e] * scale));
+      for (int i = 0; i < kRowUnroll; ++i) {
+        const int j = jr[i];
+        if (g.transform) {
+          if (valid[i]) apply_signs(v[i], sign_byte(a.sign_bits + a.order[j] * (D / 32), lir));
+          fwht_row<LANES>(v[i], lir);
+        }
+        if (!valid[i]) continue;
+        int s, js, hs;
+        slot_section(g, j, s, js, hs);
+        if (g.bits[0][s] == kRawBits) continue;
+        if (fixed_slot) {
+          my_slot = j;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            mn[e] = fminf(mn[e], v[i][e] * scale);
+            mx[e] = fmaxf(mx[e], v[i][e] * scale);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            atomicMin(&sstat[j * D + lir * 8 + e], float_to_ordered(v[i][e] * scale));
+            atomicMax(&sstat[HD + j * D + lir * 8 + e], float_to_ordered(v[i][e] * scale));
+          }
         }
       }
     }
@@ -380,44 +393,54 @@ __global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
       const int t0 = tile * a.tile_tokens;
       const int t1 = min(g.T, t0 + a.tile_tokens);
       const int nrows = (t1 - t0) * g.H;
-      for (int base = 0; base < nrows; base += kRowsPerIter) {
-        const int r = base + warp * RPW + rw;
-        const bool valid = r < nrows;
-        const int t = t0 + r / g.H, j = r % g.H;
-        float v[8];
-        uint4 raw = make_uint4(0, 0, 0, 0);
-        if (valid) {
-          const int h = a.order[j];
-          load8(src_row(a.k, t, h, a.k_tok_stride, a.k_head_stride, a.block_table, a.block_size,
-                        a.k_block_stride) + lir * 8, v, raw);
-          if (a.g.transform) apply_signs(v, sign_byte(a.sign_bits + h * (D / 32), lir));
-        } else {
+      for (int base = 0; base < nrows; base += kRowsPerIter * kRowUnroll) {
+        float v[kRowUnroll][8];
+        uint4 raw[kRowUnroll];
+        int tr[kRowUnroll], jr[kRowUnroll];
+        bool valid[kRowUnroll];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = 0.f;
-        }
-        if (g.transform) fwht_row<LANES>(v, lir);
-        if (!valid) continue;
-        int s, js, hs;
-        slot_section(g, j, s, js, hs);
-        const int bits = g.bits[0][s];
-        const int64_t sym = (int64_t(t) * hs + js) * D + lir * 8;
-        if (bits == kRawBits) {
-          *reinterpret_cast<uint4*>(a.frame + g.payload[0][s] + sym * 2) = raw;
-          continue;
+        for (int i = 0; i < kRowUnroll; ++i) {
+          const int r = base + i * kRowsPerIter + warp * RPW + rw;
+          valid[i] = r < nrows;
+          tr[i] = t0 + r / g.H;
+          jr[i] = r % g.H;
+          raw[i] = make_uint4(0, 0, 0, 0);
+          if (valid[i]) {
+            load8(src_row(a.k, tr[i], a.order[jr[i]], a.k_tok_stride, a.k_head_stride, a.block_table,
+                          a.block_size, a.k_block_stride) + lir * 8, v[i], raw[i]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
+          }
         }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] *= scale;
-        // Per-channel parameters differ per element: quantise one by one.
-        uint64_t acc = 0;
-        const float top = float(g.levels[0][s] - 1);
+        for (int i = 0; i < kRowUnroll; ++i) {
+          const int t = tr[i], j = jr[i];
+          if (g.transform) {
+            if (valid[i]) apply_signs(v[i], sign_byte(a.sign_bits + a.order[j] * (D / 32), lir));
+            fwht_row<LANES>(v[i], lir);
+          }
+          if (!valid[i]) continue;
+          int s, js, hs;
+          slot_section(g, j, s, js, hs);
+          const int bits = g.bits[0][s];
+          const int64_t sym = (int64_t(t) * hs + js) * D + lir * 8;
+          if (bits == kRawBits) {
+            *reinterpret_cast<uint4*>(a.frame + g.payload[0][s] + sym * 2) = raw[i];
+            continue;
+          }
+          // Per-channel parameters differ per element: quantise one by one.
+          uint64_t acc = 0;
+          const float top = float(g.levels[0][s] - 1);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int c = j * D + lir * 8 + e;
-          float q = rintf((v[e] - sparam[c]) * sparam[HD + c]);
-          q = fminf(fmaxf(q, 0.0f), top);
-          acc |= uint64_t(uint32_t(q)) << (e * bits);
+          for (int e = 0; e < 8; ++e) {
+            const int c = j * D + lir * 8 + e;
+            float q = rintf((v[i][e] * scale - sparam[c]) * sparam[HD + c]);
+            q = fminf(fmaxf(q, 0.0f), top);
+            acc |= uint64_t(uint32_t(q)) << (e * bits);
+          }
+          store_packed(a.frame + g.payload[0][s] + 16 + sym * bits / 8, acc, bits);
         }
-        store_packed(a.frame + g.payload[0][s] + 16 + sym * bits / 8, acc, bits);
       }
     }
   } else {
@@ -433,30 +456,49 @@ __global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
       const int t0 = tile * a.tile_tokens;
       const int t1 = min(g.T, t0 + a.tile_tokens);
       for (int t = t0 + warp; t < t1; t += kWarps) {
-        float v[kMaxRowIters][8];
+        // Every row of the token is loaded first and kept as raw bf16; the
+        // transform is evaluated twice (statistics pass, quantisation pass)
+        // instead of holding all transformed rows, which keeps the kernel
+        // at low register pressure (high occupancy).
         uint4 raw[kMaxRowIters];
-        float smin[2] = {INFINITY, INFINITY}, smax[2] = {-INFINITY, -INFINITY};
 #pragma unroll
         for (int i = 0; i < kMaxRowIters; ++i) {
           if (i >= iters) break;
           const int j = rw + RPW * i;
-          if (j < g.H) {
-            const int h = a.order[j];
-            load8(src_row(a.v, t, h, a.v_tok_stride, a.v_head_stride, a.block_table, a.block_size,
-                          a.v_block_stride) + lir * 8, v[i], raw[i]);
-            if (a.g.transform) apply_signs(v[i], sign_byte(a.sign_bits + h * (D / 32), lir));
-          } else {
+          raw[i] = j < g.H ? *reinterpret_cast<const uint4*>(
+                                 src_row(a.v, t, a.order[j], a.v_tok_stride, a.v_head_stride, a.block_table,
+                                         a.block_size, a.v_block_stride) + lir * 8)
+                           : make_uint4(0, 0, 0, 0);
+        }
+        auto transformed = [&](int i, float (&v)[8]) {
+          const int j = rw + RPW * i;
+          const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(hh[e]);
+            v[2 * e] = f.x;
+            v[2 * e + 1] = f.y;
           }
-          if (g.transform) fwht_row<LANES>(v[i], lir);
+          if (g.transform) {
+            if (j < g.H) apply_signs(v, sign_byte(a.sign_bits + a.order[j] * (D / 32), lir));
+            fwht_row<LANES>(v, lir);
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] *= scale;
+        };
+        float smin[2] = {INFINITY, INFINITY}, smax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int i = 0; i < kMaxRowIters; ++i) {
+          if (i >= iters) break;
+          float v[8];
+          transformed(i, v);
+          const int j = rw + RPW * i;
           if (j < g.H) {
             const int s = j < g.n_low ? 0 : 1;
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              v[i][e] *= scale;
-              smin[s] = fminf(smin[s], v[i][e]);
-              smax[s] = fmaxf(smax[s], v[i][e]);
+              smin[s] = fminf(smin[s], v[e]);
+              smax[s] = fmaxf(smax[s], v[e]);
             }
           }
         }
@@ -487,6 +529,8 @@ __global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
 #pragma unroll
         for (int i = 0; i < kMaxRowIters; ++i) {
           if (i >= iters) break;
+          float v[8];
+          transformed(i, v);
           const int j = rw + RPW * i;
           if (j >= g.H) continue;
           int s, js, hs;
@@ -497,7 +541,7 @@ __global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
             *reinterpret_cast<uint4*>(a.frame + g.payload[1][s] + sym * 2) = raw[i];
             continue;
           }
-          const uint64_t acc = quant_pack8(v[i], pmin[s], pinv[s], g.levels[1][s], bits);
+          const uint64_t acc = quant_pack8(v, pmin[s], pinv[s], g.levels[1][s], bits);
           store_packed(a.frame + g.payload[1][s] + 16 + sym * bits / 8, acc, bits);
         }
       }
@@ -572,64 +616,87 @@ __global__ void __launch_bounds__(kThreads) kv_decode_kernel(DecodeArgs a) {
       const int t0 = tile * a.tile_tokens;
       const int t1 = min(g.T, t0 + a.tile_tokens);
       const int nrows = (t1 - t0) * g.H;
-      for (int base = 0; base < nrows; base += kRowsPerIter) {
-        const int r = base + warp * RPW + rw;
-        const bool valid = r < nrows;
-        const int t = t0 + r / g.H, j = r % g.H;
-        int s = 0, js = 0, hs = 1;
-        if (valid) slot_section(g, j, s, js, hs);
-        const int bits = g.bits[part][s];
-        const int64_t sym = (int64_t(t) * hs + js) * D + lir * 8;
-        const bool raw = valid && bits == kRawBits;
-        // Raw rows and invalid rows skip the transform; the shuffle below
-        // still needs every lane, so the branch is per-row uniform.
-        float v[8];
-        uint4 rawv = make_uint4(0, 0, 0, 0);
-        if (valid && !raw) {
-          const uint64_t acc = load_packed(frame + g.payload[part][s] + 16 + sym * bits / 8, bits);
-          const uint64_t mask = (1ull << bits) - 1ull;
-          if (part == 0) {
+      for (int base = 0; base < nrows; base += kRowsPerIter * kRowUnroll) {
+        // packed symbols (and V parameters) of kRowUnroll rows are loaded first
+        uint64_t acc[kRowUnroll];
+        uint4 rawv[kRowUnroll];
+        float vmn[kRowUnroll], vsc[kRowUnroll];
+        int tr[kRowUnroll], jr[kRowUnroll], sr[kRowUnroll], bitsr[kRowUnroll];
+        int64_t symr[kRowUnroll];
+        bool valid[kRowUnroll];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int c = j * D + lir * 8 + e;
-              v[e] = sk[c] + float((acc >> (e * bits)) & mask) * sk[HD + c];
-            }
+        for (int i = 0; i < kRowUnroll; ++i) {
+          const int r = base + i * kRowsPerIter + warp * RPW + rw;
+          valid[i] = r < nrows;
+          tr[i] = t0 + r / g.H;
+          jr[i] = r % g.H;
+          int s = 0, js = 0, hs = 1;
+          if (valid[i]) slot_section(g, jr[i], s, js, hs);
+          sr[i] = s;
+          bitsr[i] = g.bits[part][s];
+          symr[i] = (int64_t(tr[i]) * hs + js) * D + lir * 8;
+          acc[i] = 0;
+          rawv[i] = make_uint4(0, 0, 0, 0);
+          vmn[i] = vsc[i] = 0.f;
+          if (!valid[i]) continue;
+          if (bitsr[i] == kRawBits) {
+            rawv[i] = __ldcg(reinterpret_cast<const uint4*>(frame + g.payload[part][s] + symr[i] * 2));
           } else {
-            const bf16* aux = reinterpret_cast<const bf16*>(frame + g.v_aux[s]);
-            const float mn = __bfloat162float(__ushort_as_bfloat16(
-                __ldcg(reinterpret_cast<const unsigned short*>(aux + t))));
-            const float sc = __bfloat162float(__ushort_as_bfloat16(
-                __ldcg(reinterpret_cast<const unsigned short*>(aux + g.T + t))));
-#pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = mn + float((acc >> (e * bits)) & mask) * sc;
+            acc[i] = load_packed(frame + g.payload[part][s] + 16 + symr[i] * bitsr[i] / 8, bitsr[i]);
+            if (part == 1) {
+              const bf16* aux = reinterpret_cast<const bf16*>(frame + g.v_aux[s]);
+              vmn[i] = __bfloat162float(__ushort_as_bfloat16(
+                  __ldcg(reinterpret_cast<const unsigned short*>(aux + tr[i]))));
+              vsc[i] = __bfloat162float(__ushort_as_bfloat16(
+                  __ldcg(reinterpret_cast<const unsigned short*>(aux + g.T + tr[i]))));
+            }
           }
-        } else {
-          if (raw) rawv = __ldcg(reinterpret_cast<const uint4*>(frame + g.payload[part][s] + sym * 2));
+        }
+#pragma unroll
+        for (int i = 0; i < kRowUnroll; ++i) {
+          const int t = tr[i], j = jr[i], bits = bitsr[i];
+          const bool raw = valid[i] && bits == kRawBits;
+          // Raw rows and invalid rows skip the transform; the shuffle below
+          // still needs every lane, so the branch is per-row uniform.
+          float v[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) v[e] = 0.f;
-        }
-        if (g.transform) fwht_row<LANES>(v, lir);
-        if (!valid) continue;
-        const int h = order[j];
-        const int pos = a.tok_offset + t;
-        const int blk = a.block_table[pos / a.block_size];
-        bf16* dst = cache + int64_t(blk) * a.block_stride + int64_t(pos % a.block_size) * a.token_stride +
-                    int64_t(h) * a.head_stride + lir * 8;
-        if (raw) {
-          *reinterpret_cast<uint4*>(dst) = rawv;
-          continue;
-        }
-        const uint32_t sb = g.transform ? sign_byte(sbits + h * (D / 32), lir) : 0u;
-        uint4 out;
-        __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&out);
+          if (valid[i] && !raw) {
+            const uint64_t mask = (1ull << bits) - 1ull;
+            if (part == 0) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float x0 = v[2 * i] * scale, x1 = v[2 * i + 1] * scale;
-          if ((sb >> (2 * i)) & 1u) x0 = -x0;
-          if ((sb >> (2 * i + 1)) & 1u) x1 = -x1;
-          o2[i] = __floats2bfloat162_rn(x0, x1);
+              for (int e = 0; e < 8; ++e) {
+                const int c = j * D + lir * 8 + e;
+                v[e] = sk[c] + float((acc[i] >> (e * bits)) & mask) * sk[HD + c];
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] = vmn[i] + float((acc[i] >> (e * bits)) & mask) * vsc[i];
+            }
+          }
+          if (g.transform) fwht_row<LANES>(v, lir);
+          if (!valid[i]) continue;
+          const int h = order[j];
+          const int pos = a.tok_offset + t;
+          const int blk = a.block_table[pos / a.block_size];
+          bf16* dst = cache + int64_t(blk) * a.block_stride + int64_t(pos % a.block_size) * a.token_stride +
+                      int64_t(h) * a.head_stride + lir * 8;
+          if (raw) {
+            *reinterpret_cast<uint4*>(dst) = rawv[i];
+            continue;
+          }
+          const uint32_t sb = g.transform ? sign_byte(sbits + h * (D / 32), lir) : 0u;
+          uint4 out;
+          __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float x0 = v[2 * q] * scale, x1 = v[2 * q + 1] * scale;
+            if ((sb >> (2 * q)) & 1u) x0 = -x0;
+            if ((sb >> (2 * q + 1)) & 1u) x1 = -x1;
+            o2[q] = __floats2bfloat162_rn(x0, x1);
+          }
+          *reinterpret_cast<uint4*>(dst) = out;
         }
-        *reinterpret_cast<uint4*>(dst) = out;
       }
     }
     __syncthreads();

@@ -270,7 +270,8 @@ def run(args, emit) -> None:
                            "global_batch": 1, "seq_len": args.prompt_len, "max_new_tokens": args.max_new,
                            "parallelism": f"{tp}P{tp}D-tp{tp}", "profile": args.profile,
                            "engine": f"vLLM V1 + kvserve_v1 CompressedKVConnector/NcclTransport "
-                                     f"(attention {REF_ATTENTION_BACKEND}, enforce_eager={bool(args.ref_eager)}, "
+                                     f"(attention {REF_ATTENTION_BACKEND}, "
+                                     f"enforce_eager={not getattr(args, 'ref_cuda_graphs', False)}, "
                                      f"chunked prefill off)",
                            "l2": "inputs larger than L2 (16 GB weights, 1 GiB raw KV per request)"},
                 "e2e": {"value": round(statistics.median(ttft), 3),
@@ -305,8 +306,8 @@ def _build_engine(args, role: str, tp: int, kv_port: int):
     return LLM(model=model_dir, load_format="dummy", skip_tokenizer_init=True, dtype="bfloat16",
                tensor_parallel_size=tp, max_model_len=max_len, max_num_batched_tokens=max_len,
                enable_chunked_prefill=False, enable_prefix_caching=False, gpu_memory_utilization=0.6,
-               enforce_eager=bool(args.ref_eager), kv_transfer_config=kv_cfg, disable_log_stats=False, seed=0,
-               attention_backend=REF_ATTENTION_BACKEND)
+               enforce_eager=not getattr(args, "ref_cuda_graphs", False), kv_transfer_config=kv_cfg,
+               disable_log_stats=False, seed=0, attention_backend=REF_ATTENTION_BACKEND)
 
 
 def _generate(llm, prompt: list[int], max_tokens: int, transfer_id: str, want_output: bool = False):

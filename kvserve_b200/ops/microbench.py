@@ -18,7 +18,7 @@ import argparse
 import json
 import math
 import os
-from typing import Callable
+from typing import Callable, Sequence
 
 import torch
 
@@ -251,6 +251,28 @@ def case_norm(a, pk):
     return res
 
 
+def link_model(handoff: dict, gbps: Sequence[float] = (20, 50, 100, 200, 400, 7200)) -> dict:
+    """Theoretical per-layer hand-off time at several link speeds (the
+    reference's codec-throughput tool reports 20/50/100/200 Gbps; 7200 Gbps
+    is one NVLink 5 direction): raw = bytes / link; compressed =
+    compress + packed bytes / link + decompress (serial, no overlap)."""
+    out = {}
+    for key, r in handoff.items():
+        if not key.startswith("handoff_"):
+            continue
+        raw_b = r["compress_GBps_raw"] * 1e6 * r["compress_ms"]   # bytes of bf16 K+V
+        packed = raw_b / r["ratio"]
+        row = {}
+        for g in gbps:
+            bps = g * 1e9 / 8
+            t_raw = 1e3 * raw_b / bps
+            t_c = r["compress_ms"] + 1e3 * packed / bps + r["decompress_ms"]
+            row[f"{g:g}Gbps"] = {"raw_ms": round(t_raw, 4), "compressed_ms": round(t_c, 4),
+                                 "speedup": round(t_raw / t_c, 2)}
+        out[key.replace("handoff_", "link_")] = row
+    return out
+
+
 CASES = {"gemm": case_gemm, "gemv": case_gemv, "flash": case_flash, "decode": case_decode,
          "handoff": case_handoff, "lossless": case_lossless, "norm": case_norm}
 
@@ -267,6 +289,8 @@ def main(argv=None) -> None:
     for name, fn in CASES.items():
         if a.case in ("all", name):
             out.update(fn(a, pk))
+    if any(k.startswith("handoff_") for k in out):
+        out.update(link_model(out))
     print(json.dumps(out, indent=1))
 
 
