@@ -75,6 +75,10 @@ def main() -> None:
     ap.add_argument("--link-gbps", type=float, default=0.0)
     ap.add_argument("--layers", type=int, default=0, help="override layer count (smoke runs only)")
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--ref-engine", default="handoff", choices=["handoff", "vllm"],
+                    help="reference arm: 'handoff' measures the reference's KV hand-off path (compression + "
+                         "NcclTransport) without vLLM; 'vllm' runs full PD serving (needs a vLLM the reference "
+                         "supports)")
     ap.add_argument("--ref-cuda-graphs", action="store_true",
                     help="reference arm: let vLLM capture CUDA graphs (default eager, as the reference's own PD "
                          "tests run; capture fails with its connector's per-layer save hook)")

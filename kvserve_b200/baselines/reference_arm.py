@@ -197,6 +197,9 @@ def run(args, emit) -> None:
         if REF_DIR not in sys.path:
             sys.path.insert(0, REF_DIR)
 
+    if getattr(args, "ref_engine", "handoff") == "handoff":
+        _run_handoff(args, emit, bar, rank, world, role, kv_port)
+        return
     n_req = args.warmup + args.steps
     results: list[dict] = []
     llm = None
@@ -286,6 +289,135 @@ def run(args, emit) -> None:
     finally:
         if llm is not None:
             _shutdown(llm)
+
+
+VLLM_INCOMPATIBLE = ("kvserve_v1's CompressedKVConnector does not run on the image's vLLM 0.22: its consumer "
+                     "injects KV with forward_context.virtual_engine (removed; layer.kv_cache is one tensor), "
+                     "so the decode engine dies on the first request; TTFT of the reference is unmeasured, "
+                     "its KV hand-off path is measured instead (kv_transfer_ms_p50)")
+
+
+def _run_handoff(args, emit, bar, rank: int, world: int, role: str, kv_port: int) -> None:
+    """The reference's KV hand-off data path exactly as its connector runs it
+    (compressed_kv_connector.py:393-470 producer, 235-372 consumer), without
+    vLLM: ``KVCompressionAdapter.compress`` of the stacked request KV
+    ``[L, 2, blocks, block_size, H, D]``, ``build_wire``, ``NcclTransport
+    .send_bundle``; on the consumer ``drain_received``, ``restore_from_wire``,
+    ``decompress`` and ``inject_kv_into_layer_by_blocks`` into a paged cache.
+    Time = consumer's KV-in-cache instant - shared start (host clock after
+    device synchronisation), i.e. the per-request KV-transfer time, max over
+    ranks by construction.  Synthetic N(0, 1) KV of the bench shape."""
+    import torch
+    L, H, D, bs = LLAMA_8B_CONFIG["num_hidden_layers"], LLAMA_8B_CONFIG["num_key_value_heads"], 128, 16
+    nblk = (args.prompt_len - 1 + bs - 1) // bs
+    n_req = args.warmup + args.steps
+    profile = reference_profile(args.profile)
+    rows = []
+    t = None
+    if role != "idle":
+        torch.cuda.set_device(0)
+        from kvserve_v1.transport.nccl_transport import NcclTransport
+        from kvserve_v1.compression.manager import KVCompressionAdapter, add_sentinel
+        t = NcclTransport(is_sender=(role == "producer"), host="127.0.0.1", port=kv_port, local_rank=0,
+                          channel_rank=0, recv_buffer_size=4 * 2 ** 30)
+        ad = KVCompressionAdapter(profile, H, D) if profile is not None else None
+        names = [f"model.layers.{i}.self_attn.attn" for i in range(L)]
+        g = torch.Generator(device="cuda").manual_seed(1234)
+        if role == "producer":
+            from kvserve_v1.compression.wire import build_wire
+            from kvserve_v1.connector.compressed_kv_connector import _max_nccl_chunk_bytes
+            stacked = torch.randn((L, 2, nblk, bs, H, D), generator=g, device="cuda").to(torch.bfloat16)
+        else:
+            from kvserve_v1.compression.wire import CompressedWire, restore_from_wire
+            from kvserve_v1.compression.manager import strip_sentinel, is_compressed_layer_names
+            from kvserve_v1.utils.kv_utils import inject_kv_into_layer_by_blocks
+            cache = torch.empty((L, 2, nblk + 64, bs, H, D), dtype=torch.bfloat16, device="cuda")
+            block_ids = list(range(7, 7 + nblk))
+    sampler = None
+    try:
+        for i in range(n_req):
+            if i == args.warmup and rank == 0:
+                from ..utils.clocks import ClockSampler
+                sampler = ClockSampler(list(range(world)))
+                sampler.start()
+            if t is not None:
+                torch.cuda.synchronize()
+            bar.wait()
+            if rank == 0:
+                bar.set(f"t0_{i}", repr(time.time()))
+            tid = f"kvs-ref-{i}"
+            if role == "producer":
+                t0 = float(bar.get(f"t0_{i}"))
+                if ad is not None:
+                    c = ad.compress(stacked, tid)
+                    wire = build_wire(c, _max_nccl_chunk_bytes())
+                    t.send_bundle(tid, add_sentinel(names), wire.meta, wire.body_chunks, wire.aux_tensors)
+                    nbytes = wire.nbytes
+                else:
+                    t.send(tid, names, stacked)
+                    nbytes = stacked.numel() * 2
+                t.wait_for_sent()
+                torch.cuda.synchronize()
+                bar.set(f"sent_{i}", json.dumps({"sent_ms": 1e3 * (time.time() - t0), "bytes": int(nbytes)}))
+            elif role == "consumer":
+                t0 = float(bar.get(f"t0_{i}"))
+                t.set_expected_requests([tid])
+                got = None
+                deadline = time.monotonic() + 300
+                while got is None and time.monotonic() < deadline:
+                    for key, payloads in t.drain_received().items():
+                        if key == tid:
+                            got = payloads[0]
+                    if got is None:
+                        time.sleep(0.001)
+                if got is None:
+                    raise RuntimeError(f"reference transport timed out on {tid}")
+                layer_names, payload = got
+                nb = t.payload_nbytes(payload)
+                if is_compressed_layer_names(layer_names):
+                    wire = CompressedWire(meta=payload["meta"], body_chunks=payload["body_chunks"],
+                                          aux_tensors=payload["aux_tensors"])
+                    kv = ad.decompress(restore_from_wire(wire))
+                else:
+                    kv = payload
+                for li in range(L):
+                    inject_kv_into_layer_by_blocks(cache[li], kv[li], block_ids, tid)
+                torch.cuda.synchronize()
+                t.release_received(tid, nb)
+                bar.set(f"done_{i}", repr(1e3 * (time.time() - t0)))
+        bar.wait()
+        clocks = sampler.stop() if sampler else None
+        if rank == 0:
+            tm = [float(bar.get(f"done_{i}")) for i in range(args.warmup, n_req)]
+            sent = [json.loads(bar.get(f"sent_{i}")) for i in range(args.warmup, n_req)]
+            raw = 2 * L * nblk * bs * H * D * 2
+            emit({
+                "impl": "reference",
+                "unavailable": VLLM_INCOMPATIBLE,
+                "metric": args.metric,
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "kv_transfer_ms_p50": round(statistics.median(tm), 3),
+                "kv_send_ms_p50": round(statistics.median(x["sent_ms"] for x in sent), 3),
+                "kv_payload_bytes_per_request": sent[0]["bytes"],
+                "kv_raw_bytes_per_request": raw,
+                "compression_ratio": round(raw / sent[0]["bytes"], 3),
+                "config": {"model": "llama-3.1-8b (KV shape only)", "layers": L, "seq_len": args.prompt_len,
+                           "profile": args.profile, "path": "kvserve_v1 KVCompressionAdapter + CompressedWire + "
+                                                           "NcclTransport, 1 producer -> 1 consumer",
+                           "data": "synthetic N(0,1) bf16 KV"},
+                "timing": "host clock after device synchronisation, consumer end - shared start",
+                "clocks": clocks,
+            })
+    finally:
+        if t is not None:
+            for m in ("shutdown", "close"):
+                fn = getattr(t, m, None)
+                if callable(fn):
+                    try:
+                        fn()
+                    except Exception:
+                        pass
+                    break
 
 
 def _build_engine(args, role: str, tp: int, kv_port: int):

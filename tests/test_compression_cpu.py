@@ -198,3 +198,22 @@ def test_controller_selects_and_learns(tmp_path):
     m = AnalyticalModel("reference")
     pa = Profile.from_dict(lib["accuracy_buckets"][0]["pareto_profiles"][0])
     assert m.predict_latency(pa, 1048576, 1.0, 0.0) == pytest.approx(1e3 / 20000 + 4e3)
+
+
+@pytest.mark.parametrize("name", ["original_top_lc", "original_top_nvcomp", "dct_centered_bitpack",
+                                  "haar_centered_bitpack", "hadamard_k4v2_bitpack"])
+def test_shipped_profiles_round_trip(name):
+    import json
+    import os
+    from kvserve_b200.compression.adapter import KVCompressionAdapter
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    with open(os.path.join(root, "configs", "compression", f"{name}.json")) as f:
+        cfg = json.load(f)
+    torch.manual_seed(0)
+    kv = torch.randn(2, 2, 1, 64, 8, 128).to(torch.bfloat16)
+    ad = KVCompressionAdapter(cfg, 8, 128, num_layers=2)
+    c = ad.compress(kv, "r")
+    assert c is not None and c.original_size / c.compressed_size > 2.0
+    rec = ad.decompress(c)
+    err = ((rec.float() - kv.float()).norm() / kv.float().norm()).item()
+    assert rec.shape == kv.shape and err < 0.6
