@@ -540,46 +540,71 @@ __device__ __forceinline__ float ex2_mufu(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// 2^x on the FMA pipes: 2^x = 2^n * 2^f with n = round(x) (1.5 * 2^23
-// rounding trick), f in [-0.5, 0.5]; 2^f by a cubic whose coefficients were
-// fitted for this kernel by relative-error-weighted least squares on
-// [-0.5, 0.5] (max relative error 8e-5, far below the bf16 rounding of P).
-// Arguments are clamped below at -120 so the exponent never underflows.
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -120.0f);
-  const float t = x + 12582912.0f;
-  const float n = t - 12582912.0f;
-  const float f = x - n;
-  float p = fmaf(f, 0.05516014f, 0.24258275f);
-  p = fmaf(f, p, 0.69326055f);
-  p = fmaf(f, p, 0.99993020f);
-  const int e = __float_as_int(t) - 0x4B400000;
-  return __int_as_float(__float_as_int(p) + (e << 23));
-}
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float m;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
   return m;
 }
-// (d0, d1) = (a0, a1) * b + (c, c) in one packed instruction.
-__device__ __forceinline__ void fma2s(float& d0, float& d1, float a0, float a1, float b, float c) {
-  asm("{.reg .b64 ra, rb, rc, rd;\n"
-      "mov.b64 ra, {%2,%3};\n"
-      "mov.b64 rb, {%4,%4};\n"
-      "mov.b64 rc, {%5,%5};\n"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n"
-      "mov.b64 {%0,%1}, rd;}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+// Packed f32x2 helpers on 64-bit registers (two fp32 lanes).
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
 }
-__device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
-  asm("{.reg .b64 ra, rb, rd;\n"
-      "mov.b64 ra, {%0,%1};\n"
-      "mov.b64 rb, {%2,%3};\n"
-      "add.rn.f32x2 rd, ra, rb;\n"
-      "mov.b64 {%0,%1}, rd;}"
-      : "+f"(s0), "+f"(s1)
-      : "f"(a0), "f"(a1));
+__device__ __forceinline__ void upk2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0,%1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t addv2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t subv2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// Loop-invariant operands of the softmax, packed once per tile row.
+struct PolyConsts {
+  uint64_t magic, c3, c2, c1, c0;
+};
+__device__ __forceinline__ PolyConsts poly_consts() {
+  PolyConsts k;
+  k.magic = pk2(12582912.0f, 12582912.0f);
+  k.c3 = pk2(0.05516014f, 0.05516014f);
+  k.c2 = pk2(0.24258275f, 0.24258275f);
+  k.c1 = pk2(0.69326055f, 0.69326055f);
+  k.c0 = pk2(0.99993020f, 0.99993020f);
+  return k;
+}
+// Two exponentials on the FMA pipes, in packed arithmetic:
+// 2^x = 2^n * 2^f with n = round(x) and f = x - n in [-0.5, 0.5].  With
+// t = x + 1.5*2^23 the integer n sits in t's low mantissa bits, and
+// (bits(t) << 23) == n << 23 modulo 2^32, so the exponent is added with one
+// shift-add per lane.  2^f is a cubic whose coefficients were fitted for this
+// kernel by relative-error-weighted least squares on [-0.5, 0.5] (max
+// relative error 8e-5, far below the bf16 rounding of P).  Arguments are
+// clamped below at -120 so the exponent never underflows.
+__device__ __forceinline__ void ex2_poly2(uint64_t x2, const PolyConsts& k, float& p0, float& p1) {
+  float x0, x1;
+  upk2(x2, x0, x1);
+  const uint64_t xc = pk2(fmaxf(x0, -120.0f), fmaxf(x1, -120.0f));
+  const uint64_t t = addv2(xc, k.magic);
+  const uint64_t n = subv2(t, k.magic);
+  const uint64_t f = subv2(xc, n);
+  uint64_t p = fma2(f, k.c3, k.c2);
+  p = fma2(f, p, k.c1);
+  p = fma2(f, p, k.c0);
+  float pf0, pf1, tf0, tf1;
+  upk2(p, pf0, pf1);
+  upk2(t, tf0, tf1);
+  p0 = __int_as_float(__float_as_int(pf0) + (__float_as_int(tf0) << 23));
+  p1 = __int_as_float(__float_as_int(pf1) + (__float_as_int(tf1) << 23));
 }
 }  // namespace v3
 
@@ -726,6 +751,7 @@ __global__ void __launch_bounds__(v3::kThreads, 1)
     const int q_abs = qrow0 + row;
     const int nkv = qrow0 / BKV + 1;
     const float sl2 = a.scale_log2;
+    const v3::PolyConsts pk_consts = v3::poly_consts();
     float m_ref = -INFINITY, l0 = 0.f, l1 = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
@@ -733,54 +759,63 @@ __global__ void __launch_bounds__(v3::kThreads, 1)
       if (!mbar_wait(&s_full[wg], j & 1, a.err)) ok = false;
       if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
       tc_fence_after();
-      uint32_t r[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + lane_off + c * 32, r[c]);
-      tmem_wait_ld();
+      // Pass 1: the row maximum over the whole S row.
       float mx = -INFINITY;
-      if (!diag) {
+      {
+        uint32_t r[4][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + lane_off + c * 32, r[c]);
+        tmem_wait_ld();
+        if (!diag) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) mx = v3::max3(mx, __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]));
-      } else {
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+            for (int e = 0; e < 32; e += 2)
+              mx = v3::max3(mx, __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]));
+        } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            if (c * 32 + e > row) r[c][e] = __float_as_uint(-INFINITY);
-            mx = fmaxf(mx, __uint_as_float(r[c][e]));
-          }
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (c * 32 + e <= row) mx = fmaxf(mx, __uint_as_float(r[c][e]));
+        }
       }
       const float mxs = mx * sl2;
       const bool rescale = mxs > m_ref + kRescaleThreshold;
       const float m_use = rescale ? mxs : m_ref;
-      const float neg_m = -m_use;
-      float s0 = 0.f, s1 = 0.f;
+      const uint64_t scale2 = v3::pk2(sl2, sl2), negm2 = v3::pk2(-m_use, -m_use);
+      uint64_t sum2 = v3::pk2(0.f, 0.f);
+      // Pass 2: S is re-read chunk by chunk; the TMEM load of chunk c+1 is in
+      // flight while chunk c is exponentiated.  P chunk c goes to columns
+      // [16c, 16c+16), always below the S columns still to be read.
+      uint32_t rb[2][32];
+      tmem_ld32(tS + lane_off, rb[0]);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
+        tmem_wait_ld();
+        if (c + 1 < 4) tmem_ld32(tS + lane_off + (c + 1) * 32, rb[(c + 1) & 1]);
+        const uint32_t* rc = rb[c & 1];
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          float x0, x1;
-          v3::fma2s(x0, x1, __uint_as_float(r[c][2 * e]), __uint_as_float(r[c][2 * e + 1]), sl2, neg_m);
+          const uint64_t x2 = v3::fma2(v3::pk2(__uint_as_float(rc[2 * e]), __uint_as_float(rc[2 * e + 1])),
+                                       scale2, negm2);
           float p0, p1;
           if ((v3::kPolyPairs >> (e & 7)) & 1u) {
-            p0 = v3::ex2_poly(x0);
-            p1 = v3::ex2_poly(x1);
-            if (diag) {  // the polynomial does not map -inf to 0
-              if (c * 32 + 2 * e > row) p0 = 0.f;
-              if (c * 32 + 2 * e + 1 > row) p1 = 0.f;
-            }
+            v3::ex2_poly2(x2, pk_consts, p0, p1);
           } else {
+            float x0, x1;
+            v3::upk2(x2, x0, x1);
             p0 = v3::ex2_mufu(x0);
             p1 = v3::ex2_mufu(x1);
           }
-          v3::add2(s0, s1, p0, p1);
+          if (diag) {
+            if (c * 32 + 2 * e > row) p0 = 0.f;
+            if (c * 32 + 2 * e + 1 > row) p1 = 0.f;
+          }
+          sum2 = v3::addv2(sum2, v3::pk2(p0, p1));
           pk[e] = pack_bf16x2(p0, p1);
         }
-        // P chunk c (keys 32c .. 32c+31) -> columns [16c, 16c+16) of S; the
-        // whole S row is already in registers.
         tmem_st16(tS + lane_off + c * 16, pk);
       }
       if (j > 0 && __any_sync(0xffffffffu, rescale)) {
@@ -799,8 +834,12 @@ __global__ void __launch_bounds__(v3::kThreads, 1)
       }
       tmem_wait_st();
       if (rescale) m_ref = m_use;
-      l0 += s0;
-      l1 += s1;
+      {
+        float s0, s1;
+        v3::upk2(sum2, s0, s1);
+        l0 += s0;
+        l1 += s1;
+      }
       tc_fence_before();
       mbar_arrive(&p_full[wg]);
     }

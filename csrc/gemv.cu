@@ -43,31 +43,43 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const bf16* __restrict__
                                                         const bf16* __restrict__ bias) {
   extern __shared__ uint4 xs_raw[];  // [M][K] bf16
   bf16* xs = reinterpret_cast<bf16*>(xs_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = (blockIdx.x * (kThreads / 32) + warp) * kRows;
+  const int kvec = K / 8;
+  constexpr int U = M <= 2 ? 8 : 4;  // 16-byte loads in flight per row per lane
+  // The first batch of weight loads is issued before x is staged, so the
+  // weight stream starts at kernel entry instead of after the barrier.
+  uint4 wv[kRows][U];
+  int kv = lane;
+  const bool first_full = row0 < N && kv + 32 * (U - 1) < kvec;
+  if (first_full) {
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        wv[r][u] = __ldcs(reinterpret_cast<const uint4*>(w + int64_t(min(row0 + r, N - 1)) * ldw) + kv + 32 * u);
+  }
   for (int i = threadIdx.x; i < M * K / 8; i += kThreads) {
     const int m = i / (K / 8), k8 = i % (K / 8);
     xs_raw[i] = *reinterpret_cast<const uint4*>(x + int64_t(m) * ldx + k8 * 8);
   }
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = (blockIdx.x * (kThreads / 32) + warp) * kRows;
   if (row0 >= N) return;
   float acc[kRows][M];
 #pragma unroll
   for (int r = 0; r < kRows; ++r)
 #pragma unroll
     for (int m = 0; m < M; ++m) acc[r][m] = 0.f;
-  const int kvec = K / 8;
-  constexpr int U = 4;
-  int kv = lane;
-  for (; kv + 32 * (U - 1) < kvec; kv += 32 * U) {
-    uint4 wv[kRows][U];
+  for (bool have = first_full; kv + 32 * (U - 1) < kvec; kv += 32 * U, have = false) {
+    if (!have) {
 #pragma unroll
-    for (int r = 0; r < kRows; ++r)
+      for (int r = 0; r < kRows; ++r)
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int row = min(row0 + r, N - 1);
-        wv[r][u] = __ldcs(reinterpret_cast<const uint4*>(w + int64_t(row) * ldw) + kv + 32 * u);
-      }
+        for (int u = 0; u < U; ++u) {
+          const int row = min(row0 + r, N - 1);
+          wv[r][u] = __ldcs(reinterpret_cast<const uint4*>(w + int64_t(row) * ldw) + kv + 32 * u);
+        }
+    }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int k = (kv + 32 * u) * 8;

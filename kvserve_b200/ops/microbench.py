@@ -158,11 +158,15 @@ def case_handoff(a, pk):
     from ..compression.heads import pack_sign_bits, rademacher_signs
     res = {}
     tokens = [1024, 8192, 32768] if a.quick else [1024, 4096, 8192, 32768, 131072]
+    if a.tokens:
+        tokens = [a.tokens]
     bit_sets = {"k4v2": ((16, 16), (4, 4)), "k8v8": ((256, 256), (256, 256)), "k3v3": ((8, 8), (8, 8)),
                 "k2v2": ((4, 4), (4, 4)), "k4v4": ((16, 16), (16, 16))}
     pick = ["k4v2", "k8v8"] if a.quick else list(bit_sets)
+    if a.bits:
+        pick = [a.bits]
     H = 8
-    for D in (128, 64):
+    for D in ((a.head_dim,) if a.head_dim else (128, 64)):
         signs = pack_sign_bits(rademacher_signs(0, 0, H, D)).cuda()
         order = torch.arange(H, dtype=torch.int32, device="cuda")
         for T in tokens:
@@ -283,12 +287,21 @@ def main(argv=None) -> None:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--quick", action="store_true")
     ap.add_argument("--once", action="store_true")
+    ap.add_argument("--tokens", type=int, default=0, help="handoff: only this token count")
+    ap.add_argument("--bits", default="", help="handoff: only this bit set (e.g. k4v2)")
+    ap.add_argument("--head-dim", type=int, default=0, help="handoff: only this head_dim")
     a = ap.parse_args(argv)
     pk = peaks()
     out = {"peaks": pk}
-    for name, fn in CASES.items():
-        if a.case in ("all", name):
-            out.update(fn(a, pk))
+    from ..utils.clocks import ClockSampler
+    sampler = ClockSampler([torch.cuda.current_device()])
+    sampler.start()
+    try:
+        for name, fn in CASES.items():
+            if a.case in ("all", name):
+                out.update(fn(a, pk))
+    finally:
+        out["clocks"] = sampler.stop()
     if any(k.startswith("handoff_") for k in out):
         out.update(link_model(out))
     print(json.dumps(out, indent=1))
