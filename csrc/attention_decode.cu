@@ -11,6 +11,7 @@
 #include "common.cuh"
 #include "ops.h"
 #include "attention_decode_kernels.cuh"
+#include "attention_decode_tma.cuh"
 
 namespace kvs {
 
@@ -34,6 +35,14 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tenso
   KVS_CHECK_ARG(block_tables.scalar_type() == at::kInt && ctx_lens.scalar_type() == at::kInt, "int32 tables");
   if (B == 0) return;
   const int G = Hq / Hkv;
+  // TMA-fed kernel: head_dim 128, 16-token blocks stored contiguously.
+  const bool tma_ok = D == 128 && bsz == kTmaBlk && k_cache.stride(2) == D && k_cache.stride(1) == Hkv * D &&
+                      k_cache.stride(0) == int64_t(bsz) * Hkv * D && v_cache.strides() == k_cache.strides() &&
+                      (G == 1 || G == 2 || G == 4) &&
+                      (reinterpret_cast<uintptr_t>(k_cache.data_ptr()) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(v_cache.data_ptr()) & 15) == 0;
+  // it holds two CTAs per SM: one wave of 2 x 148 CTAs
+  if (tma_ok) splits = std::max<int64_t>(1, std::min<int64_t>(splits, (2 * kNumSMs) / std::max(1, B * Hkv)));
   const int chunk = int(std::max<int64_t>(16, ((max_ctx + splits - 1) / splits + 15) / 16 * 16));
   splits = (max_ctx + chunk - 1) / chunk;
   if (splits < 1) splits = 1;
@@ -43,6 +52,45 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tenso
   dim3 grid(int(splits), Hkv, B);
   const float sl2 = float(scale) * 1.4426950408889634f;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  float* po0 = splits > 1 ? part_o.data_ptr<float>() : nullptr;
+  float* pml0 = splits > 1 ? part_ml.data_ptr<float>() : nullptr;
+  if (tma_ok) {
+    const uint64_t rows = uint64_t(k_cache.size(0)) * bsz;
+    const CUtensorMap tk = make_tmap_2d_bf16(k_cache.data_ptr(), uint64_t(Hkv) * D, rows, uint64_t(Hkv) * D * 2,
+                                             128, kTmaBlk, false);
+    const CUtensorMap tv = make_tmap_2d_bf16(v_cache.data_ptr(), uint64_t(Hkv) * D, rows, uint64_t(Hkv) * D * 2,
+                                             128, kTmaBlk, false);
+    auto qp = reinterpret_cast<const bf16*>(q.data_ptr());
+    auto op = reinterpret_cast<bf16*>(out.data_ptr());
+    const int32_t* btp = block_tables.data_ptr<int32_t>();
+    const int32_t* clp = ctx_lens.data_ptr<int32_t>();
+#define KVS_TMA_CASE(GG)                                                                                       \
+  case GG: {                                                                                                   \
+    static bool set = false;                                                                                   \
+    if (!set) {                                                                                                \
+      KVS_CUDA_CHECK(cudaFuncSetAttribute(paged_decode_tma_kernel<GG>,                                         \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kTmaSmem));             \
+      set = true;                                                                                              \
+    }                                                                                                          \
+    paged_decode_tma_kernel<GG><<<grid, kTmaThreads, kTmaSmem, st>>>(tk, tv, qp, q.stride(0), btp,             \
+                                                                     block_tables.stride(0), clp, Hq,          \
+                                                                     int(splits), chunk, sl2, po0, pml0, op,   \
+                                                                     out.stride(0), nullptr);                  \
+    break;                                                                                                     \
+  }
+    switch (G) {
+      KVS_TMA_CASE(1)
+      KVS_TMA_CASE(2)
+      KVS_TMA_CASE(4)
+    }
+#undef KVS_TMA_CASE
+    if (splits > 1) {
+      dim3 g2(Hq, B);
+      merge_splits_kernel<128><<<g2, 128, 0, st>>>(po0, pml0, Hq, int(splits), op, out.stride(0));
+    }
+    KVS_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   auto qp = reinterpret_cast<const bf16*>(q.data_ptr());
   auto kp = reinterpret_cast<const bf16*>(k_cache.data_ptr());
   auto vp = reinterpret_cast<const bf16*>(v_cache.data_ptr());

@@ -51,9 +51,29 @@ struct GemmArgs {
   const bf16* bias;
   int M, N, K;
   int act;  // 1: C[:, n] = silu(gate) * up, gate/up rows of B interleaved in blocks of BN/2
+            // 2: fused QKV projection: bias, rotary embedding on q/k heads, k/v copies
   int64_t ldc, ldr;
   uint32_t* err;
+  // act == 2 (head_dim 128, NeoX rotate-half; cos_sin [max_pos, 128] = cos[64] | sin[64])
+  const float* cos_sin;
+  const int32_t* positions;
+  int hq, hkv;
+  bf16* k_dst;
+  bf16* v_dst;
+  int64_t dst_tok_stride, dst_head_stride;
 };
+
+// Stores 32 consecutive bf16 (64 bytes) from fp32 values.
+__device__ __forceinline__ void store32_bf16(bf16* dst, const float (&f)[32]) {
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    uint4 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) oh[e] = __floats2bfloat162_rn(f[8 * v + 2 * e], f[8 * v + 2 * e + 1]);
+    *reinterpret_cast<uint4*>(dst + 8 * v) = o;
+  }
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -175,7 +195,62 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row = mb * BM + row_in_tile;
       const bool row_ok = row < p.M;
-      if (p.act) {
+      if (p.act == 2) {
+        // Two heads per tile.  Values are rounded to bf16 before the rotation
+        // (the same arithmetic as the stand-alone rope kernel, so prefill and
+        // decode agree bit for bit).
+        const int pos = row_ok ? p.positions[row] : 0;
+        const float* cs = p.cos_sin + int64_t(pos) * 128;
+#pragma unroll 1
+        for (int hl = 0; hl < BN / 128; ++hl) {
+          const int hh = nb * (BN / 128) + hl;
+          if (hh * 128 >= p.N) break;
+          const uint32_t tb = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN + hl * 128);
+          bf16* crow = p.C + int64_t(row) * p.ldc + hh * 128;
+          const bool rotary = hh < p.hq + p.hkv;
+          const bool is_k = hh >= p.hq && hh < p.hq + p.hkv;
+          bf16* extra = nullptr;
+          if (is_k && p.k_dst) extra = p.k_dst + int64_t(row) * p.dst_tok_stride + int64_t(hh - p.hq) * p.dst_head_stride;
+          if (!rotary && p.v_dst)
+            extra = p.v_dst + int64_t(row) * p.dst_tok_stride + int64_t(hh - p.hq - p.hkv) * p.dst_head_stride;
+#pragma unroll 1
+          for (int cc = 0; cc < 2; ++cc) {
+            uint32_t r1[32], r2[32];
+            tmem_ld32(tb + cc * 32, r1);
+            tmem_ld32(tb + 64 + cc * 32, r2);
+            tmem_wait_ld();
+            if (!row_ok) continue;
+            float x1[32], x2[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int d = cc * 32 + e;
+              float a1 = __uint_as_float(r1[e]), a2 = __uint_as_float(r2[e]);
+              if (p.bias) {
+                a1 += __bfloat162float(p.bias[hh * 128 + d]);
+                a2 += __bfloat162float(p.bias[hh * 128 + 64 + d]);
+              }
+              x1[e] = __bfloat162float(__float2bfloat16_rn(a1));
+              x2[e] = __bfloat162float(__float2bfloat16_rn(a2));
+            }
+            if (rotary) {
+#pragma unroll
+              for (int e = 0; e < 32; ++e) {
+                const int d = cc * 32 + e;
+                const float c = cs[d], sn = cs[64 + d];
+                const float o1 = x1[e] * c - x2[e] * sn, o2 = x2[e] * c + x1[e] * sn;
+                x1[e] = o1;
+                x2[e] = o2;
+              }
+            }
+            store32_bf16(crow + cc * 32, x1);
+            store32_bf16(crow + 64 + cc * 32, x2);
+            if (extra) {
+              store32_bf16(extra + cc * 32, x1);
+              store32_bf16(extra + 64 + cc * 32, x2);
+            }
+          }
+        }
+      } else if (p.act) {
         // gate in accumulator columns [0, 128), up in [128, 256) of the same
         // 128 output features; output columns nb*128 + [0, 128).
 #pragma unroll 1
@@ -280,7 +355,7 @@ EncodeFn get_encode_fn() {
 }  // namespace
 
 CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
-                              uint32_t box_inner, uint32_t box_outer) {
+                              uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
   KVS_CHECK_ARG((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
   KVS_CHECK_ARG(row_stride_bytes % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
   CUtensorMap m;
@@ -289,7 +364,8 @@ CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t inner, uint64_t outer, 
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
-                               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   KVS_CHECK_ARG(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
   return m;
@@ -323,6 +399,54 @@ void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, GemmArgs& p) {
   KVS_CUDA_CHECK(cudaGetLastError());
 }
 }  // namespace
+
+void gemm_qkv_rope_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, c10::optional<torch::Tensor> bias,
+                        torch::Tensor cos_sin, torch::Tensor positions, int64_t hq, int64_t hkv,
+                        c10::optional<torch::Tensor> k_dst, c10::optional<torch::Tensor> v_dst, torch::Tensor err) {
+  KVS_CHECK_ARG(a.is_cuda() && b.is_cuda() && c.is_cuda() && a.scalar_type() == at::kBFloat16 &&
+                    b.scalar_type() == at::kBFloat16 && c.scalar_type() == at::kBFloat16,
+                "gemm_qkv_rope: bf16 CUDA operands");
+  KVS_CHECK_ARG(a.dim() == 2 && b.dim() == 2 && c.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1 &&
+                    c.stride(1) == 1,
+                "gemm_qkv_rope: 2-D row-major operands");
+  const int M = int(a.size(0)), K = int(a.size(1)), N = int(b.size(0));
+  KVS_CHECK_ARG(b.size(1) == K && c.size(0) == M && c.size(1) == N && N == (hq + 2 * hkv) * 128,
+                "gemm_qkv_rope: b [(hq+2hkv)*128, K], c [M, N]");
+  KVS_CHECK_ARG(K % 8 == 0 && a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0 && c.stride(0) % 8 == 0,
+                "gemm_qkv_rope: K and leading dims must be multiples of 8");
+  KVS_CHECK_ARG(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous() && cos_sin.size(1) == 128,
+                "gemm_qkv_rope: cos_sin [max_pos, 128] fp32");
+  KVS_CHECK_ARG(positions.scalar_type() == at::kInt && positions.numel() >= M, "gemm_qkv_rope: int32 positions");
+  if (M == 0) return;
+  GemmArgs p{};
+  p.C = reinterpret_cast<bf16*>(c.data_ptr());
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = c.stride(0);
+  p.act = 2;
+  p.err = reinterpret_cast<uint32_t*>(err.data_ptr<int32_t>());
+  if (bias.has_value()) {
+    KVS_CHECK_ARG(bias->numel() == N && bias->is_contiguous() && bias->scalar_type() == at::kBFloat16,
+                  "gemm_qkv_rope: bias must be contiguous bf16 [N]");
+    p.bias = reinterpret_cast<const bf16*>(bias->data_ptr());
+  }
+  p.cos_sin = cos_sin.data_ptr<float>();
+  p.positions = positions.data_ptr<int32_t>();
+  p.hq = int(hq);
+  p.hkv = int(hkv);
+  if (k_dst.has_value() || v_dst.has_value()) {
+    KVS_CHECK_ARG(k_dst.has_value() && v_dst.has_value() && k_dst->dim() == 3 && k_dst->strides() == v_dst->strides() &&
+                      k_dst->stride(2) == 1 && k_dst->size(0) >= M && k_dst->stride(0) % 8 == 0 &&
+                      k_dst->stride(1) % 8 == 0,
+                  "gemm_qkv_rope: k_dst/v_dst [>=M, hkv, 128] with equal strides");
+    p.k_dst = reinterpret_cast<bf16*>(k_dst->data_ptr());
+    p.v_dst = reinterpret_cast<bf16*>(v_dst->data_ptr());
+    p.dst_tok_stride = k_dst->stride(0);
+    p.dst_head_stride = k_dst->stride(1);
+  }
+  launch_gemm(a, b, p);
+}
 
 void gemm_silu_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor err) {
   KVS_CHECK_ARG(a.is_cuda() && b.is_cuda() && c.is_cuda() && a.scalar_type() == at::kBFloat16 &&

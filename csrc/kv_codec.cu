@@ -69,9 +69,52 @@ struct EncodeArgs {
 __device__ __forceinline__ const bf16* src_row(const bf16* base, int t, int h, int64_t tok_stride,
                                                int64_t head_stride, const int32_t* table, int bs,
                                                int64_t block_stride) {
-  if (table != nullptr)
-    return base + int64_t(table[t / bs]) * block_stride + int64_t(t % bs) * tok_stride + int64_t(h) * head_stride;
+  if (table != nullptr) {
+    const int sh = (bs & (bs - 1)) == 0 ? __ffs(bs) - 1 : -1;
+    const int b = sh >= 0 ? (t >> sh) : t / bs, o = sh >= 0 ? (t & (bs - 1)) : t % bs;
+    return base + int64_t(table[b]) * block_stride + int64_t(o) * tok_stride + int64_t(h) * head_stride;
+  }
   return base + int64_t(t) * tok_stride + int64_t(h) * head_stride;
+}
+
+// Row -> (token, head slot) without integer division in the loop.  A row is
+// (token t, slot j) with r = (t - t0) * H + j.  When the per-iteration row
+// step is a multiple of H, a lane always sees the same slot and its token
+// advances by a constant, so both follow from one division at the start.
+struct RowMap {
+  bool fixed;
+  int tq, j0, tstep;
+};
+__device__ __forceinline__ RowMap make_rowmap(int H, int lane_row, int rows_per_iter) {
+  RowMap m;
+  m.fixed = (rows_per_iter % H) == 0;
+  m.tq = lane_row / H;
+  m.j0 = lane_row % H;
+  m.tstep = rows_per_iter / H;
+  return m;
+}
+__device__ __forceinline__ void row_at(const RowMap& m, int H, int t0, int t1, int tb, int i, int base_row,
+                                       int nrows, int& t, int& j, bool& valid) {
+  if (m.fixed) {
+    t = tb + i * m.tstep + m.tq;
+    j = m.j0;
+    valid = t < t1;
+  } else {
+    const int r = base_row;
+    valid = r < nrows;
+    t = t0 + r / H;
+    j = r % H;
+  }
+}
+// Paged lookup with a shift/mask when the block size is a power of two.
+__device__ __forceinline__ void split_pos(int pos, int bs, int bshift, int& blk, int& off) {
+  if (bshift >= 0) {
+    blk = pos >> bshift;
+    off = pos & (bs - 1);
+  } else {
+    blk = pos / bs;
+    off = pos % bs;
+  }
 }
 
 struct DecodeArgs {
@@ -143,10 +186,13 @@ __device__ __forceinline__ void fwht_row(float (&v)[8], int lir) {
   }
 #pragma unroll
   for (int m = 1; m < LANES; m <<= 1) {
+    // upper lane of the pair: o - v, lower lane: v + o, both as o + sgn * v
+    // (the product by +-1 is exact, so this is bit-identical to the two forms)
+    const float sgn = (lir & m) ? -1.0f : 1.0f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float o = __shfl_xor_sync(0xffffffffu, v[i], m);
-      v[i] = (lir & m) ? (o - v[i]) : (v[i] + o);
+      v[i] = fmaf(sgn, v[i], o);
     }
   }
 }
@@ -193,6 +239,19 @@ __device__ __forceinline__ uint64_t quant_pack8(const float (&y)[8], float mn, f
   return acc;
 }
 
+// Geometry fields indexed by runtime part/section through selects, so a
+// FrameGeom held by a kernel is never spilled to local memory.
+__device__ __forceinline__ int gbits(const FrameGeom& g, int p, int s) {
+  return p ? (s ? g.bits[1][1] : g.bits[1][0]) : (s ? g.bits[0][1] : g.bits[0][0]);
+}
+__device__ __forceinline__ int glevels(const FrameGeom& g, int p, int s) {
+  return p ? (s ? g.levels[1][1] : g.levels[1][0]) : (s ? g.levels[0][1] : g.levels[0][0]);
+}
+__device__ __forceinline__ int64_t gpayload(const FrameGeom& g, int p, int s) {
+  return p ? (s ? g.payload[1][1] : g.payload[1][0]) : (s ? g.payload[0][1] : g.payload[0][0]);
+}
+__device__ __forceinline__ int64_t gvaux(const FrameGeom& g, int s) { return s ? g.v_aux[1] : g.v_aux[0]; }
+
 // Section of head slot j and its index inside the section.
 __device__ __forceinline__ void slot_section(const FrameGeom& g, int j, int& s, int& js, int& hs) {
   s = j < g.n_low ? 0 : 1;
@@ -226,6 +285,7 @@ __global__ void __launch_bounds__(kThreads) kv_kstats_kernel(EncodeArgs a) {
   const int lir = lane % LANES, rw = lane / LANES;
   const float scale = a.g.transform ? inv_sqrt_d<D>() : 1.0f;
   const bool fixed_slot = (kRowsPerIter % g.H) == 0;
+  const RowMap rmap = make_rowmap(g.H, warp * RPW + rw, kRowsPerIter);
   float mn[8], mx[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) { mn[e] = INFINITY; mx[e] = -INFINITY; }
@@ -235,17 +295,15 @@ __global__ void __launch_bounds__(kThreads) kv_kstats_kernel(EncodeArgs a) {
     const int t0 = tile * a.tile_tokens;
     const int t1 = min(g.T, t0 + a.tile_tokens);
     const int nrows = (t1 - t0) * g.H;
-    for (int base = 0; base < nrows; base += kRowsPerIter * kRowUnroll) {
+    for (int base = 0, tb = t0; base < nrows; base += kRowsPerIter * kRowUnroll, tb += rmap.tstep * kRowUnroll) {
       // all kRowUnroll loads of this row group are issued before any use
       float v[kRowUnroll][8];
       int jr[kRowUnroll];
       bool valid[kRowUnroll];
 #pragma unroll
       for (int i = 0; i < kRowUnroll; ++i) {
-        const int r = base + i * kRowsPerIter + warp * RPW + rw;
-        valid[i] = r < nrows;
-        const int t = t0 + r / g.H;
-        jr[i] = r % g.H;
+        int t;
+        row_at(rmap, g.H, t0, t1, tb, i, base + i * kRowsPerIter + warp * RPW + rw, nrows, t, jr[i], valid[i]);
         if (valid[i]) {
           uint4 raw;
           load8(src_row(a.k, t, a.order[jr[i]], a.k_tok_stride, a.k_head_stride, a.block_table, a.block_size,
@@ -265,7 +323,7 @@ __global__ void __launch_bounds__(kThreads) kv_kstats_kernel(EncodeArgs a) {
         if (!valid[i]) continue;
         int s, js, hs;
         slot_section(g, j, s, js, hs);
-        if (g.bits[0][s] == kRawBits) continue;
+        if (gbits(g, 0, s) == kRawBits) continue;
         if (fixed_slot) {
           my_slot = j;
 #pragma unroll
@@ -297,14 +355,18 @@ __global__ void __launch_bounds__(kThreads) kv_kstats_kernel(EncodeArgs a) {
   }
 }
 
-// Completion: every CTA fences its stores system-wide, the last CTA resets
+// Completion: every CTA fences its stores system-wide (one thread after a
+// barrier), the last CTA resets
 // the statistics, writes the frame header, optionally waits out the
 // emulated link time, and publishes the frame with a release store.
 __device__ void encode_signal_done(const EncodeArgs& a) {
   __shared__ int s_last;
-  __threadfence_system();
+  // The barrier orders every thread's frame stores before thread 0's
+  // system-scope fence (fences are cumulative), so one fence per CTA
+  // suffices before the completion count.
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const uint32_t total = gridDim.x * gridDim.y;
     s_last = (atomicAdd(a.counter, 1u) == total - 1);
   }
@@ -324,8 +386,8 @@ __device__ void encode_signal_done(const EncodeArgs& a) {
     h.seq = a.seq;
     for (int p = 0; p < 2; ++p)
       for (int s = 0; s < 2; ++s) {
-        h.bits[p][s] = uint8_t(a.g.bits[p][s]);
-        h.levels[p][s] = uint8_t(a.g.levels[p][s] - 1);
+        h.bits[p][s] = uint8_t(gbits(a.g, p, s));
+        h.levels[p][s] = uint8_t(glevels(a.g, p, s) - 1);
       }
     h.transform = uint32_t(a.g.transform);
     for (int i = 0; i < 5; ++i) h.reserved[i] = 0;
@@ -349,8 +411,9 @@ __device__ void encode_signal_done(const EncodeArgs& a) {
   }
 }
 
-template <int D>
-__global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
+// ITERS: rows of one token a lane holds in the V part (ceil(H / rows per warp step)).
+template <int D, int ITERS>
+__global__ void __launch_bounds__(kThreads, ITERS <= 4 ? 3 : 1) kv_quant_kernel(EncodeArgs a) {
   constexpr int LANES = D / 8, RPW = 32 / LANES;
   constexpr int kWarps = kThreads / 32;
   constexpr int kRowsPerIter = kWarps * RPW;
@@ -370,11 +433,11 @@ __global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
     for (int c = threadIdx.x; c < HD; c += kThreads) {
       int s, js, hs;
       slot_section(g, c / D, s, js, hs);
-      if (g.bits[0][s] == kRawBits) continue;
+      if (gbits(g, 0, s) == kRawBits) continue;
       const float lo = ordered_to_float(a.stats[c]);
       const float hi = ordered_to_float(a.stats[HD + c]);
       const bf16 minb = rn(lo);
-      const bf16 sclb = rn(fmaxf(hi - to_f32(minb), 1e-5f) / float(g.levels[0][s] - 1));
+      const bf16 sclb = rn(fmaxf(hi - to_f32(minb), 1e-5f) / float(glevels(g, 0, s) - 1));
       sparam[c] = to_f32(minb);
       sparam[HD + c] = 1.0f / to_f32(sclb);
       if (blockIdx.x == 0) {
@@ -384,26 +447,38 @@ __global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
     }
     if (blockIdx.x == 0 && threadIdx.x < 2) {
       const int s = threadIdx.x;
-      if (section_heads(g, s) > 0 && g.bits[0][s] != kRawBits)
-        write_bitpack_header(a.frame + g.payload[0][s], g.bits[0][s],
+      if (section_heads(g, s) > 0 && gbits(g, 0, s) != kRawBits)
+        write_bitpack_header(a.frame + gpayload(g, 0, s), gbits(g, 0, s),
                              uint64_t(g.T) * section_heads(g, s) * D);
     }
     __syncthreads();
+    // With kRowsPerIter a multiple of H every row this lane handles belongs
+    // to the same head slot: keep its 8 channel parameters in registers.
+    const bool kslot_fixed = (kRowsPerIter % g.H) == 0;
+    const RowMap rmap = make_rowmap(g.H, warp * RPW + rw, kRowsPerIter);
+    float kmn[8], kinv[8];
+    if (kslot_fixed) {
+      const int j0 = (warp * RPW + rw) % g.H;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        kmn[e] = sparam[j0 * D + lir * 8 + e];
+        kinv[e] = sparam[HD + j0 * D + lir * 8 + e];
+      }
+    }
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
       const int t0 = tile * a.tile_tokens;
       const int t1 = min(g.T, t0 + a.tile_tokens);
       const int nrows = (t1 - t0) * g.H;
-      for (int base = 0; base < nrows; base += kRowsPerIter * kRowUnroll) {
+      for (int base = 0, tb = t0; base < nrows;
+           base += kRowsPerIter * kRowUnroll, tb += rmap.tstep * kRowUnroll) {
         float v[kRowUnroll][8];
         uint4 raw[kRowUnroll];
         int tr[kRowUnroll], jr[kRowUnroll];
         bool valid[kRowUnroll];
 #pragma unroll
         for (int i = 0; i < kRowUnroll; ++i) {
-          const int r = base + i * kRowsPerIter + warp * RPW + rw;
-          valid[i] = r < nrows;
-          tr[i] = t0 + r / g.H;
-          jr[i] = r % g.H;
+          row_at(rmap, g.H, t0, t1, tb, i, base + i * kRowsPerIter + warp * RPW + rw, nrows, tr[i], jr[i],
+                 valid[i]);
           raw[i] = make_uint4(0, 0, 0, 0);
           if (valid[i]) {
             load8(src_row(a.k, tr[i], a.order[jr[i]], a.k_tok_stride, a.k_head_stride, a.block_table,
@@ -423,23 +498,26 @@ __global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
           if (!valid[i]) continue;
           int s, js, hs;
           slot_section(g, j, s, js, hs);
-          const int bits = g.bits[0][s];
+          const int bits = gbits(g, 0, s);
           const int64_t sym = (int64_t(t) * hs + js) * D + lir * 8;
           if (bits == kRawBits) {
-            *reinterpret_cast<uint4*>(a.frame + g.payload[0][s] + sym * 2) = raw[i];
+            *reinterpret_cast<uint4*>(a.frame + gpayload(g, 0, s) + sym * 2) = raw[i];
             continue;
           }
-          // Per-channel parameters differ per element: quantise one by one.
+          // Per-channel parameters differ per element: quantise one by one
+          // (from registers when this lane always sees the same head slot).
           uint64_t acc = 0;
-          const float top = float(g.levels[0][s] - 1);
+          const float top = float(glevels(g, 0, s) - 1);
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int c = j * D + lir * 8 + e;
-            float q = rintf((v[i][e] * scale - sparam[c]) * sparam[HD + c]);
+            const float mn = kslot_fixed ? kmn[e] : sparam[c];
+            const float iv = kslot_fixed ? kinv[e] : sparam[HD + c];
+            float q = rintf((v[i][e] * scale - mn) * iv);
             q = fminf(fmaxf(q, 0.0f), top);
             acc |= uint64_t(uint32_t(q)) << (e * bits);
           }
-          store_packed(a.frame + g.payload[0][s] + 16 + sym * bits / 8, acc, bits);
+          store_packed(a.frame + gpayload(g, 0, s) + 16 + sym * bits / 8, acc, bits);
         }
       }
     }
@@ -447,8 +525,8 @@ __global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
     // ---- V: one warp per token; per-token, per-section statistics ----
     if (blockIdx.x == 0 && threadIdx.x < 2) {
       const int s = threadIdx.x;
-      if (section_heads(g, s) > 0 && g.bits[1][s] != kRawBits)
-        write_bitpack_header(a.frame + g.payload[1][s], g.bits[1][s],
+      if (section_heads(g, s) > 0 && gbits(g, 1, s) != kRawBits)
+        write_bitpack_header(a.frame + gpayload(g, 1, s), gbits(g, 1, s),
                              uint64_t(g.T) * section_heads(g, s) * D);
     }
     const int iters = (g.H + RPW - 1) / RPW;
@@ -456,13 +534,12 @@ __global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
       const int t0 = tile * a.tile_tokens;
       const int t1 = min(g.T, t0 + a.tile_tokens);
       for (int t = t0 + warp; t < t1; t += kWarps) {
-        // Every row of the token is loaded first and kept as raw bf16; the
-        // transform is evaluated twice (statistics pass, quantisation pass)
-        // instead of holding all transformed rows, which keeps the kernel
-        // at low register pressure (high occupancy).
-        uint4 raw[kMaxRowIters];
+        // Every row of the token is loaded first (all loads in flight), then
+        // transformed once and kept in registers for the statistics and the
+        // quantisation passes.
+        uint4 raw[ITERS];
 #pragma unroll
-        for (int i = 0; i < kMaxRowIters; ++i) {
+        for (int i = 0; i < ITERS; ++i) {
           if (i >= iters) break;
           const int j = rw + RPW * i;
           raw[i] = j < g.H ? *reinterpret_cast<const uint4*>(
@@ -470,35 +547,44 @@ __global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
                                          a.block_size, a.v_block_stride) + lir * 8)
                            : make_uint4(0, 0, 0, 0);
         }
-        auto transformed = [&](int i, float (&v)[8]) {
+        float vt[ITERS][8];
+#pragma unroll
+        for (int i = 0; i < ITERS; ++i) {
+          if (i >= iters) break;
           const int j = rw + RPW * i;
           const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 f = __bfloat1622float2(hh[e]);
-            v[2 * e] = f.x;
-            v[2 * e + 1] = f.y;
+            vt[i][2 * e] = f.x;
+            vt[i][2 * e + 1] = f.y;
           }
           if (g.transform) {
-            if (j < g.H) apply_signs(v, sign_byte(a.sign_bits + a.order[j] * (D / 32), lir));
-            fwht_row<LANES>(v, lir);
+            if (j < g.H) apply_signs(vt[i], sign_byte(a.sign_bits + a.order[j] * (D / 32), lir));
+            fwht_row<LANES>(vt[i], lir);
           }
 #pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] *= scale;
-        };
+          for (int e = 0; e < 8; ++e) vt[i][e] *= scale;
+        }
         float smin[2] = {INFINITY, INFINITY}, smax[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-        for (int i = 0; i < kMaxRowIters; ++i) {
+        for (int i = 0; i < ITERS; ++i) {
           if (i >= iters) break;
-          float v[8];
-          transformed(i, v);
           const int j = rw + RPW * i;
           if (j < g.H) {
-            const int s = j < g.n_low ? 0 : 1;
+            float lo = vt[i][0], hi = vt[i][0];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              smin[s] = fminf(smin[s], v[e]);
-              smax[s] = fmaxf(smax[s], v[e]);
+            for (int e = 1; e < 8; ++e) {
+              lo = fminf(lo, vt[i][e]);
+              hi = fmaxf(hi, vt[i][e]);
+            }
+            // constant indices only (a runtime index would put the arrays in local memory)
+            if (j < g.n_low) {
+              smin[0] = fminf(smin[0], lo);
+              smax[0] = fmaxf(smax[0], hi);
+            } else {
+              smin[1] = fminf(smin[1], lo);
+              smax[1] = fmaxf(smax[1], hi);
             }
           }
         }
@@ -515,34 +601,33 @@ __global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
         for (int s = 0; s < 2; ++s) {
           pmin[s] = 0.f;
           pinv[s] = 0.f;
-          if (section_heads(g, s) == 0 || g.bits[1][s] == kRawBits) continue;
+          if (section_heads(g, s) == 0 || gbits(g, 1, s) == kRawBits) continue;
           const bf16 minb = rn(smin[s]);
-          const bf16 sclb = rn(fmaxf(smax[s] - to_f32(minb), 1e-5f) / float(g.levels[1][s] - 1));
+          const bf16 sclb = rn(fmaxf(smax[s] - to_f32(minb), 1e-5f) / float(glevels(g, 1, s) - 1));
           pmin[s] = to_f32(minb);
           pinv[s] = 1.0f / to_f32(sclb);
           if (lane == 0) {
-            bf16* aux = reinterpret_cast<bf16*>(a.frame + g.v_aux[s]);
+            bf16* aux = reinterpret_cast<bf16*>(a.frame + gvaux(g, s));
             aux[t] = minb;
             aux[g.T + t] = sclb;
           }
         }
 #pragma unroll
-        for (int i = 0; i < kMaxRowIters; ++i) {
+        for (int i = 0; i < ITERS; ++i) {
           if (i >= iters) break;
-          float v[8];
-          transformed(i, v);
           const int j = rw + RPW * i;
           if (j >= g.H) continue;
           int s, js, hs;
           slot_section(g, j, s, js, hs);
-          const int bits = g.bits[1][s];
+          const int bits = gbits(g, 1, s);
           const int64_t sym = (int64_t(t) * hs + js) * D + lir * 8;
           if (bits == kRawBits) {
-            *reinterpret_cast<uint4*>(a.frame + g.payload[1][s] + sym * 2) = raw[i];
+            *reinterpret_cast<uint4*>(a.frame + gpayload(g, 1, s) + sym * 2) = raw[i];
             continue;
           }
-          const uint64_t acc = quant_pack8(v, pmin[s], pinv[s], g.levels[1][s], bits);
-          store_packed(a.frame + g.payload[1][s] + 16 + sym * bits / 8, acc, bits);
+          const uint64_t acc = quant_pack8(vt[i], s ? pmin[1] : pmin[0], s ? pinv[1] : pinv[0],
+                                           glevels(g, 1, s), bits);
+          store_packed(a.frame + gpayload(g, 1, s) + 16 + sym * bits / 8, acc, bits);
         }
       }
     }
@@ -554,7 +639,7 @@ __global__ void __launch_bounds__(kThreads) kv_quant_kernel(EncodeArgs a) {
 // Decode: frame -> paged KV cache.
 // ---------------------------------------------------------------------------
 template <int D>
-__global__ void __launch_bounds__(kThreads) kv_decode_kernel(DecodeArgs a) {
+__global__ void __launch_bounds__(kThreads, 3) kv_decode_kernel(DecodeArgs a) {
   constexpr int LANES = D / 8, RPW = 32 / LANES;
   constexpr int kRowsPerIter = (kThreads / 32) * RPW;
   extern __shared__ float sk[];  // K params: min[HD], scale[HD]
@@ -589,11 +674,13 @@ __global__ void __launch_bounds__(kThreads) kv_decode_kernel(DecodeArgs a) {
           ok = 0;
         }
       }
+      // acquire side: the flag was read with ld.acquire.sys; this fence plus
+      // the barrier below order every thread's frame reads after it
+      if (ok) asm volatile("fence.acq_rel.sys;" ::: "memory");
       s_ok = ok;
     }
     __syncthreads();
     if (!s_ok) return;
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
     const int32_t* order = a.orders + int64_t(layer) * g.H;
     const uint32_t* sbits = a.sign_bits + int64_t(layer) * g.H * (D / 32);
     bf16* cache = a.layer_ptrs != nullptr
@@ -604,7 +691,7 @@ __global__ void __launch_bounds__(kThreads) kv_decode_kernel(DecodeArgs a) {
       for (int c = threadIdx.x; c < HD; c += kThreads) {
         int s, js, hs;
         slot_section(g, c / D, s, js, hs);
-        if (g.bits[0][s] == kRawBits) continue;
+        if (gbits(g, 0, s) == kRawBits) continue;
         const unsigned short mn = __ldcg(reinterpret_cast<const unsigned short*>(kmin + c));
         const unsigned short sc = __ldcg(reinterpret_cast<const unsigned short*>(kmin + HD + c));
         sk[c] = __bfloat162float(__ushort_as_bfloat16(mn));
@@ -612,11 +699,33 @@ __global__ void __launch_bounds__(kThreads) kv_decode_kernel(DecodeArgs a) {
       }
       __syncthreads();
     }
+    // Section properties of this CTA's part as scalars (constant indices
+    // only, so the geometry copy stays in registers).
+    const int pbits0 = part ? gbits(g, 1, 0) : gbits(g, 0, 0);
+    const int pbits1 = part ? gbits(g, 1, 1) : gbits(g, 0, 1);
+    const int64_t ppay0 = part ? gpayload(g, 1, 0) : gpayload(g, 0, 0);
+    const int64_t ppay1 = part ? gpayload(g, 1, 1) : gpayload(g, 0, 1);
+    const int64_t vaux0 = gvaux(g, 0), vaux1 = gvaux(g, 1);
+    // As in the encoder: a lane always sees the same head slot when the row
+    // step is a multiple of H, so its K parameters can live in registers.
+    const bool kslot_fixed = part == 0 && (kRowsPerIter % g.H) == 0;
+    const RowMap rmap = make_rowmap(g.H, warp * RPW + rw, kRowsPerIter);
+    const int bshift = (a.block_size & (a.block_size - 1)) == 0 ? __ffs(a.block_size) - 1 : -1;
+    float kmn[8], ksc[8];
+    if (kslot_fixed) {
+      const int j0 = (warp * RPW + rw) % g.H;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        kmn[e] = sk[j0 * D + lir * 8 + e];
+        ksc[e] = sk[HD + j0 * D + lir * 8 + e];
+      }
+    }
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
       const int t0 = tile * a.tile_tokens;
       const int t1 = min(g.T, t0 + a.tile_tokens);
       const int nrows = (t1 - t0) * g.H;
-      for (int base = 0; base < nrows; base += kRowsPerIter * kRowUnroll) {
+      for (int base = 0, tb = t0; base < nrows;
+           base += kRowsPerIter * kRowUnroll, tb += rmap.tstep * kRowUnroll) {
         // packed symbols (and V parameters) of kRowUnroll rows are loaded first
         uint64_t acc[kRowUnroll];
         uint4 rawv[kRowUnroll];
@@ -626,25 +735,23 @@ __global__ void __launch_bounds__(kThreads) kv_decode_kernel(DecodeArgs a) {
         bool valid[kRowUnroll];
 #pragma unroll
         for (int i = 0; i < kRowUnroll; ++i) {
-          const int r = base + i * kRowsPerIter + warp * RPW + rw;
-          valid[i] = r < nrows;
-          tr[i] = t0 + r / g.H;
-          jr[i] = r % g.H;
+          row_at(rmap, g.H, t0, t1, tb, i, base + i * kRowsPerIter + warp * RPW + rw, nrows, tr[i], jr[i],
+                 valid[i]);
           int s = 0, js = 0, hs = 1;
           if (valid[i]) slot_section(g, jr[i], s, js, hs);
           sr[i] = s;
-          bitsr[i] = g.bits[part][s];
+          bitsr[i] = s ? pbits1 : pbits0;
           symr[i] = (int64_t(tr[i]) * hs + js) * D + lir * 8;
           acc[i] = 0;
           rawv[i] = make_uint4(0, 0, 0, 0);
           vmn[i] = vsc[i] = 0.f;
           if (!valid[i]) continue;
           if (bitsr[i] == kRawBits) {
-            rawv[i] = __ldcg(reinterpret_cast<const uint4*>(frame + g.payload[part][s] + symr[i] * 2));
+            rawv[i] = __ldcg(reinterpret_cast<const uint4*>(frame + (s ? ppay1 : ppay0) + symr[i] * 2));
           } else {
-            acc[i] = load_packed(frame + g.payload[part][s] + 16 + symr[i] * bitsr[i] / 8, bitsr[i]);
+            acc[i] = load_packed(frame + (s ? ppay1 : ppay0) + 16 + symr[i] * bitsr[i] / 8, bitsr[i]);
             if (part == 1) {
-              const bf16* aux = reinterpret_cast<const bf16*>(frame + g.v_aux[s]);
+              const bf16* aux = reinterpret_cast<const bf16*>(frame + (s ? vaux1 : vaux0));
               vmn[i] = __bfloat162float(__ushort_as_bfloat16(
                   __ldcg(reinterpret_cast<const unsigned short*>(aux + tr[i]))));
               vsc[i] = __bfloat162float(__ushort_as_bfloat16(
@@ -667,7 +774,9 @@ __global__ void __launch_bounds__(kThreads) kv_decode_kernel(DecodeArgs a) {
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
                 const int c = j * D + lir * 8 + e;
-                v[e] = sk[c] + float((acc[i] >> (e * bits)) & mask) * sk[HD + c];
+                const float mn = kslot_fixed ? kmn[e] : sk[c];
+                const float sc = kslot_fixed ? ksc[e] : sk[HD + c];
+                v[e] = mn + float((acc[i] >> (e * bits)) & mask) * sc;
               }
             } else {
 #pragma unroll
@@ -678,8 +787,10 @@ __global__ void __launch_bounds__(kThreads) kv_decode_kernel(DecodeArgs a) {
           if (!valid[i]) continue;
           const int h = order[j];
           const int pos = a.tok_offset + t;
-          const int blk = a.block_table[pos / a.block_size];
-          bf16* dst = cache + int64_t(blk) * a.block_stride + int64_t(pos % a.block_size) * a.token_stride +
+          int bi, bo;
+          split_pos(pos, a.block_size, bshift, bi, bo);
+          const int blk = a.block_table[bi];
+          bf16* dst = cache + int64_t(blk) * a.block_stride + int64_t(bo) * a.token_stride +
                       int64_t(h) * a.head_stride + lir * 8;
           if (raw) {
             *reinterpret_cast<uint4*>(dst) = rawv[i];
@@ -825,10 +936,21 @@ void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom
     if (section_heads(g, s) > 0 && g.bits[0][s] != kRawBits) any_k_quant = true;
   if (any_k_quant && g.T > 0 && (a.part_mask & 1)) launch_kstats(g.D, dim3(ctas), smem, st, a);
   dim3 grid(ctas, a.part_mask == 3 ? 2 : 1);
+  const int rows_per_step = 32 / (g.D / 8);
+  const bool few = (g.H + rows_per_step - 1) / rows_per_step <= 4;
   switch (g.D) {
-    case 64: kv_quant_kernel<64><<<grid, kThreads, smem, st>>>(a); break;
-    case 128: kv_quant_kernel<128><<<grid, kThreads, smem, st>>>(a); break;
-    case 256: kv_quant_kernel<256><<<grid, kThreads, smem, st>>>(a); break;
+    case 64:
+      if (few) kv_quant_kernel<64, 4><<<grid, kThreads, smem, st>>>(a);
+      else kv_quant_kernel<64, 8><<<grid, kThreads, smem, st>>>(a);
+      break;
+    case 128:
+      if (few) kv_quant_kernel<128, 4><<<grid, kThreads, smem, st>>>(a);
+      else kv_quant_kernel<128, 8><<<grid, kThreads, smem, st>>>(a);
+      break;
+    case 256:
+      if (few) kv_quant_kernel<256, 4><<<grid, kThreads, smem, st>>>(a);
+      else kv_quant_kernel<256, 8><<<grid, kThreads, smem, st>>>(a);
+      break;
   }
   KVS_CUDA_CHECK(cudaGetLastError());
 }

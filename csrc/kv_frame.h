@@ -89,26 +89,27 @@ KVS_HD inline bool section_is_raw(const FrameGeom& g, int p, int s) {
 }
 
 // Fills every offset of `g` from T/H/D/n_low/bits/levels.
+// (Written without loops so device code keeps a FrameGeom in registers.)
 KVS_HD inline void frame_geom_finalize(FrameGeom& g) {
   int64_t off = align_up(int64_t(sizeof(FrameHeader)), kFrameAlign);
-  bool k_quant = false;
-  for (int s = 0; s < 2; ++s)
-    if (section_heads(g, s) > 0 && !section_is_raw(g, 0, s)) k_quant = true;
+  const bool k_quant = (section_heads(g, 0) > 0 && !section_is_raw(g, 0, 0)) ||
+                       (section_heads(g, 1) > 0 && !section_is_raw(g, 0, 1));
   g.k_aux = off;
   if (k_quant) off = align_up(off + 2LL * 2 * g.H * g.D, kFrameAlign);
-  for (int s = 0; s < 2; ++s) {
-    g.v_aux[s] = off;
-    if (section_heads(g, s) > 0 && !section_is_raw(g, 1, s))
-      off = align_up(off + 2LL * 2 * g.T, kFrameAlign);
-  }
-  for (int p = 0; p < 2; ++p) {
-    for (int s = 0; s < 2; ++s) {
-      g.payload[p][s] = off;
-      if (section_heads(g, s) == 0) continue;
-      const int64_t hdr = section_is_raw(g, p, s) ? 0 : 16;
-      off = align_up(off + hdr + section_packed_bytes(g, p, s), kFrameAlign);
-    }
-  }
+  g.v_aux[0] = off;
+  if (section_heads(g, 0) > 0 && !section_is_raw(g, 1, 0)) off = align_up(off + 2LL * 2 * g.T, kFrameAlign);
+  g.v_aux[1] = off;
+  if (section_heads(g, 1) > 0 && !section_is_raw(g, 1, 1)) off = align_up(off + 2LL * 2 * g.T, kFrameAlign);
+  auto place = [&](int p, int s) -> int64_t {
+    const int64_t at = off;
+    if (section_heads(g, s) > 0)
+      off = align_up(off + (section_is_raw(g, p, s) ? 0 : 16) + section_packed_bytes(g, p, s), kFrameAlign);
+    return at;
+  };
+  g.payload[0][0] = place(0, 0);
+  g.payload[0][1] = place(0, 1);
+  g.payload[1][0] = place(1, 0);
+  g.payload[1][1] = place(1, 1);
   g.frame_bytes = off;
 }
 

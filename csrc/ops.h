@@ -59,6 +59,9 @@ void argmax_rows(torch::Tensor logits, torch::Tensor out, c10::optional<torch::T
 void decode_advance(torch::Tensor tok, torch::Tensor ids, torch::Tensor pos, torch::Tensor ctx, torch::Tensor slot,
                     torch::Tensor table, int64_t block_size, torch::Tensor out_tokens, torch::Tensor step);
 void gemm_silu_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor err);
+void gemm_qkv_rope_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, c10::optional<torch::Tensor> bias,
+                        torch::Tensor cos_sin, torch::Tensor positions, int64_t hq, int64_t hkv,
+                        c10::optional<torch::Tensor> k_dst, c10::optional<torch::Tensor> v_dst, torch::Tensor err);
 void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, c10::optional<torch::Tensor> residual,
                c10::optional<torch::Tensor> bias, torch::Tensor err);
 void gemv_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, c10::optional<torch::Tensor> bias);

@@ -178,7 +178,9 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool b_mn_major 
 }  // namespace sm100
 
 // Host: TMA descriptor creation through the driver entry point (no libcuda link).
+// swizzle128: 128-byte swizzle (UMMA operand tiles, box_inner <= 64);
+// otherwise no swizzle (plain row-major tiles, box_inner <= 256).
 CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
-                              uint32_t box_inner, uint32_t box_outer);
+                              uint32_t box_inner, uint32_t box_outer, bool swizzle128 = true);
 
 }  // namespace kvs

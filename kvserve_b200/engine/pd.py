@@ -59,7 +59,7 @@ class GenerateResult:
 class PDEngine:
     def __init__(self, cfg: ModelConfig, ctx: ParallelContext, profile: TransferProfile, max_prompt: int = 8192,
                  max_new_tokens: int = 128, block_size: int = 16, seed: int = 0, link_gbps: float = 0.0,
-                 use_graphs: bool = True, ingest_timeout_s: float = 30.0, encode_ctas: int = 296):
+                 use_graphs: bool = True, ingest_timeout_s: float = 30.0, encode_ctas: int = 222):
         self.cfg, self.ctx, self.profile = cfg, ctx, profile
         self.device = torch.device("cuda", torch.cuda.current_device())
         self.max_prompt, self.max_new, self.block_size = max_prompt, max_new_tokens, block_size

@@ -127,7 +127,7 @@ class KVTransfer:
 
     # ------------------------------------------------------------ prefill
     def encode(self, layer: int, k: torch.Tensor, v: torch.Tensor, frame_ptr: int, flag_ptr: int, seq: int,
-               pacing: Optional[torch.Tensor] = None, rate_bytes_per_ns: float = 0.0, max_ctas: int = 296) -> None:
+               pacing: Optional[torch.Tensor] = None, rate_bytes_per_ns: float = 0.0, max_ctas: int = 222) -> None:
         if self._state is None:
             self._state = kc.EncoderState(self.device)
         kc.encode_layer(k, v, self.spec(layer, k.shape[0]), self.orders[layer], self.sign_bits[layer], frame_ptr,
@@ -143,7 +143,7 @@ class KVTransfer:
 
     def ingest_all(self, T: int, slot_base: int, frame_stride: int, flags_ptr: int, kv_cache: torch.Tensor,
                    block_table: torch.Tensor, status: torch.Tensor, seq: int, timeout_ns: int,
-                   tok_offset: int = 0, max_ctas: int = 64) -> None:
+                   tok_offset: int = 0, max_ctas: int = 148) -> None:
         kc.decode_layers(slot_base, frame_stride, self.max_spec(T), self.orders, self.sign_bits, kv_cache,
                          block_table, status, tok_offset=tok_offset, flags_ptr=flags_ptr, seq=seq, layer_begin=0,
                          num_layers=self.L, timeout_ns=timeout_ns, max_ctas=max_ctas, n_lows=self.n_lows)

@@ -145,9 +145,15 @@ class LlamaShard:
         T = ids.numel()
         residual = ops.embedding(ids, self.embed)
         h = ops.rmsnorm(residual, self.layers[0].in_norm, cfg.rms_eps)
+        fused_qkv = self.D == 128 and T > ops.GEMV_MAX_M
         for l, lw in enumerate(self.layers):
-            qkv = self._qkv(h, lw)
-            ops.rope_qkv(qkv, self.hq, self.hkv, self.D, positions, self.cos_sin, k_buf[l, :T], v_buf[l, :T])
+            if fused_qkv:  # projection + bias + rotary + K/V copy in one GEMM
+                qkv = ops.gemm_qkv_rope(h, lw.qkv, self.hq, self.hkv, positions, self.cos_sin, bias=lw.qkv_bias,
+                                        k_dst=k_buf[l, :T], v_dst=v_buf[l, :T])
+            else:
+                qkv = self._qkv(h, lw)
+                ops.rope_qkv(qkv, self.hq, self.hkv, self.D, positions, self.cos_sin, k_buf[l, :T],
+                             v_buf[l, :T])
             if layer_hook is not None:
                 layer_hook(l)
             attn = ops.flash_prefill(qkv, self.hq, self.hkv, self.scale)

@@ -16,7 +16,7 @@ from ._ext import ext, available, ExtensionMissing
 
 __all__ = [
     "ext", "available", "ExtensionMissing", "linear", "gemm", "gemv", "rmsnorm", "rope_qkv",
-    "silu_mul", "gemm_silu", "interleave_gate_up", "GATE_UP_BLOCK", "embedding", "argmax", "flash_prefill", "paged_decode_attention",
+    "silu_mul", "gemm_silu", "gemm_qkv_rope", "interleave_gate_up", "GATE_UP_BLOCK", "embedding", "argmax", "flash_prefill", "paged_decode_attention",
     "device_status", "check_device_status", "STATUS_NAMES",
 ]
 
@@ -156,6 +156,23 @@ def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, block: int = GATE_U
     if I % block:
         raise ValueError("intermediate size must be a multiple of the interleave block")
     return torch.stack([gate.view(I // block, block, K), up.view(I // block, block, K)], 1).reshape(2 * I, K)
+
+
+def gemm_qkv_rope(a: torch.Tensor, w_qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int,
+                  positions: torch.Tensor, cos_sin: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                  k_dst: Optional[torch.Tensor] = None, v_dst: Optional[torch.Tensor] = None,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Fused QKV projection (head_dim 128): ``a @ w_qkv^T (+ bias)`` with the
+    rotary embedding applied to the q and k heads in the GEMM epilogue and
+    the rotated k / the v rows also written to ``k_dst``/``v_dst``
+    (``[tokens, kv_heads, 128]`` views) — the same result as :func:`linear`
+    followed by :func:`rope_qkv`."""
+    if out is None:
+        out = torch.empty((a.shape[0], w_qkv.shape[0]), dtype=a.dtype, device=a.device)
+    count_launches(1)
+    ext().gemm_qkv_rope_bf16(a, w_qkv, out, bias, cos_sin, positions, int(num_q_heads), int(num_kv_heads), k_dst,
+                             v_dst, device_status(a.device))
+    return out
 
 
 def gemm_silu(a: torch.Tensor, w_gate_up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:

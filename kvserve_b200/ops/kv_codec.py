@@ -305,12 +305,23 @@ class EncoderState:
             self._hd = hd
 
 
+def default_tile_tokens(H: int, D: int) -> int:
+    """Tokens per CTA tile: one unrolled step of the kernels' row loop
+    (8 warps x 32/(D/8) rows x 4 rows per lane = 64 rows for D=128)."""
+    rows = 8 * (32 // (D // 8)) * 4
+    return max(1, rows // H)
+
+
 def encode_layer(k: torch.Tensor, v: torch.Tensor, spec: FrameSpec, order: torch.Tensor,
                  sign_bits: torch.Tensor, frame_ptr: int, state: EncoderState, flag_ptr: int = 0,
                  seq: int = 1, layer: int = 0, pacing: Optional[torch.Tensor] = None,
-                 rate_bytes_per_ns: float = 0.0, max_ctas: int = 296, tile_tokens: int = 32,
+                 rate_bytes_per_ns: float = 0.0, max_ctas: int = 222, tile_tokens: Optional[int] = None,
                  part_mask: int = 3, block_table: Optional[torch.Tensor] = None, hnd: bool = False) -> None:
     """Launch the fused encode of one layer into ``frame_ptr`` (local or peer).
+
+    The defaults (222 CTAs per part; tiles of 64 rows = 64/H tokens, one
+    unrolled step of the row loop) give three resident CTAs per SM for the K
+    and V parts together and an even tile split.
 
     ``k``/``v`` are ``[T, H, D]`` views, or — with ``block_table`` — paged
     per-layer caches ``[num_blocks, block_size, H, D]`` (``hnd``: ``[num_blocks,
@@ -321,6 +332,8 @@ def encode_layer(k: torch.Tensor, v: torch.Tensor, spec: FrameSpec, order: torch
     count_launches(2 if (part_mask & 1) and any(spec.section_heads(s) and spec.bits[0][s] != RAW_BITS
                                                 for s in range(2)) else 1)
     state.prepare(spec.H * spec.D)
+    if tile_tokens is None:
+        tile_tokens = default_tile_tokens(spec.H, spec.D)
     ext().kv_encode_layer(k, v, spec.params(), order, sign_bits, int(frame_ptr), state.stats, state.counter,
                           int(flag_ptr), int(seq), int(layer), pacing, float(rate_bytes_per_ns), int(max_ctas),
                           int(tile_tokens), int(part_mask), block_table, bool(hnd))
@@ -330,7 +343,7 @@ def decode_layers(frame_base: int, frame_stride: int, spec: FrameSpec, orders: t
                   sign_bits: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tensor,
                   status: torch.Tensor, tok_offset: int = 0, flags_ptr: int = 0, seq: int = 1,
                   layer_begin: int = 0, num_layers: int = 1, timeout_ns: int = 5_000_000_000,
-                  max_ctas: int = 148, tile_tokens: int = 32, n_lows: Optional[torch.Tensor] = None,
+                  max_ctas: int = 222, tile_tokens: Optional[int] = None, n_lows: Optional[torch.Tensor] = None,
                   part_mask: int = 3, layer_ptrs: Optional[torch.Tensor] = None, hnd: bool = False) -> None:
     """Launch the fused decode of ``num_layers`` consecutive frames into the
     paged cache ``kv_cache`` ``[L, 2, num_blocks, block_size, H, D]``.  With
@@ -341,6 +354,8 @@ def decode_layers(frame_base: int, frame_stride: int, spec: FrameSpec, orders: t
     from ._ext import ext
     from . import count_launches
     count_launches(1)
+    if tile_tokens is None:
+        tile_tokens = default_tile_tokens(spec.H, spec.D)
     ext().kv_decode_layers(int(frame_base), int(frame_stride), spec.params(), orders, sign_bits, kv_cache,
                            block_table, int(tok_offset), int(flags_ptr), int(seq), int(layer_begin),
                            int(num_layers), int(timeout_ns), status, int(max_ctas), int(tile_tokens), n_lows,

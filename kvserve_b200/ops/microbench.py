@@ -4,7 +4,8 @@
                                           [--iters N] [--quick] [--once]
 
 Every number is a CUDA-event time on the launching stream after warm-up,
-with a synchronise on both sides.  Working sets are larger than L2 (126 MB)
+with a synchronise on both sides; decode-size kernels (GEMV, paged decode)
+are timed as a CUDA-graph replay of many calls, the way a decode step runs.  Working sets are larger than L2 (126 MB)
 or rotated across buffers whose total is, so DRAM figures are honest;
 ``--once`` runs each kernel a single time after three warm-ups (the mode to
 run under a profiler, whose numbers are never reported as timings).
@@ -22,8 +23,8 @@ from typing import Callable, Sequence
 
 import torch
 
-from . import (flash_prefill, gemm, gemm_silu, gemv, interleave_gate_up, paged_decode_attention, rmsnorm,
-               rope_qkv, silu_mul)
+from . import (flash_prefill, gemm, gemm_qkv_rope, gemm_silu, gemv, interleave_gate_up, paged_decode_attention,
+               rmsnorm, rope_qkv, silu_mul)
 from . import kv_codec as kc
 from .lossless import gpu_decode, gpu_encode
 
@@ -59,6 +60,29 @@ def time_ms(fns: list[Callable[[], None]], iters: int, once: bool = False) -> fl
     return s.elapsed_time(e) / n
 
 
+def time_graph_ms(fns: list[Callable[[], None]], iters: int) -> float:
+    """Mean ms per call of ``iters`` calls captured in one CUDA graph (the
+    way the decode step runs them), so host launch overhead is excluded."""
+    for i in range(3):
+        fns[i % len(fns)]()
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(iters):
+            fns[i % len(fns)]()
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    g.replay()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
 def copies_for(bytes_per_call: int) -> int:
     return max(1, math.ceil(2 * L2_BYTES / max(1, bytes_per_call)))
 
@@ -90,6 +114,21 @@ def case_gemm(a, pk):
     res[f"gemm_silu_{M}x{2 * I}x{K}"] = {"ms": round(t, 4), "tflops": round(2 * M * 2 * I * K / t / 1e9, 1),
                                          "frac_of_measured_bf16": round(2 * M * 2 * I * K / t / 1e9
                                                                         / pk["bf16_tflops"], 3)}
+    # QKV projection with bias-free rotary epilogue and K/V copies (Llama-3.1-8B shape)
+    Hq, Hkv, K = 32, 8, 4096
+    N = (Hq + 2 * Hkv) * 128
+    W = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) / math.sqrt(K)
+    Y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    pos = torch.arange(M, device="cuda", dtype=torch.int32)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, 128, 2, device="cuda").float() / 128))
+    ang = pos.float()[:, None] * inv[None]
+    cs = torch.cat([ang.cos(), ang.sin()], -1).contiguous()
+    kd = torch.empty(M, Hkv, 128, device="cuda", dtype=torch.bfloat16)
+    vd = torch.empty_like(kd)
+    t = time_ms([lambda: gemm_qkv_rope(A, W, Hq, Hkv, pos, cs, k_dst=kd, v_dst=vd, out=Y)], a.iters, a.once)
+    res[f"gemm_qkv_rope_{M}x{N}x{K}"] = {"ms": round(t, 4), "tflops": round(2 * M * N * K / t / 1e9, 1),
+                                         "frac_of_measured_bf16": round(2 * M * N * K / t / 1e9 / pk["bf16_tflops"],
+                                                                        3)}
     return res
 
 
@@ -100,7 +139,8 @@ def case_gemv(a, pk):
         ws = [torch.randn(N, K, device="cuda", dtype=torch.bfloat16) for _ in range(copies_for(nb))]
         x = torch.randn(1, K, device="cuda", dtype=torch.bfloat16)
         y = torch.empty(1, N, device="cuda", dtype=torch.bfloat16)
-        t = time_ms([lambda w=w: gemv(x, w, y) for w in ws], a.iters * 4, a.once)
+        fns = [lambda w=w: gemv(x, w, y) for w in ws]
+        t = time_ms(fns, a.iters * 4, a.once) if a.once else time_graph_ms(fns, a.iters * 4)
         gbs = nb / t / 1e6
         res[f"gemv_{N}x{K}"] = {"ms": round(t, 4), "GBps": round(gbs, 1),
                                 "frac_of_measured_hbm": round(gbs / pk["hbm_gbs"], 3)}
@@ -143,8 +183,8 @@ def case_decode(a, pk):
         table = torch.randperm(nblk, device="cuda", dtype=torch.int32).view(B, -1)
         lens = torch.full((B,), ctx, device="cuda", dtype=torch.int32)
         out = torch.empty_like(q)
-        t = time_ms([lambda s=s: paged_decode_attention(q, s[0], s[1], table, lens, ctx, out=out) for s in sets],
-                    a.iters * 4, a.once)
+        fns = [lambda s=s: paged_decode_attention(q, s[0], s[1], table, lens, ctx, out=out) for s in sets]
+        t = time_ms(fns, a.iters * 4, a.once) if a.once else time_graph_ms(fns, a.iters * 4)
         gbs = kv_bytes / t / 1e6
         res[f"paged_decode_B{B}_ctx{ctx}"] = {"ms": round(t, 4), "GBps": round(gbs, 1),
                                               "frac_of_measured_hbm": round(gbs / pk["hbm_gbs"], 3)}

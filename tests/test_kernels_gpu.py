@@ -49,6 +49,31 @@ def test_gemm_silu_fused_epilogue(M, I, K):
     assert _rel_err(y2, ref) < 1e-2
 
 
+@pytest.mark.parametrize("T,Hq,Hkv,bias", [(300, 32, 8, False), (129, 28, 4, True), (1024, 8, 2, False)])
+def test_gemm_qkv_rope_matches_unfused(T, Hq, Hkv, bias):
+    ops = _ops()
+    torch.manual_seed(2)
+    K = 512
+    N = (Hq + 2 * Hkv) * 128
+    a = torch.randn(T, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) / math.sqrt(K)
+    b = torch.randn(N, device="cuda", dtype=torch.bfloat16) if bias else None
+    pos = torch.randperm(4096, device="cuda")[:T].to(torch.int32)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, 128, 2, dtype=torch.float64) / 128))
+    ang = torch.outer(torch.arange(4096, dtype=torch.float64), inv)
+    cs = torch.cat([ang.cos(), ang.sin()], -1).float().cuda()
+    kd = torch.empty(T, Hkv, 128, device="cuda", dtype=torch.bfloat16)
+    vd = torch.empty_like(kd)
+    got = ops.gemm_qkv_rope(a, w, Hq, Hkv, pos, cs, bias=b, k_dst=kd, v_dst=vd)
+    ops.check_device_status()
+    ref = ops.gemm(a, w, bias=b)
+    kr, vr = torch.empty_like(kd), torch.empty_like(vd)
+    ops.rope_qkv(ref, Hq, Hkv, 128, pos, cs, kr, vr)
+    assert _rel_err(got, ref) < 1e-2
+    assert _rel_err(kd, kr) < 1e-2 and torch.equal(vd, got[:, (Hq + Hkv) * 128:].reshape(T, Hkv, 128))
+    assert torch.equal(kd, got[:, Hq * 128:(Hq + Hkv) * 128].reshape(T, Hkv, 128))
+
+
 def test_gemm_residual():
     ops = _ops()
     a = torch.randn(256, 512, device="cuda", dtype=torch.bfloat16)
