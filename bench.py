@@ -8,9 +8,11 @@ V 2-bit compressed KV hand-off.  N GPUs of one node:
 * N = 1: prefill and decode colocated on one GPU (device-local hand-off);
 * N = 2k: k prefill ranks (TP k) -> k decode ranks (TP k): 1P1D, 2P2D, 4P4D.
 
-One step = one request end to end (prefill, layer-streamed compressed KV
-push over NVLink, decode of the last prompt token = first token, then the
-remaining greedy tokens).  Timing: CUDA events per rank after a device-side
+One step = one request end to end: prefill of the whole prompt, which
+samples the first token; layer-streamed compressed KV push over NVLink; the
+decode side continues from the first token with the remaining greedy tokens.
+TTFT (max over ranks) is when both the first token exists and the decode
+side holds the prompt's KV and that token, ready for the next step.  Timing: CUDA events per rank after a device-side
 NCCL barrier, max over ranks; the prompt H2D copy (pinned) and the token D2H
 copy are inside every step.  Inputs (8192 x 32 layers of KV, 16 GB of
 weights) are far larger than L2, so no explicit flush is needed.
@@ -105,7 +107,7 @@ def main() -> None:
     if args.layers:
         cfg = cfg.with_layers(args.layers)
     profile = _profile(args.profile)
-    engine = PDEngine(cfg, ctx, profile, max_prompt=args.prompt_len - 1, max_new_tokens=args.max_new,
+    engine = PDEngine(cfg, ctx, profile, max_prompt=args.prompt_len, max_new_tokens=args.max_new,
                       link_gbps=args.link_gbps, use_graphs=not args.no_graphs)
     _log("engine built")
     engine.warmup(prompt_len=min(512, args.prompt_len))

@@ -8,7 +8,6 @@ namespace kvs {
 namespace {
 
 constexpr int kThreads = 128;
-constexpr int kMaxGroup = 8;  // query heads per KV head
 
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
   uint4 r;

@@ -31,6 +31,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fill_u32", &kvs::fill_u32);
   m.def("read_u32", &kvs::read_u32);
   m.def("store_release_u32", &kvs::store_release_u32);
+  m.def("publish_token", &kvs::publish_token);
+  m.def("take_token", &kvs::take_token);
   m.def("wait_flag", &kvs::wait_flag);
   // engine
   m.def("rmsnorm", &kvs::rmsnorm);

@@ -38,7 +38,6 @@ namespace kvs {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kMaxRowIters = 8;  // H*D <= 2048 for the fused path
 constexpr int kRowUnroll = 4;    // rows per row group whose loads are issued together
 
 struct EncodeArgs {
@@ -814,6 +813,14 @@ __global__ void __launch_bounds__(kThreads, 3) kv_decode_kernel(DecodeArgs a) {
   }
 }
 
+}  // namespace
+}  // namespace kvs
+
+#include "kv_decode_mma.cuh"
+
+namespace kvs {
+namespace {
+
 FrameGeom geom_from(const std::vector<int64_t>& p) {
   KVS_CHECK_ARG(p.size() == 12 || p.size() == 13, "frame geometry needs 12 or 13 integers");
   FrameGeom g{};
@@ -1028,11 +1035,31 @@ void kv_decode_layers(int64_t frame_base, int64_t frame_stride, std::vector<int6
   a.timeout_ns = uint64_t(timeout_ns);
   a.status = reinterpret_cast<uint32_t*>(status.data_ptr<int32_t>());
   a.tile_tokens = int(tile_tokens);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  // Tensor-core path: head_dim 128, Hadamard transform, no raw section in
+  // any layer's active parts (the per-layer low count only moves heads
+  // between the two quantised sections).
+  bool mma_ok = g.D == 128 && g.transform && g.T > 0;
+  for (int p2 = 0; p2 < 2; ++p2)
+    if (a.part_mask & (1 << p2))
+      for (int s2 = 0; s2 < 2; ++s2) mma_ok = mma_ok && g.bits[p2][s2] != kRawBits;
+  if (mma_ok) {
+    static bool attr = false;
+    if (!attr) {
+      KVS_CUDA_CHECK(cudaFuncSetAttribute(kv_decode_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          kMmaSmem));
+      attr = true;
+    }
+    const int64_t units = int64_t(a.part_mask == 3 ? 2 : 1) * g.H * ((g.T + 127) / 128) * a.num_layers;
+    const int ctas = int(std::max<int64_t>(1, std::min<int64_t>(units, std::max<int64_t>(1, max_ctas) * 2)));
+    kv_decode_mma_kernel<<<ctas, kMmaDecThreads, kMmaSmem, st>>>(a);
+    KVS_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   const int ntiles = std::max<int>(1, int(ceil_div(g.T, tile_tokens)));
   const int ctas = std::max<int>(1, std::min<int>(ntiles, int(max_ctas)));
   dim3 grid(ctas, a.part_mask == 3 ? 2 : 1);
   const size_t smem = size_t(2) * g.H * g.D * 4;
-  cudaStream_t st = at::cuda::getCurrentCUDAStream();
   switch (g.D) {
     case 64: kv_decode_kernel<64><<<grid, kThreads, smem, st>>>(a); break;
     case 128: kv_decode_kernel<128><<<grid, kThreads, smem, st>>>(a); break;

@@ -43,6 +43,9 @@ torch::Tensor tensor_from_ptr(int64_t ptr, std::vector<int64_t> shape, int64_t d
 void fill_u32(int64_t ptr, int64_t value, int64_t count);
 void read_u32(int64_t ptr, torch::Tensor out);
 void store_release_u32(int64_t ptr, int64_t value);
+void publish_token(torch::Tensor tok, int64_t dst_ptr, int64_t seq);
+void take_token(int64_t src_ptr, int64_t seq, int64_t timeout_ns, torch::Tensor out,
+                c10::optional<torch::Tensor> out2, torch::Tensor status);
 void wait_flag(int64_t flag_ptr, int64_t target, int64_t timeout_ns, torch::Tensor status);
 
 // ---- engine (engine_ops.cu, gemm_sm100.cu, gemv.cu, attention_*.cu)

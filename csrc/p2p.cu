@@ -33,7 +33,44 @@ __global__ void wait_flag_kernel(const uint32_t* flag, uint32_t target, uint64_t
                                  uint32_t* status) {
   if (!wait_flag_geq(flag, target, timeout_ns)) atomicCAS(status, 0u, uint32_t(kStatusTimeout));
 }
+// First-token hand-off: the prefill rank publishes the sampled token next to
+// the layer flags of the decode rank's receive slot (value, then the request
+// sequence number with release semantics); the decode rank acquire-waits
+// (bounded) and copies the token into its decode state.
+__global__ void publish_token_kernel(const int32_t* tok, uint32_t* dst, uint32_t seq) {
+  dst[0] = uint32_t(tok[0]);
+  __threadfence_system();
+  st_release_sys_u32(dst + 1, seq);
+}
+__global__ void take_token_kernel(const uint32_t* src, uint32_t seq, uint64_t timeout_ns, int32_t* out,
+                                  int32_t* out2, uint32_t* status) {
+  if (!wait_flag_geq(src + 1, seq, timeout_ns)) {
+    atomicCAS(status, 0u, uint32_t(kStatusTimeout));
+    return;
+  }
+  const int32_t t = int32_t(ld_acquire_sys_u32(src));
+  out[0] = t;
+  if (out2) out2[0] = t;
+}
 }  // namespace
+
+void publish_token(torch::Tensor tok, int64_t dst_ptr, int64_t seq) {
+  KVS_CHECK_ARG(tok.scalar_type() == at::kInt && tok.is_cuda() && tok.numel() >= 1, "publish_token: int32 token");
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  publish_token_kernel<<<1, 1, 0, st>>>(tok.data_ptr<int32_t>(), reinterpret_cast<uint32_t*>(dst_ptr),
+                                        uint32_t(seq));
+  KVS_CUDA_CHECK(cudaGetLastError());
+}
+
+void take_token(int64_t src_ptr, int64_t seq, int64_t timeout_ns, torch::Tensor out,
+                c10::optional<torch::Tensor> out2, torch::Tensor status) {
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  take_token_kernel<<<1, 1, 0, st>>>(reinterpret_cast<const uint32_t*>(src_ptr), uint32_t(seq),
+                                     uint64_t(timeout_ns), out.data_ptr<int32_t>(),
+                                     out2.has_value() ? out2->data_ptr<int32_t>() : nullptr,
+                                     reinterpret_cast<uint32_t*>(status.data_ptr<int32_t>()));
+  KVS_CUDA_CHECK(cudaGetLastError());
+}
 
 int64_t dev_alloc(int64_t bytes) {
   void* p = nullptr;

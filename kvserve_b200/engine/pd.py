@@ -75,6 +75,8 @@ class PDEngine:
         self.compute = torch.cuda.current_stream(self.device)
         self.seq = 0
         self.status = ops.device_status(self.device)
+        self.d_first = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._tok_host = torch.empty(1, dtype=torch.int32, pin_memory=True)
         L = cfg.num_layers
         if ctx.is_prefill:
             self.k_buf = torch.empty((L, max_prompt, m.hkv, m.D), dtype=torch.bfloat16, device=self.device)
@@ -125,6 +127,16 @@ class PDEngine:
         self.attn_scratch = (torch.empty(hq * splits * D, dtype=torch.float32, device=dev),
                              torch.empty(hq * splits * 2, dtype=torch.float32, device=dev))
 
+    def _first_host(self, tok: torch.Tensor, ev: dict, timing: "RequestTiming", t_host0: float) -> None:
+        """Record the first-token event and stream the token to the host (what
+        a server returns first)."""
+        ev["first"].record(self.compute)
+        self._tok_host.copy_(tok[:1], non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(self.compute)
+        done.synchronize()
+        timing.first_token_host = 1e3 * (time.perf_counter() - t_host0)
+
     def _decode_step(self) -> None:
         tok = self.model.decode_step(self.d_ids, self.d_pos, self.d_slot, self.kv.cache, self.d_table, self.d_ctx,
                                      self.max_prompt + self.max_new, attn_scratch=self.attn_scratch)
@@ -140,7 +152,7 @@ class PDEngine:
         h[1] = position
         h[2] = position + 1
         h[3] = blocks[position // bs] * bs + position % bs
-        h[4] = 0
+        h[4] = 1  # d_out[0] holds the first token (sampled by the prefill)
         h[5:5 + len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
         self.d_init_dev.copy_(h, non_blocking=True)
         d = self.d_init_dev
@@ -201,9 +213,11 @@ class PDEngine:
         if n_new < 1 or n_new > self.max_new:
             raise ValueError(f"max_new_tokens must be in [1, {self.max_new}]")
         T = int(prompt_ids.numel())
-        if T < 2 or T - 1 > self.max_prompt:
-            raise ValueError(f"prompt length must be in [2, {self.max_prompt + 1}]")
-        Tx = T - 1
+        if T < 1 or T > self.max_prompt:
+            raise ValueError(f"prompt length must be in [1, {self.max_prompt}]")
+        # The prefill covers the whole prompt and samples the first token; the
+        # KV of all T tokens is handed to the decode side with that token.
+        Tx = T
         self.seq += 1
         seq = self.seq
         ev = {k: torch.cuda.Event(enable_timing=True) for k in ("start", "prefill", "encode", "ingest", "first", "end")}
@@ -240,32 +254,37 @@ class PDEngine:
                         self.xfer.ingest_layer(l, Tx, self.sender.frame_ptr(0, l), self.kv.cache, table,
                                                self.status, seq)
 
-            m.prefill(ids[:Tx], self.positions[:Tx], self.k_buf, self.v_buf, layer_hook=hook)
+            first = m.prefill(ids[:Tx], self.positions[:Tx], self.k_buf, self.v_buf, layer_hook=hook, sample=True)
             ev["prefill"].record(self.compute)
+            if ctx.distributed:
+                # the token lands next to the layer flags of the decode slot
+                ops.count_launches(1)
+                ops.ext().publish_token(first, self.sender.token_ptr(0), seq)
             ev["encode"].record(enc)
             if not ctx.distributed:
                 ev["ingest"].record(enc)
+                self.d_first.copy_(first)
+            else:
+                self._first_host(first, ev, timing, t_host0)
         tokens = None
         if ctx.is_decode:
             self.compute.wait_event(ev["ingest"])
             self._ensure_graph()
-            self._load_decode_state(0, T - 1, blocks)
-            self.d_ids.copy_(ids[T - 1:T])
-            first_host = torch.empty(1, dtype=torch.int32, pin_memory=True)
-            for i in range(n_new):
+            self._load_decode_state(0, T, blocks)
+            if ctx.distributed:
+                ops.count_launches(1)
+                ops.ext().take_token(self.receiver.token_ptr(0), seq, self.ingest_timeout_ns, self.d_ids,
+                                     self.d_out, self.status)
+            else:
+                self.d_ids.copy_(self.d_first)
+                self.d_out[0:1].copy_(self.d_first)
+            self._first_host(self.d_ids, ev, timing, t_host0)
+            for _ in range(n_new - 1):
                 if self._graph is not None:
                     self._graph.replay()
                     replays += 1
                 else:
                     self._decode_step()
-                if i == 0:
-                    ev["first"].record(self.compute)
-                    # stream the first token to the host (what a server returns first)
-                    first_host.copy_(self.d_out[0:1], non_blocking=True)
-                    ev_fh = torch.cuda.Event()
-                    ev_fh.record(self.compute)
-                    ev_fh.synchronize()
-                    timing.first_token_host = 1e3 * (time.perf_counter() - t_host0)
             out_host = torch.empty(n_new, dtype=torch.int32, pin_memory=True)
             out_host.copy_(self.d_out[:n_new], non_blocking=True)
             ev["end"].record(self.compute)
@@ -282,12 +301,12 @@ class PDEngine:
         timing.launches = ops.launches() - c_launch0 + replays * getattr(self, "_graph_launches", 0)
         timing.request_host = 1e3 * (time.perf_counter() - t_host0)
         e = lambda k: ev["start"].elapsed_time(ev[k])  # noqa: E731
+        timing.first_token = e("first")
         if ctx.is_prefill:
             timing.prefill_done = e("prefill")
             timing.encode_done = e("encode")
         if ctx.is_decode:
             timing.ingest_done = e("ingest")
-            timing.first_token = e("first")
             timing.all_done = e("end")
         return GenerateResult(tokens, timing)
 

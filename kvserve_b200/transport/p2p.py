@@ -41,14 +41,19 @@ class FrameReceiver:
         self.slot_bytes = num_layers * frame_stride
         with torch.cuda.device(self.device):
             self.slots_ptr = ext().dev_alloc(num_slots * self.slot_bytes)
-            self.flags_ptr = ext().dev_alloc(max(256, num_slots * num_layers * 4))
+            # per slot: one publish flag per layer, then the first token and its flag
+            self.flags_ptr = ext().dev_alloc(max(256, num_slots * (num_layers + 2) * 4))
         self._closed = False
 
     def slot_base(self, slot: int) -> int:
         return self.slots_ptr + slot * self.slot_bytes
 
     def flags_base(self, slot: int) -> int:
-        return self.flags_ptr + slot * self.num_layers * 4
+        return self.flags_ptr + slot * (self.num_layers + 2) * 4
+
+    def token_ptr(self, slot: int) -> int:
+        """[token value, token flag] of the slot's request."""
+        return self.flags_base(slot) + self.num_layers * 4
 
     def handles(self) -> ChannelHandles:
         return ChannelHandles(ext().ipc_get_handle(self.slots_ptr), ext().ipc_get_handle(self.flags_ptr),
@@ -92,7 +97,10 @@ class FrameSender:
         return self.slots_ptr + slot * self.slot_bytes + layer * self.frame_stride
 
     def flag_ptr(self, slot: int, layer: int) -> int:
-        return self.flags_ptr + (slot * self.num_layers + layer) * 4
+        return self.flags_ptr + (slot * (self.num_layers + 2) + layer) * 4
+
+    def token_ptr(self, slot: int) -> int:
+        return self.flags_ptr + (slot * (self.num_layers + 2) + self.num_layers) * 4
 
     def close(self) -> None:
         with torch.cuda.device(self.device):

@@ -51,12 +51,17 @@ def test_first_token_matches_full_prefill_raw():
     T = 180
     ids = torch.randint(0, eng.cfg.vocab, (T,), dtype=torch.int32)
     res = eng.generate(ids, 3)
-    # single-device reference: full prefill over all T tokens then greedy
-    kb = torch.empty((eng.cfg.num_layers, T, eng.model.hkv, eng.model.D), dtype=torch.bfloat16, device="cuda")
+    # the first token is the prefill's own greedy sample; the second comes from
+    # the decode step over the handed-off KV and must equal a full prefill of
+    # prompt + first token followed by greedy sampling
+    kb = torch.empty((eng.cfg.num_layers, T + 1, eng.model.hkv, eng.model.D), dtype=torch.bfloat16, device="cuda")
     vb = torch.empty_like(kb)
-    pos = torch.arange(T, dtype=torch.int32, device="cuda")
-    tok = eng.model.prefill(ids.cuda(), pos, kb, vb, sample=True)
-    assert int(tok.item()) == res.tokens[0]
+    pos = torch.arange(T + 1, dtype=torch.int32, device="cuda")
+    tok0 = eng.model.prefill(ids.cuda(), pos[:T], kb, vb, sample=True)
+    assert int(tok0.item()) == res.tokens[0]
+    ext = torch.cat([ids, torch.tensor([res.tokens[0]], dtype=torch.int32)]).cuda()
+    tok1 = eng.model.prefill(ext, pos, kb, vb, sample=True)
+    assert int(tok1.item()) == res.tokens[1]
     eng.close()
 
 
