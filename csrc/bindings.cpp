@@ -43,6 +43,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_advance", &kvs::decode_advance);
   m.def("gemm_bf16", &kvs::gemm_bf16);
   m.def("gemm_silu_bf16", &kvs::gemm_silu_bf16);
+  m.def("gemm_allreduce_bf16", &kvs::gemm_allreduce_bf16);
   m.def("gemm_qkv_rope_bf16", &kvs::gemm_qkv_rope_bf16);
   m.def("gemv_bf16", &kvs::gemv_bf16);
   m.def("flash_prefill", &kvs::flash_prefill);

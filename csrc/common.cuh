@@ -109,6 +109,7 @@ enum Status : uint32_t {
   kStatusBadHeader = 2,
   kStatusBadSymbol = 3,
   kStatusBadSize = 4,
+  kStatusPeerTimeout = 5,  // a tensor-parallel peer's tile or flag did not arrive in time
 };
 
 }  // namespace kvs

@@ -62,6 +62,11 @@ void argmax_rows(torch::Tensor logits, torch::Tensor out, c10::optional<torch::T
 void decode_advance(torch::Tensor tok, torch::Tensor ids, torch::Tensor pos, torch::Tensor ctx, torch::Tensor slot,
                     torch::Tensor table, int64_t block_size, torch::Tensor out_tokens, torch::Tensor step);
 void gemm_silu_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor err);
+// C = all-reduce over tensor-parallel ranks of A_r B_r^T, GEMM and peer-memory
+// reduction in one launch (pointers: every rank's C, staging, flags).
+void gemm_allreduce_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, std::vector<int64_t> out_ptrs,
+                         std::vector<int64_t> stage_ptrs, std::vector<int64_t> flag_ptrs, int64_t rank,
+                         int64_t max_tiles, int64_t epoch, int64_t timeout_ns, torch::Tensor err);
 void gemm_qkv_rope_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, c10::optional<torch::Tensor> bias,
                         torch::Tensor cos_sin, torch::Tensor positions, int64_t hq, int64_t hkv,
                         c10::optional<torch::Tensor> k_dst, c10::optional<torch::Tensor> v_dst, torch::Tensor err);

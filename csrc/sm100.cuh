@@ -42,12 +42,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // *err (if non-null).  Returns false on timeout.  Kernels treat a timeout as
 // fatal for the launch: they stop issuing work and fall through to cleanup.
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                          uint64_t timeout_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t n = 0;
   while (!mbar_try_wait(bar, parity)) {
-    if ((++n & 255u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs) {
+    if ((++n & 255u) == 0 && globaltimer_ns() - t0 > timeout_ns) {
       if (err) atomicCAS(err, 0u, uint32_t(kStatusTimeout));
       return false;
     }

@@ -30,6 +30,7 @@ from .. import ops
 from ..models.config import ModelConfig
 from ..models.llama import LlamaShard
 from ..parallel.context import ParallelContext
+from ..parallel.tp_allreduce import create_tp_allreduce
 from ..transport.p2p import FrameReceiver, FrameSender
 from .kv_cache import PagedKVCache
 from .transfer import KVTransfer, TransferProfile
@@ -70,6 +71,8 @@ class PDEngine:
         self.model = LlamaShard(cfg, ctx.tp_rank, ctx.tp_size, self.device, seed, ctx.tp_group,
                                 max_position=max_prompt + max_new_tokens + block_size)
         m = self.model
+        # prefill ranks reduce their row-parallel projections inside the GEMM
+        m.tp_ar = create_tp_allreduce(ctx, max_prompt, cfg.hidden, self.device, participate=ctx.is_prefill)
         self.xfer = KVTransfer(profile, cfg.num_layers, cfg.num_kv_heads, m.hkv, m.D, ctx.tp_rank, ctx.tp_size,
                                self.device, max_prompt, cfg.score_model_name)
         self.compute = torch.cuda.current_stream(self.device)
@@ -312,6 +315,10 @@ class PDEngine:
 
     def close(self) -> None:
         self._graph = None
+        if self.model.tp_ar is not None:
+            torch.cuda.synchronize(self.device)
+            self.model.tp_ar.close()
+            self.model.tp_ar = None
         if self.sender is not None:
             self.sender.close()
         if self.receiver is not None:

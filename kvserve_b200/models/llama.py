@@ -91,6 +91,8 @@ class LlamaShard:
         self.lm_head = self._rand((self.vocab_local, cfg.hidden), -1, "lm_head")
         self.final_norm = torch.ones(cfg.hidden, dtype=torch.bfloat16, device=dev)
         self.cos_sin = rope_cache(max_position, self.D, cfg.rope_theta, dev)
+        # fused GEMM + all-reduce workspace (parallel.tp_allreduce), attached by the engine
+        self.tp_ar = None
 
     # ------------------------------------------------------------------ init
     def _rand(self, shape, layer, name, tp_shared=False, std=None) -> torch.Tensor:
@@ -110,6 +112,17 @@ class LlamaShard:
         if self.tp_size > 1:
             dist.all_reduce(x, group=self.tp_group)
 
+    def _row_parallel(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """``x @ w.T`` summed over the TP group: one fused GEMM + peer-memory
+        all-reduce launch where the workspace takes the shape, else the GEMM
+        followed by an NCCL all-reduce."""
+        ar = self.tp_ar
+        if ar is not None and ar.accepts(x.shape[0], w.shape[0]):
+            return ar.gemm_allreduce(x, w)
+        y = ops.linear(x, w)
+        self._all_reduce(y)
+        return y
+
     def _qkv(self, h: torch.Tensor, lw: LayerWeights) -> torch.Tensor:
         return ops.linear(h, lw.qkv, bias=lw.qkv_bias)
 
@@ -118,9 +131,7 @@ class LlamaShard:
             a = ops.gemm_silu(h, lw.gate_up)
         else:
             a = ops.silu_mul(ops.linear(h, lw.gate_up), block=self.gu_block)
-        d = ops.linear(a, lw.down)
-        self._all_reduce(d)
-        return d
+        return self._row_parallel(a, lw.down)
 
     def greedy(self, h_last: torch.Tensor) -> torch.Tensor:
         """Greedy next token over the vocab-parallel LM head (int32 [B])."""
@@ -157,8 +168,7 @@ class LlamaShard:
             if layer_hook is not None:
                 layer_hook(l)
             attn = ops.flash_prefill(qkv, self.hq, self.hkv, self.scale)
-            o = ops.linear(attn, lw.o)
-            self._all_reduce(o)
+            o = self._row_parallel(attn, lw.o)
             h = ops.rmsnorm(o, lw.post_norm, cfg.rms_eps, residual=residual)
             d = self._mlp(h, lw)
             nxt = self.layers[l + 1].in_norm if l + 1 < len(self.layers) else self.final_norm
@@ -186,8 +196,7 @@ class LlamaShard:
             q = qkv[:, : self.hq * self.D].view(B, self.hq, self.D)
             attn = ops.paged_decode_attention(q, kv_cache[l, 0], kv_cache[l, 1], block_tables, ctx_lens, max_ctx,
                                               self.scale, scratch=attn_scratch)
-            o = ops.linear(attn.view(B, self.hq * self.D), lw.o)
-            self._all_reduce(o)
+            o = self._row_parallel(attn.view(B, self.hq * self.D), lw.o)
             h = ops.rmsnorm(o, lw.post_norm, cfg.rms_eps, residual=residual)
             d = self._mlp(h, lw)
             nxt = self.layers[l + 1].in_norm if l + 1 < len(self.layers) else self.final_norm

@@ -369,3 +369,25 @@ def test_flash_prefill_partial_tiles_llama_heads(T):
     o = ops.flash_prefill(qkv, 32, 8)
     ops.check_device_status()
     assert _rel_err(o, _ref_causal(qkv, 32, 8)) < 2e-2
+
+
+@pytest.mark.parametrize("Ms,N,K", [((300, 1024, 129), 1024, 512), ((8192,), 4096, 2048)])
+def test_gemm_allreduce_single_rank(Ms, N, K):
+    """Mode-3 epilogue with one rank: every tile is owned locally and leaves
+    through the shared-memory slab; successive launches advance the epoch."""
+    ops = _ops()
+    from kvserve_b200.parallel.tp_allreduce import TPAllReduce
+    ws = TPAllReduce(1, 0, max(Ms), N, torch.device("cuda", 0))
+    ws.connect([None])
+    try:
+        torch.manual_seed(1)
+        b = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+        for M in Ms:
+            a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+            c = ws.gemm_allreduce(a, b).clone()
+            ops.check_device_status()
+            ref = a.float() @ b.float().T
+            assert _rel_err(c, ref) < 1e-2
+            assert torch.equal(c, ops.gemm(a, b))   # same fp32 tile, one rounding
+    finally:
+        ws.close()

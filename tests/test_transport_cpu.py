@@ -134,3 +134,27 @@ def test_logger_levels(capsys):
         assert "loud" in err and "always" in err and "quiet" not in err
     finally:
         logger.set_log_level(old)
+
+
+def test_tp_allreduce_workspace_layout():
+    from kvserve_b200.parallel.tp_allreduce import workspace_layout
+    lay = workspace_layout(4, 8192, 4096)
+    assert lay["max_tiles"] == 64 * 16
+    assert lay["stage"] == 8192 * 4096 * 2
+    assert lay["flags"] - lay["stage"] == 3 * 1024 * 128 * 256 * 2
+    assert lay["flag_bytes"] == 4 * 1024 * 4
+    assert all(lay[k] % 256 == 0 for k in ("stage", "flags", "total"))
+    one = workspace_layout(1, 300, 512)
+    assert one["max_tiles"] == 3 * 2 and one["flags"] == one["stage"]   # no staging with one rank
+    import pytest
+    with pytest.raises(ValueError):
+        workspace_layout(2, 128, 1000)
+    with pytest.raises(ValueError):
+        workspace_layout(9, 128, 1024)
+
+
+def test_tp_allreduce_not_created_without_tp():
+    import torch
+    from kvserve_b200.parallel.context import ParallelContext
+    from kvserve_b200.parallel.tp_allreduce import create_tp_allreduce
+    assert create_tp_allreduce(ParallelContext(), 128, 1024, torch.device("cpu")) is None
