@@ -14,6 +14,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   // modular pipeline kernels
   m.def("bitpack_encode", &kvs::bitpack_encode);
   m.def("bitpack_decode", &kvs::bitpack_decode);
+  m.def("codebook_quantize", &kvs::codebook_quantize);
+  m.def("codebook_dequantize", &kvs::codebook_dequantize);
   m.def("fwht_rows", &kvs::fwht_rows);
   // lossless codec
   m.def("rze_max_encoded_bytes", &kvs::rze_max_encoded_bytes);

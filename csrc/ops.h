@@ -24,6 +24,11 @@ void kv_decode_layers(int64_t frame_base, int64_t frame_stride, std::vector<int6
 // ---- modular pipeline kernels (bitpack.cu)
 void bitpack_encode(torch::Tensor src, torch::Tensor out, int64_t bits, torch::Tensor status);
 void bitpack_decode(torch::Tensor src, torch::Tensor out, int64_t bits, torch::Tensor status);
+// ---- centred Gaussian codebook quantiser (codebook.cu); part 0 keys, 1 values
+void codebook_quantize(torch::Tensor x, int64_t part, int64_t group, int64_t refinements, double alpha,
+                       torch::Tensor centers, torch::Tensor q, torch::Tensor mean, torch::Tensor scale);
+void codebook_dequantize(torch::Tensor q, int64_t part, int64_t group, torch::Tensor centers, torch::Tensor mean,
+                         torch::Tensor scale, torch::Tensor out, torch::Tensor status);
 void fwht_rows(torch::Tensor x, torch::Tensor y, c10::optional<torch::Tensor> signs, bool inverse);
 
 // ---- lossless codec (lossless.cu)

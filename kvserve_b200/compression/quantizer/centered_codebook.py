@@ -8,8 +8,11 @@ Keys: per (head, channel) over token groups of ``group_size`` tokens;
 values: per (head, token) over the head dimension.  Each group gets a mean
 (``mean_dtype``) and an RMS scale times ``scale_alpha`` (bf16), optionally
 refined by ``scale_refinements`` least-squares steps; symbols are the cell
-index of ``(x - mean) / scale``.  Works on CPU and CUDA tensors (vectorised
-torch ops).
+index of ``(x - mean) / scale``.  CUDA tensors run the sm_100a kernels of
+``csrc/codebook.cu`` (one thread per key channel over a token group, one warp
+per value row; the reference runs Triton kernels,
+kvserve_v1/compression/quantizer/centered_codebook.py:67-161); CPU tensors
+run the same arithmetic as vectorised torch ops.
 """
 from __future__ import annotations
 
@@ -91,6 +94,33 @@ class CenteredCodebookQuantizer(Quantizer):
         q = torch.bucketize(res / scale.clamp_min(1e-20), bounds)
         return mean, scale, q.to(torch.uint8)
 
+    @staticmethod
+    def _cuda_ok(t: torch.Tensor) -> bool:
+        return t.is_cuda and t.dtype in (torch.bfloat16, torch.float16, torch.float32)
+
+    def _quantize_cuda(self, tensor: torch.Tensor, cfg: dict, out: torch.Tensor) -> list[dict]:
+        from ... import ops
+        _, blocks, tokens, heads, dim = tensor.shape
+        total, group = blocks * tokens, cfg["group_size"]
+        mdt = getattr(torch, cfg["mean_dtype"])
+        ng = (total + group - 1) // group
+        parts = []
+        for part, bits in ((0, cfg["key_bits"]), (1, cfg["value_bits"])):
+            x = tensor[part].reshape(total, heads, dim).contiguous()
+            shape = (heads, ng, dim) if part == 0 else (heads, total)
+            mean = torch.empty(shape, dtype=mdt, device=tensor.device)
+            scale = torch.empty(shape, dtype=torch.bfloat16, device=tensor.device)
+            q = out[part].view(total, heads, dim) if out[part].is_contiguous() else \
+                torch.empty((total, heads, dim), dtype=torch.uint8, device=tensor.device)
+            centers = torch.tensor(lloyd_max_gaussian(bits), dtype=torch.float32)
+            ops.count_launches(1)
+            ops.ext().codebook_quantize(x, part, group, cfg["scale_refinements"], float(cfg["scale_alpha"]),
+                                        centers, q, mean, scale)
+            if q.data_ptr() != out[part].data_ptr():
+                out[part].copy_(q.view(blocks, tokens, heads, dim))
+            parts.append(dict(mean=mean, scale=scale))
+        return parts
+
     def quantize(self, layer_id: int, tensor: torch.Tensor, **kwargs: Any) -> tuple[torch.Tensor, dict]:
         self._check(tensor)
         cfg = self._settings({k: v for k, v in kwargs.items() if k != "out"})
@@ -99,6 +129,10 @@ class CenteredCodebookQuantizer(Quantizer):
         out = kwargs.get("out")
         if out is None:
             out = torch.empty(tensor.shape, dtype=torch.uint8, device=tensor.device)
+        meta = dict(format="centered_codebook_v1", config=cfg,
+                    original_dtype=str(tensor.dtype).replace("torch.", ""))
+        if self._cuda_ok(tensor):
+            return out, dict(meta, parts=self._quantize_cuda(tensor, cfg, out))
         parts = []
         mdt = getattr(torch, cfg["mean_dtype"])
         # keys: [total, heads, dim] -> groups of tokens
@@ -146,6 +180,19 @@ class CenteredCodebookQuantizer(Quantizer):
         _, blocks, tokens, heads, dim = tensor.shape
         total, group = blocks * tokens, cfg["group_size"]
         out = torch.empty(tensor.shape, dtype=dtype, device=tensor.device)
+        if tensor.is_cuda and dtype in (torch.bfloat16, torch.float16, torch.float32):
+            from ... import ops
+            status = torch.zeros(4, dtype=torch.int32, device=tensor.device)
+            for part, bits in ((0, cfg["key_bits"]), (1, cfg["value_bits"])):
+                p = meta["parts"][part]
+                centers = torch.tensor(lloyd_max_gaussian(bits), dtype=torch.float32)
+                ops.count_launches(1)
+                ops.ext().codebook_dequantize(tensor[part].reshape(total, heads, dim).contiguous(), part, group,
+                                              centers, p["mean"].contiguous(), p["scale"].contiguous(),
+                                              out[part].view(total, heads, dim), status)
+            if int(status[0].item()) != 0:
+                raise ValueError("invalid centered-codebook symbol")
+            return out
         # keys
         centers, _ = self._tables(cfg["key_bits"], tensor.device)
         q = tensor[0].reshape(total, heads, dim).long()

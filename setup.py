@@ -17,6 +17,7 @@ SOURCES = [
     "bindings.cpp",
     "kv_codec.cu",
     "bitpack.cu",
+    "codebook.cu",
     "lossless.cu",
     "engine_ops.cu",
     "gemm_sm100.cu",

@@ -391,3 +391,30 @@ def test_gemm_allreduce_single_rank(Ms, N, K):
             assert torch.equal(c, ops.gemm(a, b))   # same fp32 tile, one rounding
     finally:
         ws.close()
+
+
+@pytest.mark.parametrize("mean_dtype,refine,group,kb,vb", [("float32", 1, 128, 3, 2), ("bfloat16", 2, 32, 4, 1),
+                                                           ("float32", 0, 16, 2, 4)])
+def test_centered_codebook_cuda_matches_cpu(mean_dtype, refine, group, kb, vb):
+    from kvserve_b200.compression.quantizer.centered_codebook import CenteredCodebookQuantizer
+    torch.manual_seed(0)
+    kv = torch.randn(2, 5, 16, 4, 128, dtype=torch.bfloat16)   # 80 tokens: a partial last key group
+    kv[0, ..., :4] *= 8
+    qz = CenteredCodebookQuantizer(key_bits=kb, value_bits=vb, group_size=group, scale_refinements=refine,
+                                   mean_dtype=mean_dtype)
+    q_cpu, m_cpu = qz.quantize(0, kv)
+    q_gpu, m_gpu = qz.quantize(0, kv.cuda())
+    assert (q_gpu.cpu() == q_cpu).float().mean().item() > 0.999
+    for pc, pg in zip(m_cpu["parts"], m_gpu["parts"]):
+        assert pg["mean"].dtype == pc["mean"].dtype and pg["scale"].shape == pc["scale"].shape
+        torch.testing.assert_close(pg["scale"].cpu().float(), pc["scale"].float(), rtol=1e-2, atol=1e-3)
+        torch.testing.assert_close(pg["mean"].cpu().float(), pc["mean"].float(), rtol=1e-2, atol=1e-3)
+    # identical symbols and parameters dequantise to identical values
+    m_on_gpu = dict(m_cpu, parts=[{k: v.cuda() for k, v in p.items()} for p in m_cpu["parts"]])
+    assert torch.equal(qz.dequantize(0, q_cpu.cuda(), m_on_gpu).cpu(), qz.dequantize(0, q_cpu, m_cpu))
+    err = lambda r: ((r.float().cpu() - kv.float()).norm() / kv.float().norm()).item()  # noqa: E731
+    assert abs(err(qz.dequantize(0, q_gpu, m_gpu)) - err(qz.dequantize(0, q_cpu, m_cpu))) < 1e-3
+    bad = q_gpu.clone()
+    bad[1, 0, 0, 0, 0] = 1 << vb
+    with pytest.raises(ValueError):
+        qz.dequantize(0, bad, m_gpu)
