@@ -60,7 +60,8 @@ class GenerateResult:
 class PDEngine:
     def __init__(self, cfg: ModelConfig, ctx: ParallelContext, profile: TransferProfile, max_prompt: int = 8192,
                  max_new_tokens: int = 128, block_size: int = 16, seed: int = 0, link_gbps: float = 0.0,
-                 use_graphs: bool = True, ingest_timeout_s: float = 30.0, encode_ctas: int = 222):
+                 use_graphs: bool = True, ingest_timeout_s: float = 30.0, encode_ctas: int = 222,
+                 profiles: Optional[dict] = None):
         self.cfg, self.ctx, self.profile = cfg, ctx, profile
         self.device = torch.device("cuda", torch.cuda.current_device())
         self.max_prompt, self.max_new, self.block_size = max_prompt, max_new_tokens, block_size
@@ -73,8 +74,13 @@ class PDEngine:
         m = self.model
         # prefill ranks reduce their row-parallel projections inside the GEMM
         m.tp_ar = create_tp_allreduce(ctx, max_prompt, cfg.hidden, self.device, participate=ctx.is_prefill)
-        self.xfer = KVTransfer(profile, cfg.num_layers, cfg.num_kv_heads, m.hkv, m.D, ctx.tp_rank, ctx.tp_size,
-                               self.device, max_prompt, cfg.score_model_name)
+        # one transfer geometry per selectable profile ("default" = `profile`);
+        # the receive slot is sized for the largest frame of any of them
+        self.xfers = {name: KVTransfer(p, cfg.num_layers, cfg.num_kv_heads, m.hkv, m.D, ctx.tp_rank, ctx.tp_size,
+                                       self.device, max_prompt, cfg.score_model_name)
+                      for name, p in {"default": profile, **(profiles or {})}.items()}
+        self.xfer = self.xfers["default"]
+        frame_stride = max(x.frame_stride for x in self.xfers.values())
         self.compute = torch.cuda.current_stream(self.device)
         self.seq = 0
         self.status = ops.device_status(self.device)
@@ -99,7 +105,7 @@ class PDEngine:
         self.receiver: Optional[FrameReceiver] = None
         self.sender: Optional[FrameSender] = None
         if ctx.is_decode:
-            self.receiver = FrameReceiver(L, self.xfer.frame_stride, 1, self.device)
+            self.receiver = FrameReceiver(L, frame_stride, 1, self.device)
         if not ctx.distributed:
             self.sender = FrameSender(local=self.receiver, device=self.device)
         else:
@@ -202,9 +208,13 @@ class PDEngine:
             dist.all_reduce(self._barrier_t, group=self.ctx.world_group)
 
     def generate(self, prompt_ids: torch.Tensor, max_new_tokens: Optional[int] = None,
-                 return_tokens: bool = True, sync: bool = True) -> GenerateResult:
+                 return_tokens: bool = True, sync: bool = True, profile: Optional[str] = None,
+                 link_gbps: Optional[float] = None) -> GenerateResult:
         """Serve one request.  ``prompt_ids`` is a host int32 tensor (pinned
         preferably); the prompt is copied to the device inside the request.
+        ``profile`` names one of the engine's transfer profiles (every rank
+        must pass the same name); ``link_gbps`` paces this request's KV
+        stores at that rate (an emulated link cap; None keeps the engine's).
 
         ``sync`` aligns all ranks on a host collective before the request so
         per-request device timings share a start; with ``sync=False`` a decode
@@ -212,6 +222,10 @@ class PDEngine:
         never publishes then surfaces as a device-side timeout status)."""
         t_host0 = time.perf_counter()
         ctx, m = self.ctx, self.model
+        if profile is not None and profile not in self.xfers:
+            raise KeyError(f"unknown transfer profile {profile!r}; have {sorted(self.xfers)}")
+        xfer = self.xfers[profile or "default"]
+        rate = self.rate_bytes_per_ns if link_gbps is None else (link_gbps / 8.0 if link_gbps else 0.0)
         n_new = self.max_new if max_new_tokens is None else max_new_tokens
         if n_new < 1 or n_new > self.max_new:
             raise ValueError(f"max_new_tokens must be in [1, {self.max_new}]")
@@ -230,7 +244,7 @@ class PDEngine:
         replays = 0
         ev["start"].record(self.compute)
         ids = prompt_ids.to(self.device, non_blocking=True)
-        timing = RequestTiming(payload_bytes=self.xfer.payload_bytes(Tx), raw_bytes=self.xfer.raw_bytes(Tx))
+        timing = RequestTiming(payload_bytes=xfer.payload_bytes(Tx), raw_bytes=xfer.raw_bytes(Tx))
         blocks = None
         if ctx.is_decode:
             blocks = self.kv.allocate(T + n_new)
@@ -238,7 +252,7 @@ class PDEngine:
             if ctx.distributed:
                 self.ingest_stream.wait_stream(self.compute)
                 with torch.cuda.stream(self.ingest_stream):
-                    self.xfer.ingest_all(Tx, self.receiver.slot_base(0), self.receiver.frame_stride,
+                    xfer.ingest_all(Tx, self.receiver.slot_base(0), self.receiver.frame_stride,
                                          self.receiver.flags_base(0), self.kv.cache, table, self.status, seq,
                                          self.ingest_timeout_ns)
                     ev["ingest"].record(self.ingest_stream)
@@ -251,10 +265,10 @@ class PDEngine:
                 enc.wait_event(self.layer_events[l])
                 with torch.cuda.stream(enc):
                     flag = self.sender.flag_ptr(0, l) if ctx.distributed else 0
-                    self.xfer.encode(l, self.k_buf[l, :Tx], self.v_buf[l, :Tx], self.sender.frame_ptr(0, l), flag,
-                                     seq, self.pacing, self.rate_bytes_per_ns, self.encode_ctas)
+                    xfer.encode(l, self.k_buf[l, :Tx], self.v_buf[l, :Tx], self.sender.frame_ptr(0, l), flag,
+                                seq, self.pacing, rate, self.encode_ctas)
                     if not ctx.distributed:
-                        self.xfer.ingest_layer(l, Tx, self.sender.frame_ptr(0, l), self.kv.cache, table,
+                        xfer.ingest_layer(l, Tx, self.sender.frame_ptr(0, l), self.kv.cache, table,
                                                self.status, seq)
 
             first = m.prefill(ids[:Tx], self.positions[:Tx], self.k_buf, self.v_buf, layer_hook=hook, sample=True)

@@ -157,3 +157,35 @@ def test_worker_memory_plan_matches_runtime_plan():
     assert plan.connector_data.slot_bytes == ref.slot_bytes
     u = adjusted_utilization(100 * 2 ** 30, 0.9, plan)
     assert abs(u * 100 * 2 ** 30 - (0.9 * 100 * 2 ** 30 - plan.reserved_bytes)) < 1.0
+
+
+def test_service_aware_engine_library_and_selection():
+    """Engine profiles -> library: more bits are more accurate and less
+    compressed; the controller's choice respects the accuracy requirement."""
+    from kvserve_b200.compression.controller.online import OnlineController
+    from kvserve_b200.engine.serving import ENGINE_PROFILES, engine_library
+    from kvserve_b200.engine.transfer import KVTransfer
+
+    class _Eng:
+        pass
+    eng = _Eng()
+    eng.cfg = type("C", (), {"name": "tiny"})()
+    eng.xfers = {n: KVTransfer(p, 2, 4, 4, 128, 0, 1, "cpu", 256) for n, p in ENGINE_PROFILES.items()}
+    speeds = {"k8v8": 9e5, "k4v4": 6e5, "k4v2": 5e5, "k2v2": 4e5}
+    lib = engine_library(eng, 256, speeds)
+    prof = {p.profile_id: p for b in lib.accuracy_buckets for p in
+            (lib.get_profile(d["profile_id"]) for d in b["pareto_profiles"])}
+    import math
+    from kvserve_b200.engine.serving import profile_accuracy
+    acc = {n: profile_accuracy(ENGINE_PROFILES[n], 4, 128) for n in speeds}
+    assert acc["k8v8"] > acc["k4v4"] > acc["k4v2"] > acc["k2v2"] > 0.1
+    cr = {n: eng.xfers[n].raw_bytes(256) / eng.xfers[n].payload_bytes(256) for n in speeds}
+    assert cr["k2v2"] > cr["k4v2"] > cr["k4v4"] > cr["k8v8"] > 1.5
+    assert prof and all(math.isfinite(p.compression_ratio) for p in prof.values())
+    from kvserve_b200.engine.serving import bucket_requirement
+    ctl = OnlineController(lib, epsilon=0.0)
+    for need in (0.2, 0.5, acc["k4v4"] - 1e-4, acc["k8v8"] - 1e-4):
+        p, info = ctl.select_profile(2e9, 3125.0, 100.0, 1e9, bucket_requirement(lib, need))
+        assert p is not None and p.accuracy >= need, (need, p, info)
+    assert ctl.select_profile(2e9, 3125.0, 100.0, 1e9, bucket_requirement(lib, 0.2))[0].profile_id == "k2v2"
+    assert bucket_requirement(lib, 0.9999) is None    # nothing compressed is that accurate

@@ -78,3 +78,30 @@ def test_compressed_handoff_generates_and_graph_matches_eager():
     assert ra.tokens == rb.tokens
     assert ra.timing.payload_bytes < ra.timing.raw_bytes / 3.5
     assert ra.timing.first_token > 0 and ra.timing.launches > 0
+
+
+def test_service_aware_server_colocated():
+    """Per-request profile choice through the controller, the link cap as
+    encode pacing, every profile served by the same engine."""
+    from kvserve_b200.engine.pd import PDEngine
+    from kvserve_b200.engine.serving import ENGINE_PROFILES, ServiceAwareServer, engine_library
+    from kvserve_b200.models.config import get_config
+    from kvserve_b200.parallel.context import ParallelContext
+    eng = PDEngine(get_config("tiny-gqa"), ParallelContext(), ENGINE_PROFILES["off"], max_prompt=255,
+                   max_new_tokens=4, profiles=dict(ENGINE_PROFILES))
+    try:
+        lib = engine_library(eng, 200)
+        g = torch.Generator().manual_seed(3)
+        prompts = [torch.randint(0, 4096, (200,), generator=g, dtype=torch.int32) for _ in range(4)]
+        srv = ServiceAwareServer(eng, lib, slo_ms=1e6, acc_req=0.8)
+        served = srv.serve(prompts, 1.0, 25.0, 4)
+        assert len(served) == 4 and all(r.profile in ENGINE_PROFILES for r in served)
+        assert all(r.kv_ready_ms > 0 and r.ttft_ms >= r.queue_ms >= 0 for r in served)
+        firsts = {n: eng.generate(prompts[0], 2, profile=n).tokens[0] for n in ENGINE_PROFILES}
+        assert len(set(firsts.values())) == 1    # the first token comes from the prefill
+        paced = eng.generate(prompts[0], 1, profile="off", link_gbps=1.0).timing
+        free = eng.generate(prompts[0], 1, profile="off", link_gbps=0.0).timing
+        # 4 layers x 2 x 200 x 4 x 128 x 2 B = 1.6 MB at 1 Gb/s is ~13 ms of emulated link time
+        assert paced.ingest_done > free.ingest_done + 5.0
+    finally:
+        eng.close()

@@ -171,3 +171,42 @@ def test_bootstrap_registry_and_stats():
     st.record_failure()
     r = st.reduce()
     assert r["num_transfers"] == 2 and r["failed"] == 1 and abs(r["total_mb"] - 4) < 1e-9
+
+
+def test_heterogeneous_tp_plan_covers_every_head_once():
+    from kvserve_b200.session.tp_plan import (head_shard, source_ranks, target_ranks, tp_ratio, transfer_plan,
+                                              validate_region_lengths)
+    assert tp_ratio(4, 2) == 2 and tp_ratio(2, 4) == -2 and tp_ratio(2, 2) == 1
+    import pytest
+    with pytest.raises(ValueError):
+        tp_ratio(3, 2)
+    for H in (8, 4, 2):
+        for p in (1, 2, 4, 8):
+            for c in (1, 2, 4, 8):
+                if (p > H and p % H) or (c > H and c % H):
+                    continue
+                plan = transfer_plan(p, c, H)
+                for d in range(c):
+                    ds = head_shard(d, c, H)
+                    got = sorted(cp.dst_head + i for cp in plan if cp.dst_rank == d for i in range(cp.heads))
+                    assert got == list(range(ds.count)), (H, p, c, d, plan)
+                for cp in plan:   # a copy's global heads agree on both sides
+                    ps, ds = head_shard(cp.src_rank, p, H), head_shard(cp.dst_rank, c, H)
+                    assert ps.first + cp.src_head == ds.first + cp.dst_head
+                    assert cp.src_head + cp.heads <= ps.count and cp.dst_head + cp.heads <= ds.count
+    # homogeneous: one whole-shard copy per pair
+    assert transfer_plan(4, 4, 8) == [type(transfer_plan(1, 1, 8)[0])(r, r, 0, 0, 2) for r in range(4)]
+    # P TP2 -> D TP1: two copies into disjoint halves; P TP1 -> D TP2: two disjoint slices
+    assert [(c.src_rank, c.dst_head, c.heads) for c in transfer_plan(2, 1, 8)] == [(0, 0, 4), (1, 4, 4)]
+    assert [(c.dst_rank, c.src_head, c.heads) for c in transfer_plan(1, 2, 8)] == [(0, 0, 4), (1, 4, 4)]
+    assert target_ranks(0, 1, 4, 8) == [0, 1, 2, 3] and source_ranks(0, 4, 1, 8) == [0, 1, 2, 3]
+    assert target_ranks(3, 4, 2, 8) == [1]
+    # replicated KV heads (4 heads over TP 8): replicas alternate as senders
+    plan = transfer_plan(8, 4, 4)
+    assert [c.src_rank for c in plan] == [0, 3, 4, 7]     # consumer d reads replica d % 2 of its head
+    plan = transfer_plan(8, 8, 4)
+    assert [c.src_rank for c in plan] == list(range(8))
+    assert transfer_plan(2, 1, 8)[1].byte_range(4096) == (0, 4 * 4096, 4 * 4096)
+    assert validate_region_lengths([4 * 4096] * 3, [8 * 4096] * 3, 2, 1, 8) is None
+    assert validate_region_lengths([4 * 4096], [4 * 4096], 2, 1, 8) is not None
+    assert validate_region_lengths([1], [1, 2], 1, 1, 8) is not None
