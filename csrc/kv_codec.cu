@@ -61,6 +61,7 @@ struct EncodeArgs {
   const int32_t* block_table; // paged source: token t lives in block block_table[t / block_size]
   int block_size;
   int64_t k_block_stride, v_block_stride;
+  int vstats_len;             // tensor-core path: per-token V statistics after the K ones ([2][2][T])
 };
 
 // Address of row (token t, head h) of a K or V source that is either a
@@ -373,6 +374,9 @@ __device__ void encode_signal_done(const EncodeArgs& a) {
   if (!s_last) return;
   const int HD = a.g.H * a.g.D;
   for (int i = threadIdx.x; i < 2 * HD; i += blockDim.x) a.stats[i] = i < HD ? 0xffffffffu : 0u;
+  // per-token V statistics: [section][min T | max T]
+  for (int i = threadIdx.x; i < a.vstats_len; i += blockDim.x)
+    a.stats[2 * HD + i] = (i % (2 * a.g.T)) < a.g.T ? 0xffffffffu : 0u;
   if (threadIdx.x == 0) {
     FrameHeader h;
     h.magic = kFrameMagic;
@@ -406,7 +410,9 @@ __device__ void encode_signal_done(const EncodeArgs& a) {
     }
     *a.counter = 0;
     __threadfence_system();
-    if (a.flag != nullptr) st_release_sys_u32(a.flag, a.seq);
+    // a CTA that gave up on its tensor-core work (counter[1] set) leaves the
+    // frame unpublished: the decoder's bounded wait reports it
+    if (a.flag != nullptr && a.counter[1] == 0) st_release_sys_u32(a.flag, a.seq);
   }
 }
 
@@ -817,6 +823,7 @@ __global__ void __launch_bounds__(kThreads, 3) kv_decode_kernel(DecodeArgs a) {
 }  // namespace kvs
 
 #include "kv_decode_mma.cuh"
+#include "kv_encode_mma.cuh"
 
 namespace kvs {
 namespace {
@@ -872,7 +879,7 @@ void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom
                      torch::Tensor stats, torch::Tensor counter, int64_t flag_ptr, int64_t seq,
                      int64_t layer, c10::optional<torch::Tensor> pacing, double rate_bytes_per_ns,
                      int64_t max_ctas, int64_t tile_tokens, int64_t part_mask,
-                     c10::optional<torch::Tensor> block_table, bool hnd) {
+                     c10::optional<torch::Tensor> block_table, bool hnd, bool allow_mma) {
   const FrameGeom g = geom_from(geom);
   KVS_CHECK_ARG(part_mask >= 1 && part_mask <= 3, "part_mask must be 1 (K), 2 (V) or 3");
   KVS_CHECK_ARG(k.is_cuda() && v.is_cuda() && k.scalar_type() == at::kBFloat16 &&
@@ -937,6 +944,27 @@ void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom
   const int ntiles = std::max<int>(1, int(ceil_div(g.T, tile_tokens)));
   const int ctas = std::max<int>(1, std::min<int>(ntiles, int(max_ctas)));
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  // Tensor-core path: head_dim 128 with the transform, quantised sections only.
+  bool mma_ok = allow_mma && g.D == 128 && g.transform && g.T > 0 && g.H * g.D <= kEncMaxHD &&
+                stats.numel() >= 2 * g.H * g.D + 4 * int64_t(g.T) && counter.numel() >= 2;
+  for (int p = 0; p < 2; ++p)
+    for (int s2 = 0; s2 < 2; ++s2)
+      if (((part_mask >> p) & 1) && section_heads(g, s2) > 0 && g.bits[p][s2] == kRawBits) mma_ok = false;
+  if (mma_ok) {
+    static bool attr = false;
+    if (!attr) {
+      KVS_CUDA_CHECK(cudaFuncSetAttribute(kv_stats_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kEncSmem));
+      KVS_CUDA_CHECK(cudaFuncSetAttribute(kv_quant_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kEncSmem));
+      attr = true;
+    }
+    a.vstats_len = 4 * g.T;
+    const int64_t units = int64_t(part_mask == 3 ? 2 : 1) * g.H * ((g.T + 127) / 128);
+    const int mctas = int(std::max<int64_t>(1, std::min<int64_t>(units, 3 * int64_t(kNumSMs))));
+    kv_stats_mma_kernel<<<mctas, kEncMmaThreads, kEncSmem, st>>>(a);
+    kv_quant_mma_kernel<<<mctas, kEncMmaThreads, kEncSmem, st>>>(a);
+    KVS_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   const size_t smem = size_t(2) * g.H * g.D * 4;
   bool any_k_quant = false;
   for (int s = 0; s < 2; ++s)

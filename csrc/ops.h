@@ -13,7 +13,7 @@ void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom
                      torch::Tensor sign_bits, int64_t frame_ptr, torch::Tensor stats, torch::Tensor counter,
                      int64_t flag_ptr, int64_t seq, int64_t layer, c10::optional<torch::Tensor> pacing,
                      double rate_bytes_per_ns, int64_t max_ctas, int64_t tile_tokens, int64_t part_mask,
-                     c10::optional<torch::Tensor> block_table, bool hnd);
+                     c10::optional<torch::Tensor> block_table, bool hnd, bool allow_mma);
 void kv_decode_layers(int64_t frame_base, int64_t frame_stride, std::vector<int64_t> geom, torch::Tensor orders,
                       torch::Tensor sign_bits, torch::Tensor kv_cache, torch::Tensor block_table,
                       int64_t tok_offset, int64_t flags_ptr, int64_t seq, int64_t layer_begin, int64_t num_layers,

@@ -129,7 +129,7 @@ class KVTransfer:
     def encode(self, layer: int, k: torch.Tensor, v: torch.Tensor, frame_ptr: int, flag_ptr: int, seq: int,
                pacing: Optional[torch.Tensor] = None, rate_bytes_per_ns: float = 0.0, max_ctas: int = 222) -> None:
         if self._state is None:
-            self._state = kc.EncoderState(self.device)
+            self._state = kc.EncoderState(self.device, max_tokens=self.max_tokens)
         kc.encode_layer(k, v, self.spec(layer, k.shape[0]), self.orders[layer], self.sign_bits[layer], frame_ptr,
                         self._state, flag_ptr=flag_ptr, seq=seq, layer=layer, pacing=pacing,
                         rate_bytes_per_ns=rate_bytes_per_ns, max_ctas=max_ctas)

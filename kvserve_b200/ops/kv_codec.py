@@ -13,6 +13,8 @@ min-max quantiser kvserve_v1/compression/quantizer/kvserve_quantizer.py:171-294.
 """
 from __future__ import annotations
 
+import os
+
 import math
 from dataclasses import dataclass, field
 from typing import Optional, Sequence
@@ -282,27 +284,45 @@ def cpu_decode_frame(buf: bytes, spec: FrameSpec, order: torch.Tensor, signs: to
 
 @dataclass
 class EncoderState:
-    """Per-stream scratch of the encoder (statistics + completion counter)."""
+    """Per-stream scratch of the encoder: statistics, completion counter and
+    (``counter[1]``) the tensor-core path's error word.
+
+    ``stats`` holds the per-channel K statistics ``[min(H*D) | max(H*D)]``
+    and, for the tensor-core path (head_dim 128), the per-token V statistics
+    ``[section][min(T) | max(T)]`` after them, all as ordered uint32.  The
+    last CTA of every layer restores the identities; :meth:`prepare` sets
+    them when the geometry changes.  Size it for ``max_tokens`` up front so
+    the buffer is never reallocated while a launch may still use it."""
 
     device: torch.device
     max_hd: int = 2048
+    max_tokens: int = 0
     stats: torch.Tensor = field(init=False)
     counter: torch.Tensor = field(init=False)
 
     def __post_init__(self):
-        # [min(H*D) | max(H*D)] as ordered uint32; the last CTA of every layer
-        # restores the identities, prepare() sets them when H*D changes.
-        self.stats = torch.zeros(2 * self.max_hd, dtype=torch.int32, device=self.device)
+        self.stats = torch.zeros(2 * self.max_hd + 4 * self.max_tokens, dtype=torch.int32, device=self.device)
         self.counter = torch.zeros(4, dtype=torch.int32, device=self.device)
-        self._hd = None
+        self._geom = None
 
-    def prepare(self, hd: int) -> None:
+    def prepare(self, hd: int, tokens: int = 0) -> None:
         if hd > self.max_hd:
             raise ValueError("H*D exceeds the encoder scratch")
-        if self._hd != hd:
-            self.stats[:hd].fill_(-1)       # 0xFFFFFFFF: min identity
-            self.stats[hd:2 * hd].fill_(0)  # 0x00000000: max identity
-            self._hd = hd
+        need = 2 * self.max_hd + 4 * tokens
+        if need > self.stats.numel():
+            # grow (previous launches on any stream must be done with the old buffer)
+            torch.cuda.synchronize(self.device)
+            self.stats = torch.zeros(need, dtype=torch.int32, device=self.device)
+            self.max_tokens = tokens
+            self._geom = None
+        if self._geom != (hd, tokens):
+            st = self.stats
+            st[:hd].fill_(-1)        # 0xFFFFFFFF: min identity
+            st[hd:2 * hd].fill_(0)   # 0x00000000: max identity
+            v = st[2 * hd:2 * hd + 4 * tokens].view(2, 2, max(tokens, 0))
+            v[:, 0].fill_(-1)
+            v[:, 1].fill_(0)
+            self._geom = (hd, tokens)
 
 
 def default_tile_tokens(H: int, D: int) -> int:
@@ -312,11 +332,15 @@ def default_tile_tokens(H: int, D: int) -> int:
     return max(1, rows // H)
 
 
+_MMA_ENCODE = os.environ.get("KVSERVE_MMA_ENCODE", "0").strip().lower() in {"1", "true", "yes", "on"}
+
+
 def encode_layer(k: torch.Tensor, v: torch.Tensor, spec: FrameSpec, order: torch.Tensor,
                  sign_bits: torch.Tensor, frame_ptr: int, state: EncoderState, flag_ptr: int = 0,
                  seq: int = 1, layer: int = 0, pacing: Optional[torch.Tensor] = None,
                  rate_bytes_per_ns: float = 0.0, max_ctas: int = 222, tile_tokens: Optional[int] = None,
-                 part_mask: int = 3, block_table: Optional[torch.Tensor] = None, hnd: bool = False) -> None:
+                 part_mask: int = 3, block_table: Optional[torch.Tensor] = None, hnd: bool = False,
+                 allow_mma: Optional[bool] = None) -> None:
     """Launch the fused encode of one layer into ``frame_ptr`` (local or peer).
 
     The defaults (222 CTAs per part; tiles of 64 rows = 64/H tokens, one
@@ -326,17 +350,26 @@ def encode_layer(k: torch.Tensor, v: torch.Tensor, spec: FrameSpec, order: torch
     ``k``/``v`` are ``[T, H, D]`` views, or — with ``block_table`` — paged
     per-layer caches ``[num_blocks, block_size, H, D]`` (``hnd``: ``[num_blocks,
     H, block_size, D]``) read through the block table (fused gather).
-    ``part_mask`` selects K (1), V (2) or both (3)."""
+    ``part_mask`` selects K (1), V (2) or both (3).  With head_dim 128, the
+    transform on and no raw section the transform runs on the tensor cores
+    (``allow_mma=False`` keeps the register butterfly; None follows
+    ``KVSERVE_MMA_ENCODE``, default off).  Either way there are two launches:
+    statistics, then quantise + pack + publish."""
+    if allow_mma is None:
+        allow_mma = _MMA_ENCODE
     from ._ext import ext
     from . import count_launches
-    count_launches(2 if (part_mask & 1) and any(spec.section_heads(s) and spec.bits[0][s] != RAW_BITS
-                                                for s in range(2)) else 1)
-    state.prepare(spec.H * spec.D)
+    active = [(p, s) for p in range(2) for s in range(2) if (part_mask >> p) & 1 and spec.section_heads(s)]
+    mma = (allow_mma and spec.D == 128 and spec.transform and spec.T > 0 and spec.H * spec.D <= 1024
+           and all(spec.bits[p][s] != RAW_BITS for p, s in active))
+    count_launches(2 if mma or ((part_mask & 1) and any(spec.section_heads(s) and spec.bits[0][s] != RAW_BITS
+                                                         for s in range(2))) else 1)
+    state.prepare(spec.H * spec.D, spec.T)
     if tile_tokens is None:
         tile_tokens = default_tile_tokens(spec.H, spec.D)
     ext().kv_encode_layer(k, v, spec.params(), order, sign_bits, int(frame_ptr), state.stats, state.counter,
                           int(flag_ptr), int(seq), int(layer), pacing, float(rate_bytes_per_ns), int(max_ctas),
-                          int(tile_tokens), int(part_mask), block_table, bool(hnd))
+                          int(tile_tokens), int(part_mask), block_table, bool(hnd), bool(allow_mma))
 
 
 def decode_layers(frame_base: int, frame_stride: int, spec: FrameSpec, orders: torch.Tensor,

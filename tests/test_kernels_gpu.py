@@ -266,8 +266,10 @@ def _codec_case(T, H, D, n_low, kb, vb, raw=False):
 
 @pytest.mark.parametrize("T,H,D,n_low,kb,vb", [(256, 4, 128, 1, (2, 4), (2, 2)), (1000, 8, 128, 3, (3, 4), (2, 4)),
                                                (77, 2, 64, 0, (4, 4), (8, 8)), (33, 8, 256, 8, (4, 4), (2, 2)),
-                                               (4096, 8, 128, 6, (4, 4), (2, 2))])
-def test_kv_codec_matches_cpu_oracle(T, H, D, n_low, kb, vb):
+                                               (4096, 8, 128, 6, (4, 4), (2, 2)), (300, 8, 128, 0, (8, 8), (8, 8))])
+@pytest.mark.parametrize("allow_mma", [True, False])
+def test_kv_codec_matches_cpu_oracle(T, H, D, n_low, kb, vb, allow_mma):
+    """head_dim 128 runs the tensor-core encode unless allow_mma is off."""
     kc, k, v, order, spec, signs, sbits = _codec_case(T, H, D, n_low, kb, vb)
     ops = _ops()
     lay = kc.frame_layout(spec)
@@ -276,12 +278,22 @@ def test_kv_codec_matches_cpu_oracle(T, H, D, n_low, kb, vb):
     state = kc.EncoderState(torch.device("cuda"))
     flag = torch.zeros(4, dtype=torch.int32, device="cuda")
     kc.encode_layer(k.cuda(), v.cuda(), spec, order.cuda(), sbits.cuda(), frame.data_ptr(), state,
-                    flag_ptr=flag.data_ptr(), seq=5, layer=0)
+                    flag_ptr=flag.data_ptr(), seq=5, layer=0, allow_mma=allow_mma)
     torch.cuda.synchronize()
-    assert int(flag[0].item()) == 5
+    assert int(flag[0].item()) == 5 and int(state.counter[1].item()) == 0
     gpu = frame.cpu().numpy().tobytes()
     cpu = bytes(kc.cpu_encode_frame(k, v, spec, order, signs, layer=0, seq=5))
     assert gpu[:64] == cpu[:64]
+    # quantisation parameters (bf16): K per channel, V per token and section
+    gk = np.frombuffer(gpu[lay.k_aux:lay.k_aux + 4 * H * D], dtype=np.uint16).astype(np.int32)
+    ck = np.frombuffer(cpu[lay.k_aux:lay.k_aux + 4 * H * D], dtype=np.uint16).astype(np.int32)
+    assert np.mean(gk != ck) < 2e-2 and np.abs(gk - ck).max() <= 2
+    for s in range(2):
+        if spec.section_heads(s):
+            o = lay.v_aux[s]
+            gv = np.frombuffer(gpu[o:o + 4 * T], dtype=np.uint16).astype(np.int32)
+            cv = np.frombuffer(cpu[o:o + 4 * T], dtype=np.uint16).astype(np.int32)
+            assert np.mean(gv != cv) < 2e-2 and np.abs(gv - cv).max() <= 2
     # symbols: allow a tiny fraction of off-by-one from fp32 summation order
     for p in range(2):
         for s in range(2):
