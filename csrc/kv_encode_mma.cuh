@@ -72,14 +72,35 @@ __device__ __forceinline__ void enc_build_h(uint8_t* smem, int tid, int nthreads
   }
 }
 
-// Sign-flipped 128-token tile of one head into the SW128 tile (rows past T are zero).
-__device__ __forceinline__ void enc_load_tile(const EncodeArgs& a, uint8_t* smem, int part, int j, int t0, int tid) {
+constexpr int kEncRowsPerPass = kEncMmaThreads / 16;   // 8 rows of 16 x 16-byte chunks per pass
+constexpr int kEncLoads = 128 / kEncRowsPerPass;        // 16 loads per thread per tile
+
+// Issues the 16 loads of this thread's chunks of a 128-token tile of head
+// slot j (rows past T read as zero); the data are consumed by enc_put_tile,
+// so the loads of the next unit overlap the current unit's epilogue.
+__device__ __forceinline__ void enc_fetch_tile(const EncodeArgs& a, int part, int j, int t0, int tid,
+                                               uint4 (&buf)[kEncLoads]) {
   const bf16* base = part ? a.v : a.k;
   const int64_t tok_stride = part ? a.v_tok_stride : a.k_tok_stride;
   const int64_t head_stride = part ? a.v_head_stride : a.k_head_stride;
   const int64_t block_stride = part ? a.v_block_stride : a.k_block_stride;
   const int hsrc = a.order[j];
-  const uint32_t* sb = a.sign_bits + hsrc * 4;
+  const int c16 = tid & 15;
+#pragma unroll
+  for (int i = 0; i < kEncLoads; ++i) {
+    const int t = t0 + i * kEncRowsPerPass + (tid >> 4);
+    buf[i] = make_uint4(0, 0, 0, 0);
+    if (t < a.g.T)
+      buf[i] = __ldg(reinterpret_cast<const uint4*>(
+          src_row(base, t, hsrc, tok_stride, head_stride, a.block_table, a.block_size, block_stride) + c16 * 8));
+  }
+}
+
+// Sign flip (the bf16 sign bit of the head's negative channels; rows past T
+// stay zero) and store into the SW128 tile.
+__device__ __forceinline__ void enc_put_tile(const EncodeArgs& a, uint8_t* smem, int j, int tid,
+                                             const uint4 (&buf)[kEncLoads]) {
+  const uint32_t* sb = a.sign_bits + a.order[j] * 4;
   const int c16 = tid & 15;
   const uint32_t sbyte = (sb[c16 >> 2] >> ((c16 & 3) * 8)) & 0xffu;
   uint4 flip;
@@ -87,27 +108,14 @@ __device__ __forceinline__ void enc_load_tile(const EncodeArgs& a, uint8_t* smem
   flip.y = ((sbyte & 4u) ? 0x8000u : 0u) | ((sbyte & 8u) ? 0x80000000u : 0u);
   flip.z = ((sbyte & 16u) ? 0x8000u : 0u) | ((sbyte & 32u) ? 0x80000000u : 0u);
   flip.w = ((sbyte & 64u) ? 0x8000u : 0u) | ((sbyte & 128u) ? 0x80000000u : 0u);
-  constexpr int kRowsPerPass = kEncMmaThreads / 16;   // 8
-  uint4 buf[128 / kRowsPerPass];
 #pragma unroll
-  for (int i = 0; i < 128 / kRowsPerPass; ++i) {
-    const int row = i * kRowsPerPass + (tid >> 4);
-    const int t = t0 + row;
-    buf[i] = make_uint4(0, 0, 0, 0);
-    if (t < a.g.T)
-      buf[i] = __ldg(reinterpret_cast<const uint4*>(
-          src_row(base, t, hsrc, tok_stride, head_stride, a.block_table, a.block_size, block_stride) + c16 * 8));
-  }
-#pragma unroll
-  for (int i = 0; i < 128 / kRowsPerPass; ++i) {
-    const int row = i * kRowsPerPass + (tid >> 4);
+  for (int i = 0; i < kEncLoads; ++i) {
+    const int row = i * kEncRowsPerPass + (tid >> 4);
     uint4 x = buf[i];
-    if (t0 + row < a.g.T) {
-      x.x ^= flip.x;
-      x.y ^= flip.y;
-      x.z ^= flip.z;
-      x.w ^= flip.w;
-    }
+    x.x ^= flip.x;   // zero rows flip to -0.0, which the transform treats as 0
+    x.y ^= flip.y;
+    x.z ^= flip.z;
+    x.w ^= flip.w;
     *reinterpret_cast<uint4*>(smem + kEncOffA + sw128_off(row, c16)) = x;
   }
 }
@@ -135,6 +143,16 @@ __global__ void __launch_bounds__(kEncMmaThreads) kv_stats_mma_kernel(EncodeArgs
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kEncOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kEncOffBar + 8);
   const int tid = threadIdx.x, warp = tid >> 5;
+  const FrameGeom& g = a.g;
+  const int ntile = (g.T + 127) / 128;
+  const int nparts = a.part_mask == 3 ? 2 : 1;
+  const int64_t total = int64_t(nparts) * g.H * ntile;
+  uint4 buf[kEncLoads];
+  EncUnit e{};
+  if (blockIdx.x < total) {  // the first tile's loads overlap the set-up
+    e = enc_unit(blockIdx.x, g.H, ntile, a.part_mask);
+    enc_fetch_tile(a, e.part, e.j, e.tile * 128, tid, buf);
+  }
   enc_build_h(smem, tid, kEncMmaThreads);
   if (tid == 0) {
     mbar_init(bar, 1);
@@ -146,24 +164,24 @@ __global__ void __launch_bounds__(kEncMmaThreads) kv_stats_mma_kernel(EncodeArgs
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tile_s = smem_u32(smem + kEncOffA), h_s = smem_u32(smem + kEncOffH);
-  const FrameGeom& g = a.g;
   const float scale = inv_sqrt_d<D>();
-  const int ntile = (g.T + 127) / 128;
-  const int nparts = a.part_mask == 3 ? 2 : 1;
-  const int64_t total = int64_t(nparts) * g.H * ntile;
   const int HD = g.H * D;
   uint32_t phase = 0;
   for (int64_t u = blockIdx.x; u < total; u += gridDim.x) {
-    const EncUnit e = enc_unit(u, g.H, ntile, a.part_mask);
     const int t0 = e.tile * 128;
     const int nvalid = min(128, g.T - t0);
-    enc_load_tile(a, smem, e.part, e.j, t0, tid);
+    enc_put_tile(a, smem, e.j, tid, buf);
     fence_proxy_async_smem();
     __syncthreads();
     // K: D^T = H (s.K)^T (lane = channel); V: D = (s.V) H (lane = token)
     if (tid == 0) {
       if (e.part == 0) enc_mma(tmem, h_s, tile_s, bar);
       else enc_mma(tmem, tile_s, h_s, bar);
+    }
+    const EncUnit cur = e;
+    if (u + gridDim.x < total) {  // next unit's loads run under this unit's MMA and epilogue
+      e = enc_unit(u + gridDim.x, g.H, ntile, a.part_mask);
+      enc_fetch_tile(a, e.part, e.j, e.tile * 128, tid, buf);
     }
     const bool done = mbar_wait(bar, phase, a.counter + 1);
     if (!__syncthreads_and(done)) {
@@ -179,7 +197,7 @@ __global__ void __launch_bounds__(kEncMmaThreads) kv_stats_mma_kernel(EncodeArgs
       uint32_t r[32];
       tmem_ld32(trow + uint32_t(c * 32), r);
       tmem_wait_ld();
-      if (e.part == 0) {
+      if (cur.part == 0) {
 #pragma unroll
         for (int q = 0; q < 32; ++q)
           if (c * 32 + q < nvalid) {
@@ -194,12 +212,12 @@ __global__ void __launch_bounds__(kEncMmaThreads) kv_stats_mma_kernel(EncodeArgs
         }
       }
     }
-    if (e.part == 0) {
-      const int c = e.j * D + tid;  // lane = channel
+    if (cur.part == 0) {
+      const int c = cur.j * D + tid;  // lane = channel
       atomicMin(&a.stats[c], float_to_ordered(lo * scale));
       atomicMax(&a.stats[HD + c], float_to_ordered(hi * scale));
     } else if (tid < nvalid) {
-      const int s = e.j < g.n_low ? 0 : 1;
+      const int s = cur.j < g.n_low ? 0 : 1;
       uint32_t* vs = a.stats + 2 * HD + int64_t(s) * 2 * g.T;
       atomicMin(&vs[t0 + tid], float_to_ordered(lo * scale));
       atomicMax(&vs[g.T + t0 + tid], float_to_ordered(hi * scale));
@@ -264,6 +282,15 @@ __global__ void __launch_bounds__(kEncMmaThreads) kv_quant_mma_kernel(EncodeArgs
   const int tid = threadIdx.x, warp = tid >> 5;
   const FrameGeom& g = a.g;
   const int HD = g.H * D;
+  const int ntile = (g.T + 127) / 128;
+  const int nparts = a.part_mask == 3 ? 2 : 1;
+  const int64_t total = int64_t(nparts) * g.H * ntile;
+  uint4 buf[kEncLoads];
+  EncUnit e{};
+  if (blockIdx.x < total) {  // the first tile's loads overlap the set-up
+    e = enc_unit(blockIdx.x, g.H, ntile, a.part_mask);
+    enc_fetch_tile(a, e.part, e.j, e.tile * 128, tid, buf);
+  }
   enc_build_h(smem, tid, kEncMmaThreads);
   // K parameters of every slot from the statistics (block 0 also writes them
   // and the section headers into the frame)
@@ -300,17 +327,18 @@ __global__ void __launch_bounds__(kEncMmaThreads) kv_quant_mma_kernel(EncodeArgs
   const uint32_t tmem = *tmem_slot;
   const uint32_t tile_s = smem_u32(smem + kEncOffA), h_s = smem_u32(smem + kEncOffH);
   const float scale = inv_sqrt_d<D>();
-  const int ntile = (g.T + 127) / 128;
-  const int nparts = a.part_mask == 3 ? 2 : 1;
-  const int64_t total = int64_t(nparts) * g.H * ntile;
   uint32_t phase = 0;
   for (int64_t u = blockIdx.x; u < total; u += gridDim.x) {
-    const EncUnit e = enc_unit(u, g.H, ntile, a.part_mask);
     const int t0 = e.tile * 128;
-    enc_load_tile(a, smem, e.part, e.j, t0, tid);
+    enc_put_tile(a, smem, e.j, tid, buf);
     fence_proxy_async_smem();
     __syncthreads();
     if (tid == 0) enc_mma(tmem, tile_s, h_s, bar);   // lane = token
+    const EncUnit cur = e;
+    if (u + gridDim.x < total) {  // next unit's loads run under this unit's MMA and epilogue
+      e = enc_unit(u + gridDim.x, g.H, ntile, a.part_mask);
+      enc_fetch_tile(a, e.part, e.j, e.tile * 128, tid, buf);
+    }
     const bool done = mbar_wait(bar, phase, a.counter + 1);
     if (!__syncthreads_and(done)) {
       if (tid == 0) mbar_wait(bar, phase, nullptr);
@@ -319,13 +347,13 @@ __global__ void __launch_bounds__(kEncMmaThreads) kv_quant_mma_kernel(EncodeArgs
     phase ^= 1u;
     tc_fence_after();
     int s, js, hs;
-    slot_section(g, e.j, s, js, hs);
-    const int bits = gbits(g, e.part, s);
-    const float top = float(glevels(g, e.part, s) - 1);
+    slot_section(g, cur.j, s, js, hs);
+    const int bits = gbits(g, cur.part, s);
+    const float top = float(glevels(g, cur.part, s) - 1);
     const int t = t0 + tid;
     const bool valid = t < g.T;
     float vmn = 0.f, vinv = 0.f;
-    if (e.part == 1 && valid) {
+    if (cur.part == 1 && valid) {
       const uint32_t* vs = a.stats + 2 * HD + int64_t(s) * 2 * g.T;
       const bf16 minb = rn(ordered_to_float(vs[t]));
       const bf16 sclb = rn(fmaxf(ordered_to_float(vs[g.T + t]) - to_f32(minb), 1e-5f) / top);
@@ -338,7 +366,7 @@ __global__ void __launch_bounds__(kEncMmaThreads) kv_quant_mma_kernel(EncodeArgs
       }
     }
     const int64_t sym = (int64_t(t) * hs + js) * D;
-    uint32_t* dst = reinterpret_cast<uint32_t*>(a.frame + gpayload(g, e.part, s) + 16 + sym * bits / 8);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(a.frame + gpayload(g, cur.part, s) + 16 + sym * bits / 8);
     const uint32_t trow = tmem + (uint32_t(warp * 32) << 16);
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {
@@ -347,9 +375,9 @@ __global__ void __launch_bounds__(kEncMmaThreads) kv_quant_mma_kernel(EncodeArgs
       tmem_wait_ld();
       if (!valid) continue;
       uint32_t q[32];
-      if (e.part == 0) {
-        const float* mn = kmin + e.j * D + c * 32;
-        const float* iv = kinv + e.j * D + c * 32;
+      if (cur.part == 0) {
+        const float* mn = kmin + cur.j * D + c * 32;
+        const float* iv = kinv + cur.j * D + c * 32;
 #pragma unroll
         for (int x = 0; x < 32; ++x) {
           const float y = rintf((__uint_as_float(r[x]) * scale - mn[x]) * iv[x]);
