@@ -10,6 +10,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   // fused KV transfer codec
   m.def("kv_frame_geom", &kvs::kv_frame_geom);
   m.def("kv_encode_layer", &kvs::kv_encode_layer);
+  m.def("kv_signed_hadamard", &kvs::kv_signed_hadamard);
   m.def("kv_decode_layers", &kvs::kv_decode_layers);
   // modular pipeline kernels
   m.def("bitpack_encode", &kvs::bitpack_encode);

@@ -868,6 +868,22 @@ void launch_kstats(int D, dim3 grid, size_t smem, cudaStream_t st, const Args& a
 
 }  // namespace
 
+torch::Tensor kv_signed_hadamard(torch::Tensor sign_bits) {
+  KVS_CHECK_ARG(sign_bits.is_cuda() && sign_bits.scalar_type() == at::kInt && sign_bits.is_contiguous() &&
+                    sign_bits.numel() % 4 == 0,
+                "sign_bits: contiguous int32 [heads, 4] (head_dim 128)");
+  const int heads = int(sign_bits.numel() / 4);
+  auto out = torch::empty({int64_t(heads) * 128, 128}, sign_bits.options().dtype(at::kBFloat16));
+  if (heads == 0) return out;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int64_t n = int64_t(heads) * 128 * 128;
+  kv_signed_hadamard_kernel<<<unsigned(std::min<int64_t>((n + 255) / 256, 4096)), 256, 0, st>>>(
+      reinterpret_cast<const uint32_t*>(sign_bits.data_ptr<int32_t>()), heads,
+      reinterpret_cast<bf16*>(out.data_ptr()));
+  KVS_CUDA_CHECK(cudaGetLastError());
+  return out;
+}
+
 std::vector<int64_t> kv_frame_geom(std::vector<int64_t> params) {
   const FrameGeom g = geom_from(params);
   return {g.frame_bytes, g.k_aux, g.v_aux[0], g.v_aux[1], g.payload[0][0], g.payload[0][1],
@@ -879,7 +895,8 @@ void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom
                      torch::Tensor stats, torch::Tensor counter, int64_t flag_ptr, int64_t seq,
                      int64_t layer, c10::optional<torch::Tensor> pacing, double rate_bytes_per_ns,
                      int64_t max_ctas, int64_t tile_tokens, int64_t part_mask,
-                     c10::optional<torch::Tensor> block_table, bool hnd, bool allow_mma) {
+                     c10::optional<torch::Tensor> block_table, bool hnd, bool allow_mma,
+                     c10::optional<torch::Tensor> hs_table, int64_t hs_row0) {
   const FrameGeom g = geom_from(geom);
   KVS_CHECK_ARG(part_mask >= 1 && part_mask <= 3, "part_mask must be 1 (K), 2 (V) or 3");
   KVS_CHECK_ARG(k.is_cuda() && v.is_cuda() && k.scalar_type() == at::kBFloat16 &&
@@ -944,24 +961,39 @@ void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom
   const int ntiles = std::max<int>(1, int(ceil_div(g.T, tile_tokens)));
   const int ctas = std::max<int>(1, std::min<int>(ntiles, int(max_ctas)));
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  // Tensor-core path: head_dim 128 with the transform, quantised sections only.
+  // Tensor-core path: head_dim 128 with the transform, quantised sections
+  // only, contiguous [T, H, 128] sources (TMA rows of all heads), and the
+  // signed transform table of these heads.
   bool mma_ok = allow_mma && g.D == 128 && g.transform && g.T > 0 && g.H * g.D <= kEncMaxHD &&
-                stats.numel() >= 2 * g.H * g.D + 4 * int64_t(g.T) && counter.numel() >= 2;
+                !block_table.has_value() && hs_table.has_value() && k.dim() == 3 && k.stride(1) == g.D &&
+                v.stride(1) == g.D && stats.numel() >= 2 * g.H * g.D + 4 * int64_t(g.T) && counter.numel() >= 2;
   for (int p = 0; p < 2; ++p)
     for (int s2 = 0; s2 < 2; ++s2)
       if (((part_mask >> p) & 1) && section_heads(g, s2) > 0 && g.bits[p][s2] == kRawBits) mma_ok = false;
   if (mma_ok) {
+    KVS_CHECK_ARG(hs_table->is_cuda() && hs_table->scalar_type() == at::kBFloat16 && hs_table->dim() == 2 &&
+                      hs_table->size(1) == 128 && hs_table->is_contiguous() &&
+                      (hs_row0 + src_heads) * 128 <= hs_table->size(0),
+                  "hs_table: bf16 [(>= hs_row0 + heads) * 128, 128]");
     static bool attr = false;
     if (!attr) {
-      KVS_CUDA_CHECK(cudaFuncSetAttribute(kv_stats_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kEncSmem));
-      KVS_CUDA_CHECK(cudaFuncSetAttribute(kv_quant_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kEncSmem));
+      KVS_CUDA_CHECK(cudaFuncSetAttribute(kv_encode_ws_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          kWsSmem));
+      KVS_CUDA_CHECK(cudaFuncSetAttribute(kv_encode_ws_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          kWsSmem));
       attr = true;
     }
     a.vstats_len = 4 * g.T;
+    const CUtensorMap tk = make_tmap_2d_bf16(k.data_ptr(), uint64_t(src_heads) * 128, uint64_t(g.T),
+                                             uint64_t(k.stride(0)) * 2, 64, 128, true);
+    const CUtensorMap tv = make_tmap_2d_bf16(v.data_ptr(), uint64_t(src_heads) * 128, uint64_t(g.T),
+                                             uint64_t(v.stride(0)) * 2, 64, 128, true);
+    const CUtensorMap tm = make_tmap_2d_bf16(hs_table->data_ptr(), 128, uint64_t(hs_table->size(0)), 256, 64, 128,
+                                             true);
     const int64_t units = int64_t(part_mask == 3 ? 2 : 1) * g.H * ((g.T + 127) / 128);
-    const int mctas = int(std::max<int64_t>(1, std::min<int64_t>(units, 3 * int64_t(kNumSMs))));
-    kv_stats_mma_kernel<<<mctas, kEncMmaThreads, kEncSmem, st>>>(a);
-    kv_quant_mma_kernel<<<mctas, kEncMmaThreads, kEncSmem, st>>>(a);
+    const int wctas = int(std::max<int64_t>(1, std::min<int64_t>(units, kNumSMs)));
+    kv_encode_ws_kernel<true><<<wctas, kWsThreads, kWsSmem, st>>>(tk, tv, tm, a, int(hs_row0));
+    kv_encode_ws_kernel<false><<<wctas, kWsThreads, kWsSmem, st>>>(tk, tv, tm, a, int(hs_row0));
     KVS_CUDA_CHECK(cudaGetLastError());
     return;
   }

@@ -9,11 +9,14 @@ namespace kvs {
 
 // ---- fused KV transfer codec (kv_codec.cu)
 std::vector<int64_t> kv_frame_geom(std::vector<int64_t> params);
+// Signed Hadamard table [heads*128, 128] bf16 (rows h*128+o: H[o][i] * sign_h[i]).
+torch::Tensor kv_signed_hadamard(torch::Tensor sign_bits);
 void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom, torch::Tensor order,
                      torch::Tensor sign_bits, int64_t frame_ptr, torch::Tensor stats, torch::Tensor counter,
                      int64_t flag_ptr, int64_t seq, int64_t layer, c10::optional<torch::Tensor> pacing,
                      double rate_bytes_per_ns, int64_t max_ctas, int64_t tile_tokens, int64_t part_mask,
-                     c10::optional<torch::Tensor> block_table, bool hnd, bool allow_mma);
+                     c10::optional<torch::Tensor> block_table, bool hnd, bool allow_mma,
+                     c10::optional<torch::Tensor> hs_table, int64_t hs_row0);
 void kv_decode_layers(int64_t frame_base, int64_t frame_stride, std::vector<int64_t> geom, torch::Tensor orders,
                       torch::Tensor sign_bits, torch::Tensor kv_cache, torch::Tensor block_table,
                       int64_t tok_offset, int64_t flags_ptr, int64_t seq, int64_t layer_begin, int64_t num_layers,

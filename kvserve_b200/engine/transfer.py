@@ -130,9 +130,14 @@ class KVTransfer:
                pacing: Optional[torch.Tensor] = None, rate_bytes_per_ns: float = 0.0, max_ctas: int = 222) -> None:
         if self._state is None:
             self._state = kc.EncoderState(self.device, max_tokens=self.max_tokens)
+        if self.D == 128 and getattr(self, "_hs_table", None) is None:
+            # signed transform table of every (layer, head) for the tensor-core encoder
+            from ..ops import ext
+            self._hs_table = ext().kv_signed_hadamard(self.sign_bits.reshape(-1, 4).contiguous())
         kc.encode_layer(k, v, self.spec(layer, k.shape[0]), self.orders[layer], self.sign_bits[layer], frame_ptr,
                         self._state, flag_ptr=flag_ptr, seq=seq, layer=layer, pacing=pacing,
-                        rate_bytes_per_ns=rate_bytes_per_ns, max_ctas=max_ctas)
+                        rate_bytes_per_ns=rate_bytes_per_ns, max_ctas=max_ctas,
+                        hs_table=getattr(self, "_hs_table", None), hs_row0=layer * self.H)
 
     # ------------------------------------------------------------- decode
     def ingest_layer(self, layer: int, T: int, frame_ptr: int, kv_cache: torch.Tensor, block_table: torch.Tensor,

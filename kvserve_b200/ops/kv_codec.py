@@ -324,6 +324,18 @@ class EncoderState:
             v[:, 1].fill_(0)
             self._geom = (hd, tokens)
 
+    def signed_table(self, sign_bits: torch.Tensor) -> torch.Tensor:
+        """Signed Hadamard table of the heads of ``sign_bits`` (head_dim 128),
+        built once per sign tensor."""
+        key = (sign_bits.data_ptr(), tuple(sign_bits.shape))
+        if getattr(self, "_table_key", None) != key:
+            from ._ext import ext
+            from . import count_launches
+            count_launches(1)
+            self._table = ext().kv_signed_hadamard(sign_bits.contiguous().view(-1, 4))
+            self._table_key = key
+        return self._table
+
 
 def default_tile_tokens(H: int, D: int) -> int:
     """Tokens per CTA tile: one unrolled step of the kernels' row loop
@@ -332,7 +344,7 @@ def default_tile_tokens(H: int, D: int) -> int:
     return max(1, rows // H)
 
 
-_MMA_ENCODE = os.environ.get("KVSERVE_MMA_ENCODE", "0").strip().lower() in {"1", "true", "yes", "on"}
+_MMA_ENCODE = os.environ.get("KVSERVE_MMA_ENCODE", "1").strip().lower() not in {"0", "false", "no", "off"}
 
 
 def encode_layer(k: torch.Tensor, v: torch.Tensor, spec: FrameSpec, order: torch.Tensor,
@@ -340,7 +352,8 @@ def encode_layer(k: torch.Tensor, v: torch.Tensor, spec: FrameSpec, order: torch
                  seq: int = 1, layer: int = 0, pacing: Optional[torch.Tensor] = None,
                  rate_bytes_per_ns: float = 0.0, max_ctas: int = 222, tile_tokens: Optional[int] = None,
                  part_mask: int = 3, block_table: Optional[torch.Tensor] = None, hnd: bool = False,
-                 allow_mma: Optional[bool] = None) -> None:
+                 allow_mma: Optional[bool] = None, hs_table: Optional[torch.Tensor] = None,
+                 hs_row0: int = 0) -> None:
     """Launch the fused encode of one layer into ``frame_ptr`` (local or peer).
 
     The defaults (222 CTAs per part; tiles of 64 rows = 64/H tokens, one
@@ -351,9 +364,12 @@ def encode_layer(k: torch.Tensor, v: torch.Tensor, spec: FrameSpec, order: torch
     per-layer caches ``[num_blocks, block_size, H, D]`` (``hnd``: ``[num_blocks,
     H, block_size, D]``) read through the block table (fused gather).
     ``part_mask`` selects K (1), V (2) or both (3).  With head_dim 128, the
-    transform on and no raw section the transform runs on the tensor cores
-    (``allow_mma=False`` keeps the register butterfly; None follows
-    ``KVSERVE_MMA_ENCODE``, default off).  Either way there are two launches:
+    transform on, no raw section and a contiguous ``[T, H, 128]`` source the
+    transform runs on the tensor cores (``allow_mma=False`` keeps the
+    register butterfly; None follows ``KVSERVE_MMA_ENCODE``, default on),
+    with the signed transform table ``hs_table`` (rows of head h of this
+    layer at ``(hs_row0 + h) * 128``; built from ``sign_bits`` and cached in
+    ``state`` when not given).  Either way there are two launches:
     statistics, then quantise + pack + publish."""
     if allow_mma is None:
         allow_mma = _MMA_ENCODE
@@ -361,7 +377,10 @@ def encode_layer(k: torch.Tensor, v: torch.Tensor, spec: FrameSpec, order: torch
     from . import count_launches
     active = [(p, s) for p in range(2) for s in range(2) if (part_mask >> p) & 1 and spec.section_heads(s)]
     mma = (allow_mma and spec.D == 128 and spec.transform and spec.T > 0 and spec.H * spec.D <= 1024
+           and block_table is None and k.dim() == 3 and k.stride(1) == spec.D and v.stride(1) == spec.D
            and all(spec.bits[p][s] != RAW_BITS for p, s in active))
+    if mma and hs_table is None:
+        hs_table, hs_row0 = state.signed_table(sign_bits), 0
     count_launches(2 if mma or ((part_mask & 1) and any(spec.section_heads(s) and spec.bits[0][s] != RAW_BITS
                                                          for s in range(2))) else 1)
     state.prepare(spec.H * spec.D, spec.T)
@@ -369,7 +388,8 @@ def encode_layer(k: torch.Tensor, v: torch.Tensor, spec: FrameSpec, order: torch
         tile_tokens = default_tile_tokens(spec.H, spec.D)
     ext().kv_encode_layer(k, v, spec.params(), order, sign_bits, int(frame_ptr), state.stats, state.counter,
                           int(flag_ptr), int(seq), int(layer), pacing, float(rate_bytes_per_ns), int(max_ctas),
-                          int(tile_tokens), int(part_mask), block_table, bool(hnd), bool(allow_mma))
+                          int(tile_tokens), int(part_mask), block_table, bool(hnd), bool(mma), hs_table,
+                          int(hs_row0))
 
 
 def decode_layers(frame_base: int, frame_stride: int, spec: FrameSpec, orders: torch.Tensor,
