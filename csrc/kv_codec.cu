@@ -1106,13 +1106,14 @@ void kv_decode_layers(int64_t frame_base, int64_t frame_stride, std::vector<int6
   if (mma_ok) {
     static bool attr = false;
     if (!attr) {
-      KVS_CUDA_CHECK(cudaFuncSetAttribute(kv_decode_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          kMmaSmem));
+      KVS_CUDA_CHECK(cudaFuncSetAttribute(kv_decode_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          kDwSmem));
       attr = true;
     }
     const int64_t units = int64_t(a.part_mask == 3 ? 2 : 1) * g.H * ((g.T + 127) / 128) * a.num_layers;
-    const int ctas = int(std::max<int64_t>(1, std::min<int64_t>(units, std::max<int64_t>(1, max_ctas) * 2)));
-    kv_decode_mma_kernel<<<ctas, kMmaDecThreads, kMmaSmem, st>>>(a);
+    const int ctas = int(std::max<int64_t>(1, std::min<int64_t>(units, std::min<int64_t>(kNumSMs,
+                                                                                       std::max<int64_t>(1, max_ctas)))));
+    kv_decode_ws_kernel<<<ctas, kDwThreads, kDwSmem, st>>>(a);
     KVS_CUDA_CHECK(cudaGetLastError());
     return;
   }
