@@ -247,23 +247,24 @@ __global__ void __launch_bounds__(kMmaDecThreads) kv_decode_mma_kernel(DecodeArg
 // ---------------------------------------------------------------------------
 // Warp-specialised variant (the default): one persistent CTA per SM,
 // 544 threads.
-//   warps 0-7   two builder warpgroups taking alternate units: for a new
+//   warps 0-11  three builder warpgroups taking units in turn: for a new
 //               layer, thread 0 of the group acquire-waits (bounded) on the
 //               layer's publish flag and checks the header; then every
 //               thread dequantises one token row (its packed symbols are
 //               16*bits contiguous bytes) into the SW128 A tile of a
-//               3-stage ring;
-//   warp 8      MMA issuer: A tile x H into one of four 128-column TMEM
+//               4-stage ring;
+//   warp 12     MMA issuer: A tile x H into one of four 128-column TMEM
 //               accumulators;
-//   warps 9-16  two epilogue warpgroups (alternate units): 1/sqrt(D), the
-//               head's signs, bf16, 256-byte row store into the paged block.
+//   warps 13-16 epilogue warpgroup: 1/sqrt(D), the head's signs, bf16,
+//               256-byte row store into the paged block.
 // A timed-out flag or a bad header sets the status word and a CTA-wide
 // "bad" mark; the pipeline then keeps its protocol (no wait is left
 // pending) but no row is stored.
-constexpr int kDwGroups = 2;
-constexpr int kDwStages = 3;
+constexpr int kDwGroups = 3;       // builder warpgroups (dequantisation is the heavier side)
+constexpr int kDwEpi = 1;          // epilogue warpgroups
+constexpr int kDwStages = 4;
 constexpr int kDwAcc = 4;
-constexpr int kDwThreads = 128 * kDwGroups + 32 + 128 * kDwGroups;
+constexpr int kDwThreads = 128 * kDwGroups + 32 + 128 * kDwEpi;
 constexpr int kDwOffH = kDwStages * kMmaTile;
 constexpr int kDwOffPar = kDwOffH + kMmaTile;                 // per builder group: K min[128], scale[128]
 constexpr int kDwOffBar = kDwOffPar + kDwGroups * 2 * 128 * 4;
@@ -484,7 +485,7 @@ __global__ void __launch_bounds__(kDwThreads, 1) kv_decode_ws_kernel(DecodeArgs 
     }
   } else {
     // --------------------------------------------------------------- epilogue
-    const int ew = warp - kMmaWarp - 1;        // 0 .. 4*kDwGroups-1
+    const int ew = warp - kMmaWarp - 1;        // 0 .. 4*kDwEpi-1
     const int grp = ew >> 2;
     const int quarter = warp & 3;              // TMEM lanes quarter*32 .. +31
     const int row = quarter * 32 + lane;
@@ -492,7 +493,7 @@ __global__ void __launch_bounds__(kDwThreads, 1) kv_decode_ws_kernel(DecodeArgs 
     const int bshift = (a.block_size & (a.block_size - 1)) == 0 ? __ffs(a.block_size) - 1 : -1;
     int64_t n = grp;
     for (int64_t u = blockIdx.x + grp * int64_t(gridDim.x); u < total;
-         u += kDwGroups * int64_t(gridDim.x), n += kDwGroups) {
+         u += kDwEpi * int64_t(gridDim.x), n += kDwEpi) {
       const int acc = int(n % kDwAcc);
       const bool ready = mbar_wait(&tfull[acc], uint32_t(n / kDwAcc) & 1u, a.status);
       if (!__all_sync(0xffffffffu, ready)) break;
