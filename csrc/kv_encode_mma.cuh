@@ -12,7 +12,7 @@
 // warp-specialised CTA per SM (320 threads):
 //   warp 0     TMA producer: per unit the X tile (two 64-column SW128 boxes
 //              of the K or V rows of head order[j]; rows past T are zero
-//              filled) and M of that head into a 3-stage ring;
+//              filled) and M of that head into a 2-stage ring;
 //   warp 1     MMA issuer: eight tcgen05.mma (K = 16 each) into one of four
 //              128-column TMEM accumulators (all 512 columns);
 //   warps 2-9  two epilogue warpgroups taking alternate units, so two
@@ -37,11 +37,13 @@ namespace {
 constexpr int kWsEpiGroups = 2;                        // epilogue warpgroups (alternate units)
 constexpr int kWsAcc = 4;                              // 128-column TMEM accumulators
 constexpr int kWsThreads = 64 + 128 * kWsEpiGroups;
-constexpr int kWsStages = 3;
+constexpr int kWsStages = 2;
 constexpr int kWsStage = 2 * kMmaTile;                 // X tile + M (64 KB)
 constexpr int kEncMaxHD = 8 * 128;
 constexpr int kWsOffPar = kWsStages * kWsStage;        // K params: min[H*D], inv[H*D] fp32
-constexpr int kWsOffBar = kWsOffPar + 2 * kEncMaxHD * 4;
+constexpr int kWsStgWarp = 32 * 128;                   // per epilogue warp: 32 packed rows of <= 128 bytes
+constexpr int kWsOffStg = kWsOffPar + 2 * kEncMaxHD * 4;
+constexpr int kWsOffBar = kWsOffStg + 4 * kWsEpiGroups * kWsStgWarp;
 constexpr int kWsSmem = kWsOffBar + 256 + 1024;
 static_assert(kWsAcc % kWsEpiGroups == 0, "each warpgroup keeps its own accumulators");
 
@@ -295,14 +297,21 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             aux[g.T + t] = sclb;
           }
         }
-        uint32_t* dst = reinterpret_cast<uint32_t*>(a.frame + gpayload(g, e.part, s) + 16 +
-                                                    ((int64_t(t) * hs + js) * D) * bits / 8);
+        uint8_t* rows = a.frame + gpayload(g, e.part, s) + 16;   // row of token t at (t*hs + js) * 16*bits
+        const int64_t row_stride = int64_t(hs) * 16 * bits;
+        const int64_t row0 = (int64_t(t0) * hs + js) * 16 * bits;
+        // power-of-two widths: the warp's 32 packed rows go through shared
+        // memory so that each store instruction writes whole row pieces
+        // (16*bits contiguous bytes) instead of 16 bytes of 32 rows -- the
+        // frame is often a peer GPU's memory, where small writes waste NVLink
+        const bool staged = (bits & (bits - 1)) == 0;
+        uint32_t* stg = reinterpret_cast<uint32_t*>(smem + kWsOffStg + (warp - 2) * kWsStgWarp) + lane * 4 * bits;
+        uint32_t* dst = reinterpret_cast<uint32_t*>(rows + row0 + int64_t(r) * row_stride);
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t v[32];
           tmem_ld32(trow + uint32_t(c * 32), v);
           tmem_wait_ld();
-          if (!valid) continue;
           uint32_t q[32];
           if (e.part == 0) {
             const float* mn = kmin + e.j * D + c * 32;
@@ -319,7 +328,22 @@ __global__ void __launch_bounds__(kWsThreads, 1)
               q[x] = uint32_t(fminf(fmaxf(y, 0.0f), top));
             }
           }
-          pack32_any(q, dst + c * bits, bits);
+          if (staged) pack32_any(q, stg + c * bits, bits);
+          else if (valid) pack32_any(q, dst + c * bits, bits);
+        }
+        if (staged) {
+          __syncwarp();
+          // row pieces of 16*bits bytes = bits 16-byte chunks; 32/bits rows per instruction
+          const uint4* sp = reinterpret_cast<const uint4*>(smem + kWsOffStg + (warp - 2) * kWsStgWarp);
+          const int rows_per = 32 / bits;
+          for (int i = 0; i < bits; ++i) {
+            const int rr = i * rows_per + lane / bits, ck = lane % bits;
+            if (t0 + quarter * 32 + rr < g.T) {
+              const uint4 val = sp[rr * bits + ck];
+              *reinterpret_cast<uint4*>(rows + row0 + int64_t(quarter * 32 + rr) * row_stride + ck * 16) = val;
+            }
+          }
+          __syncwarp();
         }
       }
       tc_fence_before();
