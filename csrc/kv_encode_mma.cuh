@@ -41,7 +41,8 @@ constexpr int kWsStages = 2;
 constexpr int kWsStage = 2 * kMmaTile;                 // X tile + M (64 KB)
 constexpr int kEncMaxHD = 8 * 128;
 constexpr int kWsOffPar = kWsStages * kWsStage;        // K params: min[H*D], inv[H*D] fp32
-constexpr int kWsStgWarp = 32 * 128;                   // per epilogue warp: 32 packed rows of <= 128 bytes
+constexpr int kWsStgWarp = 32 * (128 + 16);            // per epilogue warp: 32 packed rows of <= 128 bytes,
+                                                       // each padded by 16 bytes (spreads the bank groups)
 constexpr int kWsOffStg = kWsOffPar + 2 * kEncMaxHD * 4;
 constexpr int kWsOffBar = kWsOffStg + 4 * kWsEpiGroups * kWsStgWarp;
 constexpr int kWsSmem = kWsOffBar + 256 + 1024;
@@ -305,7 +306,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         // (16*bits contiguous bytes) instead of 16 bytes of 32 rows -- the
         // frame is often a peer GPU's memory, where small writes waste NVLink
         const bool staged = (bits & (bits - 1)) == 0;
-        uint32_t* stg = reinterpret_cast<uint32_t*>(smem + kWsOffStg + (warp - 2) * kWsStgWarp) + lane * 4 * bits;
+        uint32_t* stg = reinterpret_cast<uint32_t*>(smem + kWsOffStg + (warp - 2) * kWsStgWarp) + lane * 4 * (bits + 1);
         uint32_t* dst = reinterpret_cast<uint32_t*>(rows + row0 + int64_t(r) * row_stride);
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -339,7 +340,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           for (int i = 0; i < bits; ++i) {
             const int rr = i * rows_per + lane / bits, ck = lane % bits;
             if (t0 + quarter * 32 + rr < g.T) {
-              const uint4 val = sp[rr * bits + ck];
+              const uint4 val = sp[rr * (bits + 1) + ck];
               *reinterpret_cast<uint4*>(rows + row0 + int64_t(quarter * 32 + rr) * row_stride + ck * 16) = val;
             }
           }
