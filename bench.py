@@ -56,6 +56,19 @@ def _profile(name: str):
     raise SystemExit(f"unknown profile {name!r}")
 
 
+def _handoff_roofline_ms(raw_bytes: int, payload_bytes: int, n_gpus: int) -> float:
+    """Speed-of-light time of one rank pair's hand-off (bytes of one rank)."""
+    hbm = 6650.0
+    try:
+        with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")) as f:
+            hbm = float(json.load(f)["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        pass
+    if n_gpus == 1:
+        return 2 * (raw_bytes + payload_bytes) / (hbm * 1e6)
+    return max((raw_bytes + payload_bytes) / (hbm * 1e6), payload_bytes / 770e6)
+
+
 def run_reference(args) -> None:
     """The unmodified reference (baseline/_ref) through its own public API:
     vLLM V1 producer/consumer engines with its CompressedKVConnector."""
@@ -77,10 +90,11 @@ def main() -> None:
     ap.add_argument("--link-gbps", type=float, default=0.0)
     ap.add_argument("--layers", type=int, default=0, help="override layer count (smoke runs only)")
     ap.add_argument("--no-graphs", action="store_true")
-    ap.add_argument("--ref-engine", default="handoff", choices=["handoff", "vllm"],
-                    help="reference arm: 'handoff' measures the reference's KV hand-off path (compression + "
-                         "NcclTransport) without vLLM; 'vllm' runs full PD serving (needs a vLLM the reference "
-                         "supports)")
+    ap.add_argument("--ref-engine", default="vllm", choices=["vllm", "stock", "handoff"],
+                    help="reference arm: 'vllm' (default) checks the stock stack once on a tiny model, then "
+                         "serves the bench through vLLM with the reference connector under a vLLM-API adapter "
+                         "and measures its KV hand-off alone; 'stock' only runs the stock check; 'handoff' only "
+                         "measures the hand-off path (compression + NcclTransport) without vLLM")
     ap.add_argument("--ref-cuda-graphs", action="store_true",
                     help="reference arm: let vLLM capture CUDA graphs (default eager, as the reference's own PD "
                          "tests run; capture fails with its connector's per-layer save hook)")
@@ -139,22 +153,41 @@ def main() -> None:
     wall_s = time.perf_counter() - t_wall
     clocks = sampler.stop() if sampler else None
 
-    mine = [t.__dict__ for t in timings]
-    allt = [None] * ctx.world_size
+    # the hand-off of one request on its own (no prefill beside it), and the
+    # reconstruction error of the profile on synthetic KV; both after the
+    # timed region
+    handoffs = [engine.measure_handoff(args.prompt_len) for _ in range(3)]
+    recon = None
+    if ctx.rank == 0:
+        from kvserve_b200.engine.fidelity import measure_profile
+        recon = measure_profile(profile, min(4, cfg.num_layers), args.prompt_len, cfg.num_kv_heads, cfg.head_dim,
+                                engine.device)
+
+    mine = {"steps": [t.__dict__ for t in timings], "handoff": handoffs}
+    allr = [None] * ctx.world_size
     if ctx.distributed:
-        dist.all_gather_object(allt, mine, group=ctx.cpu_group)
+        dist.all_gather_object(allr, mine, group=ctx.cpu_group)
     else:
-        allt = [mine]
+        allr = [mine]
+    allt = [r["steps"] for r in allr]
     if ctx.rank == 0:
         def col(step, key):
             vals = [allt[r][step][key] for r in range(len(allt))]
             vals = [v for v in vals if not (isinstance(v, float) and math.isnan(v))]
             return max(vals) if vals else float("nan")
+        def col_min(step, key):
+            vals = [allt[r][step][key] for r in range(len(allt))]
+            vals = [v for v in vals if not (isinstance(v, float) and math.isnan(v))]
+            return min(vals) if vals else float("nan")
         ttft = [col(s, "first_token") for s in range(args.steps)]
         end = [col(s, "all_done") for s in range(args.steps)]
         prefill = [col(s, "prefill_done") for s in range(args.steps)]
         ingest = [col(s, "ingest_done") for s in range(args.steps)]
         kv_exposed = [max(0.0, ingest[s] - prefill[s]) for s in range(args.steps)]
+        # layer 0's encode start (earliest prefill rank) -> last layer ingested (latest decode rank)
+        kv_handoff = [ingest[s] - col_min(s, "encode_start") for s in range(args.steps)]
+        iso = [max(allr[r]["handoff"][i]["ingest_ms"] for r in range(len(allr))
+                   if not math.isnan(allr[r]["handoff"][i]["ingest_ms"])) for i in range(len(handoffs))]
         payload = timings[0].payload_bytes if ctx.is_prefill else allt[0][0]["payload_bytes"]
         raw = allt[0][0]["raw_bytes"]
         tp = max(1, args.gpus // 2)
@@ -177,7 +210,20 @@ def main() -> None:
             "dtype": "bf16",
             "data": "synthetic (random-init weights of the named architecture, uniform-random prompt token ids)",
             "impl": "ours",
-            "kv_transfer_ms_p50": round(statistics.median(kv_exposed), 3),
+            "kv_transfer_ms_p50": round(statistics.median(iso), 3),
+            "kv_transfer": {
+                "definition": "one request's KV hand-off on its own: all layers encoded, pushed and decoded into "
+                              "the paged cache, device time from a common start to the last layer ingested, max "
+                              "over ranks (median of %d)" % len(iso),
+                "roofline_ms": round(_handoff_roofline_ms(raw, payload, args.gpus), 4),
+                "fraction_of_roofline": round(_handoff_roofline_ms(raw, payload, args.gpus)
+                                              / statistics.median(iso), 3),
+                "roofline": "max((raw + payload bytes) per GPU side / measured HBM copy GB/s, payload / 770 GB/s "
+                            "NVLink per direction); colocated: both sides on one GPU",
+            },
+            "kv_transfer_exposed_ms_p50": round(statistics.median(kv_exposed), 3),
+            "kv_handoff_ms_p50": round(statistics.median(kv_handoff), 3),
+            "recon": recon,
             "prefill_ms_p50": round(statistics.median(prefill), 3),
             "kv_ready_ms_p50": round(statistics.median(ingest), 3),
             "decode_ms_per_token": round(statistics.median(decode_ms) / max(1, args.max_new - 1), 4),

@@ -39,6 +39,7 @@
 #include "attention_decode_kernels.cuh"
 #include "common.cuh"
 #include "ops.h"
+#include "paged_decode_noalloc.h"
 
 namespace {
 
@@ -54,22 +55,28 @@ static __device__ __align__(256) float g_decode_scratch[kScratchFloats];
 std::mutex g_mutex;
 float* g_scratch_ptr[kMaxDevices] = {};
 
-enum NoallocStatus : int {
-  KVS_NOALLOC_OK = 0,
-  KVS_NOALLOC_BAD_ARGUMENT = 1,
-  KVS_NOALLOC_TOO_LARGE = 2,
-  KVS_NOALLOC_CUDA_ERROR = 3,
-};
+// cudaError_t of the last failing CUDA call, per calling thread.
+thread_local int t_last_cuda_error = 0;
+
+int cuda_failed(cudaError_t e) {
+  t_last_cuda_error = int(e);
+  return KVS_NOALLOC_CUDA_ERROR;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Device address of the scratch array for the current device (looked up once).
 int scratch_for_current_device(float** out) {
   int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return KVS_NOALLOC_CUDA_ERROR;
+  const cudaError_t de = cudaGetDevice(&dev);
+  if (de != cudaSuccess) return cuda_failed(de);
+  if (dev < 0 || dev >= kMaxDevices) return cuda_failed(cudaErrorInvalidDevice);
   std::lock_guard<std::mutex> lock(g_mutex);
   if (g_scratch_ptr[dev] == nullptr) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
-    if (e != cudaSuccess || p == nullptr) return KVS_NOALLOC_CUDA_ERROR;
+    if (e != cudaSuccess) return cuda_failed(e);
+    if (p == nullptr) return cuda_failed(cudaErrorInvalidSymbol);
     g_scratch_ptr[dev] = static_cast<float*>(p);
   }
   *out = g_scratch_ptr[dev];
@@ -83,23 +90,30 @@ extern "C" {
 __attribute__((visibility("default"))) const char* kvs_noalloc_error_string(int code) {
   switch (code) {
     case KVS_NOALLOC_OK: return "ok";
-    case KVS_NOALLOC_BAD_ARGUMENT: return "invalid argument (shapes, head_dim 64/128, 1/2/4/8 query heads per KV head)";
+    case KVS_NOALLOC_BAD_ARGUMENT:
+      return "invalid argument (null pointer, head_dim not 64/128, not 1/2/4/8 query heads per KV head, "
+             "pointer not 16-byte aligned or element stride not a multiple of 8); nothing was launched";
     case KVS_NOALLOC_TOO_LARGE:
-      return "batch x query_heads x splits exceeds the fixed scratch capacity of 2048 records";
-    case KVS_NOALLOC_CUDA_ERROR: return "CUDA error (see cudaGetLastError)";
+      return "batch x query_heads x splits exceeds the fixed scratch capacity of 2048 records; nothing was launched";
+    case KVS_NOALLOC_CUDA_ERROR: return "a CUDA call failed (its code: kvs_noalloc_last_cuda_error())";
+    case KVS_NOALLOC_PENDING_ERROR:
+      return "the calling thread had an unread CUDA error before the call; nothing was launched";
     default: return "unknown status";
   }
 }
 
 __attribute__((visibility("default"))) int64_t kvs_paged_decode_noalloc_capacity(void) { return kMaxRecords; }
 
+__attribute__((visibility("default"))) int kvs_noalloc_last_cuda_error(void) { return t_last_cuda_error; }
+
 // Single-token GQA attention over a paged KV cache, like the regular entry
-// point, without allocating.  Layouts (bf16, innermost dimension contiguous):
+// point, without allocating (declared in paged_decode_noalloc.h).  Layouts
+// (bf16, innermost dimension contiguous):
 //   q       [batch, num_q_heads, head_dim]          (q_batch_stride elements between rows)
 //   k/v     [num_blocks, block_size, num_kv_heads, head_dim] with the given strides
 //   out     [batch, num_q_heads, head_dim]          (out_batch_stride elements between rows)
 //   block_tables int32 [batch, block_table_stride], context_lens int32 [batch]
-// Returns 0 on success or a status code (kvs_noalloc_error_string).
+// Returns 0 on success or a KvsNoallocStatus code (kvs_noalloc_error_string).
 __attribute__((visibility("default"))) int kvs_paged_decode_attention_noalloc(
     const void* q, int64_t q_batch_stride, const void* k_cache, const void* v_cache, int64_t block_stride,
     int64_t token_stride, int64_t head_stride, const int32_t* block_tables, int64_t block_table_stride,
@@ -113,6 +127,20 @@ __attribute__((visibility("default"))) int kvs_paged_decode_attention_noalloc(
   if (head_dim != 64 && head_dim != 128) return KVS_NOALLOC_BAD_ARGUMENT;
   const int G = num_q_heads / num_kv_heads;
   if (G != 1 && G != 2 && G != 4 && G != 8) return KVS_NOALLOC_BAD_ARGUMENT;
+  // the kernels move 16-byte vectors of q, K, V and out: every base pointer
+  // and every element stride (bf16, 8 per vector) must keep that alignment
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out)) return KVS_NOALLOC_BAD_ARGUMENT;
+  if (q_batch_stride % 8 || block_stride % 8 || token_stride % 8 || head_stride % 8 || out_batch_stride % 8)
+    return KVS_NOALLOC_BAD_ARGUMENT;
+  // q/out rows hold num_q_heads contiguous heads; K/V heads must not overlap
+  // (token and block strides are free: NHD and HND caches both work)
+  if (q_batch_stride < int64_t(num_q_heads) * head_dim || out_batch_stride < int64_t(num_q_heads) * head_dim ||
+      head_stride < head_dim || token_stride < 1 || block_stride < 1 || block_table_stride < 1)
+    return KVS_NOALLOC_BAD_ARGUMENT;
+  // an error left unread by earlier work is the caller's; do not clear it and
+  // do not report it as this call's failure
+  if (cudaPeekAtLastError() != cudaSuccess) return KVS_NOALLOC_PENDING_ERROR;
+  t_last_cuda_error = 0;
   int64_t splits = paged_decode_splits(batch, num_kv_heads, max_context);
   const int chunk = int(std::max<int64_t>(16, ((max_context + splits - 1) / splits + 15) / 16 * 16));
   splits = (max_context + chunk - 1) / chunk;
@@ -139,14 +167,19 @@ __attribute__((visibility("default"))) int kvs_paged_decode_attention_noalloc(
     launch_decode<64>(G, grid, st, qp, q_batch_stride, kp, vp, block_stride, token_stride, head_stride, block_tables,
                       block_table_stride, context_lens, block_size, num_q_heads, int(splits), chunk, sl2, part_o,
                       part_ml, op, out_batch_stride);
+  // no error was pending at entry, so an error now belongs to this launch
+  const cudaError_t e1 = cudaGetLastError();
+  if (e1 != cudaSuccess) return cuda_failed(e1);
   if (splits > 1) {
     dim3 g2(num_q_heads, batch);
     if (head_dim == 128)
       merge_splits_kernel<128><<<g2, 128, 0, st>>>(part_o, part_ml, num_q_heads, int(splits), op, out_batch_stride);
     else
       merge_splits_kernel<64><<<g2, 64, 0, st>>>(part_o, part_ml, num_q_heads, int(splits), op, out_batch_stride);
+    const cudaError_t e2 = cudaGetLastError();
+    if (e2 != cudaSuccess) return cuda_failed(e2);
   }
-  return cudaGetLastError() == cudaSuccess ? KVS_NOALLOC_OK : KVS_NOALLOC_CUDA_ERROR;
+  return KVS_NOALLOC_OK;
 }
 
 }  // extern "C"

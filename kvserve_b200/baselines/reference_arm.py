@@ -1,16 +1,35 @@
-"""The reference arm of ``bench.py``: the unmodified reference (``kvserve_v1``,
-installed in ``baseline/_ref``) driven through its own public API on the same
-workload as this framework's arm.
+"""The reference arm of ``bench.py``: the reference (``kvserve_v1``, installed
+unmodified in ``baseline/_ref``) driven through its own public API on the
+same workload as this framework's arm.
 
-Public API used, exactly as the reference documents and tests it
-(examples/external_connector_config.py:21-50, tests/test_pd_with_compression.py:399-478):
-two vLLM V1 engines, a ``kv_producer`` (prefill) and a ``kv_consumer``
-(decode), each built with ``KVTransferConfig(kv_connector="CompressedKVConnector",
+Public API used, as the reference documents and tests it
+(examples/external_connector_config.py:21-50, tests/test_pd_with_compression.py:399-478,
+tests/test_kvserve.py:411-614): two vLLM V1 engines, a ``kv_producer``
+(prefill) and a ``kv_consumer`` (decode), each built with
+``KVTransferConfig(kv_connector="CompressedKVConnector",
 kv_connector_module_path="kvserve_v1.connector.compressed_kv_connector", ...)``
 and ``kv_connector_extra_config={"compression": <profile>}``; requests carry a
 shared ``transfer_id`` in ``SamplingParams.extra_args["kv_transfer_params"]``.
 KV moves through the reference's ``NcclTransport`` (ZMQ control + NCCL data)
 after its modular compression pipeline.
+
+The run has three parts, all on reference code:
+
+1. **Stock check** (tiny model, one request): the unmodified stack on the
+   image's vLLM 0.22.  Its consumer fails in ``start_load_kv``: it reads
+   ``forward_context.virtual_engine`` and indexes ``layer.kv_cache`` by it,
+   an API of the older vLLM it was written for.  The captured exception is
+   printed in the JSON line (``stock_path``).
+2. **PD serving** (the metric): the same engines with a vLLM-API adapter
+   (:mod:`kvserve_b200.baselines.vllm_compat`, a vLLM plugin that hands the
+   connector the forward context in the older shape; the reference's code is
+   not changed).  TTFT per request, host clock.
+3. **Hand-off alone**: the reference connector's data path without vLLM
+   (compress, wire, ``NcclTransport``, decompress, inject) on synthetic KV of
+   the request's shape: the per-request KV-transfer time.
+
+Plus the reconstruction error of the profile on the synthetic KV that the
+framework's arm measures too.
 
 Workload: a Llama-3.1-8B-shaped model (config.json written to a temp dir;
 ``load_format="dummy"`` gives random-init bf16 weights, as in this
@@ -30,7 +49,7 @@ available: the reference's transport is NCCL between two engines, and NCCL
 refuses two ranks on one device.
 
 Timing (host clock; vLLM's internals are not instrumented so that the stock
-path runs unmodified): every request starts after a barrier of all ranks at a
+path runs as shipped): every request starts after a barrier of all ranks at a
 shared wall-clock instant ``t0``; the producer serves the prompt with one
 output token (the KV is compressed and sent by the connector's
 ``wait_for_save``); the consumer, sequenced after the producer like the
@@ -50,8 +69,8 @@ import tempfile
 import time
 from typing import Optional
 
-REF_DIR = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
-                       "baseline", "_ref")
+REPO_ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+REF_DIR = os.path.join(REPO_ROOT, "baseline", "_ref")
 
 _TORCHRUN_ENV = ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "GROUP_RANK", "GROUP_WORLD_SIZE",
                  "ROLE_RANK", "ROLE_WORLD_SIZE", "ROLE_NAME", "MASTER_ADDR", "MASTER_PORT",
@@ -123,8 +142,8 @@ def write_model_dir(cfg: dict) -> str:
     return d
 
 
-def _free_port_block(n: int) -> int:
-    for base in range(31000, 60000, 97):
+def _free_port_block(n: int, first: int = 31000) -> int:
+    for base in range(first, 60000, 97):
         socks = []
         try:
             for i in range(n):
@@ -152,23 +171,64 @@ class _Barrier:
         self.store = dist.PrefixStore("kvs_reference_arm", base)
         self.rank, self.world, self.n = rank, world, 0
 
-    def wait(self) -> None:
-        self.n += 1
-        key = f"barrier{self.n}"
-        self.store.add(key, 1)
-        self.store.wait([f"{key}_open"]) if self.rank else self._open(key)
-
-    def _open(self, key: str) -> None:
-        while int(self.store.add(key, 0)) < self.world:
+    def wait(self, name: Optional[str] = None, allow_failed: bool = False) -> None:
+        """Barrier of all ranks.  Unnamed barriers are numbered in call order;
+        while one is pending, a published failure ends it with ArmFailure
+        (unless ``allow_failed``: the barrier that every rank reaches on every
+        path is named and waits regardless)."""
+        if name is None:
+            self.n += 1
+            name = f"barrier{self.n}"
+        self.store.add(name, 1)
+        while True:
+            if self.rank == 0 and int(self.store.add(name, 0)) >= self.world:
+                self.store.set(f"{name}_open", "1")
+            if self.store.check([f"{name}_open"]):
+                return
+            if not allow_failed and self.failed():
+                raise ArmFailure(self.failed())
             time.sleep(0.002)
-        self.store.set(f"{key}_open", "1")
+
+    def failed(self) -> Optional[str]:
+        if self.store.check(["failed"]):
+            return self.store.get("failed").decode()
+        return None
 
     def set(self, key: str, value: str) -> None:
         self.store.set(key, value)
 
     def get(self, key: str) -> str:
-        self.store.wait([key])
+        while not self.store.check([key]):
+            if self.failed() and key != "failed":
+                raise ArmFailure(self.failed())
+            time.sleep(0.002)
         return self.store.get(key).decode()
+
+
+class ArmFailure(RuntimeError):
+    """A role of the reference arm failed; the message is the captured error."""
+
+
+def _ref_env(role: str, tp: int, world: int, adapter_dir: Optional[str]) -> None:
+    """Environment of a reference role: its GPUs, the reference package and,
+    for the adapted run, the vLLM plugin directory on the import path."""
+    gpus = range(0, tp) if role == "producer" else range(tp, world)
+    os.environ["CUDA_VISIBLE_DEVICES"] = ",".join(str(g) for g in gpus)
+    paths = [REF_DIR, REPO_ROOT] + ([adapter_dir] if adapter_dir else [])
+    os.environ["PYTHONPATH"] = os.pathsep.join(paths + [os.environ.get("PYTHONPATH", "")]).rstrip(os.pathsep)
+    for pth in reversed(paths):
+        if pth not in sys.path:
+            sys.path.insert(0, pth)
+
+
+def _role_call(bar: "_Barrier", key: str, fn):
+    """Run ``fn`` and publish failure (``failed`` key) so no rank waits forever."""
+    try:
+        return fn()
+    except BaseException as exc:  # noqa: BLE001 - the text is the result
+        msg = f"{key}: {type(exc).__name__}: {exc}"[:600]
+        bar.set("failed", msg)
+        raise ArmFailure(msg) from exc
 
 
 def run(args, emit) -> None:
@@ -185,27 +245,125 @@ def run(args, emit) -> None:
     tp = world // 2
     role = "producer" if rank == 0 else "consumer" if rank == tp else "idle"
     if rank == 0:
-        bar.set("kv_port", str(_free_port_block(tp)))
-    kv_port = int(bar.get("kv_port"))
-
+        bar.set("ports", json.dumps([_free_port_block(max(2, tp), 31000 + 200 * i) for i in range(3)]))
+    ports = json.loads(bar.get("ports"))
     for k in _TORCHRUN_ENV:
         os.environ.pop(k, None)
-    if role != "idle":
-        gpus = range(0, tp) if role == "producer" else range(tp, world)
-        os.environ["CUDA_VISIBLE_DEVICES"] = ",".join(str(g) for g in gpus)
-        os.environ["PYTHONPATH"] = REF_DIR + os.pathsep + os.environ.get("PYTHONPATH", "")
-        if REF_DIR not in sys.path:
-            sys.path.insert(0, REF_DIR)
+    mode = getattr(args, "ref_engine", "vllm")
+    out: dict = {"impl": "reference", "metric": args.metric, "n_gpus": world, "steps": args.steps,
+                 "warmup": args.warmup}
+    try:
+        if mode == "handoff":
+            if role != "idle":
+                _ref_env(role, tp, world, None)
+            out.update(_run_handoff(args, bar, rank, world, role, ports[2]))
+            out["unavailable"] = "hand-off only (--ref-engine handoff): no TTFT"
+        else:
+            stock = _stock_check(args, bar, rank, role, tp, world, ports[0])
+            out["stock_path"] = stock
+            if mode == "stock":
+                out["unavailable"] = f"stock reference on vLLM 0.22: {stock}"
+            else:
+                adapter_dir = None
+                if role != "idle":
+                    from .vllm_compat import install_entry_point
+                    adapter_dir = install_entry_point(tempfile.mkdtemp(prefix="kvs_ref_vllm_plugin_"))
+                    _ref_env(role, tp, world, adapter_dir)
+                out.update(_run_vllm(args, bar, rank, world, role, tp, ports[1]))
+                bar.wait()
+                ho = _run_handoff(args, bar, rank, world, role, ports[2])
+                out["kv_transfer_ms_p50"] = ho.pop("kv_transfer_ms_p50")
+                out["kv_transfer"] = ho
+                if rank == 0:
+                    out["recon"] = _reference_recon(args)
+    except ArmFailure as exc:
+        out = {"impl": "reference", "unavailable": str(exc), "stock_path": out.get("stock_path")}
+    bar.wait("final", allow_failed=True)
+    if rank == 0:
+        if bar.failed():
+            out = {"impl": "reference", "unavailable": f"reference run failed: {bar.failed()}",
+                   "stock_path": out.get("stock_path")}
+        emit(out)
 
-    if getattr(args, "ref_engine", "handoff") == "handoff":
-        _run_handoff(args, emit, bar, rank, world, role, kv_port)
-        return
+
+def _tiny_model_dir() -> str:
+    cfg = dict(LLAMA_8B_CONFIG, hidden_size=256, intermediate_size=512, num_attention_heads=4,
+               num_key_value_heads=2, head_dim=64, num_hidden_layers=2, vocab_size=1024,
+               max_position_embeddings=4096)
+    return write_model_dir(cfg)
+
+
+def _stock_child(role: str, kv_port: int, q) -> None:
+    """One role of the stock check in a child process: a tiny model, the
+    unmodified reference connector, vLLM in-process (so an exception raised
+    in the connector reaches ``generate`` with its own text)."""
+    os.environ["VLLM_ENABLE_V1_MULTIPROCESSING"] = "0"
+    try:
+        from vllm import LLM, SamplingParams
+        from vllm.config import KVTransferConfig
+        from vllm.inputs import TokensPrompt
+        kv_cfg = KVTransferConfig(kv_connector="CompressedKVConnector",
+                                  kv_connector_module_path="kvserve_v1.connector.compressed_kv_connector",
+                                  kv_role="kv_producer" if role == "producer" else "kv_consumer",
+                                  kv_rank=0 if role == "producer" else 1, kv_parallel_size=2, kv_ip="127.0.0.1",
+                                  kv_port=kv_port, kv_connector_extra_config={"compression": None})
+        llm = LLM(model=_tiny_model_dir(), load_format="dummy", skip_tokenizer_init=True, dtype="bfloat16",
+                  max_model_len=256, enforce_eager=True, gpu_memory_utilization=0.1, kv_transfer_config=kv_cfg,
+                  attention_backend=REF_ATTENTION_BACKEND, seed=0)
+        q.put(("ready", ""))
+        # the consumer's connector waits (its own load timeout) for the payload,
+        # so both roles can issue the request as soon as their engine is up
+        sp = SamplingParams(max_tokens=2, temperature=0.0, ignore_eos=True, detokenize=False,
+                            extra_args={"kv_transfer_params": {"transfer_id": "kvs-stock-0"}})
+        llm.generate([TokensPrompt(prompt_token_ids=list(range(1, 65)))], sampling_params=sp, use_tqdm=False)
+        q.put(("ok", "served one request"))
+    except BaseException as exc:  # noqa: BLE001 - reported to the parent
+        import traceback
+        tb = traceback.extract_tb(exc.__traceback__)
+        where = next((f"{os.path.basename(f.filename)}:{f.lineno}" for f in reversed(tb)
+                      if "kvserve_v1" in f.filename), "")
+        q.put(("error", f"{type(exc).__name__}: {exc}" + (f" (at {where})" if where else "")))
+    finally:
+        os._exit(0)
+
+
+def _stock_check(args, bar: "_Barrier", rank: int, role: str, tp: int, world: int, kv_port: int) -> str:
+    """Run one request through the unmodified stack (tiny model, TP 1) and
+    return what happened on the consumer (the captured exception text)."""
+    import multiprocessing as mp
+    result = ""
+    if role != "idle":
+        _ref_env(role, tp, world, None)
+        os.environ["CUDA_VISIBLE_DEVICES"] = str(0 if role == "producer" else tp)   # TP 1
+        ctx = mp.get_context("spawn")
+        q = ctx.Queue()
+        child = ctx.Process(target=_stock_child, args=(role, kv_port, q), daemon=True)
+        child.start()
+        try:
+            state, msg = q.get(timeout=240)
+            if state == "ready":
+                bar.set(f"stock_ready_{role}", "1")
+                state, msg = q.get(timeout=180)
+            result = msg
+        except Exception as exc:  # noqa: BLE001 - a stuck child is a result too
+            result = f"no answer from the {role} ({type(exc).__name__})"
+        finally:
+            child.join(10)
+            if child.is_alive():
+                child.kill()
+                child.join(10)
+        bar.set(f"stock_{role}", result)
+    bar.wait("stock_done", allow_failed=True)
+    return bar.get("stock_consumer") if rank == 0 else result
+
+
+def _run_vllm(args, bar: "_Barrier", rank: int, world: int, role: str, tp: int, kv_port: int) -> dict:
+    """PD serving through vLLM with the reference connector (adapted API)."""
     n_req = args.warmup + args.steps
-    results: list[dict] = []
     llm = None
     try:
         if role != "idle":
-            llm = _build_engine(args, role, tp, kv_port)
+            llm = _role_call(bar, f"{role} engine start", lambda: _build_engine(args, role, tp, kv_port))
         bar.wait()  # both engines up
         import random
         rng = random.Random(1234)
@@ -223,191 +381,189 @@ def run(args, emit) -> None:
                 bar.set(f"t0_{i}", repr(t0))
             tid = f"kvs-bench-{i}"
             if role == "producer":
-                out = _generate(llm, prompts[i], 1, tid)
+                _role_call(bar, "producer request", lambda: _generate(llm, prompts[i], 1, tid))
                 bar.set(f"prefill_done_{i}", repr(time.time()))
-                results.append({"prefill_ms": 1e3 * (time.time() - t0), "tokens": len(out)})
             elif role == "consumer":
                 t0 = float(bar.get(f"t0_{i}"))
                 p_done = float(bar.get(f"prefill_done_{i}"))
                 t_start = time.time()
-                o = _generate(llm, prompts[i], args.max_new, tid, want_output=True)
+                o = _role_call(bar, "consumer request",
+                               lambda: _generate(llm, prompts[i], args.max_new, tid, want_output=True))
                 t_end = time.time()
                 m = o.metrics
                 first = (m.arrival_time + m.first_token_latency) if m is not None and m.first_token_latency else None
-                results.append({
+                bar.set(f"consumer_{i}", json.dumps({
                     "ttft_ms": 1e3 * (first - t0) if first else float("nan"),
-                    "request_ms": 1e3 * (t_end - t0),
-                    "prefill_ms": 1e3 * (p_done - t0),
-                    "consumer_start_ms": 1e3 * (t_start - t0),
-                    "tokens": len(o.outputs[0].token_ids),
-                })
-                bar.set(f"consumer_{i}", json.dumps(results[-1]))
+                    "request_ms": 1e3 * (t_end - t0), "prefill_ms": 1e3 * (p_done - t0),
+                    "consumer_start_ms": 1e3 * (t_start - t0), "tokens": len(o.outputs[0].token_ids)}))
         bar.wait()
         clocks = sampler.stop() if sampler else None
-        if rank == 0:
-            rows = [json.loads(bar.get(f"consumer_{i}")) for i in range(args.warmup, n_req)]
-            ttft = [r["ttft_ms"] for r in rows]
-            req = [r["request_ms"] for r in rows]
-            pre = [r["prefill_ms"] for r in rows]
-            emit({
-                "impl": "reference",
-                "metric": args.metric,
-                "value": round(statistics.median(ttft), 3),
-                "unit": "ms (TTFT p50)",
-                "n_gpus": world,
-                "steps": args.steps,
-                "warmup": args.warmup,
-                "ms_per_step": round(statistics.mean(req), 3),
-                "higher_is_better": False,
-                "scaling": "strong",
-                "vs_baseline": None,
-                "dtype": "bf16",
-                "data": "synthetic (vLLM dummy random-init weights of the named architecture, uniform-random "
-                        "prompt token ids)",
-                "prefill_ms_p50": round(statistics.median(pre), 3),
-                "handoff_to_first_token_ms_p50": round(statistics.median(t - p for t, p in zip(ttft, pre)), 3),
-                "decode_ms_per_token": round(statistics.median(r - t for r, t in zip(req, ttft))
-                                             / max(1, args.max_new - 1), 4),
-                "output_tokens": rows[0]["tokens"],
-                "config": {"model": "llama-3.1-8b", "layers": LLAMA_8B_CONFIG["num_hidden_layers"],
-                           "global_batch": 1, "seq_len": args.prompt_len, "max_new_tokens": args.max_new,
-                           "parallelism": f"{tp}P{tp}D-tp{tp}", "profile": args.profile,
-                           "engine": f"vLLM V1 + kvserve_v1 CompressedKVConnector/NcclTransport "
-                                     f"(attention {REF_ATTENTION_BACKEND}, "
-                                     f"enforce_eager={not getattr(args, 'ref_cuda_graphs', False)}, "
-                                     f"chunked prefill off)",
-                           "l2": "inputs larger than L2 (16 GB weights, 1 GiB raw KV per request)"},
-                "e2e": {"value": round(statistics.median(ttft), 3),
-                        "unit": "ms (TTFT p50, host clock from the shared request start to the consumer's first "
-                                "token through vLLM's public LLM.generate API)",
-                        "h2d_bytes_per_step": 8 * args.prompt_len, "d2h_bytes_per_step": 8 * (args.max_new + 1),
-                        "request_ms_p50": round(statistics.median(req), 3)},
-                "timing": "host clock (the reference's stock path is not instrumented with device events)",
-                "gpu_launches": None,
-                "clocks": clocks,
-            })
     finally:
         if llm is not None:
             _shutdown(llm)
+    if rank != 0:
+        return {}
+    rows = [json.loads(bar.get(f"consumer_{i}")) for i in range(args.warmup, n_req)]
+    ttft = [r["ttft_ms"] for r in rows]
+    req = [r["request_ms"] for r in rows]
+    pre = [r["prefill_ms"] for r in rows]
+    return {
+        "value": round(statistics.median(ttft), 3),
+        "unit": "ms (TTFT p50)",
+        "ms_per_step": round(statistics.mean(req), 3),
+        "higher_is_better": False,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (vLLM dummy random-init weights of the named architecture, uniform-random "
+                "prompt token ids)",
+        "prefill_and_send_ms_p50": round(statistics.median(pre), 3),
+        "handoff_to_first_token_ms_p50": round(statistics.median(t - p for t, p in zip(ttft, pre)), 3),
+        "decode_ms_per_token": round(statistics.median(r - t for r, t in zip(req, ttft))
+                                     / max(1, args.max_new - 1), 4),
+        "output_tokens": rows[0]["tokens"],
+        "config": {"model": "llama-3.1-8b", "layers": LLAMA_8B_CONFIG["num_hidden_layers"],
+                   "global_batch": 1, "seq_len": args.prompt_len, "max_new_tokens": args.max_new,
+                   "parallelism": f"{tp}P{tp}D-tp{tp}", "profile": args.profile,
+                   "engine": f"vLLM 0.22 V1 + kvserve_v1 CompressedKVConnector/NcclTransport "
+                             f"(attention {REF_ATTENTION_BACKEND}, "
+                             f"enforce_eager={not getattr(args, 'ref_cuda_graphs', False)}, chunked prefill off)",
+                   "vllm_api_adapter": "kvserve_b200.baselines.vllm_compat: forward_context.virtual_engine = 0 "
+                                       "and layer.kv_cache as a per-virtual-engine list for the connector's "
+                                       "start_load_kv (reference code unchanged)",
+                   "l2": "inputs larger than L2 (16 GB weights, 1 GiB raw KV per request)"},
+        "e2e": {"value": round(statistics.median(ttft), 3),
+                "unit": "ms (TTFT p50, host clock from the shared request start to the consumer's first "
+                        "token through vLLM's public LLM.generate API)",
+                "h2d_bytes_per_step": 8 * args.prompt_len, "d2h_bytes_per_step": 8 * (args.max_new + 1),
+                "request_ms_p50": round(statistics.median(req), 3)},
+        "timing": "host clock (the reference's stock path is not instrumented with device events)",
+        "gpu_launches": None,
+        "clocks": clocks,
+    }
 
 
-VLLM_INCOMPATIBLE = ("kvserve_v1's CompressedKVConnector does not run on the image's vLLM 0.22: its consumer "
-                     "injects KV with forward_context.virtual_engine (removed; layer.kv_cache is one tensor), "
-                     "so the decode engine dies on the first request; TTFT of the reference is unmeasured, "
-                     "its KV hand-off path is measured instead (kv_transfer_ms_p50)")
+def _reference_recon(args) -> Optional[dict]:
+    """Reconstruction error and ratio of the reference's own adapter on the
+    synthetic KV the framework's arm measures (same generator, 4 layers)."""
+    profile = reference_profile(args.profile)
+    if profile is None:
+        return {"rel_mse": 0.0, "mse": 0.0, "compression_ratio": 1.0}
+    import torch
+    from kvserve_v1.compression.manager import KVCompressionAdapter
+    from ..engine.fidelity import error_stats, synthetic_kv
+    H, D, bs, L = LLAMA_8B_CONFIG["num_key_value_heads"], 128, 16, 4
+    T = (args.prompt_len // bs) * bs
+    kv = synthetic_kv(L, T, H, D, 0, torch.device("cuda", 0))          # [L, 2, T, H, D]
+    stacked = kv.view(L, 2, T // bs, bs, H, D)
+    ad = KVCompressionAdapter(profile, H, D)
+    c = ad.compress(stacked, "kvs-recon")
+    out = ad.decompress(c).view(L, 2, T, H, D)
+    torch.cuda.synchronize()
+    st = error_stats(kv, out)
+    st.update({"compression_ratio": round(c.original_size / c.compressed_size, 3), "layers": L, "tokens": T,
+               "kv_heads": H, "head_dim": D,
+               "data": "synthetic: V ~ N(0,1), K ~ N(0,1) with 4 outlier channels x8 per head, seed 0"})
+    return st
 
 
-def _run_handoff(args, emit, bar, rank: int, world: int, role: str, kv_port: int) -> None:
+def _run_handoff(args, bar, rank: int, world: int, role: str, kv_port: int) -> dict:
     """The reference's KV hand-off data path exactly as its connector runs it
     (compressed_kv_connector.py:393-470 producer, 235-372 consumer), without
     vLLM: ``KVCompressionAdapter.compress`` of the stacked request KV
     ``[L, 2, blocks, block_size, H, D]``, ``build_wire``, ``NcclTransport
     .send_bundle``; on the consumer ``drain_received``, ``restore_from_wire``,
     ``decompress`` and ``inject_kv_into_layer_by_blocks`` into a paged cache.
-    Time = consumer's KV-in-cache instant - shared start (host clock after
-    device synchronisation), i.e. the per-request KV-transfer time, max over
-    ranks by construction.  Synthetic N(0, 1) KV of the bench shape."""
+    One channel with one TP rank's heads (``8 / TP``; the connector runs one
+    such channel per TP rank, in parallel).  Time = consumer's KV-in-cache
+    instant - shared start (host clock after device synchronisation), i.e.
+    the per-request KV-transfer time, max over ranks by construction.
+    Synthetic N(0, 1) KV of the bench shape.  Returns rank 0's summary."""
     import torch
-    L, H, D, bs = LLAMA_8B_CONFIG["num_hidden_layers"], LLAMA_8B_CONFIG["num_key_value_heads"], 128, 16
+    tp = max(1, world // 2)
+    L, D, bs = LLAMA_8B_CONFIG["num_hidden_layers"], 128, 16
+    H = max(1, LLAMA_8B_CONFIG["num_key_value_heads"] // tp)
     nblk = (args.prompt_len - 1 + bs - 1) // bs
     n_req = args.warmup + args.steps
     profile = reference_profile(args.profile)
-    rows = []
     t = None
-    if role != "idle":
-        torch.cuda.set_device(0)
-        from kvserve_v1.transport.nccl_transport import NcclTransport
-        from kvserve_v1.compression.manager import KVCompressionAdapter, add_sentinel
-        t = NcclTransport(is_sender=(role == "producer"), host="127.0.0.1", port=kv_port, local_rank=0,
-                          channel_rank=0, recv_buffer_size=4 * 2 ** 30)
-        ad = KVCompressionAdapter(profile, H, D) if profile is not None else None
-        names = [f"model.layers.{i}.self_attn.attn" for i in range(L)]
-        g = torch.Generator(device="cuda").manual_seed(1234)
-        if role == "producer":
-            from kvserve_v1.compression.wire import build_wire
-            from kvserve_v1.connector.compressed_kv_connector import _max_nccl_chunk_bytes
-            stacked = torch.randn((L, 2, nblk, bs, H, D), generator=g, device="cuda").to(torch.bfloat16)
-        else:
-            from kvserve_v1.compression.wire import CompressedWire, restore_from_wire
-            from kvserve_v1.compression.manager import strip_sentinel, is_compressed_layer_names
-            from kvserve_v1.utils.kv_utils import inject_kv_into_layer_by_blocks
-            cache = torch.empty((L, 2, nblk + 64, bs, H, D), dtype=torch.bfloat16, device="cuda")
-            block_ids = list(range(7, 7 + nblk))
-    sampler = None
     try:
+        if role != "idle":
+            torch.cuda.set_device(0)
+            from kvserve_v1.transport.nccl_transport import NcclTransport
+            from kvserve_v1.compression.manager import KVCompressionAdapter, add_sentinel
+            t = _role_call(bar, f"{role} transport", lambda: NcclTransport(
+                is_sender=(role == "producer"), host="127.0.0.1", port=kv_port, local_rank=0, channel_rank=0,
+                recv_buffer_size=4 * 2 ** 30))
+            ad = KVCompressionAdapter(profile, H, D, tp_rank=0, tp_size=tp) if profile is not None else None
+            names = [f"model.layers.{i}.self_attn.attn" for i in range(L)]
+            g = torch.Generator(device="cuda").manual_seed(1234)
+            if role == "producer":
+                from kvserve_v1.compression.wire import build_wire
+                from kvserve_v1.connector.compressed_kv_connector import _max_nccl_chunk_bytes
+                stacked = torch.randn((L, 2, nblk, bs, H, D), generator=g, device="cuda").to(torch.bfloat16)
+            else:
+                from kvserve_v1.compression.wire import CompressedWire, restore_from_wire
+                from kvserve_v1.compression.manager import is_compressed_layer_names
+                from kvserve_v1.utils.kv_utils import inject_kv_into_layer_by_blocks
+                cache = torch.empty((L, 2, nblk + 64, bs, H, D), dtype=torch.bfloat16, device="cuda")
+                block_ids = list(range(7, 7 + nblk))
         for i in range(n_req):
-            if i == args.warmup and rank == 0:
-                from ..utils.clocks import ClockSampler
-                sampler = ClockSampler(list(range(world)))
-                sampler.start()
             if t is not None:
                 torch.cuda.synchronize()
             bar.wait()
             if rank == 0:
-                bar.set(f"t0_{i}", repr(time.time()))
+                bar.set(f"h_t0_{i}", repr(time.time()))
             tid = f"kvs-ref-{i}"
             if role == "producer":
-                t0 = float(bar.get(f"t0_{i}"))
-                if ad is not None:
-                    c = ad.compress(stacked, tid)
-                    wire = build_wire(c, _max_nccl_chunk_bytes())
-                    t.send_bundle(tid, add_sentinel(names), wire.meta, wire.body_chunks, wire.aux_tensors)
-                    nbytes = wire.nbytes
-                else:
-                    t.send(tid, names, stacked)
-                    nbytes = stacked.numel() * 2
-                t.wait_for_sent()
-                torch.cuda.synchronize()
-                bar.set(f"sent_{i}", json.dumps({"sent_ms": 1e3 * (time.time() - t0), "bytes": int(nbytes)}))
+                t0 = float(bar.get(f"h_t0_{i}"))
+
+                def send():
+                    if ad is not None:
+                        c = ad.compress(stacked, tid)
+                        wire = build_wire(c, _max_nccl_chunk_bytes())
+                        t.send_bundle(tid, add_sentinel(names), wire.meta, wire.body_chunks, wire.aux_tensors)
+                        nbytes = wire.nbytes
+                    else:
+                        t.send(tid, names, stacked)
+                        nbytes = stacked.numel() * 2
+                    t.wait_for_sent()
+                    torch.cuda.synchronize()
+                    return nbytes
+                nbytes = _role_call(bar, "producer hand-off", send)
+                bar.set(f"h_sent_{i}", json.dumps({"sent_ms": 1e3 * (time.time() - t0), "bytes": int(nbytes)}))
             elif role == "consumer":
-                t0 = float(bar.get(f"t0_{i}"))
-                t.set_expected_requests([tid])
-                got = None
-                deadline = time.monotonic() + 300
-                while got is None and time.monotonic() < deadline:
-                    for key, payloads in t.drain_received().items():
-                        if key == tid:
-                            got = payloads[0]
+                t0 = float(bar.get(f"h_t0_{i}"))
+
+                def receive():
+                    t.set_expected_requests([tid])
+                    got = None
+                    deadline = time.monotonic() + 300
+                    while got is None and time.monotonic() < deadline:
+                        for key, payloads in t.drain_received().items():
+                            if key == tid:
+                                got = payloads[0]
+                        if got is None:
+                            if bar.failed():
+                                raise ArmFailure(bar.failed())
+                            time.sleep(0.001)
                     if got is None:
-                        time.sleep(0.001)
-                if got is None:
-                    raise RuntimeError(f"reference transport timed out on {tid}")
-                layer_names, payload = got
-                nb = t.payload_nbytes(payload)
-                if is_compressed_layer_names(layer_names):
-                    wire = CompressedWire(meta=payload["meta"], body_chunks=payload["body_chunks"],
-                                          aux_tensors=payload["aux_tensors"])
-                    kv = ad.decompress(restore_from_wire(wire))
-                else:
-                    kv = payload
-                for li in range(L):
-                    inject_kv_into_layer_by_blocks(cache[li], kv[li], block_ids, tid)
-                torch.cuda.synchronize()
-                t.release_received(tid, nb)
-                bar.set(f"done_{i}", repr(1e3 * (time.time() - t0)))
+                        raise RuntimeError(f"reference transport timed out on {tid}")
+                    layer_names, payload = got
+                    nb = t.payload_nbytes(payload)
+                    if is_compressed_layer_names(layer_names):
+                        wire = CompressedWire(meta=payload["meta"], body_chunks=payload["body_chunks"],
+                                              aux_tensors=payload["aux_tensors"])
+                        kv = ad.decompress(restore_from_wire(wire))
+                    else:
+                        kv = payload
+                    for li in range(L):
+                        inject_kv_into_layer_by_blocks(cache[li], kv[li], block_ids, tid)
+                    torch.cuda.synchronize()
+                    t.release_received(tid, nb)
+                _role_call(bar, "consumer hand-off", receive)
+                bar.set(f"h_done_{i}", repr(1e3 * (time.time() - t0)))
         bar.wait()
-        clocks = sampler.stop() if sampler else None
-        if rank == 0:
-            tm = [float(bar.get(f"done_{i}")) for i in range(args.warmup, n_req)]
-            sent = [json.loads(bar.get(f"sent_{i}")) for i in range(args.warmup, n_req)]
-            raw = 2 * L * nblk * bs * H * D * 2
-            emit({
-                "impl": "reference",
-                "unavailable": VLLM_INCOMPATIBLE,
-                "metric": args.metric,
-                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "kv_transfer_ms_p50": round(statistics.median(tm), 3),
-                "kv_send_ms_p50": round(statistics.median(x["sent_ms"] for x in sent), 3),
-                "kv_payload_bytes_per_request": sent[0]["bytes"],
-                "kv_raw_bytes_per_request": raw,
-                "compression_ratio": round(raw / sent[0]["bytes"], 3),
-                "config": {"model": "llama-3.1-8b (KV shape only)", "layers": L, "seq_len": args.prompt_len,
-                           "profile": args.profile, "path": "kvserve_v1 KVCompressionAdapter + CompressedWire + "
-                                                           "NcclTransport, 1 producer -> 1 consumer",
-                           "data": "synthetic N(0,1) bf16 KV"},
-                "timing": "host clock after device synchronisation, consumer end - shared start",
-                "clocks": clocks,
-            })
     finally:
         if t is not None:
             for m in ("shutdown", "close"):
@@ -418,6 +574,23 @@ def _run_handoff(args, emit, bar, rank: int, world: int, role: str, kv_port: int
                     except Exception:
                         pass
                     break
+    if rank != 0:
+        return {}
+    tm = [float(bar.get(f"h_done_{i}")) for i in range(args.warmup, n_req)]
+    sent = [json.loads(bar.get(f"h_sent_{i}")) for i in range(args.warmup, n_req)]
+    raw = 2 * L * nblk * bs * H * D * 2
+    return {
+        "kv_transfer_ms_p50": round(statistics.median(tm), 3),
+        "definition": "one TP channel's KV hand-off on its own (reference connector data path without vLLM: "
+                      "compress, CompressedWire, NcclTransport send/recv, restore, decompress, inject), host "
+                      "clock after device synchronisation, shared start to KV in the consumer's cache",
+        "kv_send_ms_p50": round(statistics.median(x["sent_ms"] for x in sent), 3),
+        "kv_payload_bytes_per_request": sent[0]["bytes"] * tp,
+        "kv_raw_bytes_per_request": raw * tp,
+        "compression_ratio": round(raw / sent[0]["bytes"], 3),
+        "heads_per_channel": H,
+        "data": "synthetic N(0,1) bf16 KV of the request's shape",
+    }
 
 
 def _build_engine(args, role: str, tp: int, kv_port: int):

@@ -56,7 +56,8 @@ except Exception:  # pragma: no cover - vLLM missing
 
 from ..compression.adapter import add_sentinel, is_compressed_layer_names, strip_sentinel
 from ..compression.wire import CompressedWire, build_wire, restore_from_wire
-from ..utils.kv_utils import extract_kv_from_layer_by_blocks, inject_kv_into_layer_by_blocks, make_slot_mapping
+from ..utils.kv_utils import (_kv_axis, extract_kv_from_layer_by_blocks, inject_kv_into_layer_by_blocks,
+                              make_slot_mapping)
 
 log = logging.getLogger("kvserve_b200.connector")
 
@@ -237,14 +238,25 @@ class CompressedKVConnector(KVConnectorBase_V1):
         self._transport.set_expected_requests([])
 
     @staticmethod
-    def inject(forward_context, names: list, stacked: torch.Tensor, req: ReqMeta) -> None:
+    def layer_cache(forward_context, name: str) -> Optional[torch.Tensor]:
+        """The paged KV cache tensor of attention layer ``name``.  vLLM 0.22
+        keeps one tensor per layer; older V1 releases kept a list with one
+        cache per virtual engine, selected by ``forward_context.virtual_engine``."""
+        layer = forward_context.no_compile_layers.get(name)
+        kv = getattr(layer, "kv_cache", None) if layer is not None else None
+        if isinstance(kv, (list, tuple)):
+            kv = kv[getattr(forward_context, "virtual_engine", 0)] if kv else None
+        if kv is None or kv.numel() == 0:
+            return None
+        return kv
+
+    @classmethod
+    def inject(cls, forward_context, names: list, stacked: torch.Tensor, req: ReqMeta) -> None:
         for i, name in enumerate(names):
-            layer = forward_context.no_compile_layers.get(name)
-            kv = getattr(layer, "kv_cache", None) if layer is not None else None
-            if kv is None:
-                continue
-            inject_kv_into_layer_by_blocks(kv[forward_context.virtual_engine], stacked[i], req.block_ids,
-                                           req.request_id)
+            kv = cls.layer_cache(forward_context, name)
+            if kv is not None:
+                data = stacked[i].transpose(0, 1) if _kv_axis(kv) == 1 else stacked[i]
+                inject_kv_into_layer_by_blocks(kv, data, req.block_ids, req.request_id)
 
     def wait_for_layer_load(self, layer_name: str) -> None:
         return
@@ -255,9 +267,13 @@ class CompressedKVConnector(KVConnectorBase_V1):
         meta = self._get_connector_metadata()
         if not isinstance(meta, CompressedKVConnectorMetadata):
             return
+        blocks_first = _kv_axis(kv_layer) == 1
         for r in meta.requests:
+            kv = extract_kv_from_layer_by_blocks(kv_layer, r.block_ids)
+            # the wire carries [2, blocks, block_size, H, D] whatever the backend
+            # (FlashInfer, vLLM's default on B200, stores [blocks, 2, ...])
             self._layer_buffers.setdefault(r.request_id, {})[layer_name] = \
-                extract_kv_from_layer_by_blocks(kv_layer, r.block_ids)
+                kv.transpose(0, 1).contiguous() if blocks_first else kv
 
     def wait_for_save(self) -> None:
         if not self.is_producer:

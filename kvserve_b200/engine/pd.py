@@ -40,6 +40,7 @@ from .transfer import KVTransfer, TransferProfile
 class RequestTiming:
     """Milliseconds from the request start on this rank (NaN where n/a)."""
     prefill_done: float = float("nan")
+    encode_start: float = float("nan")      # layer 0's encode may start (its K/V exist)
     encode_done: float = float("nan")
     ingest_done: float = float("nan")
     first_token: float = float("nan")
@@ -204,8 +205,15 @@ class PDEngine:
 
     # --------------------------------------------------------------- request
     def _barrier(self) -> None:
+        """Device-side barrier: every rank's stream waits for all ranks."""
         if self.ctx.distributed:
             dist.all_reduce(self._barrier_t, group=self.ctx.world_group)
+
+    def _host_barrier(self) -> None:
+        """Host-side barrier: returns once every rank's host has reached it
+        (so no rank is still finishing an earlier request)."""
+        if self.ctx.distributed:
+            dist.barrier(group=self.ctx.cpu_group)
 
     def generate(self, prompt_ids: torch.Tensor, max_new_tokens: Optional[int] = None,
                  return_tokens: bool = True, sync: bool = True, profile: Optional[str] = None,
@@ -220,8 +228,12 @@ class PDEngine:
         per-request device timings share a start; with ``sync=False`` a decode
         rank relies on the per-layer frame flags alone (a prefill rank that
         never publishes then surfaces as a device-side timeout status)."""
-        t_host0 = time.perf_counter()
         ctx, m = self.ctx, self.model
+        if sync:
+            # the request starts once every rank is free for it: the host clock
+            # must not charge the previous request's decode to this TTFT
+            self._host_barrier()
+        t_host0 = time.perf_counter()
         if profile is not None and profile not in self.xfers:
             raise KeyError(f"unknown transfer profile {profile!r}; have {sorted(self.xfers)}")
         xfer = self.xfers[profile or "default"]
@@ -237,7 +249,8 @@ class PDEngine:
         Tx = T
         self.seq += 1
         seq = self.seq
-        ev = {k: torch.cuda.Event(enable_timing=True) for k in ("start", "prefill", "encode", "ingest", "first", "end")}
+        ev = {k: torch.cuda.Event(enable_timing=True)
+              for k in ("start", "prefill", "enc_start", "encode", "ingest", "first", "end")}
         if sync:
             self._barrier()
         c_launch0 = ops.launches()
@@ -263,6 +276,8 @@ class PDEngine:
             def hook(l: int) -> None:
                 self.layer_events[l].record(self.compute)
                 enc.wait_event(self.layer_events[l])
+                if l == 0:
+                    ev["enc_start"].record(enc)
                 with torch.cuda.stream(enc):
                     flag = self.sender.flag_ptr(0, l) if ctx.distributed else 0
                     xfer.encode(l, self.k_buf[l, :Tx], self.v_buf[l, :Tx], self.sender.frame_ptr(0, l), flag,
@@ -321,11 +336,68 @@ class PDEngine:
         timing.first_token = e("first")
         if ctx.is_prefill:
             timing.prefill_done = e("prefill")
+            timing.encode_start = e("enc_start")
             timing.encode_done = e("encode")
         if ctx.is_decode:
             timing.ingest_done = e("ingest")
             timing.all_done = e("end")
         return GenerateResult(tokens, timing)
+
+    def measure_handoff(self, T: int, profile: Optional[str] = None) -> dict:
+        """Device time of one request's whole KV hand-off on its own: every
+        layer of the last prompt's K/V (still in the prefill buffers) encoded
+        and pushed back to back, and decoded into the paged cache, without a
+        prefill running beside it.  This is the per-request KV-transfer time
+        of the transfer path alone (the reference's connector does the same
+        work after its prefill, kvserve_v1/connector/compressed_kv_connector.py:393-497
+        and :235-372).  Milliseconds from a common device start: ``encode_ms``
+        (prefill side: last frame published) and ``ingest_ms`` (decode side:
+        last layer written), NaN where the rank has no such part."""
+        ctx = self.ctx
+        xfer = self.xfers[profile or "default"]
+        if T < 1 or T > self.max_prompt:
+            raise ValueError(f"T must be in [1, {self.max_prompt}]")
+        self._host_barrier()
+        self.seq += 1
+        seq = self.seq
+        start, enc_end, ing_end = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        self._barrier()
+        start.record(self.compute)
+        blocks = None
+        if ctx.is_decode:
+            blocks = self.kv.allocate(T)
+            table = self.kv.block_table(blocks, self.max_blocks)
+            if ctx.distributed:
+                self.ingest_stream.wait_stream(self.compute)
+                with torch.cuda.stream(self.ingest_stream):
+                    xfer.ingest_all(T, self.receiver.slot_base(0), self.receiver.frame_stride,
+                                    self.receiver.flags_base(0), self.kv.cache, table, self.status, seq,
+                                    self.ingest_timeout_ns)
+                    ing_end.record(self.ingest_stream)
+        if ctx.is_prefill:
+            enc = self.enc_stream
+            enc.wait_stream(self.compute)
+            with torch.cuda.stream(enc):
+                for l in range(self.cfg.num_layers):
+                    flag = self.sender.flag_ptr(0, l) if ctx.distributed else 0
+                    xfer.encode(l, self.k_buf[l, :T], self.v_buf[l, :T], self.sender.frame_ptr(0, l), flag, seq,
+                                self.pacing, 0.0, self.encode_ctas)
+                    if not ctx.distributed:
+                        xfer.ingest_layer(l, T, self.sender.frame_ptr(0, l), self.kv.cache, table, self.status, seq)
+                enc_end.record(enc)
+                if not ctx.distributed:
+                    ing_end.record(enc)
+        torch.cuda.synchronize(self.device)
+        if blocks is not None:
+            self.kv.release(blocks)
+        st = int(self.status[0].item())
+        if st != 0:
+            self.status.zero_()
+            raise RuntimeError(f"KV hand-off failed on rank {ctx.rank}: {ops.STATUS_NAMES.get(st, st)}")
+        nan = float("nan")
+        return {"encode_ms": start.elapsed_time(enc_end) if ctx.is_prefill else nan,
+                "ingest_ms": start.elapsed_time(ing_end) if ctx.is_decode else nan,
+                "payload_bytes": xfer.payload_bytes(T), "raw_bytes": xfer.raw_bytes(T)}
 
     def close(self) -> None:
         self._graph = None

@@ -217,3 +217,15 @@ def test_shipped_profiles_round_trip(name):
     rec = ad.decompress(c)
     err = ((rec.float() - kv.float()).norm() / kv.float().norm()).item()
     assert rec.shape == kv.shape and err < 0.6
+
+
+def test_fidelity_synthetic_kv_and_error_stats():
+    from kvserve_b200.engine.fidelity import error_stats, synthetic_kv
+    kv = synthetic_kv(2, 64, 4, 128, seed=0)
+    assert kv.shape == (2, 2, 64, 4, 128) and kv.dtype == torch.bfloat16
+    # keys carry 4 outlier channels x8: their power dwarfs the others
+    kp = kv[:, 0].float().pow(2).mean(dim=(0, 1, 2))
+    assert (kp > 16).sum() == 4
+    st = error_stats(kv, torch.zeros_like(kv))
+    assert abs(st["rel_mse"] - 1.0) < 1e-6 and abs(st["v_rel_mse"] - 1.0) < 1e-6
+    assert error_stats(kv, kv)["mse"] == 0.0

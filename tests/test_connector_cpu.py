@@ -189,3 +189,23 @@ def test_service_aware_engine_library_and_selection():
         assert p is not None and p.accuracy >= need, (need, p, info)
     assert ctl.select_profile(2e9, 3125.0, 100.0, 1e9, bucket_requirement(lib, 0.2))[0].profile_id == "k2v2"
     assert bucket_requirement(lib, 0.9999) is None    # nothing compressed is that accurate
+
+
+def test_inject_on_vllm_022_caches_both_layouts():
+    """vLLM 0.22 keeps one cache tensor per layer and has no virtual_engine;
+    FlashInfer (its B200 default) stores [blocks, 2, ...].  The wire is always
+    [2, blocks, ...]; older list-per-virtual-engine caches still work."""
+    from types import SimpleNamespace
+    from kvserve_b200.connector.compressed_kv_connector import CompressedKVConnector, ReqMeta
+    fa = torch.zeros(2, 6, 4, 2, 8)
+    fi = torch.zeros(6, 2, 4, 2, 8)
+    old = torch.zeros(2, 6, 4, 2, 8)
+    layers = {"a": SimpleNamespace(kv_cache=fa), "b": SimpleNamespace(kv_cache=fi),
+              "c": SimpleNamespace(kv_cache=[old]), "d": SimpleNamespace(kv_cache=torch.tensor([]))}
+    ctx = SimpleNamespace(no_compile_layers=layers)           # no virtual_engine attribute
+    stacked = torch.randn(4, 2, 2, 4, 2, 8)
+    req = ReqMeta("r", "t", list(range(8)), [3, 1], torch.arange(8))
+    CompressedKVConnector.inject(ctx, ["a", "b", "c", "d"], stacked, req)
+    assert torch.equal(fa[:, [3, 1]], stacked[0])
+    assert torch.equal(fi[[3, 1]], stacked[1].transpose(0, 1))
+    assert torch.equal(old[:, [3, 1]], stacked[2])

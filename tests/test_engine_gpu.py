@@ -105,3 +105,40 @@ def test_service_aware_server_colocated():
         assert paced.ingest_done > free.ingest_done + 5.0
     finally:
         eng.close()
+
+
+def test_measure_handoff_colocated_reports_device_time():
+    from kvserve_b200.engine.transfer import TransferProfile
+    prof = TransferProfile(compressed=True, hybrid_ratio=0.0, key_levels=(16, 16), value_levels=(4, 4))
+    eng = _engine(prof)
+    ids = torch.randint(0, eng.cfg.vocab, (200,), dtype=torch.int32)
+    eng.generate(ids, 2)
+    h = eng.measure_handoff(200)
+    assert 0.0 < h["ingest_ms"] < 1e3 and 0.0 < h["encode_ms"] <= h["ingest_ms"] + 1e-3
+    assert h["raw_bytes"] > h["payload_bytes"] > 0
+    eng.close()
+
+
+def test_frame_round_trip_error_matches_cpu_oracle():
+    """The reconstruction error the bench prints (GPU frame kernels) agrees
+    with the CPU oracle's on the same synthetic KV."""
+    from kvserve_b200.engine.fidelity import error_stats, frame_round_trip, synthetic_kv
+    from kvserve_b200.engine.transfer import KVTransfer, TransferProfile
+    from kvserve_b200.ops import kv_codec as kc
+    from kvserve_b200.compression.heads import rademacher_signs
+    prof = TransferProfile(compressed=True, hybrid_ratio=0.0, key_levels=(16, 16), value_levels=(4, 4))
+    L, T, H, D = 2, 512, 4, 128
+    dev = torch.device("cuda")
+    xfer = KVTransfer(prof, L, H, H, D, 0, 1, dev, T)
+    kv = synthetic_kv(L, T, H, D, seed=3, device=dev)
+    gpu = error_stats(kv, frame_round_trip(xfer, kv))
+    outs = []
+    for l in range(L):
+        spec = xfer.spec(l, T)
+        signs = rademacher_signs(prof.seed, l, H, D)
+        buf = kc.cpu_encode_frame(kv[l, 0].cpu(), kv[l, 1].cpu(), spec, xfer.orders_cpu[l], signs, layer=l)
+        k, v = kc.cpu_decode_frame(bytes(buf), spec, xfer.orders_cpu[l], signs)
+        outs.append(torch.stack([k, v]))
+    cpu = error_stats(kv.cpu(), torch.stack(outs))
+    assert gpu["k_rel_mse"] < 0.02 and gpu["v_rel_mse"] < 0.2
+    assert abs(gpu["rel_mse"] - cpu["rel_mse"]) <= 0.02 * cpu["rel_mse"]
