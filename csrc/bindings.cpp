@@ -49,6 +49,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_allreduce_bf16", &kvs::gemm_allreduce_bf16);
   m.def("gemm_qkv_rope_bf16", &kvs::gemm_qkv_rope_bf16);
   m.def("gemv_bf16", &kvs::gemv_bf16);
+  m.def("gemv_allreduce_bf16", &kvs::gemv_allreduce_bf16);
+  m.def("gemv_argmax_bf16", &kvs::gemv_argmax_bf16);
+  m.def("decode_epoch_bump", &kvs::decode_epoch_bump);
   m.def("flash_prefill", &kvs::flash_prefill);
   m.def("paged_decode_splits", &kvs::paged_decode_splits);
   m.def("paged_decode_attention", &kvs::paged_decode_attention);

@@ -7,34 +7,13 @@
 #include <ATen/cuda/CUDAContext.h>
 
 #include "common.cuh"
+#include "gemv_core.cuh"
 #include "ops.h"
 
 namespace kvs {
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kRows = 2;  // output rows per warp
-
-__device__ __forceinline__ void load_x8(const bf16* p, float (&f)[8]) {
-  const uint4 v = *reinterpret_cast<const uint4*>(p);
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float2 t = __bfloat1622float2(h[e]);
-    f[2 * e] = t.x;
-    f[2 * e + 1] = t.y;
-  }
-}
-__device__ __forceinline__ float dot8(const uint4& w, const float (&x)[8], float acc) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float2 t = __bfloat1622float2(h[e]);
-    acc = fmaf(t.x, x[2 * e], acc);
-    acc = fmaf(t.y, x[2 * e + 1], acc);
-  }
-  return acc;
-}
+constexpr int kThreads = kGemvThreads;
 
 template <int M>
 __global__ void __launch_bounds__(kThreads) gemv_kernel(const bf16* __restrict__ x, int64_t ldx,
@@ -42,82 +21,18 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const bf16* __restrict__
                                                         bf16* __restrict__ y, int64_t ldy, int N, int K,
                                                         const bf16* __restrict__ bias) {
   extern __shared__ uint4 xs_raw[];  // [M][K] bf16
-  bf16* xs = reinterpret_cast<bf16*>(xs_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = (blockIdx.x * (kThreads / 32) + warp) * kRows;
-  const int kvec = K / 8;
-  constexpr int U = M <= 2 ? 8 : 4;  // 16-byte loads in flight per row per lane
-  // The first batch of weight loads is issued before x is staged, so the
-  // weight stream starts at kernel entry instead of after the barrier.
-  uint4 wv[kRows][U];
-  int kv = lane;
-  const bool first_full = row0 < N && kv + 32 * (U - 1) < kvec;
-  if (first_full) {
-#pragma unroll
-    for (int r = 0; r < kRows; ++r)
-#pragma unroll
-      for (int u = 0; u < U; ++u)
-        wv[r][u] = __ldcs(reinterpret_cast<const uint4*>(w + int64_t(min(row0 + r, N - 1)) * ldw) + kv + 32 * u);
-  }
-  for (int i = threadIdx.x; i < M * K / 8; i += kThreads) {
-    const int m = i / (K / 8), k8 = i % (K / 8);
-    xs_raw[i] = *reinterpret_cast<const uint4*>(x + int64_t(m) * ldx + k8 * 8);
-  }
+  const int row0 = (blockIdx.x * (kThreads / 32) + warp) * kGemvRows;
+  GemvWarp<M> g;
+  g.prefetch(w, ldw, row0, N, K, lane);
+  gemv_stage_x<M>(x, ldx, xs_raw, K);
   __syncthreads();
   if (row0 >= N) return;
-  float acc[kRows][M];
-#pragma unroll
-  for (int r = 0; r < kRows; ++r)
-#pragma unroll
-    for (int m = 0; m < M; ++m) acc[r][m] = 0.f;
-  for (bool have = first_full; kv + 32 * (U - 1) < kvec; kv += 32 * U, have = false) {
-    if (!have) {
-#pragma unroll
-      for (int r = 0; r < kRows; ++r)
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int row = min(row0 + r, N - 1);
-          wv[r][u] = __ldcs(reinterpret_cast<const uint4*>(w + int64_t(row) * ldw) + kv + 32 * u);
-        }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int k = (kv + 32 * u) * 8;
-#pragma unroll
-      for (int m = 0; m < M; ++m) {
-        float xf[8];
-        load_x8(xs + m * K + k, xf);
-#pragma unroll
-        for (int r = 0; r < kRows; ++r) acc[r][m] = dot8(wv[r][u], xf, acc[r][m]);
-      }
-    }
-  }
-  for (; kv < kvec; kv += 32) {
-    const int k = kv * 8;
-#pragma unroll
-    for (int r = 0; r < kRows; ++r) {
-      const int row = min(row0 + r, N - 1);
-      const uint4 wv = __ldcs(reinterpret_cast<const uint4*>(w + int64_t(row) * ldw) + kv);
-#pragma unroll
-      for (int m = 0; m < M; ++m) {
-        float xf[8];
-        load_x8(xs + m * K + k, xf);
-        acc[r][m] = dot8(wv, xf, acc[r][m]);
-      }
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < kRows; ++r)
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-      float v = acc[r][m];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      acc[r][m] = v;
-    }
+  float acc[kGemvRows][M];
+  g.run(w, ldw, reinterpret_cast<const bf16*>(xs_raw), row0, N, K, lane, acc);
   if (lane == 0) {
 #pragma unroll
-    for (int r = 0; r < kRows; ++r) {
+    for (int r = 0; r < kGemvRows; ++r) {
       if (row0 + r >= N) break;
 #pragma unroll
       for (int m = 0; m < M; ++m)
@@ -156,7 +71,7 @@ void gemv_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, c10::optional<
                   "gemv: bias must be contiguous bf16 [N]");
     bp = reinterpret_cast<const bf16*>(bias->data_ptr());
   }
-  const int rows_per_cta = (kThreads / 32) * kRows;
+  const int rows_per_cta = kGemvRowsPerCta;
   const int grid = (N + rows_per_cta - 1) / rows_per_cta;
   const size_t smem = size_t(M) * K * 2;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();

@@ -81,6 +81,17 @@ void gemm_qkv_rope_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, c10::
 void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, c10::optional<torch::Tensor> residual,
                c10::optional<torch::Tensor> bias, torch::Tensor err);
 void gemv_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, c10::optional<torch::Tensor> bias);
+// decode-step fusions (decode_fused.cu): row-parallel GEMV + one-shot peer
+// all-reduce, LM-head GEMV + greedy argmax (+ TP exchange), step epoch
+void gemv_allreduce_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, std::vector<int64_t> stage_ptrs,
+                         std::vector<int64_t> flag_ptrs, int64_t rank, int64_t site, int64_t num_sites,
+                         torch::Tensor epoch, int64_t stage_ld, int64_t flag_ld, int64_t timeout_ns,
+                         torch::Tensor status);
+void gemv_argmax_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tensor part_val,
+                      torch::Tensor part_idx, torch::Tensor counter, int64_t vocab_begin,
+                      std::vector<int64_t> slot_ptrs, std::vector<int64_t> flag_ptrs, int64_t rank, int64_t site,
+                      int64_t num_sites, torch::Tensor epoch, int64_t timeout_ns, torch::Tensor status);
+void decode_epoch_bump(torch::Tensor epoch);
 void flash_prefill(torch::Tensor qkv, int64_t Hq, int64_t Hkv, double scale, torch::Tensor out, torch::Tensor err);
 int64_t paged_decode_splits(int64_t batch, int64_t hkv, int64_t max_ctx);
 void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,

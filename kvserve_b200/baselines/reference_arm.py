@@ -272,9 +272,9 @@ def run(args, emit) -> None:
                 out.update(_run_vllm(args, bar, rank, world, role, tp, ports[1]))
                 bar.wait()
                 ho = _run_handoff(args, bar, rank, world, role, ports[2])
-                out["kv_transfer_ms_p50"] = ho.pop("kv_transfer_ms_p50")
-                out["kv_transfer"] = ho
                 if rank == 0:
+                    out["kv_transfer_ms_p50"] = ho.pop("kv_transfer_ms_p50")
+                    out["kv_transfer"] = ho
                     out["recon"] = _reference_recon(args)
     except ArmFailure as exc:
         out = {"impl": "reference", "unavailable": str(exc), "stock_path": out.get("stock_path")}
@@ -324,6 +324,10 @@ def _stock_child(role: str, kv_port: int, q) -> None:
                       if "kvserve_v1" in f.filename), "")
         q.put(("error", f"{type(exc).__name__}: {exc}" + (f" (at {where})" if where else "")))
     finally:
+        # flush the queue's feeder thread before leaving without running the
+        # engine's and the transport's exit handlers (their threads may block)
+        q.close()
+        q.join_thread()
         os._exit(0)
 
 
@@ -458,7 +462,7 @@ def _reference_recon(args) -> Optional[dict]:
     stacked = kv.view(L, 2, T // bs, bs, H, D)
     ad = KVCompressionAdapter(profile, H, D)
     c = ad.compress(stacked, "kvs-recon")
-    out = ad.decompress(c).view(L, 2, T, H, D)
+    out = ad.decompress(c).reshape(L, 2, T, H, D)
     torch.cuda.synchronize()
     st = error_stats(kv, out)
     st.update({"compression_ratio": round(c.original_size / c.compressed_size, 3), "layers": L, "tokens": T,

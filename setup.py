@@ -22,6 +22,7 @@ SOURCES = [
     "engine_ops.cu",
     "gemm_sm100.cu",
     "gemv.cu",
+    "decode_fused.cu",
     "attention_prefill_sm100.cu",
     "attention_decode.cu",
     "paged_decode_noalloc.cu",

@@ -140,5 +140,6 @@ def test_frame_round_trip_error_matches_cpu_oracle():
         k, v = kc.cpu_decode_frame(bytes(buf), spec, xfer.orders_cpu[l], signs)
         outs.append(torch.stack([k, v]))
     cpu = error_stats(kv.cpu(), torch.stack(outs))
-    assert gpu["k_rel_mse"] < 0.02 and gpu["v_rel_mse"] < 0.2
+    # K: 16 levels per channel; V: 4 levels per token over 512 values (range about +-3 sigma)
+    assert gpu["k_rel_mse"] < 0.05 and gpu["v_rel_mse"] < 0.5
     assert abs(gpu["rel_mse"] - cpu["rel_mse"]) <= 0.02 * cpu["rel_mse"]
