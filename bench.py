@@ -44,12 +44,14 @@ def _log(msg: str) -> None:
 
 
 def _profile(name: str):
+    """``raw``, a named engine profile (k8v8, k4v4, k4v2, k2v2, off) or a
+    ``configs/compression`` JSON file."""
+    from kvserve_b200.engine.serving import ENGINE_PROFILES
     from kvserve_b200.engine.transfer import TransferProfile
     if name == "raw":
         return TransferProfile.raw()
-    if name == "k4v2":
-        return TransferProfile(compressed=True, hybrid_ratio=0.0, split_type="head", key_levels=(16, 16),
-                               value_levels=(4, 4))
+    if name in ENGINE_PROFILES:
+        return ENGINE_PROFILES[name]
     if os.path.exists(name):
         with open(name) as f:
             return TransferProfile.from_compression(json.load(f))
@@ -234,7 +236,8 @@ def main() -> None:
                        "seq_len": args.prompt_len, "max_new_tokens": args.max_new,
                        "parallelism": "colocated-1gpu" if args.gpus == 1 else f"{tp}P{tp}D-tp{tp}",
                        "profile": args.profile, "link_gbps": args.link_gbps or None,
-                       "l2": "inputs larger than L2 (16 GB weights, 1 GiB raw KV per request)"},
+                       "l2": "inputs larger than L2 (%.1f GB of weights per rank, %.2f GiB raw KV per request)"
+                             % (engine.model.weight_bytes() / 1e9, raw * tp / 2 ** 30)},
             "e2e": {"value": round(statistics.median(e2e_ttft), 3),
                     "unit": "ms (TTFT p50, host wall clock from PDEngine.generate() entry to the first token "
                             "on the host; prompt H2D from pinned memory and token D2H inside every step)",

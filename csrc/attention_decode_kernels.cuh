@@ -217,9 +217,13 @@ void launch_decode(int G, dim3 grid, cudaStream_t st, const bf16* q, int64_t qs,
   switch (G) {
     KVS_DEC_CASE(1)
     KVS_DEC_CASE(2)
+    KVS_DEC_CASE(3)
     KVS_DEC_CASE(4)
+    KVS_DEC_CASE(5)
+    KVS_DEC_CASE(6)
+    KVS_DEC_CASE(7)   // Qwen2.5-7B: 28 query heads over 4 KV heads
     KVS_DEC_CASE(8)
-    default: throw std::invalid_argument("paged decode: query heads per KV head must be 1, 2, 4 or 8");
+    default: throw std::invalid_argument("paged decode: query heads per KV head must be 1..8");
   }
 #undef KVS_DEC_CASE
 }

@@ -44,6 +44,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding", &kvs::embedding);
   m.def("argmax_rows", &kvs::argmax_rows);
   m.def("decode_advance", &kvs::decode_advance);
+  m.def("batch_advance", &kvs::batch_advance);
   m.def("gemm_bf16", &kvs::gemm_bf16);
   m.def("gemm_silu_bf16", &kvs::gemm_silu_bf16);
   m.def("gemm_allreduce_bf16", &kvs::gemm_allreduce_bf16);

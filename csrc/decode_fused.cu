@@ -66,38 +66,45 @@ __device__ __forceinline__ void report(uint32_t* status, uint32_t code) {
   if (status) atomicCAS(status, uint32_t(kStatusOk), code);
 }
 
+constexpr int kMaxChunks = 4;   // 16-row chunks per CTA (grid = N / (16 * chunks) must fit at once)
+
 template <int M>
 __global__ void __launch_bounds__(kGemvThreads) gemv_allreduce_kernel(
     const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ w, int64_t ldw, bf16* __restrict__ y,
-    int64_t ldy, int N, int K, PeerTable peers, int rank, int world, int site, int num_sites,
+    int64_t ldy, int N, int K, int chunks, PeerTable peers, int rank, int world, int site, int num_sites,
     const int32_t* __restrict__ epoch_ptr, int64_t stage_ld, int flag_ld, uint64_t timeout_ns,
     uint32_t* __restrict__ status) {
   extern __shared__ uint4 xs_raw[];  // [M][K] bf16
-  __shared__ __align__(16) float part[M][kGemvRowsPerCta];
+  __shared__ __align__(16) float part[kMaxChunks][M][kGemvRowsPerCta];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = blockIdx.x * kGemvRowsPerCta + warp * kGemvRows;   // N % 16 == 0: always < N
+  const int64_t col0 = int64_t(blockIdx.x) * chunks * kGemvRowsPerCta;   // N % (16 * chunks) == 0
   GemvWarp<M> g;
-  g.prefetch(w, ldw, row0, N, K, lane);
+  g.prefetch(w, ldw, int(col0) + warp * kGemvRows, N, K, lane);
   gemv_stage_x<M>(x, ldx, xs_raw, K);
   __syncthreads();
-  float acc[kGemvRows][M];
-  g.run(w, ldw, reinterpret_cast<const bf16*>(xs_raw), row0, N, K, lane, acc);
-  if (lane == 0) {
+  for (int c = 0; c < chunks; ++c) {
+    const int row0 = int(col0) + c * kGemvRowsPerCta + warp * kGemvRows;
+    float acc[kGemvRows][M];
+    if (c > 0) g.have = false;
+    g.run(w, ldw, reinterpret_cast<const bf16*>(xs_raw), row0, N, K, lane, acc);
+    if (lane == 0) {
 #pragma unroll
-    for (int r = 0; r < kGemvRows; ++r)
+      for (int r = 0; r < kGemvRows; ++r)
 #pragma unroll
-      for (int m = 0; m < M; ++m) part[m][warp * kGemvRows + r] = acc[r][m];
+        for (int m = 0; m < M; ++m) part[c][m][warp * kGemvRows + r] = acc[r][m];
+    }
   }
   __syncthreads();
   const int parity = site & 1;
   const uint32_t val = uint32_t(*epoch_ptr) * uint32_t(num_sites) + uint32_t(site) + 1u;
   // this CTA's partial rows -> slot [parity][rank][m][rows] of every rank (itself included)
-  const int64_t col0 = int64_t(blockIdx.x) * kGemvRowsPerCta;
-  for (int t = threadIdx.x; t < world * M * 4; t += blockDim.x) {
-    const int r = t / (M * 4), m = (t >> 2) % M, q = t & 3;
+  const int per_rank = chunks * M * 4;   // 16-byte pieces
+  for (int t = threadIdx.x; t < world * per_rank; t += blockDim.x) {
+    const int r = t / per_rank, rem = t % per_rank;
+    const int c = rem / (M * 4), m = (rem >> 2) % M, q = rem & 3;
     float* dst = reinterpret_cast<float*>(peers.stage[r]) + ((int64_t(parity) * world + rank) * kMaxTok + m) * stage_ld +
-                 col0 + q * 4;
-    *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(&part[m][q * 4]);
+                 col0 + c * kGemvRowsPerCta + q * 4;
+    *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(&part[c][m][q * 4]);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -115,8 +122,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_allreduce_kernel(
   }
   __syncthreads();
   const float* stage = reinterpret_cast<const float*>(peers.stage[rank]);
-  for (int t = threadIdx.x; t < M * kGemvRowsPerCta; t += blockDim.x) {
-    const int m = t / kGemvRowsPerCta, i = t % kGemvRowsPerCta;
+  const int rows = chunks * kGemvRowsPerCta;
+  for (int t = threadIdx.x; t < M * rows; t += blockDim.x) {
+    const int m = t / rows, i = t % rows;
     const float* p = stage + (int64_t(parity) * world * kMaxTok + m) * stage_ld + col0 + i;
     float s = 0.f;
     for (int r = 0; r < world; ++r) s += __ldcg(p + int64_t(r) * kMaxTok * stage_ld);   // fixed rank order
@@ -298,7 +306,14 @@ void gemv_allreduce_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, std:
   KVS_CHECK_ARG(N % kGemvRowsPerCta == 0 && N <= stage_ld && stage_ld % 4 == 0,
                 "gemv_allreduce: N must be a multiple of 16 within the staging width");
   KVS_CHECK_ARG(rank >= 0 && rank < world && site >= 0 && site < num_sites, "gemv_allreduce: rank/site");
-  const int grid = N / kGemvRowsPerCta;
+  // fewest 16-row chunks per CTA that keep the whole grid resident (one wave:
+  // 2 CTAs of 256 threads per SM at this kernel's register count)
+  int chunks = 1;
+  while (chunks < kMaxChunks && N / (kGemvRowsPerCta * chunks) > 2 * kNumSMs &&
+         N % (kGemvRowsPerCta * chunks * 2) == 0)
+    chunks *= 2;
+  KVS_CHECK_ARG(N % (kGemvRowsPerCta * chunks) == 0, "gemv_allreduce: N must split into whole chunks");
+  const int grid = N / (kGemvRowsPerCta * chunks);
   KVS_CHECK_ARG(grid <= flag_ld, "gemv_allreduce: more CTAs than flag slots");
   KVS_CHECK_ARG(epoch.is_cuda() && epoch.scalar_type() == at::kInt && status.is_cuda() &&
                     status.scalar_type() == at::kInt,
@@ -320,7 +335,7 @@ void gemv_allreduce_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, std:
       ensure_coresident(gemv_allreduce_kernel<MM>, checked_grid, checked_smem, "gemv_allreduce");              \
     }                                                                                                           \
     gemv_allreduce_kernel<MM><<<grid, kGemvThreads, smem, st>>>(                                                \
-        xp, x.stride(0), wp, w.stride(0), yp, y.stride(0), N, K, peers, int(rank), world, int(site),           \
+        xp, x.stride(0), wp, w.stride(0), yp, y.stride(0), N, K, chunks, peers, int(rank), world, int(site),   \
         int(num_sites), ep, stage_ld, int(flag_ld), uint64_t(timeout_ns), sp);                                 \
     break;                                                                                                      \
   }

@@ -233,7 +233,46 @@ __global__ void decode_advance_kernel(const int32_t* __restrict__ tok, int32_t* 
   if (b == 0) *step = s + 1;
 }
 
+// Continuous-batching variant: every row is its own request with its own
+// token count.  Rows with active[b] == 0 are padding (they point at a scratch
+// block and do not advance); out_tokens is [B, ld] with row b's t-th token at
+// out_tokens[b * ld + t].
+__global__ void batch_advance_kernel(const int32_t* __restrict__ tok, const int32_t* __restrict__ active,
+                                     int32_t* __restrict__ ids, int32_t* __restrict__ pos,
+                                     int32_t* __restrict__ ctx, int32_t* __restrict__ slot,
+                                     const int32_t* __restrict__ table, int64_t table_stride, int block_size,
+                                     int32_t* __restrict__ out_tokens, int64_t ld, int32_t* __restrict__ steps,
+                                     int B) {
+  const int b = threadIdx.x;
+  if (b >= B || !active[b]) return;
+  const int32_t t = tok[b];
+  ids[b] = t;
+  const int s = steps[b];
+  if (s < ld) out_tokens[int64_t(b) * ld + s] = t;
+  steps[b] = s + 1;
+  const int p = pos[b] + 1;
+  pos[b] = p;
+  ctx[b] = ctx[b] + 1;
+  slot[b] = table[b * table_stride + p / block_size] * block_size + p % block_size;
+}
+
 }  // namespace
+
+void batch_advance(torch::Tensor tok, torch::Tensor active, torch::Tensor ids, torch::Tensor pos, torch::Tensor ctx,
+                   torch::Tensor slot, torch::Tensor table, int64_t block_size, torch::Tensor out_tokens,
+                   torch::Tensor steps) {
+  const int B = int(ids.numel());
+  KVS_CHECK_ARG(B >= 1 && B <= 1024 && table.dim() == 2 && table.size(0) >= B && out_tokens.dim() == 2 &&
+                    out_tokens.size(0) >= B && out_tokens.stride(1) == 1 && active.numel() >= B &&
+                    steps.numel() >= B && tok.numel() >= B,
+                "batch_advance: per-row state of B rows");
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  batch_advance_kernel<<<1, std::max(32, B), 0, st>>>(
+      tok.data_ptr<int32_t>(), active.data_ptr<int32_t>(), ids.data_ptr<int32_t>(), pos.data_ptr<int32_t>(),
+      ctx.data_ptr<int32_t>(), slot.data_ptr<int32_t>(), table.data_ptr<int32_t>(), table.stride(0),
+      int(block_size), out_tokens.data_ptr<int32_t>(), out_tokens.stride(0), steps.data_ptr<int32_t>(), B);
+  KVS_CUDA_CHECK(cudaGetLastError());
+}
 
 void decode_advance(torch::Tensor tok, torch::Tensor ids, torch::Tensor pos, torch::Tensor ctx, torch::Tensor slot,
                     torch::Tensor table, int64_t block_size, torch::Tensor out_tokens, torch::Tensor step) {

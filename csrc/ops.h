@@ -67,6 +67,9 @@ void silu_mul(torch::Tensor gate_up, torch::Tensor out, int64_t blk);
 void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t vocab_begin);
 void argmax_rows(torch::Tensor logits, torch::Tensor out, c10::optional<torch::Tensor> out_val,
                  int64_t index_offset);
+void batch_advance(torch::Tensor tok, torch::Tensor active, torch::Tensor ids, torch::Tensor pos, torch::Tensor ctx,
+                   torch::Tensor slot, torch::Tensor table, int64_t block_size, torch::Tensor out_tokens,
+                   torch::Tensor steps);
 void decode_advance(torch::Tensor tok, torch::Tensor ids, torch::Tensor pos, torch::Tensor ctx, torch::Tensor slot,
                     torch::Tensor table, int64_t block_size, torch::Tensor out_tokens, torch::Tensor step);
 void gemm_silu_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor err);

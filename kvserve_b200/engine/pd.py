@@ -30,6 +30,7 @@ from .. import ops
 from ..models.config import ModelConfig
 from ..models.llama import LlamaShard
 from ..parallel.context import ParallelContext
+from ..parallel.decode_allreduce import create_decode_collectives
 from ..parallel.tp_allreduce import create_tp_allreduce
 from ..transport.p2p import FrameReceiver, FrameSender
 from .kv_cache import PagedKVCache
@@ -62,7 +63,7 @@ class PDEngine:
     def __init__(self, cfg: ModelConfig, ctx: ParallelContext, profile: TransferProfile, max_prompt: int = 8192,
                  max_new_tokens: int = 128, block_size: int = 16, seed: int = 0, link_gbps: float = 0.0,
                  use_graphs: bool = True, ingest_timeout_s: float = 30.0, encode_ctas: int = 222,
-                 profiles: Optional[dict] = None):
+                 profiles: Optional[dict] = None, num_slots: int = 2):
         self.cfg, self.ctx, self.profile = cfg, ctx, profile
         self.device = torch.device("cuda", torch.cuda.current_device())
         self.max_prompt, self.max_new, self.block_size = max_prompt, max_new_tokens, block_size
@@ -75,6 +76,9 @@ class PDEngine:
         m = self.model
         # prefill ranks reduce their row-parallel projections inside the GEMM
         m.tp_ar = create_tp_allreduce(ctx, max_prompt, cfg.hidden, self.device, participate=ctx.is_prefill)
+        # decode ranks fuse their per-step collectives into the projections
+        m.decode_coll = create_decode_collectives(ctx, cfg.hidden, m.vocab_local, m.decode_sites(), self.device,
+                                                  participate=ctx.is_decode)
         # one transfer geometry per selectable profile ("default" = `profile`);
         # the receive slot is sized for the largest frame of any of them
         self.xfers = {name: KVTransfer(p, cfg.num_layers, cfg.num_kv_heads, m.hkv, m.D, ctx.tp_rank, ctx.tp_size,
@@ -105,8 +109,12 @@ class PDEngine:
         # ---- channel between paired ranks
         self.receiver: Optional[FrameReceiver] = None
         self.sender: Optional[FrameSender] = None
+        # receive slots of the channel; request `seq` uses slot seq % num_slots
+        # and waits for the slot's credit from its previous request
+        self.num_slots = max(1, int(num_slots))
+        self._slot_seq = [0] * self.num_slots
         if ctx.is_decode:
-            self.receiver = FrameReceiver(L, frame_stride, 1, self.device)
+            self.receiver = FrameReceiver(L, frame_stride, self.num_slots, self.device)
         if not ctx.distributed:
             self.sender = FrameSender(local=self.receiver, device=self.device)
         else:
@@ -215,6 +223,29 @@ class PDEngine:
         if self.ctx.distributed:
             dist.barrier(group=self.ctx.cpu_group)
 
+    # ------------------------------------------------- slots and credits
+    def _next_seq(self) -> tuple[int, int]:
+        """(sequence number, receive slot) of the next request."""
+        self.seq += 1
+        return self.seq, self.seq % self.num_slots
+
+    def _take_credit(self, slot: int, seq: int) -> None:
+        """Producer, on the current stream before the slot's first store:
+        acquire-wait (bounded) until the decode rank has read the slot's
+        previous request out of it."""
+        prev = self._slot_seq[slot]
+        self._slot_seq[slot] = seq
+        if self.ctx.distributed and prev:
+            ops.count_launches(1)
+            ops.ext().wait_flag(self.sender.credit_ptr(slot), prev, self.ingest_timeout_ns, self.status)
+
+    def _return_credit(self, slot: int, seq: int) -> None:
+        """Consumer, on the stream of the last kernel that read the slot."""
+        self._slot_seq[slot] = seq
+        if self.ctx.distributed:
+            ops.count_launches(1)
+            ops.ext().store_release_u32(self.receiver.credit_ptr(slot), seq)
+
     def generate(self, prompt_ids: torch.Tensor, max_new_tokens: Optional[int] = None,
                  return_tokens: bool = True, sync: bool = True, profile: Optional[str] = None,
                  link_gbps: Optional[float] = None) -> GenerateResult:
@@ -247,8 +278,7 @@ class PDEngine:
         # The prefill covers the whole prompt and samples the first token; the
         # KV of all T tokens is handed to the decode side with that token.
         Tx = T
-        self.seq += 1
-        seq = self.seq
+        seq, slot = self._next_seq()
         ev = {k: torch.cuda.Event(enable_timing=True)
               for k in ("start", "prefill", "enc_start", "encode", "ingest", "first", "end")}
         if sync:
@@ -265,13 +295,16 @@ class PDEngine:
             if ctx.distributed:
                 self.ingest_stream.wait_stream(self.compute)
                 with torch.cuda.stream(self.ingest_stream):
-                    xfer.ingest_all(Tx, self.receiver.slot_base(0), self.receiver.frame_stride,
-                                         self.receiver.flags_base(0), self.kv.cache, table, self.status, seq,
-                                         self.ingest_timeout_ns)
+                    xfer.ingest_all(Tx, self.receiver.slot_base(slot), self.receiver.frame_stride,
+                                    self.receiver.flags_base(slot), self.kv.cache, table, self.status, seq,
+                                    self.ingest_timeout_ns)
                     ev["ingest"].record(self.ingest_stream)
         if ctx.is_prefill:
             enc = self.enc_stream
             enc.wait_stream(self.compute)
+
+            with torch.cuda.stream(enc):
+                self._take_credit(slot, seq)
 
             def hook(l: int) -> None:
                 self.layer_events[l].record(self.compute)
@@ -279,19 +312,19 @@ class PDEngine:
                 if l == 0:
                     ev["enc_start"].record(enc)
                 with torch.cuda.stream(enc):
-                    flag = self.sender.flag_ptr(0, l) if ctx.distributed else 0
-                    xfer.encode(l, self.k_buf[l, :Tx], self.v_buf[l, :Tx], self.sender.frame_ptr(0, l), flag,
+                    flag = self.sender.flag_ptr(slot, l) if ctx.distributed else 0
+                    xfer.encode(l, self.k_buf[l, :Tx], self.v_buf[l, :Tx], self.sender.frame_ptr(slot, l), flag,
                                 seq, self.pacing, rate, self.encode_ctas)
                     if not ctx.distributed:
-                        xfer.ingest_layer(l, Tx, self.sender.frame_ptr(0, l), self.kv.cache, table,
-                                               self.status, seq)
+                        xfer.ingest_layer(l, Tx, self.sender.frame_ptr(slot, l), self.kv.cache, table,
+                                          self.status, seq)
 
             first = m.prefill(ids[:Tx], self.positions[:Tx], self.k_buf, self.v_buf, layer_hook=hook, sample=True)
             ev["prefill"].record(self.compute)
             if ctx.distributed:
                 # the token lands next to the layer flags of the decode slot
                 ops.count_launches(1)
-                ops.ext().publish_token(first, self.sender.token_ptr(0), seq)
+                ops.ext().publish_token(first, self.sender.token_ptr(slot), seq)
             ev["encode"].record(enc)
             if not ctx.distributed:
                 ev["ingest"].record(enc)
@@ -305,8 +338,9 @@ class PDEngine:
             self._load_decode_state(0, T, blocks)
             if ctx.distributed:
                 ops.count_launches(1)
-                ops.ext().take_token(self.receiver.token_ptr(0), seq, self.ingest_timeout_ns, self.d_ids,
+                ops.ext().take_token(self.receiver.token_ptr(slot), seq, self.ingest_timeout_ns, self.d_ids,
                                      self.d_out, self.status)
+                self._return_credit(slot, seq)
             else:
                 self.d_ids.copy_(self.d_first)
                 self.d_out[0:1].copy_(self.d_first)
@@ -330,6 +364,11 @@ class PDEngine:
         if st != 0:
             self.status.zero_()
             raise RuntimeError(f"KV hand-off failed on rank {ctx.rank}: {ops.STATUS_NAMES.get(st, st)}")
+        dc = m.decode_coll
+        if dc is not None and int(dc.status[0].item()) != 0:
+            code = int(dc.status[0].item())
+            dc.status.zero_()
+            raise RuntimeError(f"decode collective failed on rank {ctx.rank}: status {code} (peer timeout)")
         timing.launches = ops.launches() - c_launch0 + replays * getattr(self, "_graph_launches", 0)
         timing.request_host = 1e3 * (time.perf_counter() - t_host0)
         e = lambda k: ev["start"].elapsed_time(ev[k])  # noqa: E731
@@ -358,8 +397,7 @@ class PDEngine:
         if T < 1 or T > self.max_prompt:
             raise ValueError(f"T must be in [1, {self.max_prompt}]")
         self._host_barrier()
-        self.seq += 1
-        seq = self.seq
+        seq, slot = self._next_seq()
         start, enc_end, ing_end = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         self._barrier()
         start.record(self.compute)
@@ -370,20 +408,23 @@ class PDEngine:
             if ctx.distributed:
                 self.ingest_stream.wait_stream(self.compute)
                 with torch.cuda.stream(self.ingest_stream):
-                    xfer.ingest_all(T, self.receiver.slot_base(0), self.receiver.frame_stride,
-                                    self.receiver.flags_base(0), self.kv.cache, table, self.status, seq,
+                    xfer.ingest_all(T, self.receiver.slot_base(slot), self.receiver.frame_stride,
+                                    self.receiver.flags_base(slot), self.kv.cache, table, self.status, seq,
                                     self.ingest_timeout_ns)
                     ing_end.record(self.ingest_stream)
+                    self._return_credit(slot, seq)
         if ctx.is_prefill:
             enc = self.enc_stream
             enc.wait_stream(self.compute)
             with torch.cuda.stream(enc):
+                self._take_credit(slot, seq)
                 for l in range(self.cfg.num_layers):
-                    flag = self.sender.flag_ptr(0, l) if ctx.distributed else 0
-                    xfer.encode(l, self.k_buf[l, :T], self.v_buf[l, :T], self.sender.frame_ptr(0, l), flag, seq,
-                                self.pacing, 0.0, self.encode_ctas)
+                    flag = self.sender.flag_ptr(slot, l) if ctx.distributed else 0
+                    xfer.encode(l, self.k_buf[l, :T], self.v_buf[l, :T], self.sender.frame_ptr(slot, l), flag,
+                                seq, self.pacing, 0.0, self.encode_ctas)
                     if not ctx.distributed:
-                        xfer.ingest_layer(l, T, self.sender.frame_ptr(0, l), self.kv.cache, table, self.status, seq)
+                        xfer.ingest_layer(l, T, self.sender.frame_ptr(slot, l), self.kv.cache, table, self.status,
+                                          seq)
                 enc_end.record(enc)
                 if not ctx.distributed:
                     ing_end.record(enc)
@@ -401,6 +442,10 @@ class PDEngine:
 
     def close(self) -> None:
         self._graph = None
+        if self.model.decode_coll is not None:
+            torch.cuda.synchronize(self.device)
+            self.model.decode_coll.close()
+            self.model.decode_coll = None
         if self.model.tp_ar is not None:
             torch.cuda.synchronize(self.device)
             self.model.tp_ar.close()

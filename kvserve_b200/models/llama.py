@@ -91,8 +91,11 @@ class LlamaShard:
         self.lm_head = self._rand((self.vocab_local, cfg.hidden), -1, "lm_head")
         self.final_norm = torch.ones(cfg.hidden, dtype=torch.bfloat16, device=dev)
         self.cos_sin = rope_cache(max_position, self.D, cfg.rope_theta, dev)
-        # fused GEMM + all-reduce workspace (parallel.tp_allreduce), attached by the engine
+        # fused GEMM + all-reduce workspace (parallel.tp_allreduce) and the
+        # decode-step collective workspace (parallel.decode_allreduce), both
+        # attached by the engine
         self.tp_ar = None
+        self.decode_coll = None
 
     # ------------------------------------------------------------------ init
     def _rand(self, shape, layer, name, tp_shared=False, std=None) -> torch.Tensor:
@@ -126,12 +129,23 @@ class LlamaShard:
     def _qkv(self, h: torch.Tensor, lw: LayerWeights) -> torch.Tensor:
         return ops.linear(h, lw.qkv, bias=lw.qkv_bias)
 
-    def _mlp(self, h: torch.Tensor, lw: LayerWeights) -> torch.Tensor:
+    def _mlp(self, h: torch.Tensor, lw: LayerWeights, site: Optional[int] = None) -> torch.Tensor:
         if self.gu_block and h.shape[0] > ops.GEMV_MAX_M:
             a = ops.gemm_silu(h, lw.gate_up)
         else:
             a = ops.silu_mul(ops.linear(h, lw.gate_up), block=self.gu_block)
-        return self._row_parallel(a, lw.down)
+        return self._decode_row_parallel(a, lw.down, site)
+
+    def decode_sites(self) -> int:
+        """Launch sites of the fused decode collectives in one step: the two
+        row-parallel projections of every layer and the LM head."""
+        return 2 * self.cfg.num_layers + 1
+
+    def _decode_row_parallel(self, x: torch.Tensor, w: torch.Tensor, site: Optional[int]) -> torch.Tensor:
+        dc = self.decode_coll
+        if site is not None and dc is not None and dc.world > 1 and x.reshape(-1, x.shape[-1]).shape[0] <= 8:
+            return dc.gemv_allreduce(x, w, site)
+        return self._row_parallel(x, w)
 
     def greedy(self, h_last: torch.Tensor) -> torch.Tensor:
         """Greedy next token over the vocab-parallel LM head (int32 [B])."""
@@ -196,9 +210,14 @@ class LlamaShard:
             q = qkv[:, : self.hq * self.D].view(B, self.hq, self.D)
             attn = ops.paged_decode_attention(q, kv_cache[l, 0], kv_cache[l, 1], block_tables, ctx_lens, max_ctx,
                                               self.scale, scratch=attn_scratch)
-            o = self._row_parallel(attn.view(B, self.hq * self.D), lw.o)
+            o = self._decode_row_parallel(attn.view(B, self.hq * self.D), lw.o, 2 * l)
             h = ops.rmsnorm(o, lw.post_norm, cfg.rms_eps, residual=residual)
-            d = self._mlp(h, lw)
+            d = self._mlp(h, lw, 2 * l + 1)
             nxt = self.layers[l + 1].in_norm if l + 1 < len(self.layers) else self.final_norm
             h = ops.rmsnorm(d, nxt, cfg.rms_eps, residual=residual)
-        return self.greedy(h)
+        dc = self.decode_coll
+        if dc is None or B > 8:
+            return self.greedy(h)
+        tok = dc.greedy(h, self.lm_head, self.vocab_begin, 2 * cfg.num_layers)
+        dc.bump()
+        return tok

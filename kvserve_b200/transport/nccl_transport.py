@@ -16,8 +16,12 @@ payload of a currently expected request may exceed the budget.  Credit is
 returned by ``release_received`` after the KV has been injected.
 
 Data plane: ``"nccl"`` (2-rank NCCL communicator, dedicated CUDA streams,
-completion threads retire events in order) or ``"gloo"`` (CPU tensors over
-a 2-rank gloo group; used for CPU runs and failure tests).
+completion threads retire events in order), ``"ipc"`` (CUDA IPC: the
+consumer exports one device receive pool, its ACK names the granted ranges
+as a third frame, the producer's copy engine writes them over NVLink — or
+within one GPU when both engines share it — and a ``DONE {request_id,
+ticket}`` message publishes the payload; no NCCL) or ``"gloo"`` (CPU tensors
+over a 2-rank gloo group; used for CPU runs and failure tests).
 Stats rows go to ``KVSERVE_TRANSPORT_STATS_PATH`` as JSONL.
 """
 from __future__ import annotations
@@ -177,6 +181,202 @@ class _GlooPlane:
         self.pg = None
 
 
+class _RangePool:
+    """First-fit allocator of byte ranges in one receive pool (256-byte aligned)."""
+
+    ALIGN = 256
+
+    def __init__(self, size: int):
+        self.size = size
+        self._free: list[list[int]] = [[0, size]]   # sorted [offset, length]
+
+    def alloc(self, nbytes: int) -> Optional[int]:
+        n = max(self.ALIGN, -(-nbytes // self.ALIGN) * self.ALIGN)
+        for i, (off, length) in enumerate(self._free):
+            if length >= n:
+                if length == n:
+                    self._free.pop(i)
+                else:
+                    self._free[i] = [off + n, length - n]
+                return off
+        return None
+
+    def free(self, off: int, nbytes: int) -> None:
+        n = max(self.ALIGN, -(-nbytes // self.ALIGN) * self.ALIGN)
+        self._free.append([off, n])
+        self._free.sort()
+        merged: list[list[int]] = []
+        for o, ln in self._free:
+            if merged and merged[-1][0] + merged[-1][1] == o:
+                merged[-1][1] += ln
+            else:
+                merged.append([o, ln])
+        self._free = merged
+
+    def free_bytes(self) -> int:
+        return sum(ln for _, ln in self._free)
+
+
+class _IpcPlane:
+    """CUDA-IPC data plane (see the module docstring).  Consumer: one pool of
+    ``capacity`` bytes; a payload that does not fit the pool's free ranges
+    (an admitted oversize or priority payload) gets its own allocation,
+    exported the same way and freed with the payload's credit."""
+
+    kind = "ipc"
+
+    def __init__(self, device: torch.device, capacity: int = 0, timeout_s: float = 60.0):
+        self.device = device
+        self.timeout_s = timeout_s
+        self.capacity = capacity
+        self.stream = None
+        self.pool_ptr = 0
+        self.pool_handle = b""
+        self._pool: Optional[_RangePool] = None
+        self._held: dict[str, deque] = defaultdict(deque)   # request -> granted ranges, oldest first
+        self._lock = threading.Lock()
+        self._tickets: dict[int, threading.Event] = {}
+        self._next_ticket = 0
+        self._mapped: dict[bytes, int] = {}                  # producer: handle -> mapped base
+
+    # --- consumer
+    def producer_init(self) -> dict:
+        return {}
+
+    def producer_connect(self) -> None:
+        self.stream = torch.cuda.Stream(device=self.device)
+
+    def consumer_connect(self, msg: dict) -> None:
+        from ..ops import ext
+        if self.pool_ptr:
+            return
+        with torch.cuda.device(self.device):
+            self.pool_ptr = ext().dev_alloc(self.capacity)
+            self.pool_handle = ext().ipc_get_handle(self.pool_ptr)
+        self._pool = _RangePool(self.capacity)
+
+    def grant(self, rid: str, specs: list) -> tuple[list, dict]:
+        """Ranges for ``specs``; returns (tensors, ACK info for the producer)."""
+        from ..ops import dtype_code, ext
+        tensors, grants, ranges = [], [], []
+        with self._lock:
+            try:
+                for sp in specs:
+                    dt = getattr(torch, sp["dtype"])
+                    nbytes = max(1, math.prod(sp["shape"]) * torch.tensor([], dtype=dt).element_size())
+                    off = self._pool.alloc(nbytes)
+                    if off is not None:
+                        ptr, grant, rng = self.pool_ptr + off, ["pool", off], ("pool", off, nbytes)
+                    else:
+                        with torch.cuda.device(self.device):
+                            ptr = ext().dev_alloc(nbytes)
+                        grant, rng = ["own", ext().ipc_get_handle(ptr)], ("own", ptr, nbytes)
+                    ranges.append(rng)
+                    tensors.append(ext().tensor_from_ptr(ptr, list(sp["shape"]), dtype_code(dt),
+                                                         self.device.index))
+                    grants.append(grant)
+            except Exception:
+                self._free_ranges(ranges)
+                raise
+            self._held[rid].append(ranges)
+            ticket = self._next_ticket
+            self._next_ticket += 1
+            self._tickets[ticket] = threading.Event()
+        return tensors, {"pool": self.pool_handle, "grants": grants, "ticket": ticket}
+
+    def alloc(self, shape, dtype) -> torch.Tensor:   # unused: grant() places tensors
+        raise NotImplementedError
+
+    def recv(self, tensors: list, ticket: int = -1):
+        return (time.perf_counter(), self._tickets[ticket], ticket)
+
+    def done(self, ticket: int) -> None:
+        ev = self._tickets.get(ticket)
+        if ev is not None:
+            ev.set()
+
+    def wait(self, handle) -> float:
+        t0, ev, ticket = handle
+        ok = ev.wait(self.timeout_s)
+        with self._lock:
+            self._tickets.pop(ticket, None)
+        if not ok:
+            raise TimeoutError(f"no DONE for ticket {ticket} within {self.timeout_s} s")
+        return time.perf_counter() - t0
+
+    def release(self, rid: str) -> None:
+        with self._lock:
+            q = self._held.get(rid)
+            if not q:
+                return
+            ranges = q.popleft()
+            if not q:
+                self._held.pop(rid, None)
+            self._free_ranges(ranges)
+
+    def _free_ranges(self, ranges: list) -> None:
+        from ..ops import ext
+        for kind, where, nbytes in ranges:
+            if kind == "pool":
+                self._pool.free(where, nbytes)
+            else:
+                with torch.cuda.device(self.device):
+                    ext().dev_free(where)
+
+    # --- producer
+    def _base(self, handle: bytes) -> int:
+        from ..ops import ext
+        base = self._mapped.get(handle)
+        if base is None:
+            with torch.cuda.device(self.device):
+                base = ext().ipc_open_handle(handle)
+            self._mapped[handle] = base
+        return base
+
+    def send(self, tensors: list, ready: Optional[torch.cuda.Event], info: Optional[dict] = None):
+        """Copy every tensor into its granted range (copy engine, peer or
+        local) and wait for the copies; returns the device seconds."""
+        from ..ops import dtype_code, ext
+        opened = []
+        with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
+            if ready is not None:
+                self.stream.wait_event(ready)
+            start = torch.cuda.Event(enable_timing=True)
+            done = torch.cuda.Event(enable_timing=True)
+            start.record(self.stream)
+            pool = self._base(info["pool"])
+            for t, (kind, where) in zip(tensors, info["grants"]):
+                if kind == "pool":
+                    ptr = pool + int(where)
+                else:
+                    ptr = ext().ipc_open_handle(where)
+                    opened.append(ptr)
+                dst = ext().tensor_from_ptr(ptr, list(t.shape), dtype_code(t.dtype), self.device.index)
+                dst.copy_(t, non_blocking=True)
+            done.record(self.stream)
+        done.synchronize()
+        with torch.cuda.device(self.device):
+            for p in opened:
+                ext().ipc_close(p)
+        return start.elapsed_time(done) / 1e3
+
+    def close(self) -> None:
+        from ..ops import ext
+        try:
+            with torch.cuda.device(self.device):
+                for base in self._mapped.values():
+                    ext().ipc_close(base)
+                self._mapped.clear()
+                for rid in list(self._held):
+                    while self._held.get(rid):
+                        self.release(rid)
+                if self.pool_ptr:
+                    ext().dev_free(self.pool_ptr)
+                    self.pool_ptr = 0
+        except Exception as exc:   # best effort at shutdown
+            log.warning("ipc data plane close: %s", exc)
+
+
 # -------------------------------------------------------------------- transport
 class NcclTransport:
     def __init__(self, is_sender: bool, host: str, port: int, local_rank: int = 0, channel_rank: int = 0,
@@ -186,7 +386,7 @@ class NcclTransport:
         self.local_rank, self.channel_rank = local_rank, channel_rank
         self.port = port + channel_rank
         self.plane_kind = data_plane
-        self.device = torch.device(f"cuda:{local_rank}") if data_plane == "nccl" else torch.device("cpu")
+        self.device = torch.device(f"cuda:{local_rank}") if data_plane in ("nccl", "ipc") else torch.device("cpu")
         self._stats_path = os.environ.get("KVSERVE_TRANSPORT_STATS_PATH")
         self._stats_lock = threading.Lock()
         self.faults = faults or FaultInjector.from_env()
@@ -196,8 +396,10 @@ class NcclTransport:
             self.plane = _NcclPlane(self.device)
         elif data_plane == "gloo":
             self.plane = _GlooPlane(host, port + 1000 + channel_rank)
+        elif data_plane == "ipc":
+            self.plane = _IpcPlane(self.device, max(1, int(recv_buffer_size)), control_timeout_s)
         else:
-            raise ValueError("data_plane must be 'nccl' or 'gloo'")
+            raise ValueError("data_plane must be 'nccl', 'ipc' or 'gloo'")
         if is_sender:
             self._sock = self._ctx.socket(zmq.DEALER)
             self._sock.setsockopt(zmq.RCVTIMEO, int(control_timeout_s * 1000))
@@ -240,7 +442,7 @@ class NcclTransport:
             self._q_cv.notify()
 
     def _ready_event(self):
-        if self.plane_kind != "nccl":
+        if self.plane_kind not in ("nccl", "ipc"):
             return None
         ev = torch.cuda.Event()
         ev.record(torch.cuda.current_stream(self.device))
@@ -332,14 +534,22 @@ class NcclTransport:
             tensors, extra = body + aux, {"kind": "bundle", "body_tensors": len(body), "aux_tensors": len(aux)}
         t0 = time.perf_counter()
         self._sock.send(msgpack.dumps(msg, use_bin_type=True))
-        ack = self._sock.recv()
+        frames = self._sock.recv_multipart()
+        ack = frames[0]
         ack_s = time.perf_counter() - t0
         if ack == ACK_RETRY:
             return _RETRY
         if ack != ACK_OK:
             log.error("consumer refused %s (ack=%r)", rid, ack)
             return None
-        handle = self.plane.send(tensors, ready)
+        if self.plane_kind == "ipc":
+            info = msgpack.loads(frames[1], raw=False)
+            copy_s = self.plane.send(tensors, ready, info)
+            self._sock.send(msgpack.dumps({"cmd": "DONE", "request_id": rid, "ticket": info["ticket"]},
+                                          use_bin_type=True))
+            handle = copy_s
+        else:
+            handle = self.plane.send(tensors, ready)
         row = {"direction": "send", "request_id": rid, "payload_bytes": nbytes, "queue_depth_at_submit": depth,
                "queued_bytes_at_submit": queued, "queue_wait_s": (started - enq_ns) / 1e9, "ack_s": ack_s,
                "_enq": enq_ns, **extra}
@@ -352,7 +562,7 @@ class NcclTransport:
                     self._done_cv.wait()
                 handle, row, nbytes, keep = self._done.popleft()
             try:
-                row["nccl_s"] = self.plane.wait(handle)
+                row["nccl_s"] = float(handle) if self.plane_kind == "ipc" else self.plane.wait(handle)
                 row["total_s"] = (time.monotonic_ns() - row.pop("_enq")) / 1e9
                 self._record_stat(row)
             except Exception as exc:
@@ -375,6 +585,8 @@ class NcclTransport:
 
     def release_received(self, request_id: str, payload_bytes: int) -> None:
         assert not self.is_sender
+        if self.plane_kind == "ipc":
+            self.plane.release(request_id)
         if payload_bytes <= 0:
             return
         with self._budget_cv:
@@ -440,11 +652,12 @@ class NcclTransport:
                 self.release_received(rid, int(row["payload_bytes"]))
                 self._mark_failed(rid)
 
-    def _reply(self, ident: bytes, code: bytes, rid: str) -> None:
+    def _reply(self, ident: bytes, code: bytes, rid: str, info: Optional[dict] = None) -> None:
         if self.faults.drop_ack(rid):
             return
         self.faults.maybe_delay()
-        self._sock.send_multipart([ident, code])
+        frames = [ident, code] if info is None else [ident, code, msgpack.dumps(info, use_bin_type=True)]
+        self._sock.send_multipart(frames)
 
     def _listen_loop(self) -> None:
         while not self._closed:
@@ -455,6 +668,9 @@ class NcclTransport:
                 if cmd == "INIT":
                     self.plane.consumer_connect(msg)
                     self._ready = True
+                    continue
+                if cmd == "DONE":
+                    self.plane.done(int(msg["ticket"]))
                     continue
                 rid = msg["request_id"]
                 start = time.monotonic_ns()
@@ -474,16 +690,20 @@ class NcclTransport:
                 if not self._reserve(rid, nbytes):
                     self._reply(ident, ACK_RETRY, rid)
                     continue
+                info = None
                 try:
-                    tensors = [self.plane.alloc(tuple(s["shape"]), getattr(torch, s["dtype"])) for s in specs]
+                    if self.plane_kind == "ipc":
+                        tensors, info = self.plane.grant(rid, specs)
+                    else:
+                        tensors = [self.plane.alloc(tuple(s["shape"]), getattr(torch, s["dtype"])) for s in specs]
                 except (torch.cuda.OutOfMemoryError, RuntimeError) as exc:
                     log.error("allocation for %s failed: %s", rid, exc)
                     self.release_received(rid, nbytes)
                     self._reply(ident, ACK_OOM, rid)
                     self._mark_failed(rid)
                     continue
-                self._reply(ident, ACK_OK, rid)
-                handle = self.plane.recv(tensors)
+                self._reply(ident, ACK_OK, rid, info)
+                handle = self.plane.recv(tensors, info["ticket"]) if info is not None else self.plane.recv(tensors)
                 if cmd == "PUT":
                     payload, kind = tensors[0], "raw"
                 else:

@@ -1,8 +1,11 @@
 """NVLink peer-memory KV channel (one prefill rank -> one decode rank).
 
 The decode rank owns ``num_slots`` receive slots (each ``num_layers`` frames
-of ``frame_stride`` bytes) and one u32 publish flag per (slot, layer), all in
-plain ``cudaMalloc`` memory exported through CUDA IPC.  The prefill rank maps
+of ``frame_stride`` bytes) and, per slot, a control block of u32 words
+
+    [layer flags x num_layers][first token][token flag][credit][pad]
+
+all in plain ``cudaMalloc`` memory exported through CUDA IPC.  The prefill rank maps
 them and its fused encode kernel stores the packed frame straight into the
 slot and release-stores the request sequence number into the flag; the
 decode rank's fused decode kernel acquire-waits (bounded) on the flag and
@@ -11,6 +14,17 @@ the NCCL data plane of kvserve_v1/transport/nccl_transport.py:312-445.
 
 In a single-process (colocated) deployment the same objects are used with
 local pointers and the decode is stream-ordered after the encode.
+
+Receiver credits (the role of kvserve_v1/transport/nccl_transport.py:519-560,
+done on the device): a slot's ``credit`` word holds the sequence number of
+the last request the decode rank has finished reading from it.  The decode
+rank release-stores it (``store_release_u32``, system scope) once the ingest
+kernels that read the slot have completed; before the prefill rank's encode
+kernels store request ``seq`` into a slot, a one-thread kernel on the same
+stream acquire-waits (bounded, over NVLink) until the credit reaches the
+sequence number of the slot's previous request.  With ``num_slots`` slots the
+prefill side runs up to ``num_slots`` requests ahead of the decode side's
+ingest.
 """
 from __future__ import annotations
 
@@ -20,6 +34,11 @@ from typing import Optional
 import torch
 
 from ..ops import ext
+
+
+def ctrl_words(num_layers: int) -> int:
+    """u32 words of one slot's control block."""
+    return num_layers + 4
 
 
 @dataclass
@@ -41,19 +60,24 @@ class FrameReceiver:
         self.slot_bytes = num_layers * frame_stride
         with torch.cuda.device(self.device):
             self.slots_ptr = ext().dev_alloc(num_slots * self.slot_bytes)
-            # per slot: one publish flag per layer, then the first token and its flag
-            self.flags_ptr = ext().dev_alloc(max(256, num_slots * (num_layers + 2) * 4))
+            # per slot: one publish flag per layer, the first token, its flag,
+            # the credit word and one pad word
+            self.flags_ptr = ext().dev_alloc(max(256, num_slots * ctrl_words(num_layers) * 4))
         self._closed = False
 
     def slot_base(self, slot: int) -> int:
         return self.slots_ptr + slot * self.slot_bytes
 
     def flags_base(self, slot: int) -> int:
-        return self.flags_ptr + slot * (self.num_layers + 2) * 4
+        return self.flags_ptr + slot * ctrl_words(self.num_layers) * 4
 
     def token_ptr(self, slot: int) -> int:
         """[token value, token flag] of the slot's request."""
         return self.flags_base(slot) + self.num_layers * 4
+
+    def credit_ptr(self, slot: int) -> int:
+        """The slot's credit word (last sequence number read out of it)."""
+        return self.flags_base(slot) + (self.num_layers + 2) * 4
 
     def handles(self) -> ChannelHandles:
         return ChannelHandles(ext().ipc_get_handle(self.slots_ptr), ext().ipc_get_handle(self.flags_ptr),
@@ -97,10 +121,13 @@ class FrameSender:
         return self.slots_ptr + slot * self.slot_bytes + layer * self.frame_stride
 
     def flag_ptr(self, slot: int, layer: int) -> int:
-        return self.flags_ptr + (slot * (self.num_layers + 2) + layer) * 4
+        return self.flags_ptr + (slot * ctrl_words(self.num_layers) + layer) * 4
 
     def token_ptr(self, slot: int) -> int:
-        return self.flags_ptr + (slot * (self.num_layers + 2) + self.num_layers) * 4
+        return self.flags_ptr + (slot * ctrl_words(self.num_layers) + self.num_layers) * 4
+
+    def credit_ptr(self, slot: int) -> int:
+        return self.flags_ptr + (slot * ctrl_words(self.num_layers) + self.num_layers + 2) * 4
 
     def close(self) -> None:
         with torch.cuda.device(self.device):

@@ -176,7 +176,8 @@ def test_flash_prefill(T, Hq, Hkv):
     assert _rel_err(o, _ref_causal(qkv, Hq, Hkv)) < 2e-2
 
 
-@pytest.mark.parametrize("B,Hq,Hkv,D,ctx", [(1, 32, 8, 128, 8193), (3, 8, 2, 128, 300), (2, 8, 8, 64, 77)])
+@pytest.mark.parametrize("B,Hq,Hkv,D,ctx", [(1, 32, 8, 128, 8193), (3, 8, 2, 128, 300), (2, 8, 8, 64, 77),
+                                             (1, 14, 2, 128, 5000), (2, 28, 4, 128, 700), (1, 24, 8, 128, 333)])
 def test_paged_decode(B, Hq, Hkv, D, ctx):
     ops = _ops()
     torch.manual_seed(2)
@@ -430,3 +431,23 @@ def test_centered_codebook_cuda_matches_cpu(mean_dtype, refine, group, kb, vb):
     bad[1, 0, 0, 0, 0] = 1 << vb
     with pytest.raises(ValueError):
         qz.dequantize(0, bad, m_gpu)
+
+
+@pytest.mark.parametrize("M", [1, 3, 8])
+def test_fused_lm_head_argmax_matches_unfused(M):
+    """LM-head GEMV + greedy argmax in one launch (one rank) picks the token
+    of the bf16 logits of the separate GEMV, ties to the smallest index."""
+    from kvserve_b200 import ops
+    from kvserve_b200.parallel.context import ParallelContext
+    from kvserve_b200.parallel.decode_allreduce import create_decode_collectives
+    V, K = 128256 // 8, 4096
+    dc = create_decode_collectives(ParallelContext(), K, V, num_sites=1, device=torch.device("cuda"))
+    g = torch.Generator(device="cuda").manual_seed(M)
+    for rep in range(2):   # the completion counter resets itself
+        h = torch.randn(M, K, device="cuda", dtype=torch.bfloat16, generator=g)
+        head = torch.randn(V, K, device="cuda", dtype=torch.bfloat16, generator=g) * 0.02
+        tok = dc.greedy(h, head, 0, site=0)
+        ref = ops.argmax(ops.linear(h, head))
+        torch.cuda.synchronize()
+        assert torch.equal(tok, ref)
+    dc.close()

@@ -158,3 +158,21 @@ def test_tp_allreduce_not_created_without_tp():
     from kvserve_b200.parallel.context import ParallelContext
     from kvserve_b200.parallel.tp_allreduce import create_tp_allreduce
     assert create_tp_allreduce(ParallelContext(), 128, 1024, torch.device("cpu")) is None
+
+
+def test_ipc_receive_pool_ranges():
+    """First-fit ranges of the CUDA-IPC data plane's receive pool: aligned,
+    disjoint, refused when full, coalesced again when freed."""
+    from kvserve_b200.transport.nccl_transport import _RangePool
+    p = _RangePool(4096)
+    a = p.alloc(100)
+    b = p.alloc(1000)
+    c = p.alloc(256)
+    assert (a, b, c) == (0, 256, 1280) and all(x % 256 == 0 for x in (a, b, c))
+    assert p.alloc(4096) is None
+    p.free(b, 1000)
+    assert p.alloc(700) == 256          # first fit reuses the hole
+    p.free(a, 100)
+    p.free(256, 700)
+    p.free(c, 256)
+    assert p.free_bytes() == 4096 and p.alloc(4096) == 0
