@@ -34,6 +34,7 @@ __global__ void __launch_bounds__(kThreads) paged_decode_kernel(
     int64_t bt_stride, const int32_t* __restrict__ ctx_lens, int block_size, int Hq, int splits, int chunk,
     float scale_log2, float* __restrict__ part_o, float* __restrict__ part_ml, bf16* __restrict__ out,
     int64_t out_tok_stride) {
+  pdl_trigger();
   constexpr int LANES = D / 8;          // lanes per token row
   constexpr int TPW = 32 / LANES;       // row groups per warp
   constexpr int kGroups = (kThreads / 32) * TPW;
@@ -187,6 +188,7 @@ __global__ void __launch_bounds__(kThreads) paged_decode_kernel(
 template <int D>
 __global__ void merge_splits_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                                     int Hq, int splits, bf16* __restrict__ out, int64_t out_tok_stride) {
+  pdl_trigger();
   const int h = blockIdx.x, b = blockIdx.y;
   const int64_t rec0 = (int64_t(b) * Hq + h) * splits;
   float mx = -INFINITY;

@@ -32,6 +32,7 @@ __global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(
     const int32_t* __restrict__ ctx_lens, int Hq, int splits, int chunk, float scale_log2,
     float* __restrict__ part_o, float* __restrict__ part_ml, bf16* __restrict__ out, int64_t out_tok_stride,
     uint32_t* err) {
+  pdl_trigger();
   using namespace sm100;
   constexpr int D = 128;
   extern __shared__ __align__(128) uint8_t dsm[];

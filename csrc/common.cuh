@@ -102,6 +102,76 @@ __device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t tar
   }
 }
 
+// Low-latency ("LL") peer words: a 64-bit word whose high half is a flag and
+// whose low half is a 32-bit payload.  A naturally aligned 64-bit access is
+// single-copy atomic, so a reader that sees the expected flag also sees the
+// payload written with it: no fence and no separate flag word are needed.
+__device__ __forceinline__ void st_ll(uint64_t* p, uint32_t payload, uint32_t flag) {
+  const uint64_t v = (uint64_t(flag) << 32) | payload;
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_ll(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded poll of an LL word until its flag reaches `flag` (wrap-safe);
+// returns the payload, or sets `ok` false after `deadline_ns` (globaltimer).
+__device__ __forceinline__ uint32_t poll_ll(const uint64_t* p, uint32_t flag, uint64_t deadline_ns, bool& ok) {
+  for (int it = 0;; ++it) {
+    const uint64_t v = ld_ll(p);
+    if (static_cast<int32_t>(uint32_t(v >> 32) - flag) >= 0) return uint32_t(v);
+    if ((it & 63) == 63 && globaltimer_ns() > deadline_ns) {
+      ok = false;
+      return 0u;
+    }
+  }
+}
+
+// Hand-off trace stamps (%globaltimer ns), four per layer: encode start,
+// frame published, ingest start (first CTA past the layer's flag), ingest
+// end.  Starts are stored as ~t with atomicMax (the earliest CTA wins), ends
+// as t with atomicMax; a zeroed buffer means "not stamped".  Null = off.
+__device__ __forceinline__ void trace_start(uint64_t* tr) {
+  if (tr != nullptr) atomicMax(reinterpret_cast<unsigned long long*>(tr), ~(unsigned long long)globaltimer_ns());
+}
+__device__ __forceinline__ void trace_end(uint64_t* tr) {
+  if (tr != nullptr) atomicMax(reinterpret_cast<unsigned long long*>(tr), (unsigned long long)globaltimer_ns());
+}
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch (PDL).  A kernel launched with the PDL
+// attribute may start while its predecessor in the stream is still running;
+// it must call pdl_wait() before it reads anything the predecessor wrote
+// (griddepcontrol.wait returns once the predecessor grid has completed and
+// its memory is visible).  pdl_trigger() lets the dependent launch early; a
+// dependent launched without the attribute still waits for completion, so
+// triggering is always safe.  Decode-step kernels trigger at entry and the
+// weight-streaming GEMVs are PDL launches that prefetch their weights before
+// waiting, which hides the launch gap between consecutive kernels.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// KVSERVE_PDL=0 turns the PDL attribute off (A/B measurements).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  KVS_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...));
+}
+
 // Status codes written by kernels into a device status word.
 enum Status : uint32_t {
   kStatusOk = 0,

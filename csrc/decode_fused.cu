@@ -3,28 +3,32 @@
 // * gemv_allreduce: a row-parallel projection (attention output, MLP down)
 //   of a decode step (M <= 8 tokens) and the tensor-parallel all-reduce of its
 //   [M, N] result in ONE launch.  Each CTA computes 16 output rows from this
-//   rank's K shard, stores its fp32 partial rows into every TP rank's staging
-//   memory over NVLink (plain peer stores, no TMA and no multicast), publishes
-//   a per-CTA flag with st.release.sys, waits (bounded by %globaltimer) for
-//   the same CTA index of every peer, and sums the partials of ranks
-//   0..world-1 in that fixed order — so every rank writes bitwise the same
-//   bf16 result.  The transfer of one CTA's rows overlaps the weight
-//   streaming of the others; there is no separate NCCL call.
+//   rank's K shard and stores every fp32 partial into every TP rank's staging
+//   memory over NVLink as a 64-bit "LL" word (high half: the launch's flag
+//   value, low half: the partial; plain peer stores, no TMA and no
+//   multicast).  It then polls its own staging, bounded by %globaltimer,
+//   until the words of all ranks carry the flag, and sums ranks 0..world-1
+//   in that fixed order — every rank writes bitwise the same bf16 result.
+//   A 64-bit aligned store is single-copy atomic, so no fence and no
+//   separate flag word are needed; the transfer of one CTA's rows overlaps
+//   the weight streaming of the others; there is no separate NCCL call.
 // * gemv_argmax: the decode step's LM-head projection fused with greedy
 //   sampling: per-CTA argmax of its 16 logits, a last-CTA reduction over the
 //   CTAs, and — with tensor parallelism over the vocabulary — an exchange of
-//   each rank's (value, index) with every peer through the same kind of
-//   flagged peer slots.  The logits never go to memory.
-// * decode_epoch_bump: advances the step epoch that tags the flags (one
+//   each rank's (value, index) with every peer as two LL words.  The logits
+//   never go to memory.
+// * decode_epoch_bump: advances the step epoch that tags the words (one
 //   thread, the last kernel of a decode step; a CUDA graph replays the step
 //   with frozen arguments, so the epoch lives in device memory).
 //
 // Flag values are epoch * num_sites + site + 1 (strictly increasing over a
-// run).  Staging and flags are double-buffered by the parity of the launch
-// site: a peer can only reach the next site of the same parity after this
-// rank has published the site in between, which it does only after it has
-// read the current one.  All CTAs of a launch must be co-resident (the host
-// checks the occupancy), so a wait never depends on an unscheduled CTA.
+// run).  Staging is double-buffered by the parity of the launch site: a
+// peer can only write the next site of the same parity after this rank has
+// published the site in between, which it does only after it has read the
+// current one.  All CTAs of a gemv_allreduce launch must be co-resident (the
+// host checks the occupancy), so a poll never depends on an unscheduled CTA.
+// The GEMVs are PDL launches: their weight prefetch overlaps the tail of the
+// previous kernel of the step.
 //
 // The reference has no decode engine (vLLM serves decode, with NCCL
 // all-reduces after its row-parallel layers); these kernels belong to the
@@ -46,21 +50,8 @@ constexpr int kMaxRanks = 8;
 constexpr int kMaxTok = 8;
 
 struct PeerTable {
-  uint64_t stage[kMaxRanks];   // byte address of each rank's staging region (peer-mapped)
-  uint64_t flags[kMaxRanks];   // byte address of each rank's flag region
+  uint64_t stage[kMaxRanks];   // byte address of each rank's LL staging region (peer-mapped)
 };
-
-__device__ __forceinline__ bool spin_flag_geq(const uint32_t* flag, uint32_t target, uint64_t timeout_ns) {
-  const uint64_t start = globaltimer_ns();
-  uint32_t backoff = 0;
-  while (true) {
-    const uint32_t v = ld_acquire_sys_u32(flag);
-    if (static_cast<int32_t>(v - target) >= 0) return true;
-    if (globaltimer_ns() - start > timeout_ns) return false;
-    if (backoff) __nanosleep(backoff);
-    backoff = backoff < 128 ? backoff + 32 : 128;
-  }
-}
 
 __device__ __forceinline__ void report(uint32_t* status, uint32_t code) {
   if (status) atomicCAS(status, uint32_t(kStatusOk), code);
@@ -68,18 +59,26 @@ __device__ __forceinline__ void report(uint32_t* status, uint32_t code) {
 
 constexpr int kMaxChunks = 4;   // 16-row chunks per CTA (grid = N / (16 * chunks) must fit at once)
 
+// Staging of rank `src`'s partial rows in rank `dst`'s region: LL words
+// [parity][src][token][stage_ld] (one 64-bit word per fp32 partial).
+__device__ __forceinline__ uint64_t* stage_word(uint64_t base, int parity, int world, int src, int m,
+                                                int64_t stage_ld, int64_t col) {
+  return reinterpret_cast<uint64_t*>(base) + ((int64_t(parity) * world + src) * kMaxTok + m) * stage_ld + col;
+}
+
 template <int M>
 __global__ void __launch_bounds__(kGemvThreads) gemv_allreduce_kernel(
     const bf16* __restrict__ x, int64_t ldx, const bf16* __restrict__ w, int64_t ldw, bf16* __restrict__ y,
     int64_t ldy, int N, int K, int chunks, PeerTable peers, int rank, int world, int site, int num_sites,
-    const int32_t* __restrict__ epoch_ptr, int64_t stage_ld, int flag_ld, uint64_t timeout_ns,
-    uint32_t* __restrict__ status) {
+    const int32_t* __restrict__ epoch_ptr, int64_t stage_ld, uint64_t timeout_ns, uint32_t* __restrict__ status) {
   extern __shared__ uint4 xs_raw[];  // [M][K] bf16
   __shared__ __align__(16) float part[kMaxChunks][M][kGemvRowsPerCta];
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t col0 = int64_t(blockIdx.x) * chunks * kGemvRowsPerCta;   // N % (16 * chunks) == 0
   GemvWarp<M> g;
   g.prefetch(w, ldw, int(col0) + warp * kGemvRows, N, K, lane);
+  pdl_wait();   // x, the epoch and the staging words of the previous site are the predecessor's
   gemv_stage_x<M>(x, ldx, xs_raw, K);
   __syncthreads();
   for (int c = 0; c < chunks; ++c) {
@@ -97,39 +96,28 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_allreduce_kernel(
   __syncthreads();
   const int parity = site & 1;
   const uint32_t val = uint32_t(*epoch_ptr) * uint32_t(num_sites) + uint32_t(site) + 1u;
-  // this CTA's partial rows -> slot [parity][rank][m][rows] of every rank (itself included)
-  const int per_rank = chunks * M * 4;   // 16-byte pieces
-  for (int t = threadIdx.x; t < world * per_rank; t += blockDim.x) {
-    const int r = t / per_rank, rem = t % per_rank;
-    const int c = rem / (M * 4), m = (rem >> 2) % M, q = rem & 3;
-    float* dst = reinterpret_cast<float*>(peers.stage[r]) + ((int64_t(parity) * world + rank) * kMaxTok + m) * stage_ld +
-                 col0 + c * kGemvRowsPerCta + q * 4;
-    *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(&part[c][m][q * 4]);
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();   // cumulative: orders the CTA's stores (seen through the barrier) before the flags
-    for (int r = 0; r < world; ++r)
-      st_release_sys_u32(reinterpret_cast<uint32_t*>(peers.flags[r]) + (int64_t(parity) * world + rank) * flag_ld +
-                             blockIdx.x, val);
-    const uint32_t* mine = reinterpret_cast<const uint32_t*>(peers.flags[rank]);
-    for (int r = 0; r < world; ++r) {
-      if (!spin_flag_geq(mine + (int64_t(parity) * world + r) * flag_ld + blockIdx.x, val, timeout_ns)) {
-        report(status, kStatusPeerTimeout);
-        break;
-      }
-    }
-  }
-  __syncthreads();
-  const float* stage = reinterpret_cast<const float*>(peers.stage[rank]);
   const int rows = chunks * kGemvRowsPerCta;
+  // push: every partial, tagged with `val`, into slot [parity][rank] of every
+  // rank (itself included) — one single-copy-atomic 64-bit store each
+  for (int t = threadIdx.x; t < world * M * rows; t += blockDim.x) {
+    const int r = t / (M * rows), rem = t % (M * rows);
+    const int m = rem / rows, i = rem % rows;
+    st_ll(stage_word(peers.stage[r], parity, world, rank, m, stage_ld, col0 + i),
+          __float_as_uint(part[i / kGemvRowsPerCta][m][i % kGemvRowsPerCta]), val);
+  }
+  // pull: poll this rank's own staging until every rank's word of the row
+  // carries `val`, then sum in rank order 0..world-1 (bitwise equal on all ranks)
+  const uint64_t deadline = globaltimer_ns() + timeout_ns;
+  bool ok = true;
   for (int t = threadIdx.x; t < M * rows; t += blockDim.x) {
     const int m = t / rows, i = t % rows;
-    const float* p = stage + (int64_t(parity) * world * kMaxTok + m) * stage_ld + col0 + i;
     float s = 0.f;
-    for (int r = 0; r < world; ++r) s += __ldcg(p + int64_t(r) * kMaxTok * stage_ld);   // fixed rank order
+    for (int r = 0; r < world && ok; ++r)
+      s += __uint_as_float(poll_ll(stage_word(peers.stage[rank], parity, world, r, m, stage_ld, col0 + i), val,
+                                   deadline, ok));
     y[int64_t(m) * ldy + col0 + i] = rn(s);
   }
+  if (!ok) report(status, kStatusPeerTimeout);
 }
 
 struct ArgmaxSlot {
@@ -153,8 +141,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_argmax_kernel(
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * kGemvRowsPerCta + warp * kGemvRows;
+  pdl_trigger();
   GemvWarp<M> g;
   g.prefetch(w, ldw, row0, N, K, lane);
+  pdl_wait();
   gemv_stage_x<M>(x, ldx, xs_raw, K);
   __syncthreads();
   float acc[kGemvRows][M];
@@ -210,36 +200,27 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_argmax_kernel(
   if (world > 1) {
     const int parity = site & 1;
     const uint32_t val = uint32_t(*epoch_ptr) * uint32_t(num_sites) + uint32_t(site) + 1u;
-    // slots: [parity][rank][M] ArgmaxSlot, then flags [parity][rank][M] u32
+    // candidate of this rank -> LL words [parity][rank][token][value, index] of every rank
     if (threadIdx.x < world * M) {
       const int r = threadIdx.x / M, m = threadIdx.x % M;
-      ArgmaxSlot* dst = reinterpret_cast<ArgmaxSlot*>(peers.stage[r]) + (int64_t(parity) * world + rank) * kMaxTok + m;
-      *reinterpret_cast<int2*>(dst) = make_int2(__float_as_int(best[m].val), best[m].idx);
+      uint64_t* dst = reinterpret_cast<uint64_t*>(peers.stage[r]) + ((int64_t(parity) * world + rank) * kMaxTok + m) * 2;
+      st_ll(dst, __float_as_uint(best[m].val), val);
+      st_ll(dst + 1, uint32_t(best[m].idx), val);
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence_system();
-      for (int r = 0; r < world; ++r)
-        st_release_sys_u32(reinterpret_cast<uint32_t*>(peers.flags[r]) + (int64_t(parity) * world + rank), val);
-      const uint32_t* mine = reinterpret_cast<const uint32_t*>(peers.flags[rank]);
-      for (int r = 0; r < world; ++r)
-        if (!spin_flag_geq(mine + int64_t(parity) * world + r, val, timeout_ns)) {
-          report(status, kStatusPeerTimeout);
-          break;
-        }
-    }
-    __syncthreads();
     if (threadIdx.x < M) {
       const int m = threadIdx.x;
-      const ArgmaxSlot* slots = reinterpret_cast<const ArgmaxSlot*>(peers.stage[rank]) +
-                                int64_t(parity) * world * kMaxTok + m;
+      const uint64_t deadline = globaltimer_ns() + timeout_ns;
+      bool ok = true;
       float bv = -INFINITY;
       int bi = 0x7fffffff;
-      for (int r = 0; r < world; ++r) {
-        const int2 raw = __ldcg(reinterpret_cast<const int2*>(slots + r * kMaxTok));
-        const float v = __int_as_float(raw.x);
-        if (better(v, raw.y, bv, bi)) { bv = v; bi = raw.y; }
+      for (int r = 0; r < world && ok; ++r) {
+        const uint64_t* src = reinterpret_cast<const uint64_t*>(peers.stage[rank]) +
+                              ((int64_t(parity) * world + r) * kMaxTok + m) * 2;
+        const float v = __uint_as_float(poll_ll(src, val, deadline, ok));
+        const int i = int(poll_ll(src + 1, val, deadline, ok));
+        if (ok && better(v, i, bv, bi)) { bv = v; bi = i; }
       }
+      if (!ok) report(status, kStatusPeerTimeout);
       out[m] = bi;
     }
   } else if (threadIdx.x < M) {
@@ -249,18 +230,17 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_argmax_kernel(
 }
 
 __global__ void decode_epoch_bump_kernel(int32_t* epoch) {
+  pdl_trigger();
   if (threadIdx.x == 0 && blockIdx.x == 0) *epoch += 1;
 }
 
-PeerTable make_table(const std::vector<int64_t>& stage, const std::vector<int64_t>& flags, int world) {
-  KVS_CHECK_ARG(world >= 1 && world <= kMaxRanks && int(stage.size()) == world && int(flags.size()) == world,
-                "decode collective: one staging and one flag address per rank (1..8 ranks)");
+PeerTable make_table(const std::vector<int64_t>& stage, int world) {
+  KVS_CHECK_ARG(world >= 1 && world <= kMaxRanks && int(stage.size()) == world,
+                "decode collective: one staging address per rank (1..8 ranks)");
   PeerTable t{};
   for (int r = 0; r < world; ++r) {
-    KVS_CHECK_ARG(stage[r] % 16 == 0 && flags[r] % 4 == 0 && stage[r] && flags[r],
-                  "decode collective: staging must be 16-byte and flags 4-byte aligned");
+    KVS_CHECK_ARG(stage[r] && stage[r] % 16 == 0, "decode collective: staging must be 16-byte aligned");
     t.stage[r] = uint64_t(stage[r]);
-    t.flags[r] = uint64_t(flags[r]);
   }
   return t;
 }
@@ -293,17 +273,16 @@ void check_gemv_args(const torch::Tensor& x, const torch::Tensor& w, int& M, int
 }  // namespace
 
 void gemv_allreduce_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, std::vector<int64_t> stage_ptrs,
-                         std::vector<int64_t> flag_ptrs, int64_t rank, int64_t site, int64_t num_sites,
-                         torch::Tensor epoch, int64_t stage_ld, int64_t flag_ld, int64_t timeout_ns,
-                         torch::Tensor status) {
+                         int64_t rank, int64_t site, int64_t num_sites, torch::Tensor epoch, int64_t stage_ld,
+                         int64_t timeout_ns, torch::Tensor status) {
   int M, K, N;
   check_gemv_args(x, w, M, K, N);
   const int world = int(stage_ptrs.size());
-  const PeerTable peers = make_table(stage_ptrs, flag_ptrs, world);
+  const PeerTable peers = make_table(stage_ptrs, world);
   KVS_CHECK_ARG(y.is_cuda() && y.scalar_type() == at::kBFloat16 && y.dim() == 2 && y.size(0) == M &&
                     y.size(1) == N && y.stride(1) == 1,
                 "gemv_allreduce: y [M, N] bf16");
-  KVS_CHECK_ARG(N % kGemvRowsPerCta == 0 && N <= stage_ld && stage_ld % 4 == 0,
+  KVS_CHECK_ARG(N % kGemvRowsPerCta == 0 && N <= stage_ld && stage_ld % 2 == 0,
                 "gemv_allreduce: N must be a multiple of 16 within the staging width");
   KVS_CHECK_ARG(rank >= 0 && rank < world && site >= 0 && site < num_sites, "gemv_allreduce: rank/site");
   // fewest 16-row chunks per CTA that keep the whole grid resident (one wave:
@@ -314,7 +293,6 @@ void gemv_allreduce_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, std:
     chunks *= 2;
   KVS_CHECK_ARG(N % (kGemvRowsPerCta * chunks) == 0, "gemv_allreduce: N must split into whole chunks");
   const int grid = N / (kGemvRowsPerCta * chunks);
-  KVS_CHECK_ARG(grid <= flag_ld, "gemv_allreduce: more CTAs than flag slots");
   KVS_CHECK_ARG(epoch.is_cuda() && epoch.scalar_type() == at::kInt && status.is_cuda() &&
                     status.scalar_type() == at::kInt,
                 "gemv_allreduce: epoch / status int32 device tensors");
@@ -334,9 +312,9 @@ void gemv_allreduce_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, std:
       checked_smem = std::max(smem, checked_smem);                                                              \
       ensure_coresident(gemv_allreduce_kernel<MM>, checked_grid, checked_smem, "gemv_allreduce");              \
     }                                                                                                           \
-    gemv_allreduce_kernel<MM><<<grid, kGemvThreads, smem, st>>>(                                                \
-        xp, x.stride(0), wp, w.stride(0), yp, y.stride(0), N, K, chunks, peers, int(rank), world, int(site),   \
-        int(num_sites), ep, stage_ld, int(flag_ld), uint64_t(timeout_ns), sp);                                 \
+    launch_pdl(gemv_allreduce_kernel<MM>, dim3(grid), dim3(kGemvThreads), smem, st, xp, x.stride(0), wp,          \
+               w.stride(0), yp, y.stride(0), N, K, chunks, peers, int(rank), world, int(site), int(num_sites), ep, \
+               stage_ld, uint64_t(timeout_ns), sp);                                                             \
     break;                                                                                                      \
   }
   switch (M) {
@@ -355,7 +333,7 @@ void gemv_allreduce_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, std:
 
 void gemv_argmax_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tensor part_val,
                       torch::Tensor part_idx, torch::Tensor counter, int64_t vocab_begin,
-                      std::vector<int64_t> slot_ptrs, std::vector<int64_t> flag_ptrs, int64_t rank, int64_t site,
+                      std::vector<int64_t> slot_ptrs, int64_t rank, int64_t site,
                       int64_t num_sites, torch::Tensor epoch, int64_t timeout_ns, torch::Tensor status) {
   int M, K, N;
   check_gemv_args(x, w, M, K, N);
@@ -367,7 +345,7 @@ void gemv_argmax_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch
   KVS_CHECK_ARG(counter.scalar_type() == at::kInt && counter.numel() >= 1, "gemv_argmax: counter int32");
   const int world = slot_ptrs.empty() ? 1 : int(slot_ptrs.size());
   PeerTable peers{};
-  if (world > 1) peers = make_table(slot_ptrs, flag_ptrs, world);
+  if (world > 1) peers = make_table(slot_ptrs, world);
   KVS_CHECK_ARG(rank >= 0 && rank < world, "gemv_argmax: rank");
   const size_t smem = size_t(M) * K * 2;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
@@ -387,10 +365,9 @@ void gemv_argmax_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch
                                           200 * 1024));                                                        \
       set = true;                                                                                              \
     }                                                                                                          \
-    gemv_argmax_kernel<MM><<<grid, kGemvThreads, smem, st>>>(xp, x.stride(0), wp, w.stride(0), N, K,          \
-                                                             vocab_begin, pv, pi, cp, op, peers, int(rank),    \
-                                                             world, int(site), int(num_sites), ep,             \
-                                                             uint64_t(timeout_ns), sp);                        \
+    launch_pdl(gemv_argmax_kernel<MM>, dim3(grid), dim3(kGemvThreads), smem, st, xp, x.stride(0), wp,         \
+               w.stride(0), N, K, int64_t(vocab_begin), pv, pi, cp, op, peers, int(rank), world, int(site),    \
+               int(num_sites), ep, uint64_t(timeout_ns), sp);                                                  \
     break;                                                                                                     \
   }
   switch (M) {

@@ -7,10 +7,21 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "ops.h"
 
 namespace kvs {
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("KVSERVE_PDL");
+    return !(e && (e[0] == '0' || e[0] == 'n' || e[0] == 'N' || e[0] == 'f' || e[0] == 'F'));
+  }();
+  return on;
+}
+
 namespace {
 
 __device__ __forceinline__ void unpack8(const uint4& raw, float (&v)[8]) {
@@ -52,6 +63,7 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_kernel(const bf16* __restric
                                                            const bf16* __restrict__ w,
                                                            bf16* __restrict__ out, int hidden,
                                                            float eps) {
+  pdl_trigger();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const bf16* xr = x + row * hidden;
@@ -99,6 +111,7 @@ __global__ void rope_qkv_kernel(bf16* __restrict__ qkv, int64_t qkv_stride, int 
                                 bf16* __restrict__ v_dst, int64_t dst_token_stride,
                                 int64_t dst_head_stride, const int32_t* __restrict__ slot_mapping,
                                 int64_t slot_base) {
+  pdl_trigger();
   const int t = blockIdx.x;
   if (t >= T) return;
   const int half = D / 2;
@@ -139,6 +152,7 @@ __global__ void rope_qkv_kernel(bf16* __restrict__ qkv, int64_t qkv_stride, int 
 // (the layout the fused GEMM epilogue consumes).
 __global__ void silu_mul_kernel(const bf16* __restrict__ gu, bf16* __restrict__ out, int64_t rows,
                                 int inter, int blk) {
+  pdl_trigger();
   const int64_t groups = rows * (inter / 8);
   for (int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; g < groups;
        g += int64_t(gridDim.x) * blockDim.x) {
@@ -161,6 +175,7 @@ __global__ void silu_mul_kernel(const bf16* __restrict__ gu, bf16* __restrict__ 
 __global__ void embedding_kernel(const int32_t* __restrict__ ids, const bf16* __restrict__ table,
                                  bf16* __restrict__ out, int T, int hidden, int64_t vocab_begin,
                                  int64_t vocab_rows) {
+  pdl_trigger();
   const int t = blockIdx.x;
   const int64_t id = int64_t(ids[t]) - vocab_begin;
   const bool mine = id >= 0 && id < vocab_rows;
@@ -175,6 +190,7 @@ __global__ void embedding_kernel(const int32_t* __restrict__ ids, const bf16* __
 __global__ void argmax_kernel(const bf16* __restrict__ logits, int64_t row_stride, int V,
                               int32_t* __restrict__ out, float* __restrict__ out_val,
                               int64_t index_offset) {
+  pdl_trigger();
   __shared__ float sv[32];
   __shared__ int si[32];
   const bf16* r = logits + int64_t(blockIdx.x) * row_stride;
@@ -217,6 +233,7 @@ __global__ void decode_advance_kernel(const int32_t* __restrict__ tok, int32_t* 
                                       int32_t* __restrict__ slot, const int32_t* __restrict__ table,
                                       int64_t table_stride, int block_size, int32_t* __restrict__ out_tokens,
                                       int32_t* __restrict__ step, int max_steps, int B) {
+  pdl_trigger();
   const int b = threadIdx.x;
   const int s = *step;
   __syncthreads();
@@ -243,6 +260,7 @@ __global__ void batch_advance_kernel(const int32_t* __restrict__ tok, const int3
                                      const int32_t* __restrict__ table, int64_t table_stride, int block_size,
                                      int32_t* __restrict__ out_tokens, int64_t ld, int32_t* __restrict__ steps,
                                      int B) {
+  pdl_trigger();
   const int b = threadIdx.x;
   if (b >= B || !active[b]) return;
   const int32_t t = tok[b];

@@ -2,7 +2,8 @@
 // Weight streaming is the whole cost, so each warp owns ROWS output rows and
 // keeps ROWS x UNROLL independent 16-byte weight loads in flight; x lives in
 // shared memory (bf16, 16-byte loads).  Used for every projection of a decode step and for
-// the LM head (where the tcgen05 tile kernel would leave SMs idle).
+// the LM head (where the tcgen05 tile kernel would leave SMs idle).  A PDL launch: the
+// first weight loads are in flight before the kernel waits for its predecessor.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 
@@ -23,8 +24,10 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const bf16* __restrict__
   extern __shared__ uint4 xs_raw[];  // [M][K] bf16
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = (blockIdx.x * (kThreads / 32) + warp) * kGemvRows;
+  pdl_trigger();
   GemvWarp<M> g;
   g.prefetch(w, ldw, row0, N, K, lane);
+  pdl_wait();   // x is the previous kernel's output
   gemv_stage_x<M>(x, ldx, xs_raw, K);
   __syncthreads();
   if (row0 >= N) return;
@@ -86,7 +89,8 @@ void gemv_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, c10::optional<
                                           200 * 1024));                                                    \
       set = true;                                                                                          \
     }                                                                                                      \
-    gemv_kernel<MM><<<grid, kThreads, smem, st>>>(xp, x.stride(0), wp, w.stride(0), yp, y.stride(0), N, K, bp); \
+    launch_pdl(gemv_kernel<MM>, dim3(grid), dim3(kThreads), smem, st, xp, x.stride(0), wp, w.stride(0), yp,     \
+               y.stride(0), N, K, bp);                                                                      \
     break;                                                                                                 \
   }
   switch (M) {

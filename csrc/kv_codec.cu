@@ -62,6 +62,7 @@ struct EncodeArgs {
   int block_size;
   int64_t k_block_stride, v_block_stride;
   int vstats_len;             // tensor-core path: per-token V statistics after the K ones ([2][2][T])
+  uint64_t* trace;            // this layer's 4 trace stamps, or null
 };
 
 // Address of row (token t, head h) of a K or V source that is either a
@@ -139,6 +140,7 @@ struct DecodeArgs {
   uint64_t timeout_ns;
   uint32_t* status;
   int tile_tokens;
+  uint64_t* trace;            // [num_layers_total][4] trace stamps, or null
 };
 
 __device__ __forceinline__ void load8(const bf16* p, float (&v)[8], uint4& raw) {
@@ -274,6 +276,7 @@ __device__ __forceinline__ void write_bitpack_header(uint8_t* dst, int bits, uin
 // ---------------------------------------------------------------------------
 template <int D>
 __global__ void __launch_bounds__(kThreads) kv_kstats_kernel(EncodeArgs a) {
+  if (threadIdx.x == 0 && a.trace != nullptr) trace_start(a.trace);
   constexpr int LANES = D / 8, RPW = 32 / LANES;
   constexpr int kRowsPerIter = (kThreads / 32) * RPW;
   extern __shared__ uint32_t sstat[];  // [2*H*D]
@@ -409,6 +412,7 @@ __device__ void encode_signal_done(const EncodeArgs& a) {
       while (int64_t(globaltimer_ns()) < done && globaltimer_ns() - t_begin < cap) __nanosleep(2000);
     }
     *a.counter = 0;
+    if (a.trace != nullptr) trace_end(a.trace + 1);
     __threadfence_system();
     // a CTA that gave up on its tensor-core work (counter[1] set) leaves the
     // frame unpublished: the decoder's bounded wait reports it
@@ -419,6 +423,7 @@ __device__ void encode_signal_done(const EncodeArgs& a) {
 // ITERS: rows of one token a lane holds in the V part (ceil(H / rows per warp step)).
 template <int D, int ITERS>
 __global__ void __launch_bounds__(kThreads, ITERS <= 4 ? 3 : 1) kv_quant_kernel(EncodeArgs a) {
+  if (threadIdx.x == 0 && a.trace != nullptr) trace_start(a.trace);
   constexpr int LANES = D / 8, RPW = 32 / LANES;
   constexpr int kWarps = kThreads / 32;
   constexpr int kRowsPerIter = kWarps * RPW;
@@ -682,6 +687,7 @@ __global__ void __launch_bounds__(kThreads, 3) kv_decode_kernel(DecodeArgs a) {
       // acquire side: the flag was read with ld.acquire.sys; this fence plus
       // the barrier below order every thread's frame reads after it
       if (ok) asm volatile("fence.acq_rel.sys;" ::: "memory");
+      if (ok && a.trace != nullptr) trace_start(a.trace + 4 * layer + 2);
       s_ok = ok;
     }
     __syncthreads();
@@ -816,6 +822,7 @@ __global__ void __launch_bounds__(kThreads, 3) kv_decode_kernel(DecodeArgs a) {
       }
     }
     __syncthreads();
+    if (threadIdx.x == 0 && a.trace != nullptr) trace_end(a.trace + 4 * layer + 3);
   }
 }
 
@@ -896,13 +903,15 @@ void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom
                      int64_t layer, c10::optional<torch::Tensor> pacing, double rate_bytes_per_ns,
                      int64_t max_ctas, int64_t tile_tokens, int64_t part_mask,
                      c10::optional<torch::Tensor> block_table, bool hnd, bool allow_mma,
-                     c10::optional<torch::Tensor> hs_table, int64_t hs_row0) {
+                     c10::optional<torch::Tensor> hs_table, int64_t hs_row0, int64_t trace_ptr) {
   const FrameGeom g = geom_from(geom);
   KVS_CHECK_ARG(part_mask >= 1 && part_mask <= 3, "part_mask must be 1 (K), 2 (V) or 3");
   KVS_CHECK_ARG(k.is_cuda() && v.is_cuda() && k.scalar_type() == at::kBFloat16 &&
                     v.scalar_type() == at::kBFloat16,
                 "k/v must be CUDA bf16");
+  KVS_CHECK_ARG(trace_ptr % 8 == 0, "trace stamps must be 8-byte aligned");
   EncodeArgs a{};
+  a.trace = reinterpret_cast<uint64_t*>(trace_ptr);
   int64_t src_heads;
   if (block_table.has_value()) {
     // paged source: [num_blocks, block_size, H, D] (NHD) or [num_blocks, H, block_size, D] (HND)
@@ -1028,11 +1037,13 @@ void kv_decode_layers(int64_t frame_base, int64_t frame_stride, std::vector<int6
                       int64_t layer_begin, int64_t num_layers, int64_t timeout_ns,
                       torch::Tensor status, int64_t max_ctas, int64_t tile_tokens,
                       c10::optional<torch::Tensor> n_lows, int64_t part_mask,
-                      c10::optional<torch::Tensor> layer_ptrs, bool hnd) {
+                      c10::optional<torch::Tensor> layer_ptrs, bool hnd, int64_t trace_ptr) {
   const FrameGeom g = geom_from(geom);
   KVS_CHECK_ARG(part_mask >= 1 && part_mask <= 3, "part_mask must be 1 (K), 2 (V) or 3");
+  KVS_CHECK_ARG(trace_ptr % 8 == 0, "trace stamps must be 8-byte aligned");
   KVS_CHECK_ARG(kv_cache.is_cuda() && kv_cache.scalar_type() == at::kBFloat16, "kv_cache must be CUDA bf16");
   DecodeArgs a{};
+  a.trace = reinterpret_cast<uint64_t*>(trace_ptr);
   int64_t L, bs;
   if (layer_ptrs.has_value()) {
     // per-layer K/V tensors; kv_cache is one of them as a layout template:

@@ -112,6 +112,7 @@ __global__ void __launch_bounds__(kMmaDecThreads) kv_decode_mma_kernel(DecodeArg
         }
       }
       if (ok) asm volatile("fence.acq_rel.sys;" ::: "memory");
+      if (ok && a.trace != nullptr) trace_start(a.trace + 4 * layer + 2);
       s_ok = ok;
       s_layer = layer;
     }
@@ -386,6 +387,7 @@ __global__ void __launch_bounds__(kDwThreads, 1) kv_decode_ws_kernel(DecodeArgs 
           }
           if (ok) asm volatile("fence.acq_rel.sys;" ::: "memory");
           else s_bad = 1;
+          if (ok && a.trace != nullptr) trace_start(a.trace + 4 * layer + 2);
           s_ok[grp] = ok;
         }
         asm volatile("bar.sync %0, 128;" ::"r"(1 + grp) : "memory");
@@ -544,6 +546,7 @@ __global__ void __launch_bounds__(kDwThreads, 1) kv_decode_ws_kernel(DecodeArgs 
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
+      if (quarter == 0 && lane == 0 && dst != nullptr && a.trace != nullptr) trace_end(a.trace + 4 * layer + 3);
     }
   }
   tc_fence_before();

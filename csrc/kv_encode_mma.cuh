@@ -130,6 +130,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   uint64_t* tempty = tfull + kWsAcc + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + kWsAcc);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0 && a.trace != nullptr) trace_start(a.trace);
   const FrameGeom& g = a.g;
   const int HD = g.H * D;
   const int ntile = (g.T + 127) / 128;

@@ -16,13 +16,13 @@ void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom
                      int64_t flag_ptr, int64_t seq, int64_t layer, c10::optional<torch::Tensor> pacing,
                      double rate_bytes_per_ns, int64_t max_ctas, int64_t tile_tokens, int64_t part_mask,
                      c10::optional<torch::Tensor> block_table, bool hnd, bool allow_mma,
-                     c10::optional<torch::Tensor> hs_table, int64_t hs_row0);
+                     c10::optional<torch::Tensor> hs_table, int64_t hs_row0, int64_t trace_ptr);
 void kv_decode_layers(int64_t frame_base, int64_t frame_stride, std::vector<int64_t> geom, torch::Tensor orders,
                       torch::Tensor sign_bits, torch::Tensor kv_cache, torch::Tensor block_table,
                       int64_t tok_offset, int64_t flags_ptr, int64_t seq, int64_t layer_begin, int64_t num_layers,
                       int64_t timeout_ns, torch::Tensor status, int64_t max_ctas, int64_t tile_tokens,
                       c10::optional<torch::Tensor> n_lows, int64_t part_mask,
-                      c10::optional<torch::Tensor> layer_ptrs, bool hnd);
+                      c10::optional<torch::Tensor> layer_ptrs, bool hnd, int64_t trace_ptr);
 
 // ---- modular pipeline kernels (bitpack.cu)
 void bitpack_encode(torch::Tensor src, torch::Tensor out, int64_t bits, torch::Tensor status);
@@ -87,12 +87,11 @@ void gemv_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, c10::optional<
 // decode-step fusions (decode_fused.cu): row-parallel GEMV + one-shot peer
 // all-reduce, LM-head GEMV + greedy argmax (+ TP exchange), step epoch
 void gemv_allreduce_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, std::vector<int64_t> stage_ptrs,
-                         std::vector<int64_t> flag_ptrs, int64_t rank, int64_t site, int64_t num_sites,
-                         torch::Tensor epoch, int64_t stage_ld, int64_t flag_ld, int64_t timeout_ns,
-                         torch::Tensor status);
+                         int64_t rank, int64_t site, int64_t num_sites, torch::Tensor epoch, int64_t stage_ld,
+                         int64_t timeout_ns, torch::Tensor status);
 void gemv_argmax_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tensor part_val,
                       torch::Tensor part_idx, torch::Tensor counter, int64_t vocab_begin,
-                      std::vector<int64_t> slot_ptrs, std::vector<int64_t> flag_ptrs, int64_t rank, int64_t site,
+                      std::vector<int64_t> slot_ptrs, int64_t rank, int64_t site,
                       int64_t num_sites, torch::Tensor epoch, int64_t timeout_ns, torch::Tensor status);
 void decode_epoch_bump(torch::Tensor epoch);
 void flash_prefill(torch::Tensor qkv, int64_t Hq, int64_t Hkv, double scale, torch::Tensor out, torch::Tensor err);

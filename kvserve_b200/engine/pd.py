@@ -33,6 +33,7 @@ from ..parallel.context import ParallelContext
 from ..parallel.decode_allreduce import create_decode_collectives
 from ..parallel.tp_allreduce import create_tp_allreduce
 from ..transport.p2p import FrameReceiver, FrameSender
+from ..utils.trace import decode_stamps, nvtx_range, summarize_stamps, trace_enabled, write_trace_row
 from .kv_cache import PagedKVCache
 from .transfer import KVTransfer, TransferProfile
 
@@ -51,6 +52,7 @@ class RequestTiming:
     launches: int = 0                        # kernels of this package launched for the request
     payload_bytes: int = 0
     raw_bytes: int = 0
+    trace: dict = field(default_factory=dict)  # device stamp summary (KVSERVE_TRACE=1)
 
 
 @dataclass
@@ -63,7 +65,7 @@ class PDEngine:
     def __init__(self, cfg: ModelConfig, ctx: ParallelContext, profile: TransferProfile, max_prompt: int = 8192,
                  max_new_tokens: int = 128, block_size: int = 16, seed: int = 0, link_gbps: float = 0.0,
                  use_graphs: bool = True, ingest_timeout_s: float = 30.0, encode_ctas: int = 222,
-                 profiles: Optional[dict] = None, num_slots: int = 2):
+                 profiles: Optional[dict] = None, num_slots: int = 2, max_batch: int = 1):
         self.cfg, self.ctx, self.profile = cfg, ctx, profile
         self.device = torch.device("cuda", torch.cuda.current_device())
         self.max_prompt, self.max_new, self.block_size = max_prompt, max_new_tokens, block_size
@@ -89,6 +91,9 @@ class PDEngine:
         self.compute = torch.cuda.current_stream(self.device)
         self.seq = 0
         self.status = ops.device_status(self.device)
+        # %globaltimer stamps of the hand-off kernels (KVSERVE_TRACE=1)
+        self.trace = torch.zeros((cfg.num_layers, 4), dtype=torch.int64, device=self.device) \
+            if trace_enabled() else None
         self.d_first = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._tok_host = torch.empty(1, dtype=torch.int32, pin_memory=True)
         L = cfg.num_layers
@@ -101,8 +106,10 @@ class PDEngine:
             self.positions = torch.arange(max_prompt, dtype=torch.int32, device=self.device)
         if ctx.is_decode:
             self.max_blocks = (max_prompt + max_new_tokens + block_size - 1) // block_size + 1
-            # block 0 is a scratch block for graph warm-up
-            self.kv = PagedKVCache(L, self.max_blocks + 1, block_size, m.hkv, m.D, self.device)
+            # room for `max_batch` requests of the largest size (continuous
+            # batching, engine.pipeline) plus one scratch block for padding rows
+            self.max_batch = max(1, int(max_batch))
+            self.kv = PagedKVCache(L, self.max_batch * self.max_blocks + 1, block_size, m.hkv, m.D, self.device)
             self._scratch_block = self.kv.allocate(1)
             self.ingest_stream = torch.cuda.Stream(self.device, priority=-1)
             self._init_decode_buffers()
@@ -246,6 +253,46 @@ class PDEngine:
             ops.count_launches(1)
             ops.ext().store_release_u32(self.receiver.credit_ptr(slot), seq)
 
+    def _launch_prefill(self, ids: torch.Tensor, seq: int, slot: int, xfer: "KVTransfer", rate: float,
+                        ev: Optional[dict] = None, table: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Prefill side of one request (asynchronous): the prompt's forward
+        pass with each layer's K/V encoded and pushed into receive slot
+        ``slot`` on the encode stream right after the layer is written (after
+        the slot's credit is taken), and the sampled first token published
+        next to the slot's flags.  Colocated, each layer is also decoded into
+        the paged cache (``table``) on the encode stream.  Returns the first
+        token (int32 [1] on the device)."""
+        ctx, m = self.ctx, self.model
+        T = int(ids.numel())
+        enc = self.enc_stream
+        enc.wait_stream(self.compute)
+        with torch.cuda.stream(enc):
+            self._take_credit(slot, seq)
+
+        def hook(l: int) -> None:
+            self.layer_events[l].record(self.compute)
+            enc.wait_event(self.layer_events[l])
+            if l == 0 and ev is not None:
+                ev["enc_start"].record(enc)
+            with torch.cuda.stream(enc), nvtx_range(f"kv encode L{l}"):
+                flag = self.sender.flag_ptr(slot, l) if ctx.distributed else 0
+                xfer.encode(l, self.k_buf[l, :T], self.v_buf[l, :T], self.sender.frame_ptr(slot, l), flag,
+                            seq, self.pacing, rate, self.encode_ctas, trace=self.trace)
+                if not ctx.distributed:
+                    xfer.ingest_layer(l, T, self.sender.frame_ptr(slot, l), self.kv.cache, table, self.status, seq,
+                                      trace=self.trace)
+
+        first = m.prefill(ids, self.positions[:T], self.k_buf, self.v_buf, layer_hook=hook, sample=True)
+        if ev is not None:
+            ev["prefill"].record(self.compute)
+        if ctx.distributed:
+            # the token lands next to the layer flags of the decode slot
+            ops.count_launches(1)
+            ops.ext().publish_token(first, self.sender.token_ptr(slot), seq)
+        if ev is not None:
+            ev["encode"].record(enc)
+        return first
+
     def generate(self, prompt_ids: torch.Tensor, max_new_tokens: Optional[int] = None,
                  return_tokens: bool = True, sync: bool = True, profile: Optional[str] = None,
                  link_gbps: Optional[float] = None) -> GenerateResult:
@@ -286,48 +333,25 @@ class PDEngine:
         c_launch0 = ops.launches()
         replays = 0
         ev["start"].record(self.compute)
+        if self.trace is not None:
+            self.trace.zero_()
         ids = prompt_ids.to(self.device, non_blocking=True)
         timing = RequestTiming(payload_bytes=xfer.payload_bytes(Tx), raw_bytes=xfer.raw_bytes(Tx))
-        blocks = None
+        blocks = table = None
         if ctx.is_decode:
             blocks = self.kv.allocate(T + n_new)
             table = self.kv.block_table(blocks, self.max_blocks)
             if ctx.distributed:
                 self.ingest_stream.wait_stream(self.compute)
-                with torch.cuda.stream(self.ingest_stream):
+                with torch.cuda.stream(self.ingest_stream), nvtx_range("kv ingest"):
                     xfer.ingest_all(Tx, self.receiver.slot_base(slot), self.receiver.frame_stride,
                                     self.receiver.flags_base(slot), self.kv.cache, table, self.status, seq,
-                                    self.ingest_timeout_ns)
+                                    self.ingest_timeout_ns, trace=self.trace)
                     ev["ingest"].record(self.ingest_stream)
         if ctx.is_prefill:
-            enc = self.enc_stream
-            enc.wait_stream(self.compute)
-
-            with torch.cuda.stream(enc):
-                self._take_credit(slot, seq)
-
-            def hook(l: int) -> None:
-                self.layer_events[l].record(self.compute)
-                enc.wait_event(self.layer_events[l])
-                if l == 0:
-                    ev["enc_start"].record(enc)
-                with torch.cuda.stream(enc):
-                    flag = self.sender.flag_ptr(slot, l) if ctx.distributed else 0
-                    xfer.encode(l, self.k_buf[l, :Tx], self.v_buf[l, :Tx], self.sender.frame_ptr(slot, l), flag,
-                                seq, self.pacing, rate, self.encode_ctas)
-                    if not ctx.distributed:
-                        xfer.ingest_layer(l, Tx, self.sender.frame_ptr(slot, l), self.kv.cache, table,
-                                          self.status, seq)
-
-            first = m.prefill(ids[:Tx], self.positions[:Tx], self.k_buf, self.v_buf, layer_hook=hook, sample=True)
-            ev["prefill"].record(self.compute)
-            if ctx.distributed:
-                # the token lands next to the layer flags of the decode slot
-                ops.count_launches(1)
-                ops.ext().publish_token(first, self.sender.token_ptr(slot), seq)
-            ev["encode"].record(enc)
+            first = self._launch_prefill(ids[:Tx], seq, slot, xfer, rate, ev, table)
             if not ctx.distributed:
-                ev["ingest"].record(enc)
+                ev["ingest"].record(self.enc_stream)
                 self.d_first.copy_(first)
             else:
                 self._first_host(first, ev, timing, t_host0)
@@ -369,6 +393,11 @@ class PDEngine:
             code = int(dc.status[0].item())
             dc.status.zero_()
             raise RuntimeError(f"decode collective failed on rank {ctx.rank}: status {code} (peer timeout)")
+        if self.trace is not None:
+            st_ = decode_stamps(self.trace.cpu())
+            timing.trace = summarize_stamps(st_)
+            write_trace_row({"rank": ctx.rank, "role": ctx.role, "seq": seq, "tokens": T,
+                             "payload_bytes": timing.payload_bytes, **timing.trace, **st_})
         timing.launches = ops.launches() - c_launch0 + replays * getattr(self, "_graph_launches", 0)
         timing.request_host = 1e3 * (time.perf_counter() - t_host0)
         e = lambda k: ev["start"].elapsed_time(ev[k])  # noqa: E731

@@ -187,6 +187,60 @@ def _p50(xs: list[float]) -> float:
     return s[len(s) // 2] if s else float("nan")
 
 
+def _pct(xs: list[float], q: float) -> float:
+    s = sorted(x for x in xs if x == x)
+    return s[min(len(s) - 1, int(q * len(s)))] if s else float("nan")
+
+
+def serve_pipelined(engine, library, prompts: list, rate_per_s: float, link_gbps: float, max_new: int, slo_ms: float,
+                    acc_req: float, t_model_ms: float, max_batch: int = 8, seed: int = 0, server=None) -> dict:
+    """Real-time Poisson arrivals on the pipelined server (prefill of one
+    request overlaps the decode of earlier ones); the prefill leader's
+    controller picks each request's profile and learns from the decode
+    leader's KV-ready times.  Returns the summary of this link cap (every
+    rank calls it; the summary is the same on all ranks)."""
+    from ..compression.controller.online import OnlineController
+    from .pipeline import PipelinedServer, Request, merge_records, poisson_schedule
+    ctx = engine.ctx
+    server = server or PipelinedServer(engine, max_batch=max_batch)
+    ctrl = OnlineController(library, epsilon=0.1, rng=random.Random(seed))
+    infos: dict[int, dict] = {}
+    arrivals = poisson_schedule(len(prompts), rate_per_s, seed)
+    reqs = [Request(i, p, max_new, a, link_gbps=link_gbps) for i, (p, a) in enumerate(zip(prompts, arrivals))]
+    t_model = [t_model_ms]
+
+    def decide(req, state):
+        if state["prefill_ms"]:
+            t_model[0] = 0.8 * t_model[0] + 0.2 * state["prefill_ms"][-1]
+        V = engine.xfer.raw_bytes(int(req.prompt.numel()))
+        need = bucket_requirement(library, acc_req)
+        if need is None:
+            infos[req.index] = {"reason": "accuracy"}
+            return "off"
+        prof, info = ctrl.select_profile(V, link_gbps * 125.0, t_model[0], slo_ms, need)
+        infos[req.index] = info
+        return prof.profile_id if prof is not None else "off"
+
+    def feedback(req, kv_ready_ms):
+        info = infos.get(req.index)
+        if info is not None and "reason" not in info:
+            ctrl.update(info, kv_ready_ms)
+
+    recs = merge_records(ctx, server.serve(reqs, decide, feedback))
+    span_s = max(r.done_ms + r.arrival_ms for r in recs) / 1e3
+    counts: dict[str, int] = {}
+    for r in recs:
+        counts[r.profile] = counts.get(r.profile, 0) + 1
+    return {"requests": len(recs), "rate_per_s": rate_per_s, "link_gbps": link_gbps,
+            "ttft_ms_p50": round(_pct([r.first_token_ms for r in recs], 0.5), 3),
+            "ttft_ms_p90": round(_pct([r.first_token_ms for r in recs], 0.9), 3),
+            "queue_ms_p50": round(_pct([r.launch_ms for r in recs], 0.5), 3),
+            "prefill_ms_p50": round(_pct([r.prefill_ms - r.launch_ms for r in recs], 0.5), 3),
+            "request_ms_p50": round(_pct([r.done_ms for r in recs], 0.5), 3),
+            "output_tokens_per_s": round(sum(len(r.tokens or []) for r in recs) / span_s, 2),
+            "profiles": counts}
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="llama-3-70b")
@@ -199,6 +253,9 @@ def main(argv=None) -> None:
     ap.add_argument("--acc-req", type=float, default=0.97)
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (smoke runs)")
     ap.add_argument("--speeds", default="", help="JSON {profile: harmonic MB/s} measured by the microbench")
+    ap.add_argument("--serial", action="store_true",
+                    help="one request at a time on a virtual clock (default: pipelined, real-time arrivals)")
+    ap.add_argument("--max-batch", type=int, default=8, help="decode rows of the pipelined server")
     a = ap.parse_args(argv)
     from ..models.config import get_config
     from ..parallel.context import destroy_parallel, init_parallel
@@ -209,7 +266,7 @@ def main(argv=None) -> None:
         import dataclasses
         cfg = dataclasses.replace(cfg, num_layers=a.layers)
     engine = PDEngine(cfg, ctx, ENGINE_PROFILES["off"], max_prompt=a.prompt_len, max_new_tokens=a.max_new,
-                      profiles=dict(ENGINE_PROFILES))
+                      profiles=dict(ENGINE_PROFILES), max_batch=1 if a.serial else a.max_batch)
     engine.warmup(prompt_len=min(512, a.prompt_len))
     g = torch.Generator().manual_seed(1)
     prompts = [torch.randint(0, cfg.vocab, (a.prompt_len,), generator=g, dtype=torch.int32).pin_memory()
@@ -222,7 +279,17 @@ def main(argv=None) -> None:
               "world": ctx.world_size, "slo_ms": round(slo, 2), "acc_req": a.acc_req,
               "library": [{"id": p.profile_id, "cr": round(p.compression_ratio, 3), "acc": round(p.accuracy, 4)}
                           for p in library.get_all_profiles()], "links": {}}
+    report["mode"] = "serial (virtual clock)" if a.serial else f"pipelined (real-time arrivals, {a.max_batch} rows)"
+    pserver = None
+    if not a.serial:
+        from .pipeline import PipelinedServer
+        pserver = PipelinedServer(engine, max_batch=a.max_batch)
     for cap in (float(x) for x in a.link_gbps.split(",") if x):
+        if pserver is not None:
+            report["links"][f"{cap:g}"] = serve_pipelined(engine, library, prompts, a.rate, cap, a.max_new, slo,
+                                                          a.acc_req, probe.timing.prefill_done, a.max_batch,
+                                                          server=pserver)
+            continue
         server = ServiceAwareServer(engine, library, slo, a.acc_req)
         server.t_model_ms = probe.timing.prefill_done
         served = server.serve(prompts, a.rate, cap, a.max_new)

@@ -127,7 +127,8 @@ class KVTransfer:
 
     # ------------------------------------------------------------ prefill
     def encode(self, layer: int, k: torch.Tensor, v: torch.Tensor, frame_ptr: int, flag_ptr: int, seq: int,
-               pacing: Optional[torch.Tensor] = None, rate_bytes_per_ns: float = 0.0, max_ctas: int = 222) -> None:
+               pacing: Optional[torch.Tensor] = None, rate_bytes_per_ns: float = 0.0, max_ctas: int = 222,
+               trace: Optional[torch.Tensor] = None) -> None:
         if self._state is None:
             self._state = kc.EncoderState(self.device, max_tokens=self.max_tokens)
         if self.D == 128 and getattr(self, "_hs_table", None) is None:
@@ -137,18 +138,21 @@ class KVTransfer:
         kc.encode_layer(k, v, self.spec(layer, k.shape[0]), self.orders[layer], self.sign_bits[layer], frame_ptr,
                         self._state, flag_ptr=flag_ptr, seq=seq, layer=layer, pacing=pacing,
                         rate_bytes_per_ns=rate_bytes_per_ns, max_ctas=max_ctas,
-                        hs_table=getattr(self, "_hs_table", None), hs_row0=layer * self.H)
+                        hs_table=getattr(self, "_hs_table", None), hs_row0=layer * self.H,
+                        trace_ptr=trace[layer].data_ptr() if trace is not None else 0)
 
     # ------------------------------------------------------------- decode
     def ingest_layer(self, layer: int, T: int, frame_ptr: int, kv_cache: torch.Tensor, block_table: torch.Tensor,
-                     status: torch.Tensor, seq: int, tok_offset: int = 0) -> None:
+                     status: torch.Tensor, seq: int, tok_offset: int = 0, trace: Optional[torch.Tensor] = None) -> None:
         spec = self.spec(layer, T)
         kc.decode_layers(frame_ptr, kc.frame_layout(spec).frame_bytes, spec, self.orders, self.sign_bits, kv_cache,
-                         block_table, status, tok_offset=tok_offset, seq=seq, layer_begin=layer, num_layers=1)
+                         block_table, status, tok_offset=tok_offset, seq=seq, layer_begin=layer, num_layers=1,
+                         trace_ptr=trace.data_ptr() if trace is not None else 0)
 
     def ingest_all(self, T: int, slot_base: int, frame_stride: int, flags_ptr: int, kv_cache: torch.Tensor,
                    block_table: torch.Tensor, status: torch.Tensor, seq: int, timeout_ns: int,
-                   tok_offset: int = 0, max_ctas: int = 148) -> None:
+                   tok_offset: int = 0, max_ctas: int = 148, trace: Optional[torch.Tensor] = None) -> None:
         kc.decode_layers(slot_base, frame_stride, self.max_spec(T), self.orders, self.sign_bits, kv_cache,
                          block_table, status, tok_offset=tok_offset, flags_ptr=flags_ptr, seq=seq, layer_begin=0,
-                         num_layers=self.L, timeout_ns=timeout_ns, max_ctas=max_ctas, n_lows=self.n_lows)
+                         num_layers=self.L, timeout_ns=timeout_ns, max_ctas=max_ctas, n_lows=self.n_lows,
+                         trace_ptr=trace.data_ptr() if trace is not None else 0)

@@ -20,6 +20,7 @@ import torch
 import torch.distributed as dist
 
 from .. import ops
+from ..utils.trace import nvtx_pop, nvtx_push
 from .config import ModelConfig
 
 
@@ -172,6 +173,7 @@ class LlamaShard:
         h = ops.rmsnorm(residual, self.layers[0].in_norm, cfg.rms_eps)
         fused_qkv = self.D == 128 and T > ops.GEMV_MAX_M
         for l, lw in enumerate(self.layers):
+            nvtx_push(f"prefill L{l}")
             if fused_qkv:  # projection + bias + rotary + K/V copy in one GEMM
                 qkv = ops.gemm_qkv_rope(h, lw.qkv, self.hq, self.hkv, positions, self.cos_sin, bias=lw.qkv_bias,
                                         k_dst=k_buf[l, :T], v_dst=v_buf[l, :T])
@@ -187,6 +189,7 @@ class LlamaShard:
             d = self._mlp(h, lw)
             nxt = self.layers[l + 1].in_norm if l + 1 < len(self.layers) else self.final_norm
             h = ops.rmsnorm(d, nxt, cfg.rms_eps, residual=residual)
+            nvtx_pop()
         if not sample:
             return None
         return self.greedy(h[T - 1:T].contiguous())

@@ -353,7 +353,7 @@ def encode_layer(k: torch.Tensor, v: torch.Tensor, spec: FrameSpec, order: torch
                  rate_bytes_per_ns: float = 0.0, max_ctas: int = 222, tile_tokens: Optional[int] = None,
                  part_mask: int = 3, block_table: Optional[torch.Tensor] = None, hnd: bool = False,
                  allow_mma: Optional[bool] = None, hs_table: Optional[torch.Tensor] = None,
-                 hs_row0: int = 0) -> None:
+                 hs_row0: int = 0, trace_ptr: int = 0) -> None:
     """Launch the fused encode of one layer into ``frame_ptr`` (local or peer).
 
     The defaults (222 CTAs per part; tiles of 64 rows = 64/H tokens, one
@@ -370,7 +370,9 @@ def encode_layer(k: torch.Tensor, v: torch.Tensor, spec: FrameSpec, order: torch
     with the signed transform table ``hs_table`` (rows of head h of this
     layer at ``(hs_row0 + h) * 128``; built from ``sign_bits`` and cached in
     ``state`` when not given).  Either way there are two launches:
-    statistics, then quantise + pack + publish."""
+    statistics, then quantise + pack + publish.  ``trace_ptr`` (8-byte
+    aligned device address, 0 = off) receives this layer's encode-start and
+    frame-published %globaltimer stamps (words 0 and 1 of its four)."""
     if allow_mma is None:
         allow_mma = _MMA_ENCODE
     from ._ext import ext
@@ -389,7 +391,7 @@ def encode_layer(k: torch.Tensor, v: torch.Tensor, spec: FrameSpec, order: torch
     ext().kv_encode_layer(k, v, spec.params(), order, sign_bits, int(frame_ptr), state.stats, state.counter,
                           int(flag_ptr), int(seq), int(layer), pacing, float(rate_bytes_per_ns), int(max_ctas),
                           int(tile_tokens), int(part_mask), block_table, bool(hnd), bool(mma), hs_table,
-                          int(hs_row0))
+                          int(hs_row0), int(trace_ptr))
 
 
 def decode_layers(frame_base: int, frame_stride: int, spec: FrameSpec, orders: torch.Tensor,
@@ -397,13 +399,16 @@ def decode_layers(frame_base: int, frame_stride: int, spec: FrameSpec, orders: t
                   status: torch.Tensor, tok_offset: int = 0, flags_ptr: int = 0, seq: int = 1,
                   layer_begin: int = 0, num_layers: int = 1, timeout_ns: int = 5_000_000_000,
                   max_ctas: int = 222, tile_tokens: Optional[int] = None, n_lows: Optional[torch.Tensor] = None,
-                  part_mask: int = 3, layer_ptrs: Optional[torch.Tensor] = None, hnd: bool = False) -> None:
+                  part_mask: int = 3, layer_ptrs: Optional[torch.Tensor] = None, hnd: bool = False,
+                  trace_ptr: int = 0) -> None:
     """Launch the fused decode of ``num_layers`` consecutive frames into the
     paged cache ``kv_cache`` ``[L, 2, num_blocks, block_size, H, D]``.  With
     ``flags_ptr`` the kernel waits (bounded by ``timeout_ns``) for each
     layer's publish flag to reach ``seq``.  ``n_lows`` (int32 [L] on the
     device) gives each layer's low-section head count when it varies; the
-    frame stride must then hold the largest frame."""
+    frame stride must then hold the largest frame.  ``trace_ptr`` (0 = off)
+    is a ``[L_total][4]`` u64 stamp array: words 2 and 3 of layer ``l`` get
+    its ingest start and end (%globaltimer)."""
     from ._ext import ext
     from . import count_launches
     count_launches(1)
@@ -412,4 +417,4 @@ def decode_layers(frame_base: int, frame_stride: int, spec: FrameSpec, orders: t
     ext().kv_decode_layers(int(frame_base), int(frame_stride), spec.params(), orders, sign_bits, kv_cache,
                            block_table, int(tok_offset), int(flags_ptr), int(seq), int(layer_begin),
                            int(num_layers), int(timeout_ns), status, int(max_ctas), int(tile_tokens), n_lows,
-                           int(part_mask), layer_ptrs, bool(hnd))
+                           int(part_mask), layer_ptrs, bool(hnd), int(trace_ptr))

@@ -7,19 +7,19 @@ its bytes, sets the cost.  Here they are epilogues of the projections that
 produce them (``csrc/decode_fused.cu``):
 
 * ``gemv_allreduce``: each CTA stores its fp32 partial rows into every TP
-  rank's staging memory, flags them, waits for the peers' rows and sums in
-  rank order (every rank gets bitwise the same result);
-* ``gemv_argmax``: LM head + greedy argmax, with a flagged exchange of each
-  rank's best (value, index) — the logits never leave the kernel;
-* ``bump``: the step epoch that tags the flags, advanced once per step.
+  rank's staging memory as 64-bit "LL" words (flag in the high half, value
+  in the low half; an aligned 64-bit store is single-copy atomic, so no fence
+  or separate flag is needed), polls its own staging for the peers' words
+  and sums in rank order (every rank gets bitwise the same result);
+* ``gemv_argmax``: LM head + greedy argmax, with an exchange of each rank's
+  best (value, index) as two LL words — the logits never leave the kernel;
+* ``bump``: the step epoch that tags the words, advanced once per step.
 
 Every rank of a TP group holds one device region, exported through CUDA IPC
 and mapped by its peers:
 
-    stage  [2 parities][world][8 tokens][hidden]  fp32   partial rows
-    flags  [2][world][hidden / 16]                u32    per-CTA flags
-    aslot  [2][world][8] (value, index)                   argmax candidates
-    aflag  [2][world][8]                          u32    argmax flags
+    stage  [2 parities][world][8 tokens][hidden]   u64   LL partial rows
+    aslot  [2][world][8 tokens][2]                 u64   LL argmax candidates
 
 The reference serves decode with vLLM, whose row-parallel layers call an
 NCCL all-reduce; this module is the standalone engine's replacement.
@@ -50,13 +50,9 @@ def region_layout(world: int, hidden: int) -> dict:
     if hidden % ROWS_PER_CTA:
         raise ValueError(f"hidden size must be a multiple of {ROWS_PER_CTA}")
     align = lambda n: (n + 255) // 256 * 256  # noqa: E731
-    flag_ld = hidden // ROWS_PER_CTA
-    stage = align(2 * world * MAX_TOKENS * hidden * 4)
-    flags = align(2 * world * flag_ld * 4)
-    aslot = align(2 * world * MAX_TOKENS * 8)
-    aflag = align(2 * world * MAX_TOKENS * 4)
-    return dict(stage=0, flags=stage, aslot=stage + flags, aflag=stage + flags + aslot,
-                total=stage + flags + aslot + aflag, flag_ld=flag_ld, stage_ld=hidden)
+    stage = align(2 * world * MAX_TOKENS * hidden * 8)
+    aslot = align(2 * world * MAX_TOKENS * 2 * 8)
+    return dict(stage=0, aslot=stage, total=stage + aslot, stage_ld=hidden)
 
 
 class DecodeCollectives:
@@ -113,19 +109,17 @@ class DecodeCollectives:
         x2 = x.reshape(-1, x.shape[-1])
         y = torch.empty((x2.shape[0], w.shape[0]), dtype=torch.bfloat16, device=x.device)
         ops.count_launches(1)
-        ops.ext().gemv_allreduce_bf16(x2, w, y, self._ptrs("stage"), self._ptrs("flags"), self.rank, site,
-                                      self.num_sites, self.epoch, self.lay["stage_ld"], self.lay["flag_ld"],
-                                      self.timeout_ns, self.status)
+        ops.ext().gemv_allreduce_bf16(x2, w, y, self._ptrs("stage"), self.rank, site, self.num_sites, self.epoch,
+                                      self.lay["stage_ld"], self.timeout_ns, self.status)
         return y
 
     def greedy(self, h: torch.Tensor, lm_head: torch.Tensor, vocab_begin: int, site: int) -> torch.Tensor:
         """Greedy next token (int32 [M]) over the vocab-parallel LM head."""
         out = torch.empty(h.shape[0], dtype=torch.int32, device=h.device)
         slots = self._ptrs("aslot") if self.world > 1 else []
-        flags = self._ptrs("aflag") if self.world > 1 else []
         ops.count_launches(1)
         ops.ext().gemv_argmax_bf16(h, lm_head, out, self.part_val, self.part_idx, self.counter, vocab_begin,
-                                   slots, flags, self.rank, site, self.num_sites, self.epoch, self.timeout_ns,
+                                   slots, self.rank, site, self.num_sites, self.epoch, self.timeout_ns,
                                    self.status)
         return out
 

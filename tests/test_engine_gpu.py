@@ -143,3 +143,25 @@ def test_frame_round_trip_error_matches_cpu_oracle():
     # K: 16 levels per channel; V: 4 levels per token over 512 values (range about +-3 sigma)
     assert gpu["k_rel_mse"] < 0.05 and gpu["v_rel_mse"] < 0.5
     assert abs(gpu["rel_mse"] - cpu["rel_mse"]) <= 0.02 * cpu["rel_mse"]
+
+
+def test_trace_stamps_cover_every_layer(monkeypatch, tmp_path):
+    """With KVSERVE_TRACE=1 the encode and decode kernels stamp every layer
+    (%globaltimer): encode start <= published <= ingest end, and the JSONL
+    row lands in KVSERVE_TRACE_FILE."""
+    import json
+    from kvserve_b200.engine.transfer import TransferProfile
+    monkeypatch.setenv("KVSERVE_TRACE", "1")
+    path = tmp_path / "trace.jsonl"
+    monkeypatch.setenv("KVSERVE_TRACE_FILE", str(path))
+    prof = TransferProfile(compressed=True, hybrid_ratio=0.0, key_levels=(16, 16), value_levels=(4, 4))
+    eng = _engine(prof)
+    ids = torch.randint(0, eng.cfg.vocab, (200,), dtype=torch.int32)
+    res = eng.generate(ids, 4)
+    t = res.timing.trace
+    assert t["encode_span_ms"] > 0 and t["ingest_span_ms"] > 0
+    rows = [json.loads(x) for x in path.read_text().splitlines()]
+    assert rows and len(rows[-1]["layers_ms"]) == eng.cfg.num_layers
+    for e0, e1, i0, i1 in rows[-1]["layers_ms"]:
+        assert 0 <= e0 <= e1 <= i1 and i0 <= i1
+    eng.close()

@@ -176,3 +176,44 @@ def test_ipc_receive_pool_ranges():
     p.free(256, 700)
     p.free(c, 256)
     assert p.free_bytes() == 4096 and p.alloc(4096) == 0
+
+
+def test_pipeline_host_helpers():
+    """Bucket choice, Poisson schedule and record merging of the pipelined
+    server (host logic; the serving loops themselves need two GPUs)."""
+    from kvserve_b200.engine.pipeline import RequestRecord, bucket_for, merge_records, poisson_schedule
+    from kvserve_b200.parallel.context import ParallelContext
+    assert [bucket_for(n) for n in (1, 2, 3, 4, 5, 8)] == [1, 2, 4, 4, 8, 8]
+    with pytest.raises(ValueError):
+        bucket_for(9)
+    a = poisson_schedule(200, 4.0, seed=1)
+    assert a == sorted(a) and a == poisson_schedule(200, 4.0, seed=1)
+    assert 30 < a[-1] < 80            # mean gap 0.25 s
+    assert poisson_schedule(3, 0.0) == [0.0, 0.0, 0.0]
+    recs = [RequestRecord(0, 0.0, first_token_ms=5.0)]
+    assert merge_records(ParallelContext(), recs) is recs
+
+
+def test_channel_control_block_layout():
+    """Per-slot control words: layer flags, first token, its flag, the
+    credit, one pad word — the producer and consumer views agree."""
+    from kvserve_b200.transport.p2p import ctrl_words
+    assert ctrl_words(32) == 36
+
+
+def test_trace_stamp_decoding():
+    """Starts are stored as ~t (atomic max keeps the earliest), ends as t;
+    zero means not stamped."""
+    import math
+    from kvserve_b200.utils.trace import decode_stamps, summarize_stamps
+    mask = (1 << 64) - 1
+    base = 1_700_000_000_000_000_000
+    enc = lambda t: (~t) & mask  # noqa: E731
+    signed = lambda u: u - (1 << 64) if u >= (1 << 63) else u  # noqa: E731
+    raw = torch.tensor([[signed(enc(base)), base + 2_000_000, signed(enc(base + 1_000_000)), base + 3_000_000],
+                        [signed(enc(base + 500_000)), base + 2_500_000, 0, 0]], dtype=torch.int64)
+    st = decode_stamps(raw)
+    assert st["base_ns"] == base
+    assert st["layers_ms"][0] == [0.0, 2.0, 1.0, 3.0]
+    assert st["layers_ms"][1][:2] == [0.5, 2.5] and math.isnan(st["layers_ms"][1][2])
+    assert summarize_stamps(st) == {"encode_span_ms": 2.5, "ingest_span_ms": 2.0}
