@@ -117,8 +117,9 @@ def main() -> None:
     import torch.distributed as dist
 
     ctx = init_parallel("nccl", timeout_s=300.0)
-    if ctx.world_size != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={ctx.world_size}")
+    if (ctx.job_world_size or ctx.world_size) != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={ctx.job_world_size or ctx.world_size}")
+    n_rep = ctx.num_replicas   # data-parallel PD replicas (KVSERVE_REPLICAS), each of ctx.world_size GPUs
     cfg = get_config(args.model)
     if args.layers:
         cfg = cfg.with_layers(args.layers)
@@ -137,7 +138,7 @@ def main() -> None:
         _log(f"warmup step {i} done")
 
     sampler = None
-    if ctx.rank == 0:
+    if ctx.global_rank == 0:
         sampler = ClockSampler(list(range(torch.cuda.device_count())) if ctx.distributed else
                                [torch.cuda.current_device()])
         sampler.start()
@@ -172,6 +173,7 @@ def main() -> None:
     else:
         allr = [mine]
     allt = [r["steps"] for r in allr]
+    out = None
     if ctx.rank == 0:
         def col(step, key):
             vals = [allt[r][step][key] for r in range(len(allt))]
@@ -192,7 +194,7 @@ def main() -> None:
                    if not math.isnan(allr[r]["handoff"][i]["ingest_ms"])) for i in range(len(handoffs))]
         payload = timings[0].payload_bytes if ctx.is_prefill else allt[0][0]["payload_bytes"]
         raw = allt[0][0]["raw_bytes"]
-        tp = max(1, args.gpus // 2)
+        tp = max(1, ctx.world_size // 2)
         ttft_p50 = statistics.median(ttft)
         decode_ms = [end[s] - ttft[s] for s in range(args.steps)]
         launches = sum(allt[r][s]["launches"] for r in range(len(allt)) for s in range(args.steps))
@@ -217,8 +219,8 @@ def main() -> None:
                 "definition": "one request's KV hand-off on its own: all layers encoded, pushed and decoded into "
                               "the paged cache, device time from a common start to the last layer ingested, max "
                               "over ranks (median of %d)" % len(iso),
-                "roofline_ms": round(_handoff_roofline_ms(raw, payload, args.gpus), 4),
-                "fraction_of_roofline": round(_handoff_roofline_ms(raw, payload, args.gpus)
+                "roofline_ms": round(_handoff_roofline_ms(raw, payload, ctx.world_size), 4),
+                "fraction_of_roofline": round(_handoff_roofline_ms(raw, payload, ctx.world_size)
                                               / statistics.median(iso), 3),
                 "roofline": "max((raw + payload bytes) per GPU side / measured HBM copy GB/s, payload / 770 GB/s "
                             "NVLink per direction); colocated: both sides on one GPU",
@@ -234,7 +236,9 @@ def main() -> None:
             "compression_ratio": round(raw / payload, 3) if payload else None,
             "config": {"model": cfg.name, "layers": cfg.num_layers, "global_batch": 1,
                        "seq_len": args.prompt_len, "max_new_tokens": args.max_new,
-                       "parallelism": "colocated-1gpu" if args.gpus == 1 else f"{tp}P{tp}D-tp{tp}",
+                       "parallelism": ("colocated-1gpu" if ctx.world_size == 1 else f"{tp}P{tp}D-tp{tp}")
+                                      if n_rep == 1 else
+                                      f"dp{n_rep}x" + ("colocated" if ctx.world_size == 1 else f"{tp}P{tp}D-tp{tp}"),
                        "profile": args.profile, "link_gbps": args.link_gbps or None,
                        "l2": "inputs larger than L2 (%.1f GB of weights per rank, %.2f GiB raw KV per request)"
                              % (engine.model.weight_bytes() / 1e9, raw * tp / 2 ** 30)},
@@ -246,7 +250,24 @@ def main() -> None:
                     "wall_ms_per_request": round(1e3 * wall_s / args.steps, 3)},
             "gpu_launches": int(launches),
             "clocks": clocks,
+            "_ttft": ttft, "_e2e": e2e_ttft,
         }
+    if n_rep > 1:
+        # every replica served its own requests: TTFT p50 over all of them,
+        # launches summed, the rest from replica 0
+        allo = [None] * ctx.job_world_size
+        dist.all_gather_object(allo, out if ctx.rank == 0 else None, group=ctx.job_cpu_group)
+        reps = [o for o in allo if o is not None]
+        if ctx.global_rank == 0:
+            out = dict(reps[0])
+            out["value"] = round(statistics.median([t for o in reps for t in o["_ttft"]]), 3)
+            out["e2e"] = dict(out["e2e"], value=round(statistics.median([t for o in reps for t in o["_e2e"]]), 3))
+            out["gpu_launches"] = int(sum(o["gpu_launches"] for o in reps))
+            out["replica_ttft_ms_p50"] = [o["value"] for o in reps]
+            out["clocks"] = clocks
+    if ctx.global_rank == 0:
+        out.pop("_ttft", None)
+        out.pop("_e2e", None)
         _emit(out)
     engine.close()
     destroy_parallel(ctx)

@@ -41,7 +41,7 @@ RUNTIME_SEQ = 1
 @dataclass
 class EncodeResult:
     event: torch.cuda.Event
-    payload: torch.Tensor          # bytes to transfer (frames or codec output), device view
+    payload: Optional[torch.Tensor]  # bytes to transfer (frames or codec output), device view; None: written to dest_ptr
     u8_bytes: int                  # frame-arena bytes (what decode expects after the codec)
     raw_tail_bytes: int = 0        # frames carry partial blocks; no separate raw tail
     _codec_bytes: Optional[torch.Tensor] = None
@@ -184,7 +184,13 @@ class CompressionRuntime:
 
     # ------------------------------------------------------------ encode
     def encode(self, slot_id: int, block_ids_by_group: Any, kv_part: Any,
-               valid_tokens_by_group: Any = None, output_slot: Optional[int] = None) -> EncodeResult:
+               valid_tokens_by_group: Any = None, output_slot: Optional[int] = None,
+               dest_ptr: Optional[int] = None) -> EncodeResult:
+        """Encode one chunk's ``kv_part`` into slot ``slot_id``.  With
+        ``dest_ptr`` (a 256-byte aligned device address, local or a peer
+        GPU's memory mapped through CUDA IPC) the payload is written there
+        instead — the frames directly, or the codec output when the pipeline
+        has a codec — so a zero-copy transport needs no staging copy."""
         if not self._bound:
             raise RuntimeError("bind_kv_caches() first")
         if self.execution == "decode":
@@ -196,21 +202,28 @@ class CompressionRuntime:
         lay = self.layout
         cur = torch.cuda.current_stream(self.device)
         self.stream.wait_stream(cur)
+        if dest_ptr is not None and dest_ptr % 256:
+            raise ValueError("dest_ptr must be 256-byte aligned")
         with torch.cuda.stream(self.stream):
-            base = slot.arena.data_ptr()
+            direct = dest_ptr is not None and not self.config.uses_codec
+            base = dest_ptr if direct else slot.arena.data_ptr()
             for e in lay.layers:
                 spec = frame_spec(self.config, e, part, T)
                 k, v = self._k[e.dense_index], self._v[e.dense_index]
                 kc.encode_layer(k, v, spec, self.orders[e.dense_index], self.sign_bits[e.dense_index],
                                 base + e.dense_index * lay.frame_stride, self._enc_state, seq=RUNTIME_SEQ,
                                 layer=e.dense_index, part_mask=1 << part, block_table=table, hnd=self.hnd)
-            payload, total = slot.arena, None
+            payload, total = (None if direct else slot.arena), None
             if self.config.uses_codec:
-                out = slot.codec_out if output_slot is None else self.output_slots[output_slot]
+                if dest_ptr is not None:
+                    out = ops.ext().tensor_from_ptr(int(dest_ptr), [lay.codec_capacity], ops.dtype_code(torch.uint8),
+                                                    self.device.index)
+                else:
+                    out = slot.codec_out if output_slot is None else self.output_slots[output_slot]
                 ops.count_launches(3)
                 ops.ext().rze_encode(slot.arena, out, slot.codec_scratch, slot.codec_total, 16384)
                 payload, total = out, slot.codec_total
-            elif output_slot is not None:
+            elif output_slot is not None and not direct:
                 out = self.output_slots[output_slot]
                 out[: lay.arena_bytes].copy_(slot.arena)
                 payload = out[: lay.arena_bytes]
@@ -230,7 +243,10 @@ class CompressionRuntime:
 
     # ------------------------------------------------------------ decode
     def decode(self, slot_id: int, block_ids_by_group: Any, kv_part: Any, codec_bytes: Optional[int] = None,
-               u8_bytes: Optional[int] = None, valid_tokens_by_group: Any = None) -> torch.cuda.Event:
+               u8_bytes: Optional[int] = None, valid_tokens_by_group: Any = None,
+               src_ptr: Optional[int] = None) -> torch.cuda.Event:
+        """Decode slot ``slot_id`` (or the payload at device address
+        ``src_ptr``, where a zero-copy transport landed it) into the blocks."""
         if not self._bound:
             raise RuntimeError("bind_kv_caches() first")
         if self.execution == "encode":
@@ -243,14 +259,21 @@ class CompressionRuntime:
         cur = torch.cuda.current_stream(self.device)
         self.stream.wait_stream(cur)
         with torch.cuda.stream(self.stream):
+            frames = slot.arena.data_ptr()
             if self.config.uses_codec:
-                n = int(codec_bytes) if codec_bytes is not None else slot.codec_out.numel()
+                src = slot.codec_out if src_ptr is None else ops.ext().tensor_from_ptr(
+                    int(src_ptr), [lay.codec_capacity], ops.dtype_code(torch.uint8), self.device.index)
+                n = int(codec_bytes) if codec_bytes is not None else src.numel()
                 ops.count_launches(2)
-                ops.ext().rze_decode(slot.codec_out[:n], slot.arena, slot.codec_scratch, 16384)
+                ops.ext().rze_decode(src[:n], slot.arena, slot.codec_scratch, 16384)
+            elif src_ptr is not None:
+                if src_ptr % 256:
+                    raise ValueError("src_ptr must be 256-byte aligned")
+                frames = int(src_ptr)
             big = max(lay.layers, key=lambda e: kc.frame_layout(frame_spec(self.config, e, part, T)).frame_bytes)
             spec = frame_spec(self.config, big, part, T)
             template = self._k[0] if part == 0 else self._v[0]
-            kc.decode_layers(slot.arena.data_ptr(), lay.frame_stride, spec, self.orders, self.sign_bits, template,
+            kc.decode_layers(frames, lay.frame_stride, spec, self.orders, self.sign_bits, template,
                              table, self._status, seq=RUNTIME_SEQ, layer_begin=0, num_layers=len(lay.layers),
                              n_lows=self.n_lows, part_mask=1 << part, layer_ptrs=self.layer_ptrs, hnd=self.hnd)
             ev = torch.cuda.Event()

@@ -34,6 +34,7 @@ from ..parallel.decode_allreduce import create_decode_collectives
 from ..parallel.tp_allreduce import create_tp_allreduce
 from ..transport.p2p import FrameReceiver, FrameSender
 from ..utils.trace import decode_stamps, nvtx_range, summarize_stamps, trace_enabled, write_trace_row
+from ..session.tp_plan import HeadCopy, head_shard, transfer_plan
 from .kv_cache import PagedKVCache
 from .transfer import KVTransfer, TransferProfile
 
@@ -81,13 +82,23 @@ class PDEngine:
         # decode ranks fuse their per-step collectives into the projections
         m.decode_coll = create_decode_collectives(ctx, cfg.hidden, m.vocab_local, m.decode_sites(), self.device,
                                                   participate=ctx.is_decode)
-        # one transfer geometry per selectable profile ("default" = `profile`);
-        # the receive slot is sized for the largest frame of any of them
-        self.xfers = {name: KVTransfer(p, cfg.num_layers, cfg.num_kv_heads, m.hkv, m.D, ctx.tp_rank, ctx.tp_size,
-                                       self.device, max_prompt, cfg.score_model_name)
-                      for name, p in {"default": profile, **(profiles or {})}.items()}
+        # ---- KV hand-off plan: the KV-head ranges each prefill rank sends to
+        # each decode rank (one full-shard copy per TP pair when both groups
+        # have the same size; heterogeneous TP splits or merges the ranges,
+        # session.tp_plan).  This rank's copies, in plan order:
+        n_pre = ctx.num_prefill if ctx.distributed else 1
+        n_dec = ctx.world_size - n_pre if ctx.distributed else 1
+        self.plan = transfer_plan(n_pre, n_dec, cfg.num_kv_heads)
+        if ctx.role == "decode":
+            self.copies = [c for c in self.plan if c.dst_rank == ctx.tp_rank]
+        else:
+            self.copies = [c for c in self.plan if c.src_rank == ctx.tp_rank]
+        # one transfer geometry per (selectable profile, copy) ("default" =
+        # `profile`); the receive slots are sized for the largest frame
+        self.xfer_sets = {name: [self._copy_transfer(p, c, n_pre, max_prompt) for c in self.copies]
+                          for name, p in {"default": profile, **(profiles or {})}.items()}
+        self.xfers = {name: xs[0] for name, xs in self.xfer_sets.items()}
         self.xfer = self.xfers["default"]
-        frame_stride = max(x.frame_stride for x in self.xfers.values())
         self.compute = torch.cuda.current_stream(self.device)
         self.seq = 0
         self.status = ops.device_status(self.device)
@@ -113,27 +124,78 @@ class PDEngine:
             self._scratch_block = self.kv.allocate(1)
             self.ingest_stream = torch.cuda.Stream(self.device, priority=-1)
             self._init_decode_buffers()
-        # ---- channel between paired ranks
-        self.receiver: Optional[FrameReceiver] = None
-        self.sender: Optional[FrameSender] = None
+        # ---- channels: one receiver (decode side) per copy, with its slots,
+        # flags and credits; the prefill side maps each of its copies' receivers
+        self.receivers: list[FrameReceiver] = []
+        self.senders: list[FrameSender] = []
         # receive slots of the channel; request `seq` uses slot seq % num_slots
         # and waits for the slot's credit from its previous request
         self.num_slots = max(1, int(num_slots))
         self._slot_seq = [0] * self.num_slots
         if ctx.is_decode:
-            self.receiver = FrameReceiver(L, frame_stride, self.num_slots, self.device)
+            for i in range(len(self.copies)):
+                stride = max(xs[i].frame_stride for xs in self.xfer_sets.values())
+                self.receivers.append(FrameReceiver(L, stride, self.num_slots, self.device))
         if not ctx.distributed:
-            self.sender = FrameSender(local=self.receiver, device=self.device)
+            self.senders = [FrameSender(local=r, device=self.device) for r in self.receivers]
         else:
-            local = self.receiver.handles() if ctx.role == "decode" else None
+            local = [r.handles() for r in self.receivers] if ctx.role == "decode" else None
             allh = [None] * ctx.world_size
             dist.all_gather_object(allh, local, group=ctx.cpu_group)
             if ctx.role == "prefill":
-                self.sender = FrameSender(handles=allh[ctx.peer_rank], device=self.device)
+                for c in self.copies:
+                    theirs = [x for x in self.plan if x.dst_rank == c.dst_rank]
+                    self.senders.append(FrameSender(handles=allh[n_pre + c.dst_rank][theirs.index(c)],
+                                                    device=self.device))
             dist.barrier(group=ctx.cpu_group)
             self._barrier_t = torch.zeros(1, dtype=torch.float32, device=self.device)
+        self.receiver: Optional[FrameReceiver] = self.receivers[0] if self.receivers else None
+        self.sender: Optional[FrameSender] = self.senders[0] if self.senders else None
         self._graph: Optional[torch.cuda.CUDAGraph] = None
         torch.cuda.synchronize(self.device)
+
+    def _copy_transfer(self, profile: TransferProfile, c: HeadCopy, n_pre: int, max_prompt: int) -> KVTransfer:
+        """Transfer geometry of one copy: its heads as an aligned slice of the
+        model's KV heads (the slice index and count play the TP rank/size)."""
+        cfg = self.cfg
+        first = head_shard(c.src_rank, n_pre, cfg.num_kv_heads).first + c.src_head
+        if cfg.num_kv_heads % c.heads or first % c.heads:
+            raise ValueError("KV-head copies must be aligned slices of the model's KV heads")
+        return KVTransfer(profile, cfg.num_layers, cfg.num_kv_heads, c.heads, self.model.D, first // c.heads,
+                          cfg.num_kv_heads // c.heads, self.device, self.max_prompt, cfg.score_model_name)
+
+    # ------------------------------------------------- hand-off per copy
+    def _cache_view(self, c: HeadCopy) -> torch.Tensor:
+        """The paged cache restricted to the copy's KV heads (a strided view)."""
+        if c.dst_head == 0 and c.heads == self.model.hkv:
+            return self.kv.cache
+        return self.kv.cache[:, :, :, :, c.dst_head:c.dst_head + c.heads]
+
+    def _encode_layer(self, l: int, T: int, slot: int, seq: int, name: str, rate: float,
+                      table: Optional[torch.Tensor] = None) -> None:
+        """Encode + push layer ``l`` of every copy of this prefill rank (on the
+        current stream); colocated, decode it into the paged cache too."""
+        dist_ = self.ctx.distributed
+        for i, (c, x, snd) in enumerate(zip(self.copies, self.xfer_sets[name], self.senders)):
+            hs = slice(c.src_head, c.src_head + c.heads)
+            tr = self.trace if i == 0 else None
+            x.encode(l, self.k_buf[l, :T, hs], self.v_buf[l, :T, hs], snd.frame_ptr(slot, l),
+                     snd.flag_ptr(slot, l) if dist_ else 0, seq, self.pacing, rate, self.encode_ctas, trace=tr)
+            if not dist_:
+                x.ingest_layer(l, T, snd.frame_ptr(slot, l), self._cache_view(c), table, self.status, seq, trace=tr)
+
+    def _ingest_all(self, T: int, slot: int, seq: int, name: str, table: torch.Tensor, max_ctas: int = 148) -> None:
+        """Decode every copy of this decode rank into its heads of the paged
+        cache (on the current stream; each kernel waits on its layer flags)."""
+        for i, (c, x, r) in enumerate(zip(self.copies, self.xfer_sets[name], self.receivers)):
+            x.ingest_all(T, r.slot_base(slot), r.frame_stride, r.flags_base(slot), self._cache_view(c), table,
+                         self.status, seq, self.ingest_timeout_ns, max_ctas=max_ctas,
+                         trace=self.trace if i == 0 else None)
+
+    def request_bytes(self, T: int, name: str = "default") -> tuple[int, int]:
+        """(payload, raw) bytes of this rank's copies of one T-token request."""
+        xs = self.xfer_sets[name]
+        return sum(x.payload_bytes(T) for x in xs), sum(x.raw_bytes(T) for x in xs)
 
     # ----------------------------------------------------------- decode state
     def _init_decode_buffers(self) -> None:
@@ -238,22 +300,35 @@ class PDEngine:
 
     def _take_credit(self, slot: int, seq: int) -> None:
         """Producer, on the current stream before the slot's first store:
-        acquire-wait (bounded) until the decode rank has read the slot's
-        previous request out of it."""
+        acquire-wait (bounded) until every decode rank this rank feeds has
+        read the slot's previous request out of it."""
         prev = self._slot_seq[slot]
         self._slot_seq[slot] = seq
         if self.ctx.distributed and prev:
-            ops.count_launches(1)
-            ops.ext().wait_flag(self.sender.credit_ptr(slot), prev, self.ingest_timeout_ns, self.status)
+            for snd in self.senders:
+                ops.count_launches(1)
+                ops.ext().wait_flag(snd.credit_ptr(slot), prev, self.ingest_timeout_ns, self.status)
 
     def _return_credit(self, slot: int, seq: int) -> None:
         """Consumer, on the stream of the last kernel that read the slot."""
         self._slot_seq[slot] = seq
         if self.ctx.distributed:
-            ops.count_launches(1)
-            ops.ext().store_release_u32(self.receiver.credit_ptr(slot), seq)
+            for r in self.receivers:
+                ops.count_launches(1)
+                ops.ext().store_release_u32(r.credit_ptr(slot), seq)
 
-    def _launch_prefill(self, ids: torch.Tensor, seq: int, slot: int, xfer: "KVTransfer", rate: float,
+    def _publish_token(self, first: torch.Tensor, slot: int, seq: int) -> None:
+        """Prefill side: the sampled first token next to the flags of every
+        receiver this rank feeds."""
+        for snd in self.senders:
+            ops.count_launches(1)
+            ops.ext().publish_token(first, snd.token_ptr(slot), seq)
+
+    def _take_token(self, slot: int, seq: int, out: torch.Tensor, out2: Optional[torch.Tensor] = None) -> None:
+        ops.count_launches(1)
+        ops.ext().take_token(self.receivers[0].token_ptr(slot), seq, self.ingest_timeout_ns, out, out2, self.status)
+
+    def _launch_prefill(self, ids: torch.Tensor, seq: int, slot: int, xfer: str, rate: float,
                         ev: Optional[dict] = None, table: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Prefill side of one request (asynchronous): the prompt's forward
         pass with each layer's K/V encoded and pushed into receive slot
@@ -275,20 +350,14 @@ class PDEngine:
             if l == 0 and ev is not None:
                 ev["enc_start"].record(enc)
             with torch.cuda.stream(enc), nvtx_range(f"kv encode L{l}"):
-                flag = self.sender.flag_ptr(slot, l) if ctx.distributed else 0
-                xfer.encode(l, self.k_buf[l, :T], self.v_buf[l, :T], self.sender.frame_ptr(slot, l), flag,
-                            seq, self.pacing, rate, self.encode_ctas, trace=self.trace)
-                if not ctx.distributed:
-                    xfer.ingest_layer(l, T, self.sender.frame_ptr(slot, l), self.kv.cache, table, self.status, seq,
-                                      trace=self.trace)
+                self._encode_layer(l, T, slot, seq, xfer, rate, table)
 
         first = m.prefill(ids, self.positions[:T], self.k_buf, self.v_buf, layer_hook=hook, sample=True)
         if ev is not None:
             ev["prefill"].record(self.compute)
         if ctx.distributed:
-            # the token lands next to the layer flags of the decode slot
-            ops.count_launches(1)
-            ops.ext().publish_token(first, self.sender.token_ptr(slot), seq)
+            # the token lands next to the layer flags of the decode slots
+            self._publish_token(first, slot, seq)
         if ev is not None:
             ev["encode"].record(enc)
         return first
@@ -314,7 +383,7 @@ class PDEngine:
         t_host0 = time.perf_counter()
         if profile is not None and profile not in self.xfers:
             raise KeyError(f"unknown transfer profile {profile!r}; have {sorted(self.xfers)}")
-        xfer = self.xfers[profile or "default"]
+        xfer = profile or "default"
         rate = self.rate_bytes_per_ns if link_gbps is None else (link_gbps / 8.0 if link_gbps else 0.0)
         n_new = self.max_new if max_new_tokens is None else max_new_tokens
         if n_new < 1 or n_new > self.max_new:
@@ -336,7 +405,8 @@ class PDEngine:
         if self.trace is not None:
             self.trace.zero_()
         ids = prompt_ids.to(self.device, non_blocking=True)
-        timing = RequestTiming(payload_bytes=xfer.payload_bytes(Tx), raw_bytes=xfer.raw_bytes(Tx))
+        pay, raw = self.request_bytes(Tx, xfer)
+        timing = RequestTiming(payload_bytes=pay, raw_bytes=raw)
         blocks = table = None
         if ctx.is_decode:
             blocks = self.kv.allocate(T + n_new)
@@ -344,9 +414,7 @@ class PDEngine:
             if ctx.distributed:
                 self.ingest_stream.wait_stream(self.compute)
                 with torch.cuda.stream(self.ingest_stream), nvtx_range("kv ingest"):
-                    xfer.ingest_all(Tx, self.receiver.slot_base(slot), self.receiver.frame_stride,
-                                    self.receiver.flags_base(slot), self.kv.cache, table, self.status, seq,
-                                    self.ingest_timeout_ns, trace=self.trace)
+                    self._ingest_all(Tx, slot, seq, xfer, table)
                     ev["ingest"].record(self.ingest_stream)
         if ctx.is_prefill:
             first = self._launch_prefill(ids[:Tx], seq, slot, xfer, rate, ev, table)
@@ -361,9 +429,7 @@ class PDEngine:
             self._ensure_graph()
             self._load_decode_state(0, T, blocks)
             if ctx.distributed:
-                ops.count_launches(1)
-                ops.ext().take_token(self.receiver.token_ptr(slot), seq, self.ingest_timeout_ns, self.d_ids,
-                                     self.d_out, self.status)
+                self._take_token(slot, seq, self.d_ids, self.d_out)
                 self._return_credit(slot, seq)
             else:
                 self.d_ids.copy_(self.d_first)
@@ -422,7 +488,7 @@ class PDEngine:
         (prefill side: last frame published) and ``ingest_ms`` (decode side:
         last layer written), NaN where the rank has no such part."""
         ctx = self.ctx
-        xfer = self.xfers[profile or "default"]
+        xfer = profile or "default"
         if T < 1 or T > self.max_prompt:
             raise ValueError(f"T must be in [1, {self.max_prompt}]")
         self._host_barrier()
@@ -430,16 +496,14 @@ class PDEngine:
         start, enc_end, ing_end = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         self._barrier()
         start.record(self.compute)
-        blocks = None
+        blocks = table = None
         if ctx.is_decode:
             blocks = self.kv.allocate(T)
             table = self.kv.block_table(blocks, self.max_blocks)
             if ctx.distributed:
                 self.ingest_stream.wait_stream(self.compute)
                 with torch.cuda.stream(self.ingest_stream):
-                    xfer.ingest_all(T, self.receiver.slot_base(slot), self.receiver.frame_stride,
-                                    self.receiver.flags_base(slot), self.kv.cache, table, self.status, seq,
-                                    self.ingest_timeout_ns)
+                    self._ingest_all(T, slot, seq, xfer, table)
                     ing_end.record(self.ingest_stream)
                     self._return_credit(slot, seq)
         if ctx.is_prefill:
@@ -448,12 +512,7 @@ class PDEngine:
             with torch.cuda.stream(enc):
                 self._take_credit(slot, seq)
                 for l in range(self.cfg.num_layers):
-                    flag = self.sender.flag_ptr(slot, l) if ctx.distributed else 0
-                    xfer.encode(l, self.k_buf[l, :T], self.v_buf[l, :T], self.sender.frame_ptr(slot, l), flag,
-                                seq, self.pacing, 0.0, self.encode_ctas)
-                    if not ctx.distributed:
-                        xfer.ingest_layer(l, T, self.sender.frame_ptr(slot, l), self.kv.cache, table, self.status,
-                                          seq)
+                    self._encode_layer(l, T, slot, seq, xfer, 0.0, table)
                 enc_end.record(enc)
                 if not ctx.distributed:
                     ing_end.record(enc)
@@ -467,7 +526,7 @@ class PDEngine:
         nan = float("nan")
         return {"encode_ms": start.elapsed_time(enc_end) if ctx.is_prefill else nan,
                 "ingest_ms": start.elapsed_time(ing_end) if ctx.is_decode else nan,
-                "payload_bytes": xfer.payload_bytes(T), "raw_bytes": xfer.raw_bytes(T)}
+                "payload_bytes": self.request_bytes(T, xfer)[0], "raw_bytes": self.request_bytes(T, xfer)[1]}
 
     def close(self) -> None:
         self._graph = None
@@ -479,8 +538,9 @@ class PDEngine:
             torch.cuda.synchronize(self.device)
             self.model.tp_ar.close()
             self.model.tp_ar = None
-        if self.sender is not None:
-            self.sender.close()
-        if self.receiver is not None:
+        for snd in self.senders:
+            snd.close()
+        if self.receivers:
             torch.cuda.synchronize(self.device)
-            self.receiver.close()
+        for r in self.receivers:
+            r.close()

@@ -212,13 +212,12 @@ class PipelinedServer:
         self.poll_s = poll_s
         self.timeout_s = timeout_s
         self.store = dist.distributed_c10d._get_default_store()
-        # role-local gloo groups (every rank creates both, in the same order)
-        import datetime
-        pre, dec = ctx.group_ranks("prefill"), ctx.group_ranks("decode")
-        td = datetime.timedelta(seconds=timeout_s)
-        self.pre_group = dist.new_group(pre, backend="gloo", timeout=td)
-        self.dec_group = dist.new_group(dec, backend="gloo", timeout=td)
-        self.leader = pre[0] if ctx.is_prefill else dec[0]
+        # the role's gloo group of this replica (created by init_parallel)
+        # and the role leader's global rank
+        if ctx.role_cpu_groups is None:
+            raise ValueError("the parallel context has no role groups (use parallel.context.init_parallel)")
+        self.dec_group = ctx.role_cpu_groups["decode"]
+        self.leader = ctx.global_ranks("prefill" if ctx.is_prefill else "decode")[0]
         self.decoder: Optional[BatchDecoder] = None
         if ctx.is_decode:
             self.decoder = BatchDecoder(engine, max_batch)
@@ -228,7 +227,7 @@ class PipelinedServer:
 
     # ----------------------------------------------------------- helpers
     def _key(self, *parts) -> str:
-        return "/".join(["kvs_pipe", str(self._run)] + [str(p) for p in parts])
+        return "/".join(["kvs_pipe", str(self.ctx.replica), str(self._run)] + [str(p) for p in parts])
 
     def _wait_key(self, key: str) -> str:
         deadline = time.monotonic() + self.timeout_s
@@ -254,7 +253,7 @@ class PipelinedServer:
         self._run = PipelinedServer._runs
         ctx = self.ctx
         t0 = torch.tensor([time.time() + 0.2], dtype=torch.float64)
-        dist.broadcast(t0, src=0, group=ctx.cpu_group)
+        dist.broadcast(t0, src=ctx.rank_offset, group=ctx.cpu_group)
         self.t0 = float(t0.item())
         recs = [RequestRecord(r.index, 1e3 * r.arrival_s) for r in requests]
         if ctx.is_prefill:
@@ -272,7 +271,7 @@ class PipelinedServer:
     # ------------------------------------------------------ prefill side
     def _serve_prefill(self, requests, recs, decide, feedback) -> None:
         eng, ctx = self.eng, self.ctx
-        lead = ctx.rank == self.leader
+        lead = ctx.global_rank == self.leader
         S = eng.num_slots
         fed = 0
         inflight: deque = deque()   # (index, compute-stream event, encode-stream event)
@@ -313,13 +312,12 @@ class PipelinedServer:
                 # the slot's previous request (the device credit wait is then short)
                 self._wait_key(self._key("ingested", i - S))
             seq, slot = eng._next_seq()
-            xfer = eng.xfers[prof]
             rate = eng.rate_bytes_per_ns if req.link_gbps is None else (req.link_gbps / 8.0 if req.link_gbps else 0.0)
             ids = req.prompt.to(eng.device, non_blocking=True)
             # this forward pass overwrites the K/V buffers the previous request's encodes read
             eng.compute.wait_stream(eng.enc_stream)
             recs[i].launch_ms = self._now_ms() - recs[i].arrival_ms
-            eng._launch_prefill(ids, seq, slot, xfer, rate)
+            eng._launch_prefill(ids, seq, slot, prof, rate)
             e1, e2 = torch.cuda.Event(), torch.cuda.Event()
             e1.record(eng.compute)
             e2.record(eng.enc_stream)
@@ -337,9 +335,8 @@ class PipelinedServer:
     # ------------------------------------------------------- decode side
     def _serve_decode(self, requests, recs) -> None:
         eng, ctx, dec = self.eng, self.ctx, self.decoder
-        lead = ctx.rank == self.leader
+        lead = ctx.global_rank == self.leader
         n = len(requests)
-        recv = eng.receiver
         dev = eng.device
         tok_dev = torch.zeros(2, dtype=torch.int32, device=dev)
         tok_host = torch.zeros(2, dtype=torch.int32).pin_memory()
@@ -372,7 +369,6 @@ class PipelinedServer:
                 req = requests[i]
                 prof = self._wait_key(self._key("decision", i))
                 recs[i].profile = prof
-                xfer = eng.xfers[prof]
                 seq, slot = eng._next_seq()
                 T = int(req.prompt.numel())
                 blocks = eng.kv.allocate(T + req.max_new)
@@ -382,11 +378,8 @@ class PipelinedServer:
                 ist.wait_stream(eng.compute)
                 k = i % 2
                 with torch.cuda.stream(ist):
-                    xfer.ingest_all(T, recv.slot_base(slot), recv.frame_stride, recv.flags_base(slot), eng.kv.cache,
-                                    table, eng.status, seq, eng.ingest_timeout_ns, max_ctas=self.ingest_ctas)
-                    ops.count_launches(1)
-                    ops.ext().take_token(recv.token_ptr(slot), seq, eng.ingest_timeout_ns, tok_dev[k:k + 1], None,
-                                         eng.status)
+                    eng._ingest_all(T, slot, seq, prof, table, max_ctas=self.ingest_ctas)
+                    eng._take_token(slot, seq, tok_dev[k:k + 1])
                     eng._return_credit(slot, seq)
                     tok_host[k:k + 1].copy_(tok_dev[k:k + 1], non_blocking=True)
                     ev = torch.cuda.Event()

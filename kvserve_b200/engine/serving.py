@@ -138,7 +138,7 @@ class ServiceAwareServer:
         if not self.ctx.distributed:
             return obj
         box = [obj]
-        dist.broadcast_object_list(box, src=0, group=self.ctx.cpu_group)
+        dist.broadcast_object_list(box, src=self.ctx.rank_offset, group=self.ctx.cpu_group)
         return box[0]
 
     def _max(self, vals: list[float]) -> list[float]:

@@ -154,10 +154,14 @@ def case_flash(a, pk):
     for T, Hq, Hkv in [(8192, 32, 8), (4096, 32, 8)] + ([] if a.quick else [(16384, 32, 8), (32768, 28, 4)]):
         qkv = torch.randn(T, (Hq + 2 * Hkv) * 128, device="cuda", dtype=torch.bfloat16)
         out = torch.empty(T, Hq * 128, device="cuda", dtype=torch.bfloat16)
-        t = time_ms([lambda: flash_prefill(qkv, Hq, Hkv, out=out)], max(3, a.iters // 2), a.once)
         fl = 4 * T * T * 128 * Hq / 2
-        r = {"ms": round(t, 4), "tflops": round(fl / t / 1e9, 1),
-             "frac_of_measured_bf16": round(fl / t / 1e9 / pk["bf16_tflops"], 3)}
+        r = {}
+        for var in (4, 3):   # v4 (two softmax threads per row) first: the default
+            t = time_ms([lambda: flash_prefill(qkv, Hq, Hkv, out=out, variant=var)], max(3, a.iters // 2), a.once)
+            r[f"v{var}"] = {"ms": round(t, 4), "tflops": round(fl / t / 1e9, 1),
+                            "frac_of_measured_bf16": round(fl / t / 1e9 / pk["bf16_tflops"], 3)}
+            if a.once:
+                break
         if not a.once and T <= 16384:
             import torch.nn.functional as F
             q = qkv[:, :Hq * 128].view(T, Hq, 128).transpose(0, 1).unsqueeze(0).contiguous()

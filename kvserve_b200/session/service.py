@@ -73,6 +73,7 @@ class ProducerService:
             return
         d_req, remote_blocks = meta.req_blocks[tid]
         s.d_req_id, s.remote_block_ids, s.nonce = d_req, remote_blocks, m.nonce
+        s.remote_meta = meta
         s.remote_session = ident.hex()
         s.logical_block_count = len(remote_blocks[0]) if remote_blocks else 0
         s.total_chunks = _chunks(s.logical_block_count, meta.logical_blocks_per_chunk)

@@ -99,6 +99,7 @@ class ProducerSession(_Session):
     inflight_chunks: int = 0
     send_meta: Any = None
     execution: Any = None
+    remote_meta: Any = None     # the consumer's XferMetadata (its arena's IPC handle, slot geometry)
 
 
 @dataclass

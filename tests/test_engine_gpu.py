@@ -165,3 +165,62 @@ def test_trace_stamps_cover_every_layer(monkeypatch, tmp_path):
     for e0, e1, i0, i1 in rows[-1]["layers_ms"]:
         assert 0 <= e0 <= e1 <= i1 and i0 <= i1
     eng.close()
+
+
+@pytest.mark.parametrize("profile_kind", ["raw", "k4v2"])
+def test_head_range_copies_of_heterogeneous_tp(profile_kind):
+    """The hand-off of heterogeneous TP moves KV-head ranges: two producer
+    shards of 2 heads each (TP2) encode strided [T, 2, D] slices of their
+    buffers, and one consumer (TP1) decodes both frames into head offsets 0
+    and 2 of its 4-head paged cache.  Raw: bitwise; K4/V2: the same cache as
+    one whole-shard copy of the same heads (each head's codec is independent
+    of its neighbours)."""
+    from kvserve_b200.engine.kv_cache import PagedKVCache
+    from kvserve_b200.engine.transfer import KVTransfer, TransferProfile
+    from kvserve_b200.session.tp_plan import transfer_plan
+    from kvserve_b200.transport.p2p import FrameReceiver, FrameSender
+    prof = TransferProfile.raw() if profile_kind == "raw" else TransferProfile(
+        compressed=True, hybrid_ratio=0.0, key_levels=(16, 16), value_levels=(4, 4))
+    L, H, D, T, dev = 2, 4, 128, 300, torch.device("cuda")
+    g = torch.Generator(device="cuda").manual_seed(5)
+    k = torch.randn(L, T, H, D, device=dev, dtype=torch.bfloat16, generator=g)
+    v = torch.randn(L, T, H, D, device=dev, dtype=torch.bfloat16, generator=g)
+    plan = transfer_plan(2, 1, H)
+    assert [(c.src_rank, c.dst_head, c.heads) for c in plan] == [(0, 0, 2), (1, 2, 2)]
+    cache = PagedKVCache(L, 40, 16, H, D, dev)
+    blocks = cache.allocate(T)
+    table = cache.block_table(blocks, 40)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    for c in plan:
+        x = KVTransfer(prof, L, H, c.heads, D, c.src_rank, 2, dev, T)
+        rcv = FrameReceiver(L, x.frame_stride, 1, dev)
+        snd = FrameSender(local=rcv, device=dev)
+        src = slice(c.src_rank * 2, c.src_rank * 2 + 2)     # the producer shard's heads in the full tensor
+        view = cache.cache[:, :, :, :, c.dst_head:c.dst_head + c.heads]
+        for l in range(L):
+            x.encode(l, k[l][:, src], v[l][:, src], snd.frame_ptr(0, l), 0, 1)
+            x.ingest_layer(l, T, snd.frame_ptr(0, l), view, table, status, 1)
+        torch.cuda.synchronize()
+        rcv.close()
+    assert int(status[0]) == 0
+    idx = torch.tensor(blocks, device=dev).long()
+    got = cache.cache[:, :, idx].reshape(L, 2, -1, H, D)[:, :, :T]
+    if profile_kind == "raw":
+        assert torch.equal(got[:, 0], k) and torch.equal(got[:, 1], v)
+    else:
+        # reference: each shard as its own whole-shard transfer into a 2-head cache
+        for r in range(2):
+            x = KVTransfer(prof, L, H, 2, D, r, 2, dev, T)
+            rcv = FrameReceiver(L, x.frame_stride, 1, dev)
+            snd = FrameSender(local=rcv, device=dev)
+            ref = PagedKVCache(L, 40, 16, 2, D, dev)
+            rb = ref.allocate(T)
+            rt = ref.block_table(rb, 40)
+            for l in range(L):
+                x.encode(l, k[l][:, 2 * r:2 * r + 2].contiguous(), v[l][:, 2 * r:2 * r + 2].contiguous(),
+                         snd.frame_ptr(0, l), 0, 1)
+                x.ingest_layer(l, T, snd.frame_ptr(0, l), ref.cache, rt, status, 1)
+            torch.cuda.synchronize()
+            want = ref.cache[:, :, torch.tensor(rb, device=dev).long()].reshape(L, 2, -1, 2, D)[:, :, :T]
+            assert torch.equal(got[..., 2 * r:2 * r + 2, :], want)
+            rcv.close()

@@ -68,3 +68,22 @@ def test_simulated_hf_cache_degrades_prefill_kv():
     k_ref = ref.layers[0].keys if hasattr(ref, "layers") else ref.key_cache[0]
     k_sim = cache.layers[0].keys if hasattr(cache, "layers") else cache.key_cache[0]
     assert k_ref.shape == k_sim.shape and not torch.equal(k_ref, k_sim)
+
+
+def test_kivi_and_cachegen_style_baselines_round_trip():
+    """The PyTorch restatements of KIVI's group quantisation (keys per channel
+    over token groups, values per token over channel groups) and of the
+    CacheGen-style delta quantiser invert their own packing: the error is
+    that of the quantiser (4 bits < 2 bits)."""
+    import torch
+    from kvserve_b200.offline_search.component_speed import kivi_compress, kivi_decompress
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(256, 4, 128, generator=g).bfloat16()
+    errs = {}
+    for per_channel in (True, False):
+        for bits in (2, 4):
+            y = kivi_decompress(*kivi_compress(x, bits, per_channel), bits, per_channel)
+            y = y.reshape(256, 4, 128) if per_channel else y.reshape(256, 4, 128)
+            errs[(per_channel, bits)] = float(((y.float() - x.float()) ** 2).mean())
+    for pc in (True, False):
+        assert errs[(pc, 4)] < 0.01 < errs[(pc, 2)] < 0.25

@@ -217,3 +217,41 @@ def test_trace_stamp_decoding():
     assert st["layers_ms"][0] == [0.0, 2.0, 1.0, 3.0]
     assert st["layers_ms"][1][:2] == [0.5, 2.5] and math.isnan(st["layers_ms"][1][2])
     assert summarize_stamps(st) == {"encode_span_ms": 2.5, "ingest_span_ms": 2.0}
+
+
+def _replica_worker(rank, world, port, q):
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port))
+    import torch.distributed as dist
+    from kvserve_b200.parallel.context import destroy_parallel, init_parallel
+    ctx = init_parallel("gloo", timeout_s=60, replicas=2)
+    # a broadcast inside the replica from its local rank 0 (global rank rank_offset)
+    t = torch.tensor([float(ctx.replica * 10 + ctx.rank)])
+    dist.broadcast(t, src=ctx.rank_offset, group=ctx.cpu_group)
+    allr = [None] * ctx.job_world_size
+    dist.all_gather_object(allr, ctx.global_rank, group=ctx.job_cpu_group)
+    q.put({"rank": rank, "replica": ctx.replica, "local": ctx.rank, "world": ctx.world_size, "role": ctx.role,
+           "peer": ctx.peer_rank, "offset": ctx.rank_offset, "bcast": float(t.item()), "all": allr,
+           "leaders": [ctx.global_ranks("prefill"), ctx.global_ranks("decode")]})
+    destroy_parallel(ctx)
+
+
+def test_data_parallel_replicas_layout():
+    """Four gloo ranks as two independent 1P1D replicas: replica-local ranks,
+    roles and peers, replica-scoped collectives, a job-wide group."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_replica_worker, args=(r, 4, port, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    res = {r["rank"]: r for r in (q.get(timeout=120) for _ in procs)}
+    for p in procs:
+        p.join(30)
+    assert [res[r]["replica"] for r in range(4)] == [0, 0, 1, 1]
+    assert [res[r]["role"] for r in range(4)] == ["prefill", "decode", "prefill", "decode"]
+    assert [res[r]["peer"] for r in range(4)] == [1, 0, 1, 0]
+    assert [res[r]["offset"] for r in range(4)] == [0, 0, 2, 2]
+    assert [res[r]["bcast"] for r in range(4)] == [0.0, 0.0, 10.0, 10.0]
+    assert all(res[r]["all"] == [0, 1, 2, 3] for r in range(4))
+    assert res[3]["leaders"] == [[2], [3]]
