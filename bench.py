@@ -166,7 +166,11 @@ def main() -> None:
         recon = measure_profile(profile, min(4, cfg.num_layers), args.prompt_len, cfg.num_kv_heads, cfg.head_dim,
                                 engine.device)
 
-    mine = {"steps": [t.__dict__ for t in timings], "handoff": handoffs}
+    wire = None
+    if ctx.is_prefill and profile.lossless:
+        torch.cuda.synchronize()
+        wire = int(sum(int(x.wire_bytes.item()) for x in engine.xfer_sets["default"]))
+    mine = {"steps": [t.__dict__ for t in timings], "handoff": handoffs, "wire": wire}
     allr = [None] * ctx.world_size
     if ctx.distributed:
         dist.all_gather_object(allr, mine, group=ctx.cpu_group)
@@ -234,6 +238,8 @@ def main() -> None:
             "kv_payload_bytes_per_request": int(payload) * tp,
             "kv_raw_bytes_per_request": int(raw) * tp,
             "compression_ratio": round(raw / payload, 3) if payload else None,
+            "kv_wire_bytes_per_request": (sum(r["wire"] for r in allr if r["wire"] is not None)
+                                          if any(r["wire"] is not None for r in allr) else None),
             "config": {"model": cfg.name, "layers": cfg.num_layers, "global_batch": 1,
                        "seq_len": args.prompt_len, "max_new_tokens": args.max_new,
                        "parallelism": ("colocated-1gpu" if ctx.world_size == 1 else f"{tp}P{tp}D-tp{tp}")

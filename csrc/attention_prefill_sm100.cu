@@ -1,9 +1,8 @@
 // Causal GQA prefill flash attention on tcgen05 tensor cores (head_dim 128).
 //
 // One CTA per SM holds two 128-row query tiles of one head (a "pair") and
-// streams the pair's K/V tiles; pairs are launched heaviest-first.  Two
-// variants share the TMA producer and the MMA issuer: v3 (one softmax
-// thread per S row) and v4 (two threads per row, one per 64-key half).
+// streams the pair's K/V tiles; pairs are launched heaviest-first.  K tiles
+// go through a ring of 2 or 3 stages (3 by default), V tiles through 2.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 
@@ -54,10 +53,19 @@ namespace v3 {
 constexpr int kThreads = 320;
 constexpr int OFF_Q0 = 0;
 constexpr int OFF_Q1 = TILE;
-constexpr int OFF_K = 2 * TILE;  // 2 stages
-constexpr int OFF_V = 4 * TILE;  // 2 stages
-constexpr int OFF_BAR = 6 * TILE;
-constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr int OFF_K = 2 * TILE;  // KS stages of K, then 2 of V
+template <int KS>
+struct Layout {
+  static constexpr int OFF_V = (2 + KS) * TILE;
+  static constexpr int OFF_BAR = (4 + KS) * TILE;
+  static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+  // barriers: q_full, k_full[KS], k_empty[KS], v_full[2], v_empty[2],
+  // s_full[2], p_full[2], o_done[2], drain; then the TMEM address
+  static constexpr int B_KFULL = 1, B_KEMPTY = 1 + KS, B_VFULL = 1 + 2 * KS, B_VEMPTY = 3 + 2 * KS,
+                       B_SFULL = 5 + 2 * KS, B_PFULL = 7 + 2 * KS, B_ODONE = 9 + 2 * KS, B_DRAIN = 11 + 2 * KS,
+                       NUM_BARS = 12 + 2 * KS;
+};
+static_assert(Layout<3>::SMEM_BYTES <= 232448, "3 K stages must fit in shared memory");
 constexpr uint32_t kTmemCols = 512;
 // Of every 16 consecutive key columns (8 pairs), pairs whose bit is set in
 // this mask take the polynomial exponential.
@@ -113,6 +121,7 @@ __device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
 
 // TMA producer of both flash kernels (one thread): Q0, Q1, then K and V of
 // each KV tile into two-stage rings.
+template <int KS>
 __device__ __forceinline__ void flash_produce(uint8_t* smem, const CUtensorMap* tmp, const AttnArgs& a, int h,
                                               int kvh, int q0, int n1, uint64_t* q_full, uint64_t* k_full,
                                               uint64_t* k_empty, uint64_t* v_full, uint64_t* v_empty) {
@@ -126,29 +135,30 @@ __device__ __forceinline__ void flash_produce(uint8_t* smem, const CUtensorMap* 
   tma_load_2d(smem + v3::OFF_Q1 + PANEL, &tm, xq + 64, q0 + BQ, q_full);
   int kdone = -1, vdone = -1;
   for (int j = 0; j < n1; ++j) {
-    const int st = j & 1;
-    const uint32_t ph = (j >> 1) & 1;
+    const int ks = j % KS, vs = j & 1;
+    const uint32_t kph = (j / KS) & 1, vph = (j >> 1) & 1;
     const int k0 = j * BKV;
-    if (!mbar_wait(&k_empty[st], ph ^ 1, a.err)) break;
-    mbar_arrive_expect_tx(&k_full[st], TILE);
-    tma_load_2d(smem + v3::OFF_K + st * TILE, &tm, xk, k0, &k_full[st]);
-    tma_load_2d(smem + v3::OFF_K + st * TILE + PANEL, &tm, xk + 64, k0, &k_full[st]);
+    if (!mbar_wait(&k_empty[ks], kph ^ 1, a.err)) break;
+    mbar_arrive_expect_tx(&k_full[ks], TILE);
+    tma_load_2d(smem + v3::OFF_K + ks * TILE, &tm, xk, k0, &k_full[ks]);
+    tma_load_2d(smem + v3::OFF_K + ks * TILE + PANEL, &tm, xk + 64, k0, &k_full[ks]);
     kdone = j;
-    if (!mbar_wait(&v_empty[st], ph ^ 1, a.err)) break;
-    mbar_arrive_expect_tx(&v_full[st], TILE);
-    tma_load_2d(smem + v3::OFF_V + st * TILE, &tm, xv, k0, &v_full[st]);
-    tma_load_2d(smem + v3::OFF_V + st * TILE + PANEL, &tm, xv + 64, k0, &v_full[st]);
+    if (!mbar_wait(&v_empty[vs], vph ^ 1, a.err)) break;
+    mbar_arrive_expect_tx(&v_full[vs], TILE);
+    tma_load_2d(smem + v3::Layout<KS>::OFF_V + vs * TILE, &tm, xv, k0, &v_full[vs]);
+    tma_load_2d(smem + v3::Layout<KS>::OFF_V + vs * TILE + PANEL, &tm, xv + 64, k0, &v_full[vs]);
     vdone = j;
   }
   // every issued copy lands before the CTA may exit (the last use of each
   // stage is the newest phase of its barrier)
   mbar_wait(q_full, 0, nullptr);
-  for (int j = (kdone > 0 ? kdone - 1 : 0); j <= kdone; ++j) mbar_wait(&k_full[j & 1], (j >> 1) & 1, nullptr);
+  for (int j = (kdone >= KS ? kdone - KS + 1 : 0); j <= kdone; ++j) mbar_wait(&k_full[j % KS], (j / KS) & 1, nullptr);
   for (int j = (vdone > 0 ? vdone - 1 : 0); j <= vdone; ++j) mbar_wait(&v_full[j & 1], (j >> 1) & 1, nullptr);
 }
 
 // MMA issuer of both flash kernels (one thread): S_i = Q_i K^T into TMEM and
 // O_i += P_i V with P read from TMEM, in the ping-pong order described above.
+template <int KS>
 __device__ __forceinline__ void flash_mma(uint8_t* smem, const AttnArgs& a, uint32_t tmem, int n0, int n1,
                                           uint64_t* q_full, uint64_t* k_full, uint64_t* k_empty, uint64_t* v_full,
                                           uint64_t* v_empty, uint64_t* s_full, uint64_t* p_full, uint64_t* o_done,
@@ -157,9 +167,9 @@ __device__ __forceinline__ void flash_mma(uint8_t* smem, const AttnArgs& a, uint
   constexpr uint32_t idesc_qk = idesc_bf16(BQ, BKV, false);
   constexpr uint32_t idesc_pv = idesc_bf16(BQ, D, true);
   const uint32_t q0a = smem_u32(smem + v3::OFF_Q0), q1a = smem_u32(smem + v3::OFF_Q1);
-  const uint32_t kb0 = smem_u32(smem + v3::OFF_K), vb0 = smem_u32(smem + v3::OFF_V);
+  const uint32_t kb0 = smem_u32(smem + v3::OFF_K), vb0 = smem_u32(smem + v3::Layout<KS>::OFF_V);
   auto qk = [&](uint32_t dst, uint32_t qa, int j) {
-    const uint32_t kb = kb0 + (j & 1) * TILE;
+    const uint32_t kb = kb0 + (j % KS) * TILE;
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
       const uint32_t off = (kk >> 2) * PANEL + (kk & 3) * 32;
@@ -195,7 +205,7 @@ __device__ __forceinline__ void flash_mma(uint8_t* smem, const AttnArgs& a, uint
       pv(tO0, tS0, j);
       if (j == n0 - 1) umma_commit(&o_done[0]);
       if (j + 1 < n0) {
-        if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, a.err)) { ok = false; break; }
+        if (!mbar_wait(&k_full[(j + 1) % KS], ((j + 1) / KS) & 1, a.err)) { ok = false; break; }
         k_next_ready = true;
         tc_fence_after();
         qk(tS0, q0a, j + 1);
@@ -208,11 +218,11 @@ __device__ __forceinline__ void flash_mma(uint8_t* smem, const AttnArgs& a, uint
     umma_commit(&v_empty[st]);
     if (j == n1 - 1) umma_commit(&o_done[1]);
     if (j + 1 < n1) {
-      if (!k_next_ready && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, a.err)) { ok = false; break; }
+      if (!k_next_ready && !mbar_wait(&k_full[(j + 1) % KS], ((j + 1) / KS) & 1, a.err)) { ok = false; break; }
       tc_fence_after();
       qk(tS1, q1a, j + 1);
       umma_commit(&s_full[1]);
-      umma_commit(&k_empty[(j + 1) & 1]);
+      umma_commit(&k_empty[(j + 1) % KS]);
     }
   }
   umma_commit(drain);
@@ -220,22 +230,24 @@ __device__ __forceinline__ void flash_mma(uint8_t* smem, const AttnArgs& a, uint
 }
 
 
+template <int KS>
 __global__ void __launch_bounds__(v3::kThreads, 1)
     flash_prefill_v3_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
+  using Lay = v3::Layout<KS>;
   using namespace sm100;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + v3::OFF_BAR);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Lay::OFF_BAR);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2] per query tile
-  uint64_t* p_full = bars + 11;  // [2] per query tile (128 arrivals)
-  uint64_t* o_done = bars + 13;  // [2] per query tile
-  uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* k_full = bars + Lay::B_KFULL;     // [KS]
+  uint64_t* k_empty = bars + Lay::B_KEMPTY;   // [KS]
+  uint64_t* v_full = bars + Lay::B_VFULL;     // [2]
+  uint64_t* v_empty = bars + Lay::B_VEMPTY;   // [2]
+  uint64_t* s_full = bars + Lay::B_SFULL;     // [2] per query tile
+  uint64_t* p_full = bars + Lay::B_PFULL;     // [2] per query tile (128 arrivals)
+  uint64_t* o_done = bars + Lay::B_ODONE;     // [2] per query tile
+  uint64_t* drain = bars + Lay::B_DRAIN;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Lay::NUM_BARS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x;
@@ -247,8 +259,8 @@ __global__ void __launch_bounds__(v3::kThreads, 1)
   const int n1 = n0 + 1;        // ... and by query tile 1
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 15; ++i) mbar_init(&bars[i], (i == 11 || i == 12) ? 128 : 1);
-    mbar_init(drain, 1);
+    for (int i = 0; i < Lay::NUM_BARS; ++i)
+      mbar_init(&bars[i], (i == Lay::B_PFULL || i == Lay::B_PFULL + 1) ? 128 : 1);
     fence_barrier_init();
     tma_prefetch_desc(&tm);
   }
@@ -259,10 +271,10 @@ __global__ void __launch_bounds__(v3::kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 8) {
-    if (lane == 0) flash_produce(smem, &tm, a, h, kvh, q0, n1, q_full, k_full, k_empty, v_full, v_empty);
+    if (lane == 0) flash_produce<KS>(smem, &tm, a, h, kvh, q0, n1, q_full, k_full, k_empty, v_full, v_empty);
   } else if (warp == 9) {
-    if (lane == 0) flash_mma(smem, a, tmem, n0, n1, q_full, k_full, k_empty, v_full, v_empty, s_full, p_full, o_done,
-                             drain);
+    if (lane == 0) flash_mma<KS>(smem, a, tmem, n0, n1, q_full, k_full, k_empty, v_full, v_empty, s_full, p_full,
+                                 o_done, drain);
   } else {
     const int wg = warp >> 2;
     const int row = (warp & 3) * 32 + lane;
@@ -386,238 +398,20 @@ __global__ void __launch_bounds__(v3::kThreads, 1)
 }
 
 
-// ---------------------------------------------------------------------------
-// v4: the v3 schedule (two query tiles in ping-pong, TMA warp, MMA warp) with
-// every S row split across TWO softmax threads, one per 64-key half:
-//   warps 0..7   query tile 0 (warps 0-3: keys 0..63, warps 4-7: keys 64..127)
-//   warps 8..15  query tile 1 (same split)
-//   warp 16      TMA producer, warp 17 MMA issuer
-// Warps w and w+4 hold the same TMEM lane quarter (rows); they exchange their
-// partial row maxima through shared memory with a 64-thread named barrier,
-// which also orders both halves' S loads before either writes P over them.
-// Each thread keeps half a row (64 scores instead of 128), so a tile's
-// softmax latency is about half of v3's and four softmax warps share each
-// SM sub-partition instead of two: the tensor pipe waits less for the
-// exponentials.  The row sum is kept per half and added in the epilogue.
-// ---------------------------------------------------------------------------
-namespace v4 {
-constexpr int kThreads = 576;
-constexpr int kTmaWarp = 16, kMmaWarp = 17;
-constexpr int OFF_XM = v3::OFF_BAR + 256;            // [2 parity][2 tiles][2 halves][128] row maxima
-constexpr int OFF_XL = OFF_XM + 2 * 2 * 2 * 128 * 4;  // [2 tiles][2 halves][128] row sums
-constexpr int OFF_XF = OFF_XL + 2 * 2 * 128 * 4;      // [2 parity][2 tiles][2 halves][4 quarters] ok flags
-constexpr int SMEM_BYTES = OFF_XF + 128 + 1024;
-}  // namespace v4
-
-__global__ void __launch_bounds__(v4::kThreads, 1)
-    flash_prefill_v4_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
-  using namespace sm100;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + v3::OFF_BAR);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2] per query tile
-  uint64_t* p_full = bars + 11;  // [2] per query tile (256 arrivals: both halves)
-  uint64_t* o_done = bars + 13;  // [2] per query tile
-  uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.x;
-  const int npairs = (a.T + 2 * BQ - 1) / (2 * BQ);
-  const int pair = npairs - 1 - int(blockIdx.y);
-  const int q0 = pair * 2 * BQ;
-  const int kvh = h / (a.Hq / a.Hkv);
-  const int n0 = q0 / BKV + 1;  // KV tiles seen by query tile 0
-  const int n1 = n0 + 1;        // ... and by query tile 1
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < 15; ++i) mbar_init(&bars[i], (i == 11 || i == 12) ? 256 : 1);
-    mbar_init(drain, 1);
-    fence_barrier_init();
-    tma_prefetch_desc(&tm);
-  }
-  if (warp == v4::kMmaWarp) tmem_alloc<v3::kTmemCols>(tmem_slot);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == v4::kTmaWarp) {
-    if (lane == 0) flash_produce(smem, &tm, a, h, kvh, q0, n1, q_full, k_full, k_empty, v_full, v_empty);
-  } else if (warp == v4::kMmaWarp) {
-    if (lane == 0) flash_mma(smem, a, tmem, n0, n1, q_full, k_full, k_empty, v_full, v_empty, s_full, p_full, o_done,
-                             drain);
-  } else {
-    const int wg = warp >> 3;             // query tile
-    const int half = (warp >> 2) & 1;     // keys [64 * half, 64 * half + 64) of each KV tile
-    const int quarter = warp & 3;         // TMEM lane quarter
-    const int row = quarter * 32 + lane;
-    const uint32_t lane_off = uint32_t(quarter * 32) << 16;
-    const uint32_t tS = tmem + wg * 128, tO = tmem + 256 + wg * 128 + half * 64;
-    const int bar_id = 1 + wg * 4 + quarter;   // warps (w, w + 4): the two halves of these rows
-    float* xm = reinterpret_cast<float*>(smem + v4::OFF_XM);
-    float* xl = reinterpret_cast<float*>(smem + v4::OFF_XL);
-    int* xf = reinterpret_cast<int*>(smem + v4::OFF_XF);
-    const int qrow0 = q0 + wg * BQ;
-    const int q_abs = qrow0 + row;
-    const int nkv = qrow0 / BKV + 1;
-    const float sl2 = a.scale_log2;
-    const int kbase = half * 64;
-    float m_ref = -INFINITY, l0 = 0.f, l1 = 0.f;
-    bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
-      const bool diag = (j == nkv - 1);
-      // a failed (timed-out) wait still takes part in this tile's pair
-      // barrier; both halves leave the loop together after it
-      if (!mbar_wait(&s_full[wg], j & 1, a.err)) ok = false;
-      ok = __all_sync(0xffffffffu, ok);
-      tc_fence_after();
-      uint32_t r[2][32];
-      if (ok) {
-#pragma unroll
-        for (int c = 0; c < 2; ++c) tmem_ld32(tS + lane_off + kbase + c * 32, r[c]);
-        tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) r[c][e] = 0u;
-      }
-      float mx = -INFINITY;
-      if (!diag) {
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) mx = v3::max3(mx, __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]));
-      } else {
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            if (kbase + c * 32 + e > row) r[c][e] = __float_as_uint(-INFINITY);
-            mx = fmaxf(mx, __uint_as_float(r[c][e]));
-          }
-      }
-      // row maximum over both halves; the barrier also orders both halves'
-      // S loads before either half overwrites S with P
-      float* xmj = xm + ((j & 1) * 2 + wg) * 2 * 128;
-      int* xfj = xf + ((j & 1) * 2 + wg) * 8;
-      xmj[half * 128 + row] = mx;
-      if (lane == 0) xfj[half * 4 + quarter] = ok;
-      asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-      if (!ok || !xfj[(half ^ 1) * 4 + quarter]) {
-        ok = false;
-        break;
-      }
-      mx = fmaxf(mx, xmj[(half ^ 1) * 128 + row]);
-      const float mxs = mx * sl2;
-      const bool rescale = mxs > m_ref + kRescaleThreshold;
-      const float m_use = rescale ? mxs : m_ref;
-      const float neg_m = -m_use;
-      float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float x0, x1;
-          v3::fma2s(x0, x1, __uint_as_float(r[c][2 * e]), __uint_as_float(r[c][2 * e + 1]), sl2, neg_m);
-          float p0, p1;
-          if ((v3::kPolyPairs >> (e & 7)) & 1u) {
-            p0 = v3::ex2_poly(x0);
-            p1 = v3::ex2_poly(x1);
-            if (diag) {  // the polynomial does not map -inf to 0
-              if (kbase + c * 32 + 2 * e > row) p0 = 0.f;
-              if (kbase + c * 32 + 2 * e + 1 > row) p1 = 0.f;
-            }
-          } else {
-            p0 = v3::ex2_mufu(x0);
-            p1 = v3::ex2_mufu(x1);
-          }
-          v3::add2(s0, s1, p0, p1);
-          pk[e] = pack_bf16x2(p0, p1);
-        }
-        // P of keys kbase + 32c .. + 31 -> S columns [(kbase + 32c) / 2, + 16)
-        tmem_st16(tS + lane_off + (kbase + c * 32) / 2, pk);
-      }
-      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
-        const float f = rescale ? v3::ex2_mufu(m_ref - m_use) : 1.0f;
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + lane_off + c * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-          tmem_st32(tO + lane_off + c * 32, o);
-        }
-        l0 *= f;
-        l1 *= f;
-      }
-      tmem_wait_st();
-      if (rescale) m_ref = m_use;
-      l0 += s0;
-      l1 += s1;
-      tc_fence_before();
-      mbar_arrive(&p_full[wg]);
-    }
-    // both halves of a row finish the loop together (every tile has a barrier)
-    xl[(wg * 2 + half) * 128 + row] = l0 + l1;
-    asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-    if (ok) {
-      const bool done = mbar_wait(&o_done[wg], 0, a.err);
-      if (__all_sync(0xffffffffu, done)) {
-        tc_fence_after();
-        const float l = xl[(wg * 2) * 128 + row] + xl[(wg * 2 + 1) * 128 + row];
-        const float inv = l > 0.f ? 1.0f / l : 0.f;
-        bf16* orow = a.out + int64_t(q_abs) * a.ldo + int64_t(h) * D + half * 64;
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + lane_off + c * 32, o);
-          tmem_wait_ld();
-          if (q_abs < a.T) {
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 w;
-              w.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
-              w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
-              w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
-              w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
-              *reinterpret_cast<uint4*>(orow + c * 32 + v * 8) = w;
-            }
-          }
-        }
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == v4::kMmaWarp) {
-    tc_fence_after();
-    tmem_dealloc<v3::kTmemCols>(tmem);
-  }
-}
-
 }  // namespace
 
-// Kernel variant: 3 (one softmax thread per S row) or 4 (two per row); 0
-// takes KVSERVE_FLASH (default 4).
-static int flash_default_variant() {
+// K-tile stages of the kernel: 3 (default) or 2 (KVSERVE_FLASH_KSTAGES=2);
+// `kstages` 0 takes that default.
+static int flash_default_kstages() {
   static const int v = [] {
-    const char* e = std::getenv("KVSERVE_FLASH");
-    return (e && e[0] == '3') ? 3 : 4;
+    const char* e = std::getenv("KVSERVE_FLASH_KSTAGES");
+    return (e && e[0] == '2') ? 2 : 3;
   }();
   return v;
 }
 
 void flash_prefill(torch::Tensor qkv, int64_t Hq, int64_t Hkv, double scale, torch::Tensor out, torch::Tensor err,
-                   int64_t variant) {
+                   int64_t kstages) {
   KVS_CHECK_ARG(qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 2 && qkv.stride(1) == 1,
                 "flash_prefill: qkv [T, (Hq+2Hkv)*128] bf16");
   KVS_CHECK_ARG(qkv.size(1) == (Hq + 2 * Hkv) * D && Hq % Hkv == 0, "flash_prefill: head_dim 128 only");
@@ -638,20 +432,20 @@ void flash_prefill(torch::Tensor qkv, int64_t Hq, int64_t Hkv, double scale, tor
       make_tmap_2d_bf16(qkv.data_ptr(), uint64_t(qkv.size(1)), uint64_t(T), uint64_t(qkv.stride(0)) * 2, 64, 128);
   static bool attr = false;
   if (!attr) {
-    KVS_CUDA_CHECK(cudaFuncSetAttribute(flash_prefill_v3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        v3::SMEM_BYTES));
-    KVS_CUDA_CHECK(cudaFuncSetAttribute(flash_prefill_v4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        v4::SMEM_BYTES));
+    KVS_CUDA_CHECK(cudaFuncSetAttribute(flash_prefill_v3_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        v3::Layout<2>::SMEM_BYTES));
+    KVS_CUDA_CHECK(cudaFuncSetAttribute(flash_prefill_v3_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        v3::Layout<3>::SMEM_BYTES));
     attr = true;
   }
-  if (variant == 0) variant = flash_default_variant();
-  KVS_CHECK_ARG(variant == 3 || variant == 4, "flash_prefill: variant must be 3 or 4");
+  const int ks = kstages == 0 ? flash_default_kstages() : int(kstages);
+  KVS_CHECK_ARG(ks == 2 || ks == 3, "flash_prefill: K-tile stages must be 2 or 3");
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   dim3 grid(int(Hq), (T + 2 * BQ - 1) / (2 * BQ));
-  if (variant == 4)
-    flash_prefill_v4_kernel<<<grid, v4::kThreads, v4::SMEM_BYTES, st>>>(tm, a);
+  if (ks == 3)
+    flash_prefill_v3_kernel<3><<<grid, v3::kThreads, v3::Layout<3>::SMEM_BYTES, st>>>(tm, a);
   else
-    flash_prefill_v3_kernel<<<grid, v3::kThreads, v3::SMEM_BYTES, st>>>(tm, a);
+    flash_prefill_v3_kernel<2><<<grid, v3::kThreads, v3::Layout<2>::SMEM_BYTES, st>>>(tm, a);
   KVS_CUDA_CHECK(cudaGetLastError());
 }
 

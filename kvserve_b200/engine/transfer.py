@@ -31,6 +31,7 @@ from ..compression.heads import (get_scores, low_precision_mask, pack_sign_bits,
 from ..ops import kv_codec as kc
 
 DEFAULT_SEED = 3237919422
+RZE_CHUNK = 16384
 
 
 @dataclass(frozen=True)
@@ -43,6 +44,7 @@ class TransferProfile:
     value_levels: tuple = (4, 8)
     score_model: Optional[str] = None
     score_path: Optional[str] = None
+    lossless: bool = False          # kvs-rze-v1 stage after the frame (the profile's lossless codec)
 
     @classmethod
     def raw(cls) -> "TransferProfile":
@@ -63,12 +65,15 @@ class TransferProfile:
             return cls.raw()
         qc = spec.get("quantizer_config") or {}
         tc = spec.get("transformer_config") or {}
+        cc = spec.get("codec_config") or {}
+        lossless = "codec" in spec.get("pipeline", []) and cc.get("codec_type", "bitpack") != "bitpack"
         seed = qc.get("base_seed", qc.get("seed", tc.get("seed", DEFAULT_SEED)))
         return cls(compressed=True, seed=int(seed), hybrid_ratio=float(qc.get("hybrid_ratio", 0.8)),
                    split_type=qc.get("split_type", "head"),
                    key_levels=(int(qc.get("low_key_max_value", 6)), int(qc.get("high_key_max_value", 12))),
                    value_levels=(int(qc.get("low_value_max_value", 4)), int(qc.get("high_value_max_value", 8))),
-                   score_model=qc.get("model_name") or model_name, score_path=qc.get("score_path"))
+                   score_model=qc.get("model_name") or model_name, score_path=qc.get("score_path"),
+                   lossless=lossless)
 
     def to_compression(self) -> Optional[dict]:
         if not self.compressed:
@@ -80,7 +85,8 @@ class TransferProfile:
                                      "low_value_max_value": self.value_levels[0],
                                      "high_value_max_value": self.value_levels[1],
                                      "model_name": self.score_model, "axis_key": "channel", "axis_value": "token"},
-                "codec_config": {"codec_type": "bitpack", "bitpack_bits": 8}}
+                "codec_config": {"codec_type": "lc", "lc_algorithm": "kvs-rze-v1"} if self.lossless else
+                {"codec_type": "bitpack", "bitpack_bits": 8}}
 
 
 class KVTransfer:
@@ -106,8 +112,21 @@ class KVTransfer:
         signs = torch.stack([rademacher_signs(profile.seed, l, local_heads, head_dim) for l in range(num_layers)])
         self.sign_bits = pack_sign_bits(signs).to(self.device)   # [L, H, D/32]
         self.max_tokens = max_tokens
-        self.frame_stride = max(kc.frame_layout(self.spec(l, max_tokens)).frame_bytes for l in range(num_layers))
+        # bytes of the largest frame, and the bytes a slot reserves per layer
+        # (the lossless codec's worst case when the profile has that stage)
+        self.frame_bytes_max = max(kc.frame_layout(self.spec(l, max_tokens)).frame_bytes for l in range(num_layers))
+        self.frame_stride = self.frame_bytes_max
         self._state: Optional[kc.EncoderState] = None
+        if profile.lossless:
+            from ..ops import ext
+            cap = ext().rze_max_encoded_bytes(self.frame_bytes_max, RZE_CHUNK)
+            self.frame_stride = (cap + 255) // 256 * 256
+            dev = self.device
+            self._stage = torch.empty(self.frame_bytes_max, dtype=torch.uint8, device=dev)
+            self._scratch = torch.empty(ext().rze_scratch_bytes(self.frame_bytes_max, RZE_CHUNK), dtype=torch.uint8,
+                                        device=dev)
+            self._total = torch.zeros(1, dtype=torch.int64, device=dev)
+            self.wire_bytes = torch.zeros(1, dtype=torch.int64, device=dev)   # encoded bytes of the last request
 
     def spec(self, layer: int, T: int) -> kc.FrameSpec:
         n_low = int(self.n_lows_cpu[layer])
@@ -135,16 +154,52 @@ class KVTransfer:
             # signed transform table of every (layer, head) for the tensor-core encoder
             from ..ops import ext
             self._hs_table = ext().kv_signed_hadamard(self.sign_bits.reshape(-1, 4).contiguous())
-        kc.encode_layer(k, v, self.spec(layer, k.shape[0]), self.orders[layer], self.sign_bits[layer], frame_ptr,
-                        self._state, flag_ptr=flag_ptr, seq=seq, layer=layer, pacing=pacing,
+        spec = self.spec(layer, k.shape[0])
+        lossless = self.profile.lossless
+        # with the lossless stage the frame goes to local staging first and
+        # the codec's output is what lands in the slot, published afterwards
+        kc.encode_layer(k, v, spec, self.orders[layer], self.sign_bits[layer],
+                        self._stage.data_ptr() if lossless else frame_ptr, self._state,
+                        flag_ptr=0 if lossless else flag_ptr, seq=seq, layer=layer, pacing=pacing,
                         rate_bytes_per_ns=rate_bytes_per_ns, max_ctas=max_ctas,
                         hs_table=getattr(self, "_hs_table", None), hs_row0=layer * self.H,
                         trace_ptr=trace[layer].data_ptr() if trace is not None else 0)
+        if lossless:
+            from .. import ops
+            n = kc.frame_layout(spec).frame_bytes
+            out = ops.ext().tensor_from_ptr(int(frame_ptr), [self.frame_stride], ops.dtype_code(torch.uint8),
+                                            self.device.index)
+            ops.count_launches(3)
+            ops.ext().rze_encode(self._stage[:n], out, self._scratch, self._total, RZE_CHUNK)
+            if layer == 0:
+                self.wire_bytes.zero_()
+            self.wire_bytes.add_(self._total)
+            if flag_ptr:
+                ops.count_launches(1)
+                ops.ext().store_release_u32(int(flag_ptr), int(seq))
+
+    def _unpack_lossless(self, layer: int, T: int, frame_ptr: int, flag_ptr: int, seq: int, timeout_ns: int,
+                         status: torch.Tensor) -> int:
+        """Lossless stage of the decode side: (wait for the layer's flag, then)
+        decode the slot's codec payload into local staging; returns the
+        staging address of the frame."""
+        from .. import ops
+        if flag_ptr:
+            ops.count_launches(1)
+            ops.ext().wait_flag(int(flag_ptr), int(seq), int(timeout_ns), status)
+        n = kc.frame_layout(self.spec(layer, T)).frame_bytes
+        src = ops.ext().tensor_from_ptr(int(frame_ptr), [self.frame_stride], ops.dtype_code(torch.uint8),
+                                        self.device.index)
+        ops.count_launches(2)
+        ops.ext().rze_decode(src, self._stage[:n], self._scratch, RZE_CHUNK)
+        return self._stage.data_ptr()
 
     # ------------------------------------------------------------- decode
     def ingest_layer(self, layer: int, T: int, frame_ptr: int, kv_cache: torch.Tensor, block_table: torch.Tensor,
                      status: torch.Tensor, seq: int, tok_offset: int = 0, trace: Optional[torch.Tensor] = None) -> None:
         spec = self.spec(layer, T)
+        if self.profile.lossless:
+            frame_ptr = self._unpack_lossless(layer, T, frame_ptr, 0, seq, 0, status)
         kc.decode_layers(frame_ptr, kc.frame_layout(spec).frame_bytes, spec, self.orders, self.sign_bits, kv_cache,
                          block_table, status, tok_offset=tok_offset, seq=seq, layer_begin=layer, num_layers=1,
                          trace_ptr=trace.data_ptr() if trace is not None else 0)
@@ -152,6 +207,16 @@ class KVTransfer:
     def ingest_all(self, T: int, slot_base: int, frame_stride: int, flags_ptr: int, kv_cache: torch.Tensor,
                    block_table: torch.Tensor, status: torch.Tensor, seq: int, timeout_ns: int,
                    tok_offset: int = 0, max_ctas: int = 148, trace: Optional[torch.Tensor] = None) -> None:
+        if self.profile.lossless:
+            # per layer: bounded flag wait, codec decode into staging, frame decode
+            for l in range(self.L):
+                ptr = self._unpack_lossless(l, T, slot_base + l * frame_stride, flags_ptr + 4 * l, seq, timeout_ns,
+                                            status)
+                spec = self.spec(l, T)
+                kc.decode_layers(ptr, kc.frame_layout(spec).frame_bytes, spec, self.orders, self.sign_bits, kv_cache,
+                                 block_table, status, tok_offset=tok_offset, seq=seq, layer_begin=l, num_layers=1,
+                                 max_ctas=max_ctas, trace_ptr=trace.data_ptr() if trace is not None else 0)
+            return
         kc.decode_layers(slot_base, frame_stride, self.max_spec(T), self.orders, self.sign_bits, kv_cache,
                          block_table, status, tok_offset=tok_offset, flags_ptr=flags_ptr, seq=seq, layer_begin=0,
                          num_layers=self.L, timeout_ns=timeout_ns, max_ctas=max_ctas, n_lows=self.n_lows,

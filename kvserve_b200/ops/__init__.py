@@ -206,16 +206,17 @@ def argmax(logits: torch.Tensor, index_offset: int = 0, out_val: Optional[torch.
 
 def flash_prefill(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int,
                   scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
-                  variant: int = 0) -> torch.Tensor:
+                  kstages: int = 0) -> torch.Tensor:
     """Causal GQA attention over a fused (already rotated) QKV tensor, head_dim 128.
-    ``variant`` 3 or 4 picks the kernel (0: ``KVSERVE_FLASH``, default 4)."""
+    ``kstages`` (2 or 3) sets the depth of the kernel's K-tile ring (0:
+    ``KVSERVE_FLASH_KSTAGES``, default 3)."""
     d = 128
     if scale is None:
         scale = 1.0 / math.sqrt(d)
     if out is None:
         out = torch.empty((qkv.shape[0], num_q_heads * d), dtype=qkv.dtype, device=qkv.device)
     count_launches(1)
-    ext().flash_prefill(qkv, num_q_heads, num_kv_heads, scale, out, device_status(qkv.device), int(variant))
+    ext().flash_prefill(qkv, num_q_heads, num_kv_heads, scale, out, device_status(qkv.device), int(kstages))
     return out
 
 

@@ -156,9 +156,9 @@ def case_flash(a, pk):
         out = torch.empty(T, Hq * 128, device="cuda", dtype=torch.bfloat16)
         fl = 4 * T * T * 128 * Hq / 2
         r = {}
-        for var in (4, 3):   # v4 (two softmax threads per row) first: the default
-            t = time_ms([lambda: flash_prefill(qkv, Hq, Hkv, out=out, variant=var)], max(3, a.iters // 2), a.once)
-            r[f"v{var}"] = {"ms": round(t, 4), "tflops": round(fl / t / 1e9, 1),
+        for ks in (3, 2):   # K-tile ring depth; 3 (the default) first
+            t = time_ms([lambda: flash_prefill(qkv, Hq, Hkv, out=out, kstages=ks)], max(3, a.iters // 2), a.once)
+            r[f"kstages{ks}"] = {"ms": round(t, 4), "tflops": round(fl / t / 1e9, 1),
                             "frac_of_measured_bf16": round(fl / t / 1e9 / pk["bf16_tflops"], 3)}
             if a.once:
                 break

@@ -53,7 +53,7 @@ def _port_block():
     raise RuntimeError("no free port")
 
 
-def _engine(q, role, model_dir, port, profile, max_tokens):
+def _engine(q, role, model_dir, port, profile, max_tokens, ready=None):
     os.environ["VLLM_ENABLE_V1_MULTIPROCESSING"] = "0"
     os.environ["KVSERVE_LOAD_TIMEOUT_S"] = "300"    # the producer may still be starting
     out = None
@@ -63,6 +63,12 @@ def _engine(q, role, model_dir, port, profile, max_tokens):
         from vllm.inputs import TokensPrompt
         kw = dict(model=model_dir, load_format="dummy", skip_tokenizer_init=True, dtype="bfloat16",
                   max_model_len=512, enforce_eager=True, gpu_memory_utilization=0.2, seed=0)
+        if role == "producer" and ready is not None:
+            # vLLM sizes its KV cache from the memory it sees while profiling:
+            # engines starting at the same time on one GPU count each other's
+            # allocations, so the producer starts once the consumer is built
+            if not ready.wait(300):
+                raise RuntimeError("the consumer engine did not start")
         if role == "reference":
             llm = LLM(enable_prefix_caching=True, **kw)
         else:
@@ -73,6 +79,8 @@ def _engine(q, role, model_dir, port, profile, max_tokens):
                                   kv_port=port, kv_buffer_size=64 << 20,
                                   kv_connector_extra_config={"compression": profile, "data_plane": "ipc"})
             llm = LLM(enable_prefix_caching=False, kv_transfer_config=kv, **kw)
+            if role == "consumer" and ready is not None:
+                ready.set()
         sp = SamplingParams(max_tokens=max_tokens, temperature=0.0, ignore_eos=True, detokenize=False,
                             extra_args={"kv_transfer_params": {"transfer_id": "kvs-vllm-test-0"}})
         runs = 2 if role == "reference" else 1
@@ -96,20 +104,25 @@ def _run(profile, max_tokens=8):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port_block()
-    procs = [ctx.Process(target=_engine, args=(q, role, d, port, profile, 1 if role == "producer" else max_tokens))
-             for role in ("consumer", "producer", "reference")]
-    for p in procs:
-        p.start()
+    ready = ctx.Event()
     res = {}
-    try:
-        for _ in procs:
-            role, out = q.get(timeout=600)
-            res[role] = out
-    finally:
+    # the PD pair first (started one after the other), then the reference
+    # engine on its own
+    for roles in (("consumer", "producer"), ("reference",)):
+        procs = [ctx.Process(target=_engine, args=(q, role, d, port, profile,
+                                                   1 if role == "producer" else max_tokens, ready))
+                 for role in roles]
         for p in procs:
-            p.join(30)
-            if p.is_alive():
-                p.kill()
+            p.start()
+        try:
+            for _ in procs:
+                role, out = q.get(timeout=600)
+                res[role] = out
+        finally:
+            for p in procs:
+                p.join(30)
+                if p.is_alive():
+                    p.kill()
     return res
 
 

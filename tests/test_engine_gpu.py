@@ -224,3 +224,28 @@ def test_head_range_copies_of_heterogeneous_tp(profile_kind):
             want = ref.cache[:, :, torch.tensor(rb, device=dev).long()].reshape(L, 2, -1, 2, D)[:, :, :T]
             assert torch.equal(got[..., 2 * r:2 * r + 2, :], want)
             rcv.close()
+
+
+def test_lossless_stage_is_exact_in_the_engine():
+    """A profile with the lossless codec stage (kvs-rze-v1 between the frame
+    and the slot) hands off exactly the frame of the same profile without
+    it: the decode side's cache, hence the greedy tokens, are identical, and
+    the codec's byte count is reported."""
+    import json
+    import os
+    from kvserve_b200.engine.transfer import TransferProfile
+    path = os.path.join(os.path.dirname(__file__), "..", "configs", "compression", "hadamard_k4v4_lc.json")
+    with open(path) as f:
+        lc = TransferProfile.from_compression(json.load(f))
+    assert lc.lossless
+    plain = TransferProfile(**{**lc.__dict__, "lossless": False})
+    ids = torch.randint(0, 4096, (240,), dtype=torch.int32)
+    toks = []
+    for prof in (plain, lc):
+        eng = _engine(prof)
+        toks.append(eng.generate(ids, 8).tokens)
+        if prof.lossless:
+            torch.cuda.synchronize()
+            assert int(eng.xfer.wire_bytes.item()) > 0
+        eng.close()
+    assert toks[0] == toks[1]

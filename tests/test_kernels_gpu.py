@@ -166,13 +166,13 @@ def _ref_causal(qkv, Hq, Hkv, D=128):
     return (s.softmax(-1) @ v).transpose(0, 1).reshape(T, Hq * D)
 
 
-@pytest.mark.parametrize("variant", [3, 4])
+@pytest.mark.parametrize("kstages", [2, 3])
 @pytest.mark.parametrize("T,Hq,Hkv", [(128, 1, 1), (200, 4, 2), (1000, 8, 2), (2048, 32, 8)])
-def test_flash_prefill(T, Hq, Hkv, variant):
+def test_flash_prefill(T, Hq, Hkv, kstages):
     ops = _ops()
     torch.manual_seed(1)
     qkv = torch.randn(T, (Hq + 2 * Hkv) * 128, device="cuda", dtype=torch.bfloat16)
-    o = ops.flash_prefill(qkv, Hq, Hkv, variant=variant)
+    o = ops.flash_prefill(qkv, Hq, Hkv, kstages=kstages)
     ops.check_device_status()
     assert _rel_err(o, _ref_causal(qkv, Hq, Hkv)) < 2e-2
 
