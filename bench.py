@@ -166,11 +166,19 @@ def main() -> None:
         recon = measure_profile(profile, min(4, cfg.num_layers), args.prompt_len, cfg.num_kv_heads, cfg.head_dim,
                                 engine.device)
 
+    # optional: per-kernel device time of a decode step (profiler; not a
+    # timing of record), the table the N=8 scaling analysis needs
+    ktable = None
+    if os.environ.get("KVSERVE_PROFILE_DECODE", "1") != "0":
+        try:
+            ktable = engine.decode_kernel_table(prompts[0])
+        except Exception as exc:  # the table is optional evidence; never fail the bench for it
+            _log(f"decode kernel table skipped: {exc!r}")
     wire = None
     if ctx.is_prefill and profile.lossless:
         torch.cuda.synchronize()
         wire = int(sum(int(x.wire_bytes.item()) for x in engine.xfer_sets["default"]))
-    mine = {"steps": [t.__dict__ for t in timings], "handoff": handoffs, "wire": wire}
+    mine = {"steps": [t.__dict__ for t in timings], "handoff": handoffs, "wire": wire, "ktable": ktable}
     allr = [None] * ctx.world_size
     if ctx.distributed:
         dist.all_gather_object(allr, mine, group=ctx.cpu_group)
@@ -256,6 +264,7 @@ def main() -> None:
                     "wall_ms_per_request": round(1e3 * wall_s / args.steps, 3)},
             "gpu_launches": int(launches),
             "clocks": clocks,
+            "decode_kernel_table": next((r["ktable"][:16] for r in allr if r["ktable"]), None),
             "_ttft": ttft, "_e2e": e2e_ttft,
         }
     if n_rep > 1:

@@ -528,6 +528,30 @@ class PDEngine:
                 "ingest_ms": start.elapsed_time(ing_end) if ctx.is_decode else nan,
                 "payload_bytes": self.request_bytes(T, xfer)[0], "raw_bytes": self.request_bytes(T, xfer)[1]}
 
+    def decode_kernel_table(self, prompt_ids: torch.Tensor, steps: int = 8) -> list:
+        """Per-kernel device time of this rank's decode steps, taken with the
+        PyTorch profiler (CUPTI) around ``steps`` graph replays after one
+        request's prefill and hand-off: ``[(kernel, calls_per_step,
+        us_per_step)]`` sorted by time.  Evidence of where a decode step goes,
+        not a timing of record (a profiler adds overhead).  Every rank calls
+        it (it serves one request)."""
+        from torch.profiler import ProfilerActivity, profile
+        res = self.generate(prompt_ids, min(self.max_new, steps + 1))
+        table = []
+        if self.ctx.is_decode and self._graph is not None:
+            torch.cuda.synchronize(self.device)
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                for _ in range(steps):
+                    self._graph.replay()
+                torch.cuda.synchronize(self.device)
+            for ev in prof.key_averages():
+                t = getattr(ev, "device_time_total", None) or getattr(ev, "cuda_time_total", 0)
+                if t and ev.count:
+                    table.append((ev.key[:90], round(ev.count / steps, 2), round(t / steps, 2)))
+            table.sort(key=lambda r: -r[2])
+        del res
+        return table
+
     def close(self) -> None:
         self._graph = None
         if self.model.decode_coll is not None:

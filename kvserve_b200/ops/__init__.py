@@ -209,7 +209,7 @@ def flash_prefill(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int,
                   kstages: int = 0) -> torch.Tensor:
     """Causal GQA attention over a fused (already rotated) QKV tensor, head_dim 128.
     ``kstages`` (2 or 3) sets the depth of the kernel's K-tile ring (0:
-    ``KVSERVE_FLASH_KSTAGES``, default 3)."""
+    ``KVSERVE_FLASH_KSTAGES``, default 2)."""
     d = 128
     if scale is None:
         scale = 1.0 / math.sqrt(d)
