@@ -69,7 +69,7 @@ static_assert(Layout<3>::SMEM_BYTES <= 232448, "3 K stages must fit in shared me
 constexpr uint32_t kTmemCols = 512;
 // Of every 16 consecutive key columns (8 pairs), pairs whose bit is set in
 // this mask take the polynomial exponential.
-constexpr uint32_t kPolyPairs = 0x11u;  // 2 of 8 pairs = 25 %
+constexpr uint32_t kPolyPairs = 0x11u;  // default: 2 of 8 pairs = 25 %
 
 __device__ __forceinline__ float ex2_mufu(float x) {
   float y;
@@ -230,7 +230,7 @@ __device__ __forceinline__ void flash_mma(uint8_t* smem, const AttnArgs& a, uint
 }
 
 
-template <int KS>
+template <int KS, uint32_t POLY>
 __global__ void __launch_bounds__(v3::kThreads, 1)
     flash_prefill_v3_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
   using Lay = v3::Layout<KS>;
@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(v3::kThreads, 1)
           float x0, x1;
           v3::fma2s(x0, x1, __uint_as_float(r[c][2 * e]), __uint_as_float(r[c][2 * e + 1]), sl2, neg_m);
           float p0, p1;
-          if ((v3::kPolyPairs >> (e & 7)) & 1u) {
+          if ((POLY >> (e & 7)) & 1u) {
             p0 = v3::ex2_poly(x0);
             p1 = v3::ex2_poly(x1);
             if (diag) {  // the polynomial does not map -inf to 0
@@ -412,7 +412,7 @@ static int flash_default_kstages() {
 }
 
 void flash_prefill(torch::Tensor qkv, int64_t Hq, int64_t Hkv, double scale, torch::Tensor out, torch::Tensor err,
-                   int64_t kstages) {
+                   int64_t kstages, int64_t poly) {
   KVS_CHECK_ARG(qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 2 && qkv.stride(1) == 1,
                 "flash_prefill: qkv [T, (Hq+2Hkv)*128] bf16");
   KVS_CHECK_ARG(qkv.size(1) == (Hq + 2 * Hkv) * D && Hq % Hkv == 0, "flash_prefill: head_dim 128 only");
@@ -431,22 +431,29 @@ void flash_prefill(torch::Tensor qkv, int64_t Hq, int64_t Hkv, double scale, tor
   a.err = reinterpret_cast<uint32_t*>(err.data_ptr<int32_t>());
   const CUtensorMap tm =
       make_tmap_2d_bf16(qkv.data_ptr(), uint64_t(qkv.size(1)), uint64_t(T), uint64_t(qkv.stride(0)) * 2, 64, 128);
-  static bool attr = false;
-  if (!attr) {
-    KVS_CUDA_CHECK(cudaFuncSetAttribute(flash_prefill_v3_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        v3::Layout<2>::SMEM_BYTES));
-    KVS_CUDA_CHECK(cudaFuncSetAttribute(flash_prefill_v3_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        v3::Layout<3>::SMEM_BYTES));
-    attr = true;
-  }
-  const int ks = kstages == 0 ? flash_default_kstages() : int(kstages);
-  KVS_CHECK_ARG(ks == 2 || ks == 3, "flash_prefill: K-tile stages must be 2 or 3");
+  if (kstages == 0) kstages = flash_default_kstages();
+  if (poly == 0) poly = v3::kPolyPairs;
+  KVS_CHECK_ARG(kstages == 2 || kstages == 3, "flash_prefill: K-tile stages must be 2 or 3");
+  KVS_CHECK_ARG(kstages == 2 || poly == v3::kPolyPairs, "flash_prefill: 3 K stages use the default exponential mix");
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   dim3 grid(int(Hq), (T + 2 * BQ - 1) / (2 * BQ));
-  if (ks == 3)
-    flash_prefill_v3_kernel<3><<<grid, v3::kThreads, v3::Layout<3>::SMEM_BYTES, st>>>(tm, a);
-  else
-    flash_prefill_v3_kernel<2><<<grid, v3::kThreads, v3::Layout<2>::SMEM_BYTES, st>>>(tm, a);
+#define KVS_FLASH_LAUNCH(KS, PM)                                                                                 \
+  {                                                                                                            \
+    static bool set = false;                                                                                   \
+    if (!set) {                                                                                                \
+      KVS_CUDA_CHECK(cudaFuncSetAttribute(flash_prefill_v3_kernel<KS, PM>,                                     \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, v3::Layout<KS>::SMEM_BYTES)); \
+      set = true;                                                                                              \
+    }                                                                                                          \
+    flash_prefill_v3_kernel<KS, PM><<<grid, v3::kThreads, v3::Layout<KS>::SMEM_BYTES, st>>>(tm, a);            \
+  }
+  if (kstages == 3) KVS_FLASH_LAUNCH(3, 0x11u)
+  else if (poly == 0x11) KVS_FLASH_LAUNCH(2, 0x11u)
+  else if (poly == 0x100) KVS_FLASH_LAUNCH(2, 0x00u)
+  else if (poly == 0x55) KVS_FLASH_LAUNCH(2, 0x55u)
+  else if (poly == 0xFF) KVS_FLASH_LAUNCH(2, 0xFFu)
+  else KVS_CHECK_ARG(false, "flash_prefill: polynomial-exponential mask must be 0x11, 0x55, 0xFF or 0x100 (none)");
+#undef KVS_FLASH_LAUNCH
   KVS_CUDA_CHECK(cudaGetLastError());
 }
 

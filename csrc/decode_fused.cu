@@ -37,6 +37,9 @@
 #include <ATen/cuda/CUDAContext.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <utility>
 #include <vector>
 
 #include "common.cuh"
@@ -57,7 +60,7 @@ __device__ __forceinline__ void report(uint32_t* status, uint32_t code) {
   if (status) atomicCAS(status, uint32_t(kStatusOk), code);
 }
 
-constexpr int kMaxChunks = 4;   // 16-row chunks per CTA (grid = N / (16 * chunks) must fit at once)
+constexpr int kMaxChunks = 8;   // 16-row chunks per CTA (grid = N / (16 * chunks) must fit at once)
 
 // Staging of rank `src`'s partial rows in rank `dst`'s region: LL words
 // [parity][src][token][stage_ld] (one 64-bit word per fp32 partial).
@@ -245,16 +248,22 @@ PeerTable make_table(const std::vector<int64_t>& stage, int world) {
   return t;
 }
 
+// CTAs of `kern` (kGemvThreads threads, `smem` bytes of dynamic shared
+// memory) that fit on the GPU at once (cached per kernel and size).
 template <typename Kern>
-void ensure_coresident(Kern kern, int grid, size_t smem, const char* what) {
+int resident_capacity(Kern kern, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, size_t>, int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(reinterpret_cast<const void*>(kern), smem);
+  const auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
   KVS_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-  int per_sm = 0;
+  int per_sm = 0, dev = 0, sms = 0;
   KVS_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGemvThreads, smem));
-  int dev = 0, sms = 0;
   KVS_CUDA_CHECK(cudaGetDevice(&dev));
   KVS_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  KVS_CHECK_ARG(int64_t(per_sm) * sms >= grid,
-                std::string(what) + ": the grid does not fit on the GPU at once (peer waits need co-resident CTAs)");
+  return cache[key] = per_sm * sms;
 }
 
 void check_gemv_args(const torch::Tensor& x, const torch::Tensor& w, int& M, int& K, int& N) {
@@ -285,14 +294,6 @@ void gemv_allreduce_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, std:
   KVS_CHECK_ARG(N % kGemvRowsPerCta == 0 && N <= stage_ld && stage_ld % 2 == 0,
                 "gemv_allreduce: N must be a multiple of 16 within the staging width");
   KVS_CHECK_ARG(rank >= 0 && rank < world && site >= 0 && site < num_sites, "gemv_allreduce: rank/site");
-  // fewest 16-row chunks per CTA that keep the whole grid resident (one wave:
-  // 2 CTAs of 256 threads per SM at this kernel's register count)
-  int chunks = 1;
-  while (chunks < kMaxChunks && N / (kGemvRowsPerCta * chunks) > 2 * kNumSMs &&
-         N % (kGemvRowsPerCta * chunks * 2) == 0)
-    chunks *= 2;
-  KVS_CHECK_ARG(N % (kGemvRowsPerCta * chunks) == 0, "gemv_allreduce: N must split into whole chunks");
-  const int grid = N / (kGemvRowsPerCta * chunks);
   KVS_CHECK_ARG(epoch.is_cuda() && epoch.scalar_type() == at::kInt && status.is_cuda() &&
                     status.scalar_type() == at::kInt,
                 "gemv_allreduce: epoch / status int32 device tensors");
@@ -303,15 +304,17 @@ void gemv_allreduce_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, std:
   auto yp = reinterpret_cast<bf16*>(y.data_ptr());
   auto ep = reinterpret_cast<const int32_t*>(epoch.data_ptr());
   auto sp = reinterpret_cast<uint32_t*>(status.data_ptr());
+// The fewest 16-row chunks per CTA that keep the whole grid resident (the
+// peer polls need every CTA running): large K at M = 8 leaves one CTA per SM.
 #define KVS_GAR_CASE(MM)                                                                                        \
   case MM: {                                                                                                    \
-    static int checked_grid = 0;                                                                                \
-    static size_t checked_smem = 0;                                                                             \
-    if (grid > checked_grid || smem > checked_smem) {                                                           \
-      checked_grid = std::max(grid, checked_grid);                                                              \
-      checked_smem = std::max(smem, checked_smem);                                                              \
-      ensure_coresident(gemv_allreduce_kernel<MM>, checked_grid, checked_smem, "gemv_allreduce");              \
-    }                                                                                                           \
+    const int cap = resident_capacity(gemv_allreduce_kernel<MM>, smem);                                        \
+    int chunks = 1;                                                                                             \
+    while (chunks < kMaxChunks && N / (kGemvRowsPerCta * chunks) > cap && N % (kGemvRowsPerCta * chunks * 2) == 0) \
+      chunks *= 2;                                                                                              \
+    const int grid = N / (kGemvRowsPerCta * chunks);                                                            \
+    KVS_CHECK_ARG(N % (kGemvRowsPerCta * chunks) == 0 && grid <= cap,                                           \
+                  "gemv_allreduce: the grid does not fit on the GPU at once (peer waits need co-resident CTAs)"); \
     launch_pdl(gemv_allreduce_kernel<MM>, dim3(grid), dim3(kGemvThreads), smem, st, xp, x.stride(0), wp,          \
                w.stride(0), yp, y.stride(0), N, K, chunks, peers, int(rank), world, int(site), int(num_sites), ep, \
                stage_ld, uint64_t(timeout_ns), sp);                                                             \

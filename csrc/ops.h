@@ -95,7 +95,7 @@ void gemv_argmax_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch
                       int64_t num_sites, torch::Tensor epoch, int64_t timeout_ns, torch::Tensor status);
 void decode_epoch_bump(torch::Tensor epoch);
 void flash_prefill(torch::Tensor qkv, int64_t Hq, int64_t Hkv, double scale, torch::Tensor out, torch::Tensor err,
-                   int64_t kstages);
+                   int64_t kstages, int64_t poly);
 int64_t paged_decode_splits(int64_t batch, int64_t hkv, int64_t max_ctx);
 void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                             torch::Tensor block_tables, torch::Tensor ctx_lens, int64_t max_ctx, double scale,

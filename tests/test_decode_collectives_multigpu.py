@@ -70,6 +70,24 @@ def _worker(rank, world, port, q):
             full = torch.cat(allv, dim=1).float()
             out["tokens_ok"].append(bool(torch.equal(tok.long().cpu(), full.argmax(1).cpu())))
             dc.bump()
+        # a 70B-like down projection at M = 8: x takes 112 KB of shared memory,
+        # one CTA fits per SM, so each CTA must take several 16-row chunks
+        dc2 = create_decode_collectives(ctx, 8192, V, num_sites=2, device=torch.device("cuda", rank), timeout_s=5.0)
+        g = torch.Generator(device="cuda").manual_seed(7 + rank)
+        x = torch.randn(8, 7168, device="cuda", dtype=torch.bfloat16, generator=g)
+        w = (torch.randn(8192, 7168, device="cuda", dtype=torch.bfloat16, generator=g) * 0.02).to(torch.bfloat16)
+        y = dc2.gemv_allreduce(x, w, site=0).clone()
+        torch.cuda.synchronize()
+        assert int(dc2.status[0].item()) == 0
+        ref = x.float() @ w.float().T
+        dist.all_reduce(ref)
+        out["errs"].append(((y.float() - ref).norm() / ref.norm()).item())
+        gathered = [torch.empty_like(y) for _ in range(world)]
+        dist.all_gather(gathered, y)
+        out["same"].append(all(torch.equal(gathered[0], t) for t in gathered))
+        torch.cuda.synchronize()
+        dist.barrier(group=cpu)
+        dc2.close()
         # graph replay: capture one step (all-reduce, greedy, bump) and replay it
         x = torch.randn(1, K, device="cuda", dtype=torch.bfloat16)
         w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05

@@ -166,13 +166,13 @@ def _ref_causal(qkv, Hq, Hkv, D=128):
     return (s.softmax(-1) @ v).transpose(0, 1).reshape(T, Hq * D)
 
 
-@pytest.mark.parametrize("kstages", [2, 3])
+@pytest.mark.parametrize("kstages,poly", [(2, 0), (3, 0), (2, 0x100), (2, 0xFF)])
 @pytest.mark.parametrize("T,Hq,Hkv", [(128, 1, 1), (200, 4, 2), (1000, 8, 2), (2048, 32, 8)])
-def test_flash_prefill(T, Hq, Hkv, kstages):
+def test_flash_prefill(T, Hq, Hkv, kstages, poly):
     ops = _ops()
     torch.manual_seed(1)
     qkv = torch.randn(T, (Hq + 2 * Hkv) * 128, device="cuda", dtype=torch.bfloat16)
-    o = ops.flash_prefill(qkv, Hq, Hkv, kstages=kstages)
+    o = ops.flash_prefill(qkv, Hq, Hkv, kstages=kstages, poly=poly)
     ops.check_device_status()
     assert _rel_err(o, _ref_causal(qkv, Hq, Hkv)) < 2e-2
 
