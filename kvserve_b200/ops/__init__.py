@@ -206,17 +206,19 @@ def argmax(logits: torch.Tensor, index_offset: int = 0, out_val: Optional[torch.
 
 def flash_prefill(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int,
                   scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
-                  kstages: int = 0) -> torch.Tensor:
+                  kstages: int = 0, poly: int = 0) -> torch.Tensor:
     """Causal GQA attention over a fused (already rotated) QKV tensor, head_dim 128.
     ``kstages`` (2 or 3) sets the depth of the kernel's K-tile ring (0:
-    ``KVSERVE_FLASH_KSTAGES``, default 2)."""
+    ``KVSERVE_FLASH_KSTAGES``, default 2); ``poly`` picks which of every 8
+    exponential pairs run as a polynomial on the FMA pipes instead of the
+    MUFU (bit mask: 0x11 default, 0x55, 0xFF; 0x100 = none)."""
     d = 128
     if scale is None:
         scale = 1.0 / math.sqrt(d)
     if out is None:
         out = torch.empty((qkv.shape[0], num_q_heads * d), dtype=qkv.dtype, device=qkv.device)
     count_launches(1)
-    ext().flash_prefill(qkv, num_q_heads, num_kv_heads, scale, out, device_status(qkv.device), int(kstages))
+    ext().flash_prefill(qkv, num_q_heads, num_kv_heads, scale, out, device_status(qkv.device), int(kstages), int(poly))
     return out
 
 

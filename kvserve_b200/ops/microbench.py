@@ -156,9 +156,12 @@ def case_flash(a, pk):
         out = torch.empty(T, Hq * 128, device="cuda", dtype=torch.bfloat16)
         fl = 4 * T * T * 128 * Hq / 2
         r = {}
-        for ks in (2, 3):   # K-tile ring depth; 2 (the default) first
-            t = time_ms([lambda: flash_prefill(qkv, Hq, Hkv, out=out, kstages=ks)], max(3, a.iters // 2), a.once)
-            r[f"kstages{ks}"] = {"ms": round(t, 4), "tflops": round(fl / t / 1e9, 1),
+        # the default kernel first, then the K-ring and exponential-mix variants
+        for name, ks, pm in (("default", 0, 0), ("kstages3", 3, 0), ("poly_none", 2, 0x100),
+                             ("poly_55", 2, 0x55), ("poly_ff", 2, 0xFF)):
+            t = time_ms([lambda: flash_prefill(qkv, Hq, Hkv, out=out, kstages=ks, poly=pm)], max(3, a.iters // 2),
+                        a.once)
+            r[name] = {"ms": round(t, 4), "tflops": round(fl / t / 1e9, 1),
                             "frac_of_measured_bf16": round(fl / t / 1e9 / pk["bf16_tflops"], 3)}
             if a.once:
                 break
