@@ -136,16 +136,19 @@ def case_gemm(a, pk):
 
 def case_gemv(a, pk):
     res = {}
-    for N, K in [(6144, 4096), (4096, 4096), (28672, 4096), (4096, 14336), (128256, 4096)]:
+    # M = 1 on the 8B shapes; M = 1/4/8 on the 70B TP4 shapes a batched decode step runs
+    shapes = [(1, 6144, 4096), (1, 4096, 4096), (1, 28672, 4096), (1, 4096, 14336), (1, 128256, 4096)]
+    shapes += [(m, 14336, 8192) for m in (1, 4, 8)] + [(m, 8192, 7168) for m in (1, 8)]
+    for M, N, K in shapes:
         nb = N * K * 2
         ws = [torch.randn(N, K, device="cuda", dtype=torch.bfloat16) for _ in range(copies_for(nb))]
-        x = torch.randn(1, K, device="cuda", dtype=torch.bfloat16)
-        y = torch.empty(1, N, device="cuda", dtype=torch.bfloat16)
+        x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
         fns = [lambda w=w: gemv(x, w, y) for w in ws]
         t = time_ms(fns, a.iters * 4, a.once) if a.once else time_graph_ms(fns, a.iters * 4)
         gbs = nb / t / 1e6
-        res[f"gemv_{N}x{K}"] = {"ms": round(t, 4), "GBps": round(gbs, 1),
-                                "frac_of_measured_hbm": round(gbs / pk["hbm_gbs"], 3)}
+        res[f"gemv_M{M}_{N}x{K}"] = {"ms": round(t, 4), "GBps": round(gbs, 1),
+                                     "frac_of_measured_hbm": round(gbs / pk["hbm_gbs"], 3)}
     return res
 
 
@@ -179,8 +182,10 @@ def case_flash(a, pk):
 
 def case_decode(a, pk):
     res = {}
-    for B, ctx in [(1, 8192), (8, 8192), (32, 4096)]:
-        Hq, Hkv, D, bs = 32, 8, 128, 16
+    # Llama-3.1-8B (32 q / 8 KV heads) and Llama-3-70B at TP4 (16 q / 2 KV heads: 8 per KV head)
+    for B, ctx, Hq, Hkv in [(1, 8192, 32, 8), (8, 8192, 32, 8), (32, 4096, 32, 8), (1, 16384, 16, 2),
+                            (8, 16384, 16, 2)]:
+        D, bs = 128, 16
         nblk = B * ctx // bs
         kv_bytes = 2 * nblk * bs * Hkv * D * 2
         sets = []
@@ -195,7 +200,7 @@ def case_decode(a, pk):
         fns = [lambda s=s: paged_decode_attention(q, s[0], s[1], table, lens, ctx, out=out) for s in sets]
         t = time_ms(fns, a.iters * 4, a.once) if a.once else time_graph_ms(fns, a.iters * 4)
         gbs = kv_bytes / t / 1e6
-        res[f"paged_decode_B{B}_ctx{ctx}"] = {"ms": round(t, 4), "GBps": round(gbs, 1),
+        res[f"paged_decode_B{B}_ctx{ctx}_q{Hq}_kv{Hkv}"] = {"ms": round(t, 4), "GBps": round(gbs, 1),
                                               "frac_of_measured_hbm": round(gbs / pk["hbm_gbs"], 3)}
     return res
 
