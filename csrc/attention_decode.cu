@@ -35,21 +35,26 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tenso
   KVS_CHECK_ARG(block_tables.scalar_type() == at::kInt && ctx_lens.scalar_type() == at::kInt, "int32 tables");
   if (B == 0) return;
   const int G = Hq / Hkv;
-  // TMA-fed kernel: head_dim 128, 16-token blocks stored contiguously.
+  // TMA-fed kernel: head_dim 128, 16-token blocks stored contiguously, 1, 2,
+  // 4 or 8 query heads per KV head.
   const bool tma_ok = D == 128 && bsz == kTmaBlk && k_cache.stride(2) == D && k_cache.stride(1) == Hkv * D &&
                       k_cache.stride(0) == int64_t(bsz) * Hkv * D && v_cache.strides() == k_cache.strides() &&
-                      (G == 1 || G == 2 || G == 4) &&
+                      (G == 1 || G == 2 || G == 4 || G == 8) &&
                       (reinterpret_cast<uintptr_t>(k_cache.data_ptr()) & 15) == 0 &&
                       (reinterpret_cast<uintptr_t>(v_cache.data_ptr()) & 15) == 0;
+  // 8 query heads per KV head: two CTAs of 4 query heads per KV head (the
+  // TMA kernel keeps 4 heads' queries and accumulators in registers)
+  const int kv_shift = (tma_ok && G == 8) ? 1 : 0;
+  const int Gl = G >> kv_shift, Hl = Hkv << kv_shift;
   // it holds two CTAs per SM: one wave of 2 x 148 CTAs
-  if (tma_ok) splits = std::max<int64_t>(1, std::min<int64_t>(splits, (2 * kNumSMs) / std::max(1, B * Hkv)));
+  if (tma_ok) splits = std::max<int64_t>(1, std::min<int64_t>(splits, (2 * kNumSMs) / std::max(1, B * Hl)));
   const int chunk = int(std::max<int64_t>(16, ((max_ctx + splits - 1) / splits + 15) / 16 * 16));
   splits = (max_ctx + chunk - 1) / chunk;
   if (splits < 1) splits = 1;
   if (splits > 1)
     KVS_CHECK_ARG(part_o.numel() >= int64_t(B) * Hq * splits * D && part_ml.numel() >= int64_t(B) * Hq * splits * 2,
                   "paged decode: split scratch too small");
-  dim3 grid(int(splits), Hkv, B);
+  dim3 grid(int(splits), tma_ok ? Hl : Hkv, B);
   const float sl2 = float(scale) * 1.4426950408889634f;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   float* po0 = splits > 1 ? part_o.data_ptr<float>() : nullptr;
@@ -75,10 +80,10 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tenso
     paged_decode_tma_kernel<GG><<<grid, kTmaThreads, kTmaSmem, st>>>(tk, tv, qp, q.stride(0), btp,             \
                                                                      block_tables.stride(0), clp, Hq,          \
                                                                      int(splits), chunk, sl2, po0, pml0, op,   \
-                                                                     out.stride(0), nullptr);                  \
+                                                                     out.stride(0), nullptr, kv_shift);        \
     break;                                                                                                     \
   }
-    switch (G) {
+    switch (Gl) {
       KVS_TMA_CASE(1)
       KVS_TMA_CASE(2)
       KVS_TMA_CASE(4)

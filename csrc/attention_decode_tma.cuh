@@ -1,7 +1,9 @@
 // TMA-fed paged decode attention for head_dim 128 and 16-token paged blocks
 // stored contiguously ([num_blocks, 16, Hkv, 128]).
 //
-// One CTA = one (split, kv head, sequence), 160 threads:
+// One CTA = one (split, kv head, sequence), 160 threads (with kv_shift = 1
+// a "kv head" index covers half of a real KV head's G query heads: 8 query
+// heads per KV head run as two CTAs of 4, each streaming the KV once):
 //   warp 4      producer: one 2-D TMA load per paged block for K and one for V
 //               (16 rows x 256 bytes each) into an 8-stage shared-memory ring;
 //   warps 0..3  consumers: thread (t, q) = token slot t (0..15) of every block
@@ -31,7 +33,7 @@ __global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(
     int64_t q_tok_stride, const int32_t* __restrict__ block_tables, int64_t bt_stride,
     const int32_t* __restrict__ ctx_lens, int Hq, int splits, int chunk, float scale_log2,
     float* __restrict__ part_o, float* __restrict__ part_ml, bf16* __restrict__ out, int64_t out_tok_stride,
-    uint32_t* err) {
+    uint32_t* err, int kv_shift) {
   pdl_trigger();
   using namespace sm100;
   constexpr int D = 128;
@@ -71,8 +73,8 @@ __global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(
         if (!mbar_wait(&empty[s], ph ^ 1, err)) break;
         const int row = bt[blk_begin + i] * kTmaBlk;
         mbar_arrive_expect_tx(&full[s], 2 * kTmaTile);
-        tma_load_2d(sK + s * kTmaTile, &tmK, kvh * D, row, &full[s]);
-        tma_load_2d(sV + s * kTmaTile, &tmV, kvh * D, row, &full[s]);
+        tma_load_2d(sK + s * kTmaTile, &tmK, (kvh >> kv_shift) * D, row, &full[s]);
+        tma_load_2d(sV + s * kTmaTile, &tmV, (kvh >> kv_shift) * D, row, &full[s]);
         issued = i + 1;
       }
       // every issued copy lands before the CTA may exit

@@ -211,7 +211,7 @@ def flash_prefill(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int,
     ``kstages`` (2 or 3) sets the depth of the kernel's K-tile ring (0:
     ``KVSERVE_FLASH_KSTAGES``, default 2); ``poly`` picks which of every 8
     exponential pairs run as a polynomial on the FMA pipes instead of the
-    MUFU (bit mask: 0x11 default, 0x55, 0xFF; 0x100 = none)."""
+    MUFU (bit mask 0x11, 0x55 or 0xFF; 0x100 = none, the default)."""
     d = 128
     if scale is None:
         scale = 1.0 / math.sqrt(d)
