@@ -25,6 +25,16 @@ __device__ __forceinline__ void gemv_load_x8(const bf16* p, float (&f)[8]) {
   }
 }
 
+__device__ __forceinline__ void gemv_unpack8(const uint4& w, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 t = __bfloat1622float2(h[e]);
+    f[2 * e] = t.x;
+    f[2 * e + 1] = t.y;
+  }
+}
+
 __device__ __forceinline__ float gemv_dot8(const uint4& w, const float (&x)[8], float acc) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
 #pragma unroll
@@ -69,50 +79,32 @@ struct GemvWarp {
 #pragma unroll
       for (int m = 0; m < M; ++m) acc[r][m] = 0.f;
     int kv = lane;
-    auto load = [&](uint4 (&dst)[kGemvRows][U], int at) {
+    for (bool h = have; kv + 32 * (U - 1) < kvec; kv += 32 * U, h = false) {
+      if (!h) {
 #pragma unroll
-      for (int r = 0; r < kGemvRows; ++r)
+        for (int r = 0; r < kGemvRows; ++r)
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int row = min(row0 + r, N - 1);
-          dst[r][u] = __ldcs(reinterpret_cast<const uint4*>(w + int64_t(row) * ldw) + at + 32 * u);
-        }
-    };
-    auto compute = [&](const uint4 (&src)[kGemvRows][U], int at) {
+          for (int u = 0; u < U; ++u) {
+            const int row = min(row0 + r, N - 1);
+            wv[r][u] = __ldcs(reinterpret_cast<const uint4*>(w + int64_t(row) * ldw) + kv + 32 * u);
+          }
+      }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        const int k = (at + 32 * u) * 8;
+        const int k = (kv + 32 * u) * 8;
+        // each weight vector is converted once and reused for every token
+        float wf[kGemvRows][8];
+#pragma unroll
+        for (int r = 0; r < kGemvRows; ++r) gemv_unpack8(wv[r][u], wf[r]);
 #pragma unroll
         for (int m = 0; m < M; ++m) {
           float xf[8];
           gemv_load_x8(xs + m * K + k, xf);
 #pragma unroll
-          for (int r = 0; r < kGemvRows; ++r) acc[r][m] = gemv_dot8(src[r][u], xf, acc[r][m]);
-        }
-      }
-    };
-    if constexpr (M >= 4) {
-      // several tokens: the FMAs of a batch are long enough to matter, so
-      // the next batch's weight loads are issued before computing this one
-      // (two batches in flight per warp; x in shared memory caps a CTA of
-      // M = 8 at one per SM)
-      if (!have && kv + 32 * (U - 1) < kvec) load(wv, kv);
-      for (; kv + 32 * (U - 1) < kvec; kv += 32 * U) {
-        uint4 nx[kGemvRows][U];
-        const bool more = kv + 32 * U + 32 * (U - 1) < kvec;
-        if (more) load(nx, kv + 32 * U);
-        compute(wv, kv);
-        if (more) {
-#pragma unroll
           for (int r = 0; r < kGemvRows; ++r)
 #pragma unroll
-            for (int u = 0; u < U; ++u) wv[r][u] = nx[r][u];
+            for (int e = 0; e < 8; ++e) acc[r][m] = fmaf(wf[r][e], xf[e], acc[r][m]);
         }
-      }
-    } else {
-      for (bool h = have; kv + 32 * (U - 1) < kvec; kv += 32 * U, h = false) {
-        if (!h) load(wv, kv);
-        compute(wv, kv);
       }
     }
     for (; kv < kvec; kv += 32) {
