@@ -7,6 +7,11 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "ops.h"
@@ -23,25 +28,48 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const bf16* __restrict__
                                                         const bf16* __restrict__ bias) {
   extern __shared__ uint4 xs_raw[];  // [M][K] bf16
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = (blockIdx.x * (kThreads / 32) + warp) * kGemvRows;
+  const int nblk = (N + kGemvRowsPerCta - 1) / kGemvRowsPerCta;
   pdl_trigger();
   GemvWarp<M> g;
-  g.prefetch(w, ldw, row0, N, K, lane);
+  g.prefetch(w, ldw, (blockIdx.x * (kThreads / 32) + warp) * kGemvRows, N, K, lane);
   pdl_wait();   // x is the previous kernel's output
   gemv_stage_x<M>(x, ldx, xs_raw, K);
   __syncthreads();
-  if (row0 >= N) return;
-  float acc[kGemvRows][M];
-  g.run(w, ldw, reinterpret_cast<const bf16*>(xs_raw), row0, N, K, lane, acc);
-  if (lane == 0) {
+  // a CTA takes 16-row blocks blockIdx.x, blockIdx.x + gridDim.x, ... so x is
+  // staged once per CTA (with several tokens the grid is one wave)
+  for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+    const int row0 = (blk * (kThreads / 32) + warp) * kGemvRows;
+    if (row0 < N) {
+      float acc[kGemvRows][M];
+      g.run(w, ldw, reinterpret_cast<const bf16*>(xs_raw), row0, N, K, lane, acc);
+      if (lane == 0) {
 #pragma unroll
-    for (int r = 0; r < kGemvRows; ++r) {
-      if (row0 + r >= N) break;
+        for (int r = 0; r < kGemvRows; ++r) {
+          if (row0 + r >= N) break;
 #pragma unroll
-      for (int m = 0; m < M; ++m)
-        y[int64_t(m) * ldy + row0 + r] = rn(acc[r][m] + (bias ? to_f32(bias[row0 + r]) : 0.f));
+          for (int m = 0; m < M; ++m)
+            y[int64_t(m) * ldy + row0 + r] = rn(acc[r][m] + (bias ? to_f32(bias[row0 + r]) : 0.f));
+        }
+      }
     }
+    g.have = false;
   }
+}
+
+// CTAs of a GEMV kernel resident at once with `smem` bytes of x (cached).
+template <typename Kern>
+int gemv_wave(Kern kern, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, size_t>, int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(reinterpret_cast<const void*>(kern), smem);
+  const auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int per_sm = 0, dev = 0, sms = 0;
+  KVS_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem));
+  KVS_CUDA_CHECK(cudaGetDevice(&dev));
+  KVS_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  return cache[key] = std::max(1, per_sm) * sms;
 }
 
 }  // namespace
@@ -74,8 +102,7 @@ void gemv_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, c10::optional<
                   "gemv: bias must be contiguous bf16 [N]");
     bp = reinterpret_cast<const bf16*>(bias->data_ptr());
   }
-  const int rows_per_cta = kGemvRowsPerCta;
-  const int grid = (N + rows_per_cta - 1) / rows_per_cta;
+  const int nblk = (N + kGemvRowsPerCta - 1) / kGemvRowsPerCta;
   const size_t smem = size_t(M) * K * 2;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   auto xp = reinterpret_cast<const bf16*>(x.data_ptr());
@@ -89,6 +116,9 @@ void gemv_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor y, c10::optional<
                                           200 * 1024));                                                    \
       set = true;                                                                                          \
     }                                                                                                      \
+    /* few tokens: one 16-row block per CTA; 4+ tokens: one wave, so each */                                \
+    /* CTA stages x (re-read from L2 per CTA) once for all its blocks */                                    \
+    const int grid = MM >= 4 ? std::min(nblk, gemv_wave(gemv_kernel<MM>, smem)) : nblk;                    \
     launch_pdl(gemv_kernel<MM>, dim3(grid), dim3(kThreads), smem, st, xp, x.stride(0), wp, w.stride(0), yp,     \
                y.stride(0), N, K, bp);                                                                      \
     break;                                                                                                 \
