@@ -299,26 +299,34 @@ __global__ void __launch_bounds__(v3::kThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(tS + lane_off + c * 32, r[c]);
       tmem_wait_ld();
-      float mx = -INFINITY;
-      if (!diag) {
+      if (diag) {
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) mx = v3::max3(mx, __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]));
-      } else {
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
+          for (int e = 0; e < 32; ++e)
             if (c * 32 + e > row) r[c][e] = __float_as_uint(-INFINITY);
-            mx = fmaxf(mx, __uint_as_float(r[c][e]));
-          }
       }
+      // row max as 8 independent 3-input-max chains (a single chain of 64
+      // dependent max3 put its latency on every tile's critical path)
+      float mxa[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mxa[i] = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int e = 0; e < 32; e += 2)
+          mxa[c * 2 + (e >> 4)] = v3::max3(mxa[c * 2 + (e >> 4)], __uint_as_float(r[c][e]),
+                                           __uint_as_float(r[c][e + 1]));
+      const float mx = fmaxf(v3::max3(mxa[0], mxa[1], mxa[2]), v3::max3(mxa[3], mxa[4], v3::max3(mxa[5], mxa[6],
+                                                                                                 mxa[7])));
       const float mxs = mx * sl2;
       const bool rescale = mxs > m_ref + kRescaleThreshold;
       const float m_use = rescale ? mxs : m_ref;
       const float neg_m = -m_use;
-      float s0 = 0.f, s1 = 0.f;
+      // row sum: one packed accumulator pair per 32-key chunk (independent chains)
+      float sa[4][2];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) sa[c][0] = sa[c][1] = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
@@ -338,13 +346,15 @@ __global__ void __launch_bounds__(v3::kThreads, 1)
             p0 = v3::ex2_mufu(x0);
             p1 = v3::ex2_mufu(x1);
           }
-          v3::add2(s0, s1, p0, p1);
+          v3::add2(sa[c][0], sa[c][1], p0, p1);
           pk[e] = pack_bf16x2(p0, p1);
         }
         // P chunk c (keys 32c .. 32c+31) -> columns [16c, 16c+16) of S; the
         // whole S row is already in registers.
         tmem_st16(tS + lane_off + c * 16, pk);
       }
+      const float s0 = (sa[0][0] + sa[1][0]) + (sa[2][0] + sa[3][0]);
+      const float s1 = (sa[0][1] + sa[1][1]) + (sa[2][1] + sa[3][1]);
       if (j > 0 && __any_sync(0xffffffffu, rescale)) {
         const float f = rescale ? v3::ex2_mufu(m_ref - m_use) : 1.0f;
 #pragma unroll 1
