@@ -1000,7 +1000,7 @@ void kv_encode_layer(torch::Tensor k, torch::Tensor v, std::vector<int64_t> geom
     const CUtensorMap tm = make_tmap_2d_bf16(hs_table->data_ptr(), 128, uint64_t(hs_table->size(0)), 256, 64, 128,
                                              true);
     const int64_t units = int64_t(part_mask == 3 ? 2 : 1) * g.H * ((g.T + 127) / 128);
-    const int wctas = int(std::max<int64_t>(1, std::min<int64_t>(units, kNumSMs)));
+    const int wctas = int(std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(units, kNumSMs), max_ctas)));
     kv_encode_ws_kernel<true><<<wctas, kWsThreads, kWsSmem, st>>>(tk, tv, tm, a, int(hs_row0));
     kv_encode_ws_kernel<false><<<wctas, kWsThreads, kWsSmem, st>>>(tk, tv, tm, a, int(hs_row0));
     KVS_CUDA_CHECK(cudaGetLastError());

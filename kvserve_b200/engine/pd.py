@@ -19,6 +19,7 @@ aligned to within the barrier skew and the max over ranks is meaningful.
 """
 from __future__ import annotations
 
+import os
 import time
 from dataclasses import dataclass, field
 from typing import Optional
@@ -72,7 +73,9 @@ class PDEngine:
         self.max_prompt, self.max_new, self.block_size = max_prompt, max_new_tokens, block_size
         self.use_graphs = use_graphs
         self.ingest_timeout_ns = int(ingest_timeout_s * 1e9)
-        self.encode_ctas = encode_ctas
+        # CTAs of each layer's encode launches (KVSERVE_ENCODE_CTAS overrides):
+        # fewer leave more SMs to the prefill's own kernels beside them
+        self.encode_ctas = int(os.environ.get("KVSERVE_ENCODE_CTAS", encode_ctas))
         self.rate_bytes_per_ns = link_gbps / 8.0 if link_gbps else 0.0
         self.model = LlamaShard(cfg, ctx.tp_rank, ctx.tp_size, self.device, seed, ctx.tp_group,
                                 max_position=max_prompt + max_new_tokens + block_size)
