@@ -9,10 +9,12 @@
 // the same M is the B operand of (X M^T) and the A operand of (M X^T).
 //
 // Work unit = (part, head slot j, 128-token tile).  One persistent,
-// warp-specialised CTA per SM (320 threads):
+// warp-specialised CTA per SM (320 threads) takes a contiguous range of
+// units (consecutive units mostly share a head):
 //   warp 0     TMA producer: per unit the X tile (two 64-column SW128 boxes
 //              of the K or V rows of head order[j]; rows past T are zero
-//              filled) and M of that head into a 2-stage ring;
+//              filled) into a 3-stage ring, and M of the head into one of
+//              two M buffers only when the head changes;
 //   warp 1     MMA issuer: eight tcgen05.mma (K = 16 each) into one of four
 //              128-column TMEM accumulators (all 512 columns);
 //   warps 2-9  two epilogue warpgroups taking alternate units, so two
@@ -37,10 +39,11 @@ namespace {
 constexpr int kWsEpiGroups = 2;                        // epilogue warpgroups (alternate units)
 constexpr int kWsAcc = 4;                              // 128-column TMEM accumulators
 constexpr int kWsThreads = 64 + 128 * kWsEpiGroups;
-constexpr int kWsStages = 2;
-constexpr int kWsStage = 2 * kMmaTile;                 // X tile + M (64 KB)
+constexpr int kWsStages = 3;                           // ring of X tiles (32 KB each)
+constexpr int kWsStage = kMmaTile;
+constexpr int kWsOffM = kWsStages * kWsStage;          // two 32 KB buffers of a head's signed transform M
 constexpr int kEncMaxHD = 8 * 128;
-constexpr int kWsOffPar = kWsStages * kWsStage;        // K params: min[H*D], inv[H*D] fp32
+constexpr int kWsOffPar = kWsOffM + 2 * kMmaTile;      // K params: min[H*D], inv[H*D] fp32
 constexpr int kWsStgWarp = 32 * (128 + 16);            // per epilogue warp: 32 packed rows of <= 128 bytes,
                                                        // each padded by 16 bytes (spreads the bank groups)
 constexpr int kWsOffStg = kWsOffPar + 2 * kEncMaxHD * 4;
@@ -126,7 +129,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   float* kinv = kmin + kEncMaxHD;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kWsOffBar);
   uint64_t* empty = full + kWsStages;
-  uint64_t* tfull = empty + kWsStages;   // [0, kWsAcc): accumulator ready; [kWsAcc]: abort drain
+  uint64_t* mfull = empty + kWsStages;   // [2] M buffer loaded
+  uint64_t* mempty = mfull + 2;          // [2] M buffer free (its MMAs retired)
+  uint64_t* tfull = mempty + 2;          // [0, kWsAcc): accumulator ready; [kWsAcc]: abort drain
   uint64_t* tempty = tfull + kWsAcc + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + kWsAcc);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -135,6 +140,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   const int HD = g.H * D;
   const int ntile = (g.T + 127) / 128;
   const int64_t total = int64_t(a.part_mask == 3 ? 2 : 1) * g.H * ntile;
+  // a contiguous range of units per CTA: consecutive units mostly share a
+  // head, so its transform matrix is loaded once for several tiles
+  const int64_t u_begin = total * blockIdx.x / gridDim.x, u_end = total * (blockIdx.x + 1) / gridDim.x;
   if (!kStats) {
     // K parameters of every slot (block 0 also writes them and the section
     // headers into the frame)
@@ -166,6 +174,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&mfull[b], 1);
+      mbar_init(&mempty[b], 1);
+    }
     for (int b = 0; b < kWsAcc; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 128);
@@ -184,41 +196,61 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
+      int stage = 0, prev_h = -1;
+      uint32_t phase = 0, mloads = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
-      for (int64_t u = blockIdx.x; u < total; u += gridDim.x) {
+      for (int64_t u = u_begin; u < u_end; ++u) {
         const EncUnit e = enc_unit(u, g.H, ntile, a.part_mask);
-        if (!mbar_wait(&empty[stage], phase ^ 1, a.counter + 1)) { ok = false; break; }
         const int h = a.order[e.j];
+        if (h != prev_h) {   // the head's signed transform into the next M buffer
+          const int mb = int(mloads & 1u);
+          if (!mbar_wait(&mempty[mb], ((mloads >> 1) & 1u) ^ 1u, a.counter + 1)) { ok = false; break; }
+          uint8_t* mdst = smem + kWsOffM + mb * kMmaTile;
+          mbar_arrive_expect_tx(&mfull[mb], kMmaTile);
+          tma_load_2d(mdst, &tmM, 0, (m_head0 + h) * 128, &mfull[mb]);
+          tma_load_2d(mdst + kMmaPanel, &tmM, 64, (m_head0 + h) * 128, &mfull[mb]);
+          ++mloads;
+          prev_h = h;
+        }
+        if (!mbar_wait(&empty[stage], phase ^ 1, a.counter + 1)) { ok = false; break; }
         uint8_t* st = smem + stage * kWsStage;
         mbar_arrive_expect_tx(&full[stage], kWsStage);
         const CUtensorMap* tx = e.part ? &tmV : &tmK;
         tma_load_2d(st, tx, h * D, e.tile * 128, &full[stage]);
         tma_load_2d(st + kMmaPanel, tx, h * D + 64, e.tile * 128, &full[stage]);
-        tma_load_2d(st + kMmaTile, &tmM, 0, (m_head0 + h) * 128, &full[stage]);
-        tma_load_2d(st + kMmaTile + kMmaPanel, &tmM, 64, (m_head0 + h) * 128, &full[stage]);
         issued_mask |= 1u << stage;
         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
         if (++stage == kWsStages) { stage = 0; phase ^= 1; }
       }
-      if (!ok)  // every issued copy lands before the CTA may exit
+      if (!ok) {  // every issued copy lands before the CTA may exit
         for (int i = 0; i < kWsStages; ++i)
           if (issued_mask & (1u << i)) mbar_wait(&full[i], (issued_parity >> i) & 1u, nullptr);
+        for (uint32_t k = (mloads > 2 ? mloads - 2 : 0); k < mloads; ++k)
+          mbar_wait(&mfull[k & 1u], (k >> 1) & 1u, nullptr);
+      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16(128, 128, false);
-      int stage = 0, acc = 0;
-      uint32_t phase = 0, acc_phase = 0;
+      int stage = 0, acc = 0, prev_h = -1, mb = 0;
+      uint32_t phase = 0, acc_phase = 0, mloads = 0;
       bool ok = true;
-      for (int64_t u = blockIdx.x; u < total; u += gridDim.x) {
+      for (int64_t u = u_begin; u < u_end; ++u) {
         const EncUnit e = enc_unit(u, g.H, ntile, a.part_mask);
+        const int h = a.order[e.j];
+        if (h != prev_h) {
+          // the previous head's M buffer is free once its MMAs retire
+          if (prev_h >= 0) umma_commit(&mempty[mb]);
+          mb = int(mloads & 1u);
+          if (!mbar_wait(&mfull[mb], (mloads >> 1) & 1u, a.counter + 1)) { ok = false; break; }
+          ++mloads;
+          prev_h = h;
+        }
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, a.counter + 1)) { ok = false; break; }
         if (!mbar_wait(&full[stage], phase, a.counter + 1)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t x_s = smem_u32(smem + stage * kWsStage), m_s = x_s + kMmaTile;
+        const uint32_t x_s = smem_u32(smem + stage * kWsStage), m_s = smem_u32(smem + kWsOffM + mb * kMmaTile);
         // statistics of K: M X^T (lane = channel); everything else X M^T (lane = token)
         const bool chan = kStats && e.part == 0;
         const uint32_t a_s = chan ? m_s : x_s, b_s = chan ? x_s : m_s;
@@ -245,8 +277,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     const int grp = (warp - 2) >> 2;       // this warpgroup takes local units grp, grp + 2, ...
     const float scale = inv_sqrt_d<D>();
     int64_t n = grp;
-    for (int64_t u = blockIdx.x + grp * int64_t(gridDim.x); u < total;
-         u += kWsEpiGroups * int64_t(gridDim.x), n += kWsEpiGroups) {
+    for (int64_t u = u_begin + grp; u < u_end; u += kWsEpiGroups, n += kWsEpiGroups) {
       const EncUnit e = enc_unit(u, g.H, ntile, a.part_mask);
       const int acc = int(n % kWsAcc);
       const uint32_t acc_phase = uint32_t(n / kWsAcc) & 1u;
