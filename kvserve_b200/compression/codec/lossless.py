@@ -122,6 +122,8 @@ class LosslessCodec:
     def __init__(self, **kwargs: Any) -> None:
         self.chunk = int(kwargs.get("chunk_bytes", CHUNK))
         self.algorithm = kwargs.get("lc_algorithm", "TUPL8_1 BIT_8 RZE_2")
+        if self.algorithm == self.codec_id:   # the container name selects its one chain
+            self.algorithm = "TUPL8_1 BIT_8 RZE_2"
         if self.algorithm not in ("TUPL8_1 BIT_8 RZE_2",):
             raise ValueError(f"unsupported lossless chain {self.algorithm!r}")
 

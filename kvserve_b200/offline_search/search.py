@@ -7,10 +7,14 @@ constraint-aware Bayesian search for each accuracy tolerance.  Phase 3
 turns the measured profiles into a controller profile library.
 
     python -m kvserve_b200.offline_search.search --out results/ \
-        [--kv kv.pt] [--tolerances 1 3 5] [--budget 24]
+        [--kv kv.pt] [--tolerances 1 3 5] [--budget 24] [--accuracy model]
 
-Without ``--kv`` a synthetic sample with outlier key channels is used and
-the quality metric is the attention-fidelity proxy.
+Without ``--kv`` a synthetic sample with outlier key channels is used.  The
+quality metric is the attention-fidelity proxy on the sample, or with
+``--accuracy model`` the language-model evaluator of
+:mod:`kvserve_b200.offline_search.model_eval` (a local checkpoint given by
+``--hf-model``, else a random-init tiny Llama; its score in percent of the
+default cache, as a fraction).
 """
 from __future__ import annotations
 
@@ -37,7 +41,11 @@ def synthetic_kv(layers: int = 4, tokens: int = 512, heads: int = 8, dim: int = 
 
 
 def run(out_dir: str, kv: Optional[torch.Tensor] = None, tolerances=(1.0, 3.0, 5.0), budget: int = 24,
-        model_name: str = "synthetic", levels=(16, 12, 8, 6, 4), ratios=(0.0, 0.4, 0.8, 1.0)) -> dict:
+        model_name: str = "synthetic", levels=(16, 12, 8, 6, 4), ratios=(0.0, 0.4, 0.8, 1.0),
+        model_accuracy=None) -> dict:
+    """``model_accuracy``: optional ``profile -> percent`` (e.g.
+    :meth:`ModelAccuracyEvaluator.evaluate`) used instead of the
+    attention-fidelity proxy."""
     os.makedirs(out_dir, exist_ok=True)
     kv = synthetic_kv() if kv is None else kv
     L, _, B, S, H, D = kv.shape
@@ -55,8 +63,11 @@ def run(out_dir: str, kv: Optional[torch.Tensor] = None, tolerances=(1.0, 3.0, 5
 
     def accuracy(p):
         if p not in recon_cache:
-            _, rec = comp.evaluate(cfgs[p])
-            recon_cache[p] = fid.accuracy(rec)
+            if model_accuracy is not None:
+                recon_cache[p] = model_accuracy(cfgs[p]) / 100.0
+            else:
+                _, rec = comp.evaluate(cfgs[p])
+                recon_cache[p] = fid.accuracy(rec)
         return recon_cache[p]
 
     # accuracy tolerances are relative to the highest-precision point of the space
@@ -93,9 +104,21 @@ def main() -> None:
     ap.add_argument("--tolerances", type=float, nargs="+", default=[1.0, 3.0, 5.0])
     ap.add_argument("--budget", type=int, default=24)
     ap.add_argument("--model-name", default="synthetic")
+    ap.add_argument("--accuracy", choices=("fidelity", "model"), default="fidelity")
+    ap.add_argument("--hf-model", default=None, help="local checkpoint for --accuracy model")
     args = ap.parse_args()
     kv = torch.load(args.kv) if args.kv else None
-    out = run(args.out, kv, tuple(args.tolerances), args.budget, args.model_name)
+    model_accuracy = None
+    if args.accuracy == "model":
+        from .model_eval import ModelAccuracyEvaluator, synthetic_prompts, tiny_llama
+        if args.hf_model:
+            from transformers import AutoModelForCausalLM
+            lm = AutoModelForCausalLM.from_pretrained(args.hf_model, torch_dtype=torch.float32).eval()
+        else:
+            lm = tiny_llama()
+        ev = ModelAccuracyEvaluator(lm, synthetic_prompts(4, 256, lm.config.vocab_size))
+        model_accuracy = ev.evaluate
+    out = run(args.out, kv, tuple(args.tolerances), args.budget, args.model_name, model_accuracy=model_accuracy)
     print(json.dumps(out["results"], indent=2))
 
 

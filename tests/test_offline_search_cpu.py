@@ -87,3 +87,38 @@ def test_kivi_and_cachegen_style_baselines_round_trip():
             errs[(per_channel, bits)] = float(((y.float() - x.float()) ** 2).mean())
     for pc in (True, False):
         assert errs[(pc, 4)] < 0.01 < errs[(pc, 2)] < 0.25
+
+
+def _profile(k_levels, v_levels, enabled=True):
+    with open("configs/compression/hadamard_k4v2_bitpack.json") as f:
+        p = json.load(f)
+    q = p["quantizer_config"]
+    q["high_key_max_value"] = q["low_key_max_value"] = k_levels
+    q["high_value_max_value"] = q["low_value_max_value"] = v_levels
+    p["codec_config"]["bitpack_bits"] = max((k_levels - 1).bit_length(), (v_levels - 1).bit_length())
+    p["enabled"] = enabled
+    return p
+
+
+def test_model_accuracy_evaluator_scores_profiles_through_a_language_model():
+    """The reference's accuracy evaluator shape: the same model with its
+    default cache and with the profile's restored prefill KV, scores
+    normalised to the default (100 = unchanged)."""
+    from kvserve_b200.offline_search.model_eval import ModelAccuracyEvaluator, synthetic_prompts, tiny_llama
+    lm = tiny_llama(layers=2, hidden=128, heads=2, kv_heads=1, vocab=256)
+    ev = ModelAccuracyEvaluator(lm, synthetic_prompts(2, 96, 256), new_tokens=8)
+    assert ev.evaluate(_profile(16, 16, enabled=False)) == 100.0
+    hi = ev.evaluate(_profile(254, 254))
+    lo = ev.evaluate(_profile(4, 4))
+    assert 0.0 <= lo <= hi <= 100.0 and hi >= 95.0
+    assert ev.last["compression_ratio"] > 1.5
+
+
+def test_search_runs_on_the_model_evaluator(tmp_path):
+    from kvserve_b200.offline_search.model_eval import ModelAccuracyEvaluator, synthetic_prompts, tiny_llama
+    lm = tiny_llama(layers=2, hidden=128, heads=2, kv_heads=1, vocab=256)
+    ev = ModelAccuracyEvaluator(lm, synthetic_prompts(1, 64, 256), new_tokens=4)
+    kv = synthetic_kv(layers=2, tokens=64, heads=1, dim=64)
+    out = run(str(tmp_path), kv, tolerances=(50.0,), budget=4, levels=(16, 4), ratios=(0.0,),
+              model_accuracy=ev.evaluate)
+    assert 0.0 <= out["results"]["baseline"]["accuracy"] <= 1.0
