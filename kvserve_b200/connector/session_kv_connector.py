@@ -1,0 +1,503 @@
+"""vLLM V1 KV connector over the chunked compression session: the decode
+engine pulls the prompt KV chunk by chunk, the prefill engine encodes each
+pulled chunk straight into the decode GPU's receive slot (role of the
+in-tree MooncakeConnector, kvsfuse-vllm0.30.0/mooncake/mooncake_connector.py:
+615-788 connector, 790-1087 scheduler side, 1090-3957 worker side).
+
+Load it into vLLM with::
+
+    KVTransferConfig(kv_connector="SessionKVConnector",
+                     kv_connector_module_path="kvserve_b200.connector.session_kv_connector",
+                     kv_role="kv_producer" | "kv_consumer", kv_ip=<prefill host>,
+                     kv_connector_extra_config={"session_port": 26100, "num_slots": 4,
+                                                "compression": {...runtime keys...}})
+
+The ``compression`` object uses the runtime's keys
+(``enable-compression-pipeline``, ``pipeline``, ``logical_blocks_per_chunk``,
+the level keys, ...); both engines must use the same one.
+
+Router contract (``kv_transfer_params``), the same shape as vLLM's own
+pull-based connectors:
+
+* prefill request: ``{"do_remote_decode": True, "transfer_id": T}``; the
+  prefill engine's output carries ``{"do_remote_prefill": True,
+  "transfer_id": T, "remote_host": h, "remote_port": p, "remote_tp_size": n}``;
+* decode request: that dict unchanged.
+
+Flow:
+
+* prefill scheduler: ``request_finished`` keeps the blocks of a finished
+  (length-capped) remote-decode request (``delay_free_blocks``) and queues a
+  send for the worker; the next step's metadata registers it with the
+  worker's :class:`~kvserve_b200.session.service.ProducerService`;
+* decode scheduler: claims ``prompt - computed`` tokens as an asynchronous
+  load, records the request's unhashed (new) blocks after allocation, and
+  the next step's metadata opens a session;
+* workers: each runs its session service on a thread of its own (ZeroMQ
+  sockets stay in that thread); the prefill side's encode job is
+  :class:`~kvserve_b200.session.gpu_jobs.RuntimeEncodeJob` over the
+  compression runtime bound to vLLM's paged cache, the decode side's
+  :class:`~kvserve_b200.session.gpu_jobs.RuntimeDecodeJob` decodes each
+  chunk from its CUDA-IPC receive arena into the request's blocks;
+* ``get_finished`` reports finished sends (the prefill engine frees the
+  blocks) and finished loads (the decode engine schedules the request);
+  a failed load reports its blocks through ``get_block_ids_with_load_errors``
+  so vLLM recomputes them.
+
+A decode engine that already holds a block-aligned prefix (prefix caching)
+pulls only the suffix: the producer sends its last blocks and counts
+tokens from the suffix start.  Each decode TP rank pulls from the prefill
+rank of the same TP index (``session_port + tp_rank``); equal TP sizes.
+Finished sessions append a JSONL row to ``KVSERVE_SESSION_STATS_PATH``.
+"""
+from __future__ import annotations
+
+import json
+import logging
+import os
+import queue
+import re
+import threading
+import time
+from dataclasses import dataclass, field
+from typing import Any, Callable, Optional
+
+import torch
+
+try:  # vLLM is only needed when the connector is used inside vLLM
+    from vllm.distributed.kv_transfer.kv_connector.v1.base import (KVConnectorBase_V1, KVConnectorMetadata,
+                                                                   KVConnectorRole)
+except Exception:  # pragma: no cover - vLLM missing
+    class KVConnectorBase_V1:  # type: ignore[no-redef]
+        def __init__(self, *a, **k):
+            pass
+
+    class KVConnectorMetadata:  # type: ignore[no-redef]
+        pass
+
+    class KVConnectorRole:  # type: ignore[no-redef]
+        SCHEDULER = 0
+        WORKER = 1
+
+log = logging.getLogger("kvserve_b200.session_connector")
+
+DEFAULT_SESSION_PORT = 26100
+
+
+@dataclass
+class SendReq:
+    request_id: str
+    transfer_id: str
+    block_ids: list
+    num_tokens: int
+
+
+@dataclass
+class RecvReq:
+    request_id: str
+    transfer_id: str
+    host: str
+    port: int
+    block_ids: list
+    num_tokens: int
+
+
+@dataclass
+class SessionConnectorMetadata(KVConnectorMetadata):
+    sends: list = field(default_factory=list)     # prompt KV complete after this step's forward
+    recvs: list = field(default_factory=list)
+    cancels: list = field(default_factory=list)   # registered sends whose request freed its blocks
+
+
+def layer_index(name: str, fallback: int) -> int:
+    """The layer number in a vLLM attention-layer name
+    (``model.layers.7.self_attn.attn`` -> 7)."""
+    nums = re.findall(r"\.(\d+)\.", f".{name}.")
+    return int(nums[-1]) if nums else fallback
+
+
+def kv_pair(t: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(K, V) views ``[blocks, block_size, H, D]`` of one layer's paged cache
+    in either vLLM layout (``[2, blocks, ...]`` or ``[blocks, 2, ...]``)."""
+    if t.dim() != 5:
+        raise ValueError(f"expected a 5-D paged KV cache, got {tuple(t.shape)}")
+    if t.shape[0] == 2:
+        return t[0], t[1]
+    if t.shape[1] == 2:
+        return t[:, 0], t[:, 1]
+    raise ValueError(f"cannot find the K/V axis of a cache of shape {tuple(t.shape)}")
+
+
+def write_session_stats(row: dict) -> None:
+    path = os.environ.get("KVSERVE_SESSION_STATS_PATH")
+    if not path:
+        return
+    try:
+        with open(path, "a") as f:
+            f.write(json.dumps(dict(row, wall_time=time.time()), sort_keys=True) + "\n")
+    except OSError as exc:
+        log.warning("cannot write session stats: %s", exc)
+
+
+class ServiceThread(threading.Thread):
+    """Owns one session service: builds it on its own thread (ZeroMQ sockets
+    are single-threaded), runs queued commands against it and polls it."""
+
+    def __init__(self, make_service: Callable[[], Any], device: Optional[torch.device] = None,
+                 after_poll: Optional[Callable[[Any], None]] = None, poll_ms: int = 2):
+        super().__init__(daemon=True, name="kvserve-session")
+        self._make, self._device, self._after = make_service, device, after_poll
+        self._poll_ms = poll_ms
+        self._cmds: "queue.SimpleQueue" = queue.SimpleQueue()
+        self._halt = threading.Event()
+        self._ready = threading.Event()
+        self.error: Optional[BaseException] = None
+        self.service = None
+
+    def submit(self, fn: Callable[[Any], None]) -> None:
+        self._cmds.put(fn)
+
+    def wait_ready(self, timeout: float = 60.0) -> None:
+        if not self._ready.wait(timeout):
+            raise TimeoutError("the session service did not start")
+        if self.error is not None:
+            raise RuntimeError(f"the session service failed to start: {self.error}")
+
+    def run(self) -> None:
+        try:
+            if self._device is not None and self._device.type == "cuda":
+                torch.cuda.set_device(self._device)
+            self.service = self._make()
+        except BaseException as exc:  # noqa: BLE001 - reported through wait_ready
+            self.error = exc
+            self._ready.set()
+            return
+        self._ready.set()
+        while not self._halt.is_set():
+            try:
+                while True:
+                    try:
+                        fn = self._cmds.get_nowait()
+                    except queue.Empty:
+                        break
+                    fn(self.service)
+                self.service.poll(self._poll_ms)
+                if self._after is not None:
+                    self._after(self.service)
+            except BaseException as exc:  # noqa: BLE001 - a broken service ends the thread, loudly
+                log.exception("session service failed")
+                self.error = exc
+                break
+        try:
+            self.service.close()
+        except Exception:  # noqa: BLE001
+            pass
+
+    def stop(self, timeout: float = 5.0) -> None:
+        self._halt.set()
+        if self.is_alive():
+            self.join(timeout)
+
+
+class SessionKVConnector(KVConnectorBase_V1):
+    def __init__(self, vllm_config, role, kv_cache_config=None):
+        super().__init__(vllm_config, role, kv_cache_config)
+        cfg = vllm_config.kv_transfer_config
+        extra = dict(cfg.kv_connector_extra_config or {})
+        self.is_producer = cfg.is_kv_producer
+        self._block_size = vllm_config.cache_config.block_size
+        self._host = str(extra.get("session_host") or cfg.kv_ip or "127.0.0.1")
+        self._port = int(extra.get("session_port", DEFAULT_SESSION_PORT))
+        self._num_slots = int(extra.get("num_slots", 4))
+        self._open_timeout_s = float(extra.get("open_timeout_s", 120.0))
+        self._session_timeout_s = float(extra.get("session_timeout_s", 120.0))
+        self._extra = extra
+        self._tp_size = int(getattr(vllm_config.parallel_config, "tensor_parallel_size", 1) or 1)
+        self._tp_rank = 0
+        # scheduler state
+        self._pending_sends: list[SendReq] = []
+        self._pending_recvs: list[RecvReq] = []
+        # worker state
+        self._lock = threading.Lock()
+        self._send_rid: dict[str, str] = {}          # transfer id -> prefill request id
+        self._recv: dict[str, RecvReq] = {}          # transfer id -> load
+        self._done_sending: set[str] = set()
+        self._done_recving: set[str] = set()
+        self._finished_seen: set[str] = set()
+        self._load_errors: set[int] = set()
+        self._thread: Optional[ServiceThread] = None
+        self._closers: list[Callable[[], None]] = []
+        self._per_chunk = 1
+        self._device: Optional[torch.device] = None
+        self._sends_this_step: list[SendReq] = []
+        # scheduler: remote-decode requests -> (transfer id, prompt length,
+        # blocks so far); transfer ids whose send was registered
+        self._remote_decode: dict[str, tuple[str, int, list]] = {}
+        self._registered: set[str] = set()
+        self._pending_cancels: list[str] = []
+        if role == KVConnectorRole.WORKER:
+            try:
+                from vllm.distributed.parallel_state import get_tensor_model_parallel_rank
+                self._tp_rank = get_tensor_model_parallel_rank()
+            except Exception:  # noqa: BLE001 - no TP group (tests)
+                self._tp_rank = 0
+
+    # ------------------------------------------------------------ helpers
+    def runtime_config(self):
+        from ..compression.runtime import CompressionConfig
+        comp = self._extra.get("compression")
+        if not isinstance(comp, dict):
+            raise ValueError("SessionKVConnector needs kv_connector_extra_config['compression'] "
+                             "with the runtime's keys")
+        cfg = CompressionConfig.from_extra_config({"compression": comp})
+        if not cfg.enabled:
+            raise ValueError("SessionKVConnector runs the compression runtime; set enable-compression-pipeline")
+        return cfg
+
+    def _build_runtime(self, kv_caches: dict, execution: str):
+        from ..compression.runtime import CacheSpec, build_memory_plan, create_runtime
+        cfg = self.runtime_config()
+        specs, pairs = {}, {}
+        for i, (name, t) in enumerate(kv_caches.items()):
+            k, v = kv_pair(t)
+            specs[name] = CacheSpec(layer_index(name, i), k.shape[1], k.shape[2], k.shape[3], k.dtype)
+            pairs[name] = (k, v)
+        dev = next(iter(kv_caches.values())).device
+        plan = build_memory_plan(cfg, specs, tp_size=self._tp_size, tp_rank=self._tp_rank, device=dev)
+        rt = create_runtime(plan, "NHD", 1, dev, execution=execution)
+        rt.bind_kv_caches(pairs)
+        return rt, cfg
+
+    # ------------------------------------------------------------ worker
+    def register_kv_caches(self, kv_caches: dict) -> None:
+        from ..session.service import ConsumerService, ProducerService
+        caches = {n: t for n, t in kv_caches.items() if isinstance(t, torch.Tensor) and t.numel() > 0}
+        if not caches:
+            raise ValueError("no paged KV caches to register")
+        dev = next(iter(caches.values())).device
+        self._device = dev
+        if self.is_producer:
+            job = self.make_encode_job(caches)
+            endpoint = f"tcp://*:{self._port + self._tp_rank}"
+            self._thread = ServiceThread(lambda: ProducerService(endpoint, job, self._open_timeout_s), dev,
+                                         self._collect_sends)
+        else:
+            job, slot_bytes, handle = self.make_decode_job(caches)
+            name = f"kvs-d{self._tp_rank}-{os.getpid()}"
+            self._thread = ServiceThread(
+                lambda: ConsumerService(name, self._num_slots, slot_bytes, job, self._on_recv_done,
+                                        self._session_timeout_s, arena_ipc_handle=handle), dev,
+                lambda svc: svc.finished.clear())
+        self._thread.start()
+        self._thread.wait_ready()
+
+    def make_encode_job(self, caches: dict):
+        """The producer's ``encode_job``: the compression runtime bound to
+        vLLM's paged cache, encoding each pulled chunk into the consumer's
+        IPC-mapped slot."""
+        from ..session.gpu_jobs import RuntimeEncodeJob
+        rt, cfg = self._build_runtime(caches, "encode")
+        self._per_chunk = cfg.logical_blocks_per_chunk
+        job = RuntimeEncodeJob(rt, self._block_size, cfg.logical_blocks_per_chunk)
+        self._closers.append(job.close)
+        return job
+
+    def make_decode_job(self, caches: dict):
+        """The consumer's ``decode_job`` plus its receive arena's slot size
+        and CUDA-IPC handle."""
+        from ..session.gpu_jobs import ReceiveArena, RuntimeDecodeJob, part_bytes
+        rt, cfg = self._build_runtime(caches, "decode")
+        self._per_chunk = cfg.logical_blocks_per_chunk
+        arena = ReceiveArena(self._num_slots, 2 * part_bytes(rt), rt.device)
+        self._closers.append(arena.close)
+        return RuntimeDecodeJob(rt, arena, self._block_size, cfg.logical_blocks_per_chunk), arena.slot_bytes, \
+            arena.handle
+
+    def start_load_kv(self, forward_context, **kwargs) -> None:
+        meta = self._get_connector_metadata()
+        if not isinstance(meta, SessionConnectorMetadata) or self._thread is None:
+            return
+        for tid in meta.cancels:
+            with self._lock:
+                self._send_rid.pop(tid, None)
+            self._thread.submit(lambda svc, tid=tid: svc.cancel(tid, "request not sent"))
+        # sends are registered once this step's forward (which completes
+        # their prompt KV) is enqueued: see wait_for_save
+        self._sends_this_step = list(meta.sends)
+        for r in meta.recvs:
+            with self._lock:
+                self._recv[r.transfer_id] = r
+            endpoint = f"tcp://{r.host}:{r.port + self._tp_rank}"
+            self._thread.submit(lambda svc, r=r, ep=endpoint, pc=self._per_chunk: svc.open(
+                ep, r.transfer_id, r.request_id, [list(r.block_ids)], r.num_tokens, block_size=self._block_size,
+                logical_blocks_per_chunk=pc))
+
+    def wait_for_save(self) -> None:
+        """After the forward that completes the sends' prompt KV has been
+        enqueued: register each send with an event on the forward's stream,
+        which the encode job waits for before it reads the blocks."""
+        sends, self._sends_this_step = self._sends_this_step, []
+        if not sends or self._thread is None:
+            return
+        ev = None
+        if self._device is not None and self._device.type == "cuda":
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self._device))
+        for snd in sends:
+            with self._lock:
+                self._send_rid[snd.transfer_id] = snd.request_id
+            self._thread.submit(lambda svc, snd=snd: svc.add_send(snd.transfer_id, [list(snd.block_ids)],
+                                                                  snd.num_tokens, send_meta=ev))
+
+    def _collect_sends(self, svc) -> None:
+        """Producer thread: move ended sessions into the finished-sending set."""
+        if not svc.finished:
+            return
+        ended, svc.finished[:] = list(svc.finished), []
+        for s in ended:
+            write_session_stats({"direction": "send", "transfer_id": s.transfer_id, "state": s.state.name,
+                                 "chunks": s.completed_chunks, "error": s.error})
+            with self._lock:
+                rid = self._send_rid.pop(s.transfer_id, None)
+                if rid is not None:
+                    self._done_sending.add(rid)
+
+    def _on_recv_done(self, s) -> None:
+        """Consumer thread: a load ended (complete, failed or timed out)."""
+        from ..session.state import SessionState
+        with self._lock:
+            r = self._recv.pop(s.transfer_id, None)
+            if r is None:
+                return
+            if s.state is not SessionState.COMPLETE:
+                self._load_errors.update(r.block_ids)
+            self._done_recving.add(r.request_id)
+        write_session_stats({"direction": "recv", "transfer_id": s.transfer_id, "request_id": r.request_id,
+                             "state": s.state.name, "chunks": s.completed_chunks, "total_chunks": s.total_chunks,
+                             "error": s.error})
+
+    def wait_for_layer_load(self, layer_name: str) -> None:
+        return
+
+    def save_kv_layer(self, layer_name: str, kv_layer: torch.Tensor, attn_metadata, **kwargs) -> None:
+        return
+
+    def get_finished(self, finished_req_ids: set):
+        if self._thread is not None and self._thread.error is not None:
+            raise RuntimeError(f"session service failed: {self._thread.error}")
+        with self._lock:
+            self._finished_seen.update(finished_req_ids or ())
+            # a send is reported once the scheduler has told this worker that
+            # its request finished (vLLM's contract for delayed frees)
+            sending = {r for r in self._done_sending if r in self._finished_seen}
+            self._done_sending -= sending
+            self._finished_seen -= sending
+            recving, self._done_recving = self._done_recving, set()
+        return (sending or None), (recving or None)
+
+    def get_block_ids_with_load_errors(self) -> set:
+        with self._lock:
+            out, self._load_errors = self._load_errors, set()
+        return out
+
+    def shutdown(self) -> None:
+        if self._thread is not None:
+            self._thread.stop()
+            self._thread = None
+        for close in self._closers:
+            try:
+                close()
+            except Exception:  # noqa: BLE001
+                pass
+        self._closers = []
+
+    @classmethod
+    def get_required_kvcache_layout(cls, vllm_config) -> Optional[str]:
+        if vllm_config.model_config is None or vllm_config.model_config.use_mla:
+            return None
+        return "NHD"
+
+    # ---------------------------------------------------------- scheduler
+    def get_num_new_matched_tokens(self, request, num_computed_tokens: int):
+        params = getattr(request, "kv_transfer_params", None) or {}
+        if self.is_producer or not params.get("do_remote_prefill") or "remote_port" not in params:
+            return 0, False
+        n = len(request.prompt_token_ids or []) - num_computed_tokens
+        return (n, True) if n > 0 else (0, False)
+
+    def update_state_after_alloc(self, request, blocks, num_external_tokens: int) -> None:
+        params = getattr(request, "kv_transfer_params", None) or {}
+        if self.is_producer:
+            if params.get("do_remote_decode") and params.get("transfer_id") \
+                    and request.request_id not in self._remote_decode:
+                self._remote_decode[request.request_id] = (str(params["transfer_id"]),
+                                                           len(request.prompt_token_ids or []), [])
+            return
+        if not params.get("do_remote_prefill"):
+            return
+        params["do_remote_prefill"] = False      # one load per request
+        if num_external_tokens <= 0:
+            return
+        get = getattr(blocks, "get_unhashed_block_ids_all_groups", None)
+        ids = get()[0] if get is not None else blocks.get_block_ids()[0]
+        prompt = len(request.prompt_token_ids or [])
+        full = -(-prompt // self._block_size)
+        # the prompt's last `len(ids)` blocks are loaded; tokens from their start
+        suffix = prompt - (full - len(ids)) * self._block_size
+        self._pending_recvs.append(RecvReq(request.request_id, str(params["transfer_id"]),
+                                           str(params.get("remote_host", self._host)), int(params["remote_port"]),
+                                           list(ids), suffix))
+
+    def build_connector_meta(self, scheduler_output):
+        if self.is_producer and scheduler_output is not None:
+            self._track_prefills(scheduler_output)
+        # a send queued and cancelled before the worker saw it is dropped
+        dropped = {s.transfer_id for s in self._pending_sends} & set(self._pending_cancels)
+        meta = SessionConnectorMetadata(sends=[s for s in self._pending_sends if s.transfer_id not in dropped],
+                                        recvs=self._pending_recvs,
+                                        cancels=[t for t in self._pending_cancels if t not in dropped])
+        self._pending_sends, self._pending_recvs, self._pending_cancels = [], [], []
+        return meta
+
+    def _track_prefills(self, so) -> None:
+        """Queue a send for every remote-decode request whose prompt KV is
+        complete after this step (its last prefill chunk is scheduled now)."""
+        def step(rid, new_blocks, computed, resumed=False):
+            tid, prompt, blocks = self._remote_decode[rid]
+            blocks = list(new_blocks) if resumed else blocks + list(new_blocks)
+            self._remote_decode[rid] = (tid, prompt, blocks)
+            if tid not in self._registered and computed + so.num_scheduled_tokens.get(rid, 0) >= prompt:
+                need = -(-prompt // self._block_size)
+                self._pending_sends.append(SendReq(rid, tid, blocks[:need], prompt))
+                self._registered.add(tid)
+        for nr in so.scheduled_new_reqs:
+            if nr.req_id in self._remote_decode:
+                step(nr.req_id, nr.block_ids[0], nr.num_computed_tokens)
+        cached = so.scheduled_cached_reqs
+        resumed = getattr(cached, "resumed_req_ids", set()) or set()
+        for i, rid in enumerate(cached.req_ids):
+            if rid in self._remote_decode and cached.new_block_ids[i] is not None:
+                step(rid, cached.new_block_ids[i][0], cached.num_computed_tokens[i], rid in resumed)
+            elif rid in self._remote_decode:
+                step(rid, [], cached.num_computed_tokens[i])
+
+    def request_finished(self, request, block_ids):
+        rid = request.request_id
+        entry = self._remote_decode.pop(rid, None)
+        if not self.is_producer or entry is None:
+            return False, None
+        tid = entry[0]
+        status = getattr(request, "status", None)
+        sendable = tid in self._registered and (status is None or
+                                                getattr(status, "name", "") == "FINISHED_LENGTH_CAPPED")
+        ids = block_ids[0] if block_ids and isinstance(block_ids[0], (list, tuple)) else list(block_ids or [])
+        if not sendable or not ids:
+            # aborted, stopped early or never prefilled: free now, send nothing
+            if tid in self._registered:
+                self._registered.discard(tid)
+                self._pending_cancels.append(tid)
+            return False, None
+        self._registered.discard(tid)
+        return True, {"do_remote_prefill": True, "do_remote_decode": False, "transfer_id": tid,
+                      "remote_host": self._host, "remote_port": self._port, "remote_tp_size": self._tp_size,
+                      "remote_num_tokens": entry[1]}

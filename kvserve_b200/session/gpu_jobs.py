@@ -85,6 +85,9 @@ class RuntimeEncodeJob:
             raise RuntimeError("the consumer sent no receive arena")
         if meta.slot_bytes < 2 * self.part:
             raise RuntimeError(f"consumer slots of {meta.slot_bytes} bytes can not hold 2 x {self.part}")
+        ready = session.send_meta
+        if isinstance(ready, torch.cuda.Event):
+            ready.synchronize()    # the forward that wrote these blocks has finished
         dest = self._arena(meta.arena_ipc_handle) + pull.slot_offset
         blocks = _chunk(session.local_block_ids[0], pull.chunk_id, self.per_chunk)
         valid = _valid(session.valid_tokens_by_group[0], pull.chunk_id, self.per_chunk, self.block_size)

@@ -29,6 +29,7 @@ import zmq
 from .protocol import (ChunkPull, ChunkReady, SessionAbort, SessionAbortAck, SessionOpen, SessionOpened,
                        XferMetadata, decode_request, decode_response, encode_message)
 from .state import (ConsumerSession, ProducerSession, ReceiveSlot, ReceiveSlotState, SessionState)
+from .tokens import suffix_token_counts
 
 
 def _chunks(logical_blocks: int, per_chunk: int) -> int:
@@ -37,7 +38,9 @@ def _chunks(logical_blocks: int, per_chunk: int) -> int:
 
 class ProducerService:
     """Prefill side: ROUTER bound on ``endpoint``; answers opens and pulls
-    for the transfers registered with :meth:`add_send`."""
+    for the transfers registered with :meth:`add_send`.  An open may arrive
+    before its send is registered (the consumer's router can be faster than
+    the prefill engine's bookkeeping): it waits up to ``open_timeout_s``."""
 
     def __init__(self, endpoint: str, encode_job: Callable, open_timeout_s: float = 30.0):
         self.ctx = zmq.Context.instance()
@@ -48,6 +51,9 @@ class ProducerService:
         self.open_timeout_s = open_timeout_s
         self.sessions: dict[str, ProducerSession] = {}
         self.finished: list[ProducerSession] = []
+        # opens that arrived before their send was registered: answered by
+        # add_send, or refused when the open timeout passes
+        self._early: dict[str, tuple[bytes, SessionOpen, float]] = {}
         self.stats = {"opens": 0, "pulls": 0, "aborts": 0, "expired": 0, "payload_bytes": 0, "data_bytes": 0}
 
     def add_send(self, transfer_id: str, local_block_ids: list, num_tokens: int, send_meta=None) -> None:
@@ -55,6 +61,9 @@ class ProducerService:
         s.valid_tokens_by_group = {0: num_tokens}
         s.deadline = time.monotonic() + self.open_timeout_s
         self.sessions[transfer_id] = s
+        early = self._early.pop(transfer_id, None)
+        if early is not None:
+            self._on_open(early[0], transfer_id, early[1])
 
     def _reply(self, ident: bytes, tid: str, msg) -> None:
         self.sock.send_multipart([ident, tid.encode(), encode_message(msg)])
@@ -68,10 +77,23 @@ class ProducerService:
         self.stats["opens"] += 1
         s = self.sessions.get(tid)
         meta: XferMetadata = m.metadata
+        if s is None and tid in meta.req_blocks:
+            self._early[tid] = (ident, m, time.monotonic() + self.open_timeout_s)
+            return
         if s is None or s.state is not SessionState.PLANNED or tid not in meta.req_blocks:
             self._reply(ident, tid, SessionOpened(0, 0, error=f"unknown or busy transfer {tid}"))
             return
         d_req, remote_blocks = meta.req_blocks[tid]
+        local = s.local_block_ids
+        if remote_blocks and local and len(remote_blocks[0]) > len(local[0]):
+            self._reply(ident, tid, SessionOpened(0, 0, error=f"{tid}: consumer asks for more blocks than sent"))
+            return
+        if remote_blocks and local and len(remote_blocks[0]) < len(local[0]):
+            # the consumer holds a block-aligned prefix: send the last blocks,
+            # counting tokens from the suffix start
+            total = s.valid_tokens_by_group[0]
+            s.local_block_ids = [ids[len(ids) - len(r):] for ids, r in zip(local, remote_blocks)]
+            s.valid_tokens_by_group = suffix_token_counts(total, remote_blocks, {0: meta.block_size})
         s.d_req_id, s.remote_block_ids, s.nonce = d_req, remote_blocks, m.nonce
         s.remote_meta = meta
         s.remote_session = ident.hex()
@@ -107,16 +129,29 @@ class ProducerService:
 
     def _on_abort(self, ident: bytes, tid: str, m: SessionAbort) -> None:
         self.stats["aborts"] += 1
+        self._early.pop(tid, None)
         s = self.sessions.get(tid)
         if s is not None and not s.done:
             s.error = m.reason
             self._finish(s, SessionState.CANCELLED)
         self._reply(ident, tid, SessionAbortAck(tid, m.d_req_id, m.nonce))
 
+    def cancel(self, transfer_id: str, reason: str) -> None:
+        """Withdraw a registered send (its blocks are being freed); a later
+        open or pull of it is refused."""
+        s = self.sessions.get(transfer_id)
+        if s is not None and not s.done:
+            s.error = reason
+            self._finish(s, SessionState.CANCELLED)
+
     def sweep(self, now: Optional[float] = None) -> list:
         """Expire registered sends that no consumer opened in time."""
         now = time.monotonic() if now is None else now
         out = []
+        for tid, (ident, _, deadline) in list(self._early.items()):
+            if now > deadline:
+                del self._early[tid]
+                self._reply(ident, tid, SessionOpened(0, 0, error=f"unknown transfer {tid}"))
         for s in list(self.sessions.values()):
             if s.state is SessionState.PLANNED and now > s.deadline:
                 s.error = "open timeout"

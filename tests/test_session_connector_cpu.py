@@ -1,0 +1,219 @@
+"""The session-protocol vLLM connector on CPU: scheduler and worker halves
+of a prefill and a decode connector driven the way vLLM's scheduler and
+model runner call them, with the session services on their threads over
+ZeroMQ and fake encode/decode jobs that move CPU tensor blocks through a
+shared arena (the GPU jobs are covered by the session GPU test).
+
+Checked: the prefill side keeps its blocks and hands out the router's
+parameters; the decode side claims an asynchronous load of the prompt,
+pulls every chunk into the request's blocks and reports the request in
+``get_finished``; the prefill side then reports the send; a decode engine
+with a cached prefix pulls only the suffix; an unknown transfer reports its
+blocks as load errors."""
+import socket
+import time
+from types import SimpleNamespace as NS
+
+import torch
+
+from kvserve_b200.connector.session_kv_connector import (KVConnectorRole, SessionConnectorMetadata,
+                                                         SessionKVConnector, kv_pair, layer_index)
+
+BS, NB, PER_CHUNK = 16, 40, 2
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _vllm_config(producer: bool, port: int):
+    comp = {"enable-compression-pipeline": True, "pipeline": ["transformer", "quantizer"],
+            "logical_blocks_per_chunk": PER_CHUNK}
+    return NS(kv_transfer_config=NS(is_kv_producer=producer, kv_ip="127.0.0.1",
+                                    kv_connector_extra_config={"session_port": port, "num_slots": 2,
+                                                               "compression": comp, "open_timeout_s": 5.0,
+                                                               "session_timeout_s": 10.0}),
+              cache_config=NS(block_size=BS), parallel_config=NS(tensor_parallel_size=1),
+              model_config=NS(use_mla=False))
+
+
+class FakeJobs(SessionKVConnector):
+    """Encode = copy the chunk's source blocks into the granted arena slot;
+    decode = copy the slot into the request's destination blocks."""
+    arena: dict = {}
+    seen: list = []
+
+    def make_encode_job(self, caches):
+        cache = next(iter(caches.values()))
+        self._per_chunk = PER_CHUNK
+
+        def enc(session, pull):
+            ids = session.local_block_ids[0][pull.chunk_id * PER_CHUNK:(pull.chunk_id + 1) * PER_CHUNK]
+            FakeJobs.seen.append((tuple(ids), session.valid_tokens_by_group[0]))
+            FakeJobs.arena[pull.slot_id] = cache[:, ids].clone()
+            n = FakeJobs.arena[pull.slot_id].numel() * 2
+            return n, n
+        return enc
+
+    def make_decode_job(self, caches):
+        cache = next(iter(caches.values()))
+        self._per_chunk = PER_CHUNK
+
+        def dec(session, slot, ready):
+            ids = session.block_ids[0][ready.chunk_id * PER_CHUNK:(ready.chunk_id + 1) * PER_CHUNK]
+            cache[:, ids] = FakeJobs.arena[slot.slot_id]
+        return dec, 1 << 20, b""
+
+
+class Blocks:
+    def __init__(self, ids, unhashed):
+        self.ids, self.unhashed = ids, unhashed
+
+    def get_block_ids(self):
+        return (self.ids,)
+
+    def get_unhashed_block_ids_all_groups(self):
+        return [self.unhashed]
+
+
+def _req(rid, prompt_len, params, status="FINISHED_LENGTH_CAPPED"):
+    return NS(request_id=rid, prompt_token_ids=list(range(prompt_len)), kv_transfer_params=params,
+              status=NS(name=status))
+
+
+def _pair(port):
+    src = torch.randn(2, NB, BS, 2, 64).to(torch.bfloat16)
+    dst = torch.zeros_like(src)
+    p_sched = FakeJobs(_vllm_config(True, port), KVConnectorRole.SCHEDULER)
+    d_sched = FakeJobs(_vllm_config(False, port), KVConnectorRole.SCHEDULER)
+    p_work = FakeJobs(_vllm_config(True, port), KVConnectorRole.WORKER)
+    d_work = FakeJobs(_vllm_config(False, port), KVConnectorRole.WORKER)
+    p_work.register_kv_caches({"model.layers.0.self_attn.attn": src})
+    d_work.register_kv_caches({"model.layers.0.self_attn.attn": dst})
+    return src, dst, p_sched, d_sched, p_work, d_work
+
+
+def _sched_out(new=(), finished=()):
+    """A scheduler output with ``new`` = [(req_id, block_ids, prompt_len)]
+    scheduled in full this step."""
+    return NS(scheduled_new_reqs=[NS(req_id=r, block_ids=(b,), num_computed_tokens=0) for r, b, _ in new],
+              num_scheduled_tokens={r: n for r, _, n in new},
+              scheduled_cached_reqs=NS(req_ids=[], new_block_ids=[], num_computed_tokens=[], resumed_req_ids=set()),
+              finished_req_ids=set(finished))
+
+
+def _step(sched, work, finished=(), so=None):
+    work.bind_connector_metadata(sched.build_connector_meta(so if so is not None else _sched_out()))
+    work.start_load_kv(None)
+    work.wait_for_save()
+    out = work.get_finished(set(finished))
+    work.clear_connector_metadata()
+    return out
+
+
+def _prefill(p_sched, p_work, rid, tid, prompt, blocks):
+    """The prefill engine: allocation, the full-prompt step, the finish."""
+    req = _req(rid, prompt, {"do_remote_decode": True, "transfer_id": tid})
+    p_sched.update_state_after_alloc(req, Blocks(blocks, blocks), 0)
+    _step(p_sched, p_work, so=_sched_out([(rid, blocks, prompt)]))
+    delay, params = p_sched.request_finished(req, blocks)
+    _step(p_sched, p_work, finished={rid})
+    return delay, params
+
+
+def _wait_recv(d_sched, d_work, rid, timeout=20.0):
+    deadline = time.monotonic() + timeout
+    while time.monotonic() < deadline:
+        _, recving = _step(d_sched, d_work)
+        if recving and rid in recving:
+            return True
+        time.sleep(0.01)
+    return False
+
+
+def test_helpers_parse_vllm_names_and_layouts():
+    assert layer_index("model.layers.17.self_attn.attn", 0) == 17
+    assert layer_index("attn", 5) == 5
+    t = torch.zeros(2, 3, 16, 2, 8)
+    assert kv_pair(t)[0].shape == (3, 16, 2, 8)
+    t2 = torch.zeros(3, 2, 16, 2, 8)
+    k, v = kv_pair(t2)
+    assert k.shape == (3, 16, 2, 8) and k.stride() == v.stride()
+
+
+def test_pull_moves_every_chunk_and_both_sides_report():
+    FakeJobs.seen.clear()
+    src, dst, p_sched, d_sched, p_work, d_work = _pair(_port())
+    try:
+        prompt, p_blocks, d_blocks = 100, list(range(0, 7)), list(range(20, 27))
+        delay, params = _prefill(p_sched, p_work, "p1", "t1", prompt, p_blocks)
+        assert delay and params["do_remote_prefill"] and params["transfer_id"] == "t1"
+        dreq = _req("d1", prompt, dict(params), status="WAITING_FOR_REMOTE_KVS")
+        assert d_sched.get_num_new_matched_tokens(dreq, 0) == (prompt, True)
+        d_sched.update_state_after_alloc(dreq, Blocks(d_blocks, d_blocks), prompt)
+        assert dreq.kv_transfer_params["do_remote_prefill"] is False
+        assert _wait_recv(d_sched, d_work, "d1")
+        assert torch.equal(dst[:, d_blocks], src[:, p_blocks])
+        assert not d_work.get_block_ids_with_load_errors()
+        deadline = time.monotonic() + 10
+        sending = None
+        while time.monotonic() < deadline and not sending:
+            sending, _ = _step(p_sched, p_work)
+            time.sleep(0.01)
+        assert sending == {"p1"}
+        assert len(FakeJobs.seen) == 4 and all(v == prompt for _, v in FakeJobs.seen)
+    finally:
+        p_work.shutdown()
+        d_work.shutdown()
+
+
+def test_cached_prefix_pulls_only_the_suffix():
+    FakeJobs.seen.clear()
+    src, dst, p_sched, d_sched, p_work, d_work = _pair(_port())
+    try:
+        prompt, p_blocks = 100, list(range(0, 7))
+        d_blocks, suffix = list(range(30, 37)), list(range(34, 37))   # 4 blocks already cached
+        _, params = _prefill(p_sched, p_work, "p2", "t2", prompt, p_blocks)
+        dreq = _req("d2", prompt, dict(params), status="WAITING_FOR_REMOTE_KVS")
+        assert d_sched.get_num_new_matched_tokens(dreq, 64) == (prompt - 64, True)
+        d_sched.update_state_after_alloc(dreq, Blocks(d_blocks, suffix), prompt - 64)
+        assert _wait_recv(d_sched, d_work, "d2")
+        assert torch.equal(dst[:, suffix], src[:, p_blocks[4:]])
+        assert dst[:, d_blocks[:4]].abs().sum() == 0
+        assert [ids for ids, _ in FakeJobs.seen] == [(4, 5), (6,)]
+        assert all(v == prompt - 64 for _, v in FakeJobs.seen)
+    finally:
+        p_work.shutdown()
+        d_work.shutdown()
+
+
+def test_unknown_transfer_reports_load_errors():
+    src, dst, p_sched, d_sched, p_work, d_work = _pair(_port())
+    try:
+        params = {"do_remote_prefill": True, "transfer_id": "nope", "remote_host": "127.0.0.1",
+                  "remote_port": p_sched._port}
+        dreq = _req("d3", 40, params, status="WAITING_FOR_REMOTE_KVS")
+        assert d_sched.get_num_new_matched_tokens(dreq, 0) == (40, True)
+        d_sched.update_state_after_alloc(dreq, Blocks([5, 6, 7], [5, 6, 7]), 40)
+        assert _wait_recv(d_sched, d_work, "d3")
+        assert d_work.get_block_ids_with_load_errors() == {5, 6, 7}
+        # a request without router parameters is not the connector's
+        assert d_sched.get_num_new_matched_tokens(_req("d4", 40, None), 0) == (0, False)
+        # an aborted prefill frees its blocks at once and withdraws its send
+        req = _req("p4", 40, {"do_remote_decode": True, "transfer_id": "x"}, status="FINISHED_ABORTED")
+        p_sched.update_state_after_alloc(req, Blocks([1, 2, 3], [1, 2, 3]), 0)
+        _step(p_sched, p_work, so=_sched_out([("p4", [1, 2, 3], 40)]))
+        assert p_sched.request_finished(req, [1, 2, 3]) == (False, None)
+        meta = p_sched.build_connector_meta(_sched_out())
+        assert meta.cancels == ["x"] and not meta.sends
+        # a prefill still in progress is not sent before its last chunk
+        req5 = _req("p5", 64, {"do_remote_decode": True, "transfer_id": "y"})
+        p_sched.update_state_after_alloc(req5, Blocks([8, 9], [8, 9]), 0)
+        assert not p_sched.build_connector_meta(_sched_out([("p5", [8, 9], 32)])).sends
+    finally:
+        p_work.shutdown()
+        d_work.shutdown()

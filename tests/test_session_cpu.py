@@ -100,10 +100,10 @@ def test_producer_consumer_exchange_reuses_slots():
 
 def test_unknown_transfer_fails_session_and_abort_is_acknowledged():
     ep = f"tcp://127.0.0.1:{_port()}"
-    prod = ProducerService(ep, lambda s, m: (0, 0))
+    prod = ProducerService(ep, lambda s, m: (0, 0), open_timeout_s=0.5)
     done = []
     cons = ConsumerService("d0", 1, 64, lambda *a: None, done.append)
-    cons.open(ep, "missing", "r", [[1]], 16)
+    cons.open(ep, "missing", "r", [[1]], 16)     # never registered: refused after the open timeout
     t0 = time.monotonic()
     while not done and time.monotonic() - t0 < 10:
         prod.poll(2)
@@ -116,6 +116,26 @@ def test_unknown_transfer_fails_session_and_abort_is_acknowledged():
     while "t2" in prod.sessions and time.monotonic() - t0 < 10:
         prod.poll(2)
     assert prod.finished[-1].state is SessionState.CANCELLED
+    prod.close()
+    cons.close()
+
+
+def test_open_before_registration_waits_for_the_send():
+    ep = f"tcp://127.0.0.1:{_port()}"
+    prod = ProducerService(ep, lambda s, m: (64, 8), open_timeout_s=10.0)
+    done = []
+    cons = ConsumerService("d0", 1, 64, lambda *a: None, done.append)
+    cons.open(ep, "late", "r", [[1, 2]], 32)
+    for _ in range(20):
+        prod.poll(2)
+        cons.poll(2)
+    assert not done and "late" in prod._early
+    prod.add_send("late", [[7, 8]], 32)
+    t0 = time.monotonic()
+    while not done and time.monotonic() - t0 < 10:
+        prod.poll(2)
+        cons.poll(2)
+    assert done[0].state is SessionState.COMPLETE and not prod._early
     prod.close()
     cons.close()
 
