@@ -301,6 +301,8 @@ class ConsumerService:
     def poll(self, timeout_ms: int = 0) -> int:
         n = 0
         socks = list(self.socks.values())
+        if not socks and timeout_ms > 0:
+            time.sleep(timeout_ms / 1000.0)   # nothing to wait on yet: do not spin
         if socks:
             poller = zmq.Poller()
             for sk in socks:
