@@ -8,6 +8,13 @@ seeded Rademacher vectors of :mod:`kvserve_b200.compression.heads`.
 
 CUDA tensors go through the ``fwht_rows`` sm_100a kernel; CPU tensors use an
 fp32 matrix product with the Sylvester Hadamard matrix (same maths).
+
+``numerics="bf16-stagewise"`` reproduces the reference runtime's symbols
+instead (kvserve_v1/compression/runtime/csrc/kvs_compress.cu:119-161 and its
+CPU twin, runtime/pipeline.py:307-335): the signed input is rounded to bf16,
+every butterfly stage (strides 1, 2, 4, ...) is rounded to bf16, and so is
+the final ``1/sqrt(n)`` scale; the inverse runs the same transform and then
+multiplies by the signs (rounded).  Power-of-two head sizes only.
 """
 from __future__ import annotations
 
@@ -44,9 +51,34 @@ def fwht_cpu(x: torch.Tensor) -> torch.Tensor:
     return torch.cat(outs, dim=-1)
 
 
+def fwht_bf16_stagewise(x: torch.Tensor) -> torch.Tensor:
+    """Normalised FWHT of the last dim (a power of two) with a bf16 rounding
+    after every butterfly stage and after the scale; bf16 result."""
+    n = x.shape[-1]
+    if n & (n - 1):
+        raise ValueError("the stage-wise bf16 FWHT needs a power-of-two size")
+    lead = x.shape[:-1]
+    y = x.to(torch.bfloat16).to(torch.float32)
+    step = 1
+    while step < n:
+        pairs = y.reshape(*lead, n // (2 * step), 2, step)
+        a, b = pairs[..., 0, :], pairs[..., 1, :]
+        y = torch.stack((a + b, a - b), dim=-2).to(torch.bfloat16).to(torch.float32)
+        step *= 2
+    # 1/sqrt(n) evaluated in fp32, as the kernel does
+    scale = torch.tensor(1.0, dtype=torch.float32) / torch.sqrt(torch.tensor(float(n), dtype=torch.float32))
+    return (y.reshape(x.shape) * scale.to(y.device)).to(torch.bfloat16)
+
+
+NUMERICS = ("fp32", "bf16-stagewise")
+
+
 class HadamardTransform:
-    def __init__(self, base_seed: int = 0xC0FEBABE):
+    def __init__(self, base_seed: int = 0xC0FEBABE, numerics: str = "fp32"):
+        if numerics not in NUMERICS:
+            raise ValueError(f"numerics must be one of {NUMERICS}, got {numerics!r}")
         self.base_seed = int(base_seed)
+        self.numerics = numerics
         self._signs: dict = {}
 
     def signs(self, layer_id: int, num_heads: int, head_dim: int, device, dtype=torch.float32) -> torch.Tensor:
@@ -61,6 +93,11 @@ class HadamardTransform:
         if tensor.dim() != 4:
             raise ValueError(f"expected [num_blocks, block_size, num_heads, head_dim], got {tuple(tensor.shape)}")
         heads, dim = tensor.shape[-2], tensor.shape[-1]
+        if self.numerics == "bf16-stagewise":
+            signs = self.signs(layer_id, heads, dim, tensor.device, torch.bfloat16)
+            if not inverse:
+                return fwht_bf16_stagewise(tensor.to(torch.bfloat16) * signs).to(tensor.dtype)
+            return (fwht_bf16_stagewise(tensor) * signs).to(tensor.dtype)
         if tensor.is_cuda and tensor.dtype == torch.bfloat16:
             from ...ops import ext
             src = tensor.contiguous()

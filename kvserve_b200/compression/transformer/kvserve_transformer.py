@@ -10,7 +10,9 @@ dim]``) are applied to each half; whole-layer entries receive the layer.
 
 Kinds and parameters match the profiles of
 kvserve_v1/compression/transformer/kvserve_transformer.py:7-51 (``hadamard``,
-``dct``, ``haar``; an integer ``seed``).  A profile that omits the seed
+``dct``, ``haar``; an integer ``seed``), plus ``hadamard_bf16``: the same
+transform with the reference runtime's numerics (bf16 rounding after every
+butterfly stage), which reproduces that runtime's quantisation symbols.  A profile that omits the seed
 implies ``DEFAULT_SEED``: it selects the random signs, so both peers (and a
 reference peer) must derive the same value.  New kinds are added with
 :func:`register_transform`.
@@ -60,6 +62,11 @@ def _hadamard(seed: int):
     return HadamardTransform(seed)
 
 
+def _hadamard_bf16(seed: int):
+    from .hadamard import HadamardTransform
+    return HadamardTransform(seed, numerics="bf16-stagewise")
+
+
 def _rotation(kind: str) -> Callable[[int], Any]:
     def make(seed: int):
         from .orthogonal import OrthogonalTransform
@@ -68,6 +75,8 @@ def _rotation(kind: str) -> Callable[[int], Any]:
 
 
 register_transform("hadamard", _hadamard, per_half=True)
+# the reference runtime's numerics (bf16 rounding after every butterfly stage)
+register_transform("hadamard_bf16", _hadamard_bf16, per_half=True)
 register_transform("dct", _rotation("dct"))
 register_transform("haar", _rotation("haar"))
 

@@ -229,3 +229,17 @@ def test_fidelity_synthetic_kv_and_error_stats():
     st = error_stats(kv, torch.zeros_like(kv))
     assert abs(st["rel_mse"] - 1.0) < 1e-6 and abs(st["v_rel_mse"] - 1.0) < 1e-6
     assert error_stats(kv, kv)["mse"] == 0.0
+
+
+def test_hadamard_bf16_kind_round_trips_and_differs_from_fp32_only_by_rounding():
+    from kvserve_b200.compression.transformer.kvserve_transformer import KVServeTransformer, registered_transforms
+    assert "hadamard_bf16" in registered_transforms()
+    g = torch.Generator().manual_seed(5)
+    layer = torch.randn((2, 3, 16, 4, 128), generator=g).to(torch.bfloat16)
+    ref = KVServeTransformer(transform_type="hadamard", seed=77)
+    stg = KVServeTransformer(transform_type="hadamard_bf16", seed=77)
+    a, b = ref.transform(3, layer).float(), stg.transform(3, layer).float()
+    assert not torch.equal(a, b)                      # per-stage rounding changes some values
+    assert (a - b).abs().max() <= 0.05 * a.abs().max()
+    back = stg.inverse(3, stg.transform(3, layer)).float()
+    assert ((back - layer.float()).norm() / layer.float().norm()) < 0.02

@@ -138,3 +138,17 @@ def test_wire_from_here_restores_in_reference():
     theirs = ref_restore(RefWire(meta=w.meta, body_chunks=w.body_chunks, aux_tensors=w.aux_tensors))
     out = RefAdapter(QUANT_ONLY, 8, 128).decompress(theirs)
     assert torch.equal(out, ours.decompress(c))
+
+
+@pytest.mark.parametrize("n", [64, 128, 256])
+def test_stagewise_bf16_fwht_matches_reference_runtime(n):
+    """``hadamard_bf16`` reproduces the reference runtime's transform bit for
+    bit (its CPU path, kvserve_v1/compression/runtime/pipeline.py:307-335,
+    which rounds every butterfly stage to bf16 like its CUDA kernel)."""
+    from kvserve_v1.compression.runtime.pipeline import CompressionPipeline as RefPipeline
+    from kvserve_b200.compression.transformer.hadamard import fwht_bf16_stagewise
+    g = torch.Generator().manual_seed(n)
+    x = (torch.randn((37, 4, n), generator=g) * 3).to(torch.bfloat16)
+    ref_out = torch.empty_like(x)
+    RefPipeline._hadamard_transform(x.clone(), ref_out, n)
+    assert torch.equal(fwht_bf16_stagewise(x), ref_out)
