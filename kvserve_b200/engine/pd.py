@@ -312,6 +312,15 @@ class PDEngine:
                 ops.count_launches(1)
                 ops.ext().wait_flag(snd.credit_ptr(slot), prev, self.ingest_timeout_ns, self.status)
 
+    def check_slots(self) -> None:
+        """With ``KVSERVE_SLOT_CANARIES=1``: fail if a producer wrote past a
+        receive slot into its guard region (no-op without guards)."""
+        for i, r in enumerate(self.receivers):
+            bad = r.damaged_slots()
+            if bad:
+                raise RuntimeError(f"KV hand-off: receive channel {i} slot(s) {bad} overran into their guard "
+                                   f"region (frame layout mismatch between the peers?)")
+
     def _return_credit(self, slot: int, seq: int) -> None:
         """Consumer, on the stream of the last kernel that read the slot."""
         self._slot_seq[slot] = seq
@@ -457,6 +466,7 @@ class PDEngine:
         if st != 0:
             self.status.zero_()
             raise RuntimeError(f"KV hand-off failed on rank {ctx.rank}: {ops.STATUS_NAMES.get(st, st)}")
+        self.check_slots()
         dc = m.decode_coll
         if dc is not None and int(dc.status[0].item()) != 0:
             code = int(dc.status[0].item())
@@ -526,6 +536,7 @@ class PDEngine:
         if st != 0:
             self.status.zero_()
             raise RuntimeError(f"KV hand-off failed on rank {ctx.rank}: {ops.STATUS_NAMES.get(st, st)}")
+        self.check_slots()
         nan = float("nan")
         return {"encode_ms": start.elapsed_time(enc_end) if ctx.is_prefill else nan,
                 "ingest_ms": start.elapsed_time(ing_end) if ctx.is_decode else nan,

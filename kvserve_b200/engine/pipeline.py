@@ -266,6 +266,7 @@ class PipelinedServer:
             self.eng.status.zero_()
             raise RuntimeError(f"pipelined serving failed on rank {ctx.rank}: {ops.STATUS_NAMES.get(st, st)}")
         dist.barrier(group=ctx.cpu_group)
+        self.eng.check_slots()
         return recs
 
     # ------------------------------------------------------ prefill side

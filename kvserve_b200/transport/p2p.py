@@ -25,6 +25,10 @@ stream acquire-waits (bounded, over NVLink) until the credit reaches the
 sequence number of the slot's previous request.  With ``num_slots`` slots the
 prefill side runs up to ``num_slots`` requests ahead of the decode side's
 ingest.
+
+Slots are ``slot_stride`` bytes apart: the slot proper (``num_layers x
+frame_stride``) and, with ``KVSERVE_SLOT_CANARIES=1``, a guard region that
+:meth:`FrameReceiver.damaged_slots` checks for overruns (:mod:`.canary`).
 """
 from __future__ import annotations
 
@@ -34,6 +38,7 @@ from typing import Optional
 import torch
 
 from ..ops import ext
+from .canary import GUARD_BYTES, canaries_enabled, damaged_slots, fill_guards
 
 
 def ctrl_words(num_layers: int) -> int:
@@ -49,24 +54,46 @@ class ChannelHandles:
     num_slots: int
     num_layers: int
     frame_stride: int
+    slot_stride: int = 0      # bytes between slots (slot_bytes plus a guard); 0 = slot_bytes
 
 
 class FrameReceiver:
     """Decode-side receive slots + publish flags (device memory)."""
 
-    def __init__(self, num_layers: int, frame_stride: int, num_slots: int = 1, device=None):
+    def __init__(self, num_layers: int, frame_stride: int, num_slots: int = 1, device=None,
+                 guard_bytes: Optional[int] = None):
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         self.num_layers, self.frame_stride, self.num_slots = num_layers, frame_stride, num_slots
         self.slot_bytes = num_layers * frame_stride
+        self.guard_bytes = (GUARD_BYTES if canaries_enabled() else 0) if guard_bytes is None else int(guard_bytes)
+        if self.guard_bytes % 256:
+            raise ValueError("guard_bytes must keep slots 256-byte aligned")
+        self.slot_stride = self.slot_bytes + self.guard_bytes
         with torch.cuda.device(self.device):
-            self.slots_ptr = ext().dev_alloc(num_slots * self.slot_bytes)
+            self.slots_ptr = ext().dev_alloc(num_slots * self.slot_stride)
             # per slot: one publish flag per layer, the first token, its flag,
             # the credit word and one pad word
             self.flags_ptr = ext().dev_alloc(max(256, num_slots * ctrl_words(num_layers) * 4))
         self._closed = False
+        if self.guard_bytes:
+            fill_guards(self._slots_view(), num_slots, self.slot_stride, self.slot_bytes)
+
+    def _slots_view(self) -> torch.Tensor:
+        from ..ops import dtype_code
+        return ext().tensor_from_ptr(self.slots_ptr, [self.num_slots * self.slot_stride], dtype_code(torch.uint8),
+                                     self.device.index)
+
+    def damaged_slots(self) -> list[int]:
+        """Slots whose guard region was written (empty without guards);
+        synchronises with the device."""
+        if not self.guard_bytes:
+            return []
+        return damaged_slots(self._slots_view(), self.num_slots, self.slot_stride, self.slot_bytes)
 
     def slot_base(self, slot: int) -> int:
-        return self.slots_ptr + slot * self.slot_bytes
+        return self.slots_ptr + slot * self.slot_stride
 
     def flags_base(self, slot: int) -> int:
         return self.flags_ptr + slot * ctrl_words(self.num_layers) * 4
@@ -81,7 +108,8 @@ class FrameReceiver:
 
     def handles(self) -> ChannelHandles:
         return ChannelHandles(ext().ipc_get_handle(self.slots_ptr), ext().ipc_get_handle(self.flags_ptr),
-                              self.slot_bytes, self.num_slots, self.num_layers, self.frame_stride)
+                              self.slot_bytes, self.num_slots, self.num_layers, self.frame_stride,
+                              self.slot_stride)
 
     def flags_view(self, slot: int) -> torch.Tensor:
         from ..ops import dtype_code
@@ -107,7 +135,7 @@ class FrameSender:
         if local is not None:
             self.slots_ptr, self.flags_ptr = local.slots_ptr, local.flags_ptr
             self.slot_bytes, self.num_layers, self.frame_stride = local.slot_bytes, local.num_layers, local.frame_stride
-            self.num_slots = local.num_slots
+            self.num_slots, self.slot_stride = local.num_slots, local.slot_stride
             return
         assert handles is not None
         with torch.cuda.device(self.device):
@@ -116,9 +144,10 @@ class FrameSender:
         self._opened = [self.slots_ptr, self.flags_ptr]
         self.slot_bytes, self.num_layers = handles.slot_bytes, handles.num_layers
         self.frame_stride, self.num_slots = handles.frame_stride, handles.num_slots
+        self.slot_stride = handles.slot_stride or handles.slot_bytes
 
     def frame_ptr(self, slot: int, layer: int) -> int:
-        return self.slots_ptr + slot * self.slot_bytes + layer * self.frame_stride
+        return self.slots_ptr + slot * self.slot_stride + layer * self.frame_stride
 
     def flag_ptr(self, slot: int, layer: int) -> int:
         return self.flags_ptr + (slot * ctrl_words(self.num_layers) + layer) * 4

@@ -249,3 +249,26 @@ def test_lossless_stage_is_exact_in_the_engine():
             assert int(eng.xfer.wire_bytes.item()) > 0
         eng.close()
     assert toks[0] == toks[1]
+
+
+def test_slot_guards_stay_intact_and_catch_an_overrun(monkeypatch):
+    """With KVSERVE_SLOT_CANARIES=1 every receive slot is followed by a guard
+    region: real requests (raw and compressed frames) leave it intact, and a
+    write past a slot's end is reported by the engine's slot check."""
+    from kvserve_b200 import ops
+    from kvserve_b200.engine.transfer import TransferProfile
+    monkeypatch.setenv("KVSERVE_SLOT_CANARIES", "1")
+    for prof in (TransferProfile.raw(),
+                 TransferProfile(compressed=True, hybrid_ratio=0.0, key_levels=(16, 16), value_levels=(4, 4))):
+        eng = _engine(prof)
+        r = eng.receivers[0]
+        assert r.guard_bytes == 256 and r.slot_stride == r.slot_bytes + 256
+        assert eng.senders[0].frame_ptr(0, 1) == r.slot_base(0) + r.frame_stride
+        ids = torch.randint(0, eng.cfg.vocab, (255,), dtype=torch.int32)
+        assert len(eng.generate(ids, 4).tokens) == 4      # checks the guards after the request
+        view = ops.ext().tensor_from_ptr(r.slots_ptr, [r.num_slots * r.slot_stride], ops.dtype_code(torch.uint8),
+                                         r.device.index)
+        view[r.slot_bytes:r.slot_bytes + 8].fill_(0)       # slot 0 overran
+        with pytest.raises(RuntimeError, match="overran"):
+            eng.check_slots()
+        eng.close()

@@ -255,3 +255,16 @@ def test_data_parallel_replicas_layout():
     assert [res[r]["bcast"] for r in range(4)] == [0.0, 0.0, 10.0, 10.0]
     assert all(res[r]["all"] == [0, 1, 2, 3] for r in range(4))
     assert res[3]["leaders"] == [[2], [3]]
+
+
+def test_slot_guards_detect_an_overrun_into_the_next_slot():
+    from kvserve_b200.transport.canary import GUARD_PATTERN, damaged_slots, fill_guards
+    slots, payload, guard = 3, 1024, 256
+    buf = torch.zeros(slots * (payload + guard), dtype=torch.uint8)
+    fill_guards(buf, slots, payload + guard, payload)
+    buf[:payload] = 7                              # in-bounds frames leave the guards alone
+    buf[(payload + guard) + 5] = 1
+    assert damaged_slots(buf, slots, payload + guard, payload) == []
+    buf[2 * (payload + guard) - 3] = GUARD_PATTERN ^ 1   # slot 1 wrote 253 bytes past its end
+    assert damaged_slots(buf, slots, payload + guard, payload) == [1]
+    assert damaged_slots(buf, slots, payload, payload) == []   # no guards configured
