@@ -19,6 +19,8 @@ raw), then the chunks back to back, each starting on a 4-byte boundary.
 """
 from __future__ import annotations
 
+import os
+
 import struct
 from typing import Any
 
@@ -121,7 +123,9 @@ class LosslessCodec:
 
     def __init__(self, **kwargs: Any) -> None:
         self.chunk = int(kwargs.get("chunk_bytes", CHUNK))
-        self.algorithm = kwargs.get("lc_algorithm", "TUPL8_1 BIT_8 RZE_2")
+        # KVSERVE_LC_ALGORITHM is the reference's environment default for the
+        # chain; KVSERVE_LC_META_PATH (its generated LC runtime) has no role here
+        self.algorithm = kwargs.get("lc_algorithm") or os.environ.get("KVSERVE_LC_ALGORITHM") or "TUPL8_1 BIT_8 RZE_2"
         if self.algorithm == self.codec_id:   # the container name selects its one chain
             self.algorithm = "TUPL8_1 BIT_8 RZE_2"
         if self.algorithm not in ("TUPL8_1 BIT_8 RZE_2",):

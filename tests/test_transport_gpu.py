@@ -1,11 +1,16 @@
-"""The transport's CUDA-IPC data plane on real GPUs (no NCCL on the KV path).
+"""The transport's GPU data planes on real GPUs.
 
-A producer process and a consumer process (both on GPU 0, or on GPUs 0 and
-1 when two are visible) exchange raw and bundle payloads; the consumer's
-pool grants ranges, the producer's copy engine writes them, ``DONE``
-publishes them.  Checked: the bytes arrive intact, credit released ranges
-are reused, and a payload larger than the pool (admitted into an empty
-buffer, the oversize rule) travels through its own exported allocation.
+* CUDA IPC (no NCCL on the KV path): a producer process and a consumer
+  process (both on GPU 0, or on GPUs 0 and 1 when two are visible) exchange
+  raw and bundle payloads; the consumer's pool grants ranges, the producer's
+  copy engine writes them, ``DONE`` publishes them.
+* NCCL (the reference's own data plane, kvserve_v1/transport/
+  nccl_transport.py:312-445, 600-725): the same exchange over a two-rank NCCL
+  communicator, which needs two GPUs (skipped with one).
+
+Checked: the bytes arrive intact, credit-released ranges are reused, and a
+payload larger than the receive budget (admitted into an empty buffer, the
+oversize rule) still travels.
 """
 import multiprocessing as mp
 import os
@@ -31,10 +36,10 @@ def _payload(i: int, n: int) -> torch.Tensor:
     return torch.randint(0, 255, (n,), generator=g, dtype=torch.uint8)
 
 
-def _consumer(port, dev, q, expect):
+def _consumer(port, dev, q, expect, plane="ipc"):
     torch.cuda.set_device(dev)
     from kvserve_b200.transport.nccl_transport import NcclTransport
-    t = NcclTransport(False, "127.0.0.1", port, local_rank=dev, data_plane="ipc", recv_buffer_size=4 << 20)
+    t = NcclTransport(False, "127.0.0.1", port, local_rank=dev, data_plane=plane, recv_buffer_size=4 << 20)
     got = {}
     deadline = time.time() + 120
     while len(got) < expect and time.time() < deadline:
@@ -50,15 +55,16 @@ def _consumer(port, dev, q, expect):
                     got[rid] = ("raw", names, payload.cpu().clone())
                 t.release_received(rid, t.payload_nbytes(payload))
         time.sleep(0.005)
-    q.put({"got": got, "free": t.plane._pool.free_bytes(), "cap": t.plane._pool.size})
+    pool = getattr(t.plane, "_pool", None)
+    q.put({"got": got, "free": pool.free_bytes() if pool else 0, "cap": pool.size if pool else 0})
     time.sleep(0.5)
     t.close()
 
 
-def _producer(port, dev, q):
+def _producer(port, dev, q, plane="ipc"):
     torch.cuda.set_device(dev)
     from kvserve_b200.transport.nccl_transport import NcclTransport
-    t = NcclTransport(True, "127.0.0.1", port, local_rank=dev, data_plane="ipc", control_timeout_s=30)
+    t = NcclTransport(True, "127.0.0.1", port, local_rank=dev, data_plane=plane, control_timeout_s=30)
     for i in range(6):   # 6 x 1.5 MiB through a 4 MiB pool: ranges must be reused
         t.send(f"r{i}", ["l0"], _payload(i, 3 << 19).cuda())
     t.send_bundle("b0", ["__compressed__", "l0"], {"k": 1}, [_payload(10, 1000).cuda(), _payload(11, 77).cuda()],
@@ -69,13 +75,18 @@ def _producer(port, dev, q):
     t.close()
 
 
-def test_ipc_data_plane_moves_payloads():
+@pytest.mark.parametrize("plane", ["ipc", pytest.param("nccl", marks=pytest.mark.multigpu)])
+def test_data_plane_moves_payloads(plane):
+    if plane == "nccl" and torch.cuda.device_count() < 2:
+        pytest.skip("the NCCL data plane needs two GPUs")
+    if plane == "nccl":
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
     devs = (0, 1) if torch.cuda.device_count() > 1 else (0, 0)
     ctx = mp.get_context("spawn")
     port = _free_port()
     qc, qp = ctx.Queue(), ctx.Queue()
-    c = ctx.Process(target=_consumer, args=(port, devs[1], qc, 8))
-    p = ctx.Process(target=_producer, args=(port, devs[0], qp))
+    c = ctx.Process(target=_consumer, args=(port, devs[1], qc, 8, plane))
+    p = ctx.Process(target=_producer, args=(port, devs[0], qp, plane))
     c.start()
     time.sleep(1.0)
     p.start()
@@ -95,4 +106,5 @@ def test_ipc_data_plane_moves_payloads():
     for d, seed, n in zip(data, (10, 11, 12), (1000, 77, 40)):
         assert torch.equal(d, _payload(seed, n))
     assert torch.equal(got["big"][2], _payload(20, 6 << 20))
-    assert res["free"] == res["cap"]          # every granted range came back
+    if plane == "ipc":
+        assert res["free"] == res["cap"]      # every granted range came back
