@@ -174,11 +174,20 @@ def main() -> None:
             ktable = engine.decode_kernel_table(prompts[0])
         except Exception as exc:  # the table is optional evidence; never fail the bench for it
             _log(f"decode kernel table skipped: {exc!r}")
+    # optional: per-kernel device time of one request's prefill (profiler;
+    # not a timing of record), every rank in step
+    ptable = None
+    if os.environ.get("KVSERVE_PROFILE_PREFILL", "1") != "0":
+        try:
+            ptable = engine.prefill_kernel_table(prompts[0])
+        except Exception as exc:  # optional evidence; never fail the bench for it
+            _log(f"prefill kernel table skipped: {exc!r}")
     wire = None
     if ctx.is_prefill and profile.lossless:
         torch.cuda.synchronize()
         wire = int(sum(int(x.wire_bytes.item()) for x in engine.xfer_sets["default"]))
-    mine = {"steps": [t.__dict__ for t in timings], "handoff": handoffs, "wire": wire, "ktable": ktable}
+    mine = {"steps": [t.__dict__ for t in timings], "handoff": handoffs, "wire": wire, "ktable": ktable,
+            "ptable": ptable if ctx.is_prefill else None}
     allr = [None] * ctx.world_size
     if ctx.distributed:
         dist.all_gather_object(allr, mine, group=ctx.cpu_group)
@@ -265,6 +274,7 @@ def main() -> None:
             "gpu_launches": int(launches),
             "clocks": clocks,
             "decode_kernel_table": next((r["ktable"][:16] for r in allr if r["ktable"]), None),
+            "prefill_kernel_table": next((r["ptable"][:16] for r in allr if r["ptable"]), None),
             "_ttft": ttft, "_e2e": e2e_ttft,
         }
     if n_rep > 1:

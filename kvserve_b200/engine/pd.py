@@ -566,6 +566,28 @@ class PDEngine:
         del res
         return table
 
+    def prefill_kernel_table(self, prompt_ids: torch.Tensor, top: int = 24) -> list:
+        """Per-kernel device time of one request on this rank, taken with the
+        PyTorch profiler (CUPTI) around the whole request (prefill, hand-off
+        and one decode step): ``[(kernel, calls, us)]`` sorted by time.  On a
+        prefill rank this is the prefill's breakdown (GEMMs, attention,
+        norms, encode); on a decode rank the ingest and the step.  Evidence,
+        not a timing of record.  Every rank calls it (it serves one request)
+        and every rank profiles, so the ranks stay in step."""
+        from torch.profiler import ProfilerActivity, profile
+        torch.cuda.synchronize(self.device)
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            res = self.generate(prompt_ids, min(self.max_new, 2))
+            torch.cuda.synchronize(self.device)
+        table = []
+        for ev in prof.key_averages():
+            t = getattr(ev, "device_time_total", None) or getattr(ev, "cuda_time_total", 0)
+            if t and ev.count:
+                table.append((ev.key[:90], int(ev.count), round(float(t), 1)))
+        table.sort(key=lambda r: -r[2])
+        del res
+        return table[:top]
+
     def close(self) -> None:
         self._graph = None
         if self.model.decode_coll is not None:
