@@ -243,3 +243,15 @@ def test_hadamard_bf16_kind_round_trips_and_differs_from_fp32_only_by_rounding()
     assert (a - b).abs().max() <= 0.05 * a.abs().max()
     back = stg.inverse(3, stg.transform(3, layer)).float()
     assert ((back - layer.float()).norm() / layer.float().norm()) < 0.02
+
+
+def test_config0_end_to_end_over_two_gloo_processes():
+    """The CPU benchmark configuration as a whole: compress the seeded sample,
+    send the real wire bundle from a producer process to a consumer process
+    over the credit transport's gloo data plane, decompress there, report
+    CR and reconstruction error."""
+    from kvserve_b200.engine.config0 import run
+    r = run()
+    assert r["error"] is None, r["error"]
+    assert r["transferred"] and 3.9 < r["compression_ratio"] < 4.0 and r["wire_ratio"] > 3.8
+    assert r["mse"] < 0.05 * r["signal_power"] and r["relative_error"] < 0.2
