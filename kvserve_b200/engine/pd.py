@@ -577,6 +577,10 @@ class PDEngine:
         from torch.profiler import ProfilerActivity, profile
         torch.cuda.synchronize(self.device)
         with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            if self.ctx.distributed:
+                # the profiler's start-up time differs per rank: line up first
+                import torch.distributed as dist
+                dist.barrier(group=self.ctx.cpu_group)
             res = self.generate(prompt_ids, min(self.max_new, 2))
             torch.cuda.synchronize(self.device)
         table = []
