@@ -46,8 +46,17 @@ Flow:
 
 A decode engine that already holds a block-aligned prefix (prefix caching)
 pulls only the suffix: the producer sends its last blocks and counts
-tokens from the suffix start.  Each decode TP rank pulls from the prefill
-rank of the same TP index (``session_port + tp_rank``); equal TP sizes.
+tokens from the suffix start.
+
+Tensor parallelism: prefill rank ``r`` serves on ``session_port + r``.  The
+two engines may use different TP sizes (``prefill_tp_size`` /
+``decode_tp_size`` in the extra config, defaults: this engine's size): the
+KV-head transfer plan (:func:`~kvserve_b200.session.tp_plan.transfer_plan`)
+gives each decode rank its heads as copies from the prefill ranks that hold
+them, and every copy is one session (transfer id ``T#<decode rank>.<first
+head>``) whose runtimes on both sides are bound to that head range of the
+caches; a request is loaded (or sent) once all its copies have ended.  Equal
+TP sizes are the one-copy case.
 Finished sessions append a JSONL row to ``KVSERVE_SESSION_STATS_PATH``.
 """
 from __future__ import annotations
@@ -214,13 +223,23 @@ class SessionKVConnector(KVConnectorBase_V1):
         self._extra = extra
         self._tp_size = int(getattr(vllm_config.parallel_config, "tensor_parallel_size", 1) or 1)
         self._tp_rank = 0
+        # TP sizes of the two engines (heterogeneous TP: KV-head copies)
+        self._p_tp = int(extra.get("prefill_tp_size", self._tp_size))
+        self._d_tp = int(extra.get("decode_tp_size", self._tp_size))
+        if (self._p_tp if cfg.is_kv_producer else self._d_tp) != self._tp_size:
+            raise ValueError("prefill_tp_size / decode_tp_size must match this engine's tensor_parallel_size")
+        total = getattr(getattr(vllm_config, "model_config", None), "get_total_num_kv_heads", None)
+        self._num_kv_heads = int(extra.get("num_kv_heads") or (total() if callable(total) else 0))
+        self._copies: list = []
         # scheduler state
         self._pending_sends: list[SendReq] = []
         self._pending_recvs: list[RecvReq] = []
         # worker state
         self._lock = threading.Lock()
-        self._send_rid: dict[str, str] = {}          # transfer id -> prefill request id
-        self._recv: dict[str, RecvReq] = {}          # transfer id -> load
+        self._send_rid: dict[str, str] = {}          # copy transfer id -> prefill request id
+        self._send_pending: dict[str, set] = {}      # prefill request id -> copy sessions not ended
+        self._recv: dict[str, RecvReq] = {}          # copy transfer id -> load
+        self._recv_pending: dict[str, set] = {}      # decode request id -> copy sessions not ended
         self._done_sending: set[str] = set()
         self._done_recving: set[str] = set()
         self._finished_seen: set[str] = set()
@@ -254,16 +273,54 @@ class SessionKVConnector(KVConnectorBase_V1):
             raise ValueError("SessionKVConnector runs the compression runtime; set enable-compression-pipeline")
         return cfg
 
-    def _build_runtime(self, kv_caches: dict, execution: str):
+    # ------------------------------------------------- heterogeneous TP
+    def copies(self) -> list:
+        """``(key, HeadCopy)`` of this worker: the KV-head ranges it sends
+        (prefill) or receives (decode) under the transfer plan between the
+        two TP groups; equal TP sizes give one full-shard copy."""
+        from ..session.tp_plan import transfer_plan
+        plan = transfer_plan(self._p_tp, self._d_tp, self._num_kv_heads)
+        mine = [c for c in plan if (c.src_rank if self.is_producer else c.dst_rank) == self._tp_rank]
+        return [(f"{c.dst_rank}.{c.dst_head}", c) for c in mine]
+
+    @staticmethod
+    def copy_tid(transfer_id: str, key: str) -> str:
+        return f"{transfer_id}#{key}"
+
+    @staticmethod
+    def copy_key(copy_transfer_id: str) -> str:
+        return copy_transfer_id.rsplit("#", 1)[1]
+
+    def _global_first(self, c) -> int:
+        from ..session.tp_plan import head_shard
+        if self.is_producer:
+            return head_shard(c.src_rank, self._p_tp, self._num_kv_heads).first + c.src_head
+        return head_shard(c.dst_rank, self._d_tp, self._num_kv_heads).first + c.dst_head
+
+    def _build_runtime(self, kv_caches: dict, execution: str, copy=None):
+        """The compression runtime over ``copy``'s KV heads of vLLM's caches
+        (all local heads without a copy).  Both peers build the runtime of a
+        copy over the same global heads, as the shard of a virtual TP split
+        into ``copy.heads``-head pieces, so head selection and signs agree."""
         from ..compression.runtime import CacheSpec, build_memory_plan, create_runtime
         cfg = self.runtime_config()
         specs, pairs = {}, {}
         for i, (name, t) in enumerate(kv_caches.items()):
             k, v = kv_pair(t)
+            if copy is not None:
+                h0 = copy.src_head if self.is_producer else copy.dst_head
+                k, v = k[:, :, h0:h0 + copy.heads], v[:, :, h0:h0 + copy.heads]
             specs[name] = CacheSpec(layer_index(name, i), k.shape[1], k.shape[2], k.shape[3], k.dtype)
             pairs[name] = (k, v)
         dev = next(iter(kv_caches.values())).device
-        plan = build_memory_plan(cfg, specs, tp_size=self._tp_size, tp_rank=self._tp_rank, device=dev)
+        if copy is None:
+            tp_size, tp_rank = self._tp_size, self._tp_rank
+        else:
+            first = self._global_first(copy)
+            if self._num_kv_heads % copy.heads or first % copy.heads:
+                raise ValueError(f"KV-head copy {copy} does not align with {self._num_kv_heads} heads")
+            tp_size, tp_rank = self._num_kv_heads // copy.heads, first // copy.heads
+        plan = build_memory_plan(cfg, specs, tp_size=tp_size, tp_rank=tp_rank, device=dev)
         rt = create_runtime(plan, "NHD", 1, dev, execution=execution)
         rt.bind_kv_caches(pairs)
         return rt, cfg
@@ -276,6 +333,9 @@ class SessionKVConnector(KVConnectorBase_V1):
             raise ValueError("no paged KV caches to register")
         dev = next(iter(caches.values())).device
         self._device = dev
+        if self._num_kv_heads <= 0:   # no model config: heads split (not replicated) over this TP group
+            self._num_kv_heads = kv_pair(next(iter(caches.values())))[0].shape[2] * self._tp_size
+        self._copies = self.copies()
         if self.is_producer:
             job = self.make_encode_job(caches)
             endpoint = f"tcp://*:{self._port + self._tp_rank}"
@@ -292,50 +352,65 @@ class SessionKVConnector(KVConnectorBase_V1):
         self._thread.wait_ready()
 
     def make_encode_job(self, caches: dict):
-        """The producer's ``encode_job``: the compression runtime bound to
-        vLLM's paged cache, encoding each pulled chunk into the consumer's
-        IPC-mapped slot."""
+        """The producer's ``encode_job``: per KV-head copy, the compression
+        runtime bound to those heads of vLLM's paged cache, encoding each
+        pulled chunk into the consumer's IPC-mapped slot; a session's copy
+        is named by its transfer id."""
         from ..session.gpu_jobs import RuntimeEncodeJob
-        rt, cfg = self._build_runtime(caches, "encode")
-        self._per_chunk = cfg.logical_blocks_per_chunk
-        job = RuntimeEncodeJob(rt, self._block_size, cfg.logical_blocks_per_chunk)
-        self._closers.append(job.close)
-        return job
+        jobs = {}
+        for key, c in self._copies:
+            rt, cfg = self._build_runtime(caches, "encode", c)
+            self._per_chunk = cfg.logical_blocks_per_chunk
+            jobs[key] = RuntimeEncodeJob(rt, self._block_size, cfg.logical_blocks_per_chunk)
+            self._closers.append(jobs[key].close)
+        return lambda session, pull: jobs[self.copy_key(session.transfer_id)](session, pull)
 
     def make_decode_job(self, caches: dict):
-        """The consumer's ``decode_job`` plus its receive arena's slot size
-        and CUDA-IPC handle."""
+        """The consumer's ``decode_job`` (per KV-head copy, the runtime bound
+        to those heads of its cache, reading one shared receive arena) plus
+        the arena's slot size and CUDA-IPC handle."""
         from ..session.gpu_jobs import ReceiveArena, RuntimeDecodeJob, part_bytes
-        rt, cfg = self._build_runtime(caches, "decode")
-        self._per_chunk = cfg.logical_blocks_per_chunk
-        arena = ReceiveArena(self._num_slots, 2 * part_bytes(rt), rt.device)
+        built = [(key, *self._build_runtime(caches, "decode", c)) for key, c in self._copies]
+        self._per_chunk = built[0][2].logical_blocks_per_chunk
+        arena = ReceiveArena(self._num_slots, 2 * max(part_bytes(rt) for _, rt, _ in built), built[0][1].device)
         self._closers.append(arena.close)
-        return RuntimeDecodeJob(rt, arena, self._block_size, cfg.logical_blocks_per_chunk), arena.slot_bytes, \
-            arena.handle
+        jobs = {key: RuntimeDecodeJob(rt, arena, self._block_size, cfg.logical_blocks_per_chunk)
+                for key, rt, cfg in built}
+        return (lambda session, slot, ready: jobs[self.copy_key(session.transfer_id)](session, slot, ready)), \
+            arena.slot_bytes, arena.handle
 
     def start_load_kv(self, forward_context, **kwargs) -> None:
         meta = self._get_connector_metadata()
         if not isinstance(meta, SessionConnectorMetadata) or self._thread is None:
             return
         for tid in meta.cancels:
-            with self._lock:
-                self._send_rid.pop(tid, None)
-            self._thread.submit(lambda svc, tid=tid: svc.cancel(tid, "request not sent"))
+            for key, _ in self._copies:
+                ct = self.copy_tid(tid, key)
+                with self._lock:
+                    rid = self._send_rid.pop(ct, None)
+                    if rid is not None:
+                        self._send_pending.pop(rid, None)
+                self._thread.submit(lambda svc, ct=ct: svc.cancel(ct, "request not sent"))
         # sends are registered once this step's forward (which completes
         # their prompt KV) is enqueued: see wait_for_save
         self._sends_this_step = list(meta.sends)
         for r in meta.recvs:
             with self._lock:
-                self._recv[r.transfer_id] = r
-            endpoint = f"tcp://{r.host}:{r.port + self._tp_rank}"
-            self._thread.submit(lambda svc, r=r, ep=endpoint, pc=self._per_chunk: svc.open(
-                ep, r.transfer_id, r.request_id, [list(r.block_ids)], r.num_tokens, block_size=self._block_size,
-                logical_blocks_per_chunk=pc))
+                self._recv_pending[r.request_id] = {self.copy_tid(r.transfer_id, k) for k, _ in self._copies}
+                for key, _ in self._copies:
+                    self._recv[self.copy_tid(r.transfer_id, key)] = r
+            for key, c in self._copies:
+                endpoint = f"tcp://{r.host}:{r.port + c.src_rank}"
+                self._thread.submit(lambda svc, r=r, ep=endpoint, ct=self.copy_tid(r.transfer_id, key),
+                                    pc=self._per_chunk: svc.open(
+                    ep, ct, r.request_id, [list(r.block_ids)], r.num_tokens, block_size=self._block_size,
+                    logical_blocks_per_chunk=pc))
 
     def wait_for_save(self) -> None:
         """After the forward that completes the sends' prompt KV has been
-        enqueued: register each send with an event on the forward's stream,
-        which the encode job waits for before it reads the blocks."""
+        enqueued: register each send (one session per KV-head copy) with an
+        event on the forward's stream, which the encode job waits for before
+        it reads the blocks."""
         sends, self._sends_this_step = self._sends_this_step, []
         if not sends or self._thread is None:
             return
@@ -344,13 +419,18 @@ class SessionKVConnector(KVConnectorBase_V1):
             ev = torch.cuda.Event()
             ev.record(torch.cuda.current_stream(self._device))
         for snd in sends:
+            cts = [self.copy_tid(snd.transfer_id, key) for key, _ in self._copies]
             with self._lock:
-                self._send_rid[snd.transfer_id] = snd.request_id
-            self._thread.submit(lambda svc, snd=snd: svc.add_send(snd.transfer_id, [list(snd.block_ids)],
-                                                                  snd.num_tokens, send_meta=ev))
+                self._send_pending[snd.request_id] = set(cts)
+                for ct in cts:
+                    self._send_rid[ct] = snd.request_id
+            for ct in cts:
+                self._thread.submit(lambda svc, ct=ct, snd=snd: svc.add_send(ct, [list(snd.block_ids)],
+                                                                            snd.num_tokens, send_meta=ev))
 
     def _collect_sends(self, svc) -> None:
-        """Producer thread: move ended sessions into the finished-sending set."""
+        """Producer thread: ended sessions; a request is sent once every
+        copy's session has ended."""
         if not svc.finished:
             return
         ended, svc.finished[:] = list(svc.finished), []
@@ -359,11 +439,16 @@ class SessionKVConnector(KVConnectorBase_V1):
                                  "chunks": s.completed_chunks, "error": s.error})
             with self._lock:
                 rid = self._send_rid.pop(s.transfer_id, None)
-                if rid is not None:
-                    self._done_sending.add(rid)
+                pending = self._send_pending.get(rid) if rid is not None else None
+                if pending is not None:
+                    pending.discard(s.transfer_id)
+                    if not pending:
+                        del self._send_pending[rid]
+                        self._done_sending.add(rid)
 
     def _on_recv_done(self, s) -> None:
-        """Consumer thread: a load ended (complete, failed or timed out)."""
+        """Consumer thread: one copy's load ended (complete, failed or timed
+        out); the request is reported once all its copies have ended."""
         from ..session.state import SessionState
         with self._lock:
             r = self._recv.pop(s.transfer_id, None)
@@ -371,7 +456,12 @@ class SessionKVConnector(KVConnectorBase_V1):
                 return
             if s.state is not SessionState.COMPLETE:
                 self._load_errors.update(r.block_ids)
-            self._done_recving.add(r.request_id)
+            pending = self._recv_pending.get(r.request_id)
+            if pending is not None:
+                pending.discard(s.transfer_id)
+                if not pending:
+                    del self._recv_pending[r.request_id]
+                    self._done_recving.add(r.request_id)
         write_session_stats({"direction": "recv", "transfer_id": s.transfer_id, "request_id": r.request_id,
                              "state": s.state.name, "chunks": s.completed_chunks, "total_chunks": s.total_chunks,
                              "error": s.error})
@@ -421,6 +511,11 @@ class SessionKVConnector(KVConnectorBase_V1):
     def get_num_new_matched_tokens(self, request, num_computed_tokens: int):
         params = getattr(request, "kv_transfer_params", None) or {}
         if self.is_producer or not params.get("do_remote_prefill") or "remote_port" not in params:
+            return 0, False
+        if int(params.get("remote_tp_size", self._p_tp)) != self._p_tp:
+            # the copy plan is built for the configured prefill TP size: compute locally instead
+            log.warning("request %s comes from a prefill engine of TP %s, configured for %s: not loaded",
+                        request.request_id, params.get("remote_tp_size"), self._p_tp)
             return 0, False
         n = len(request.prompt_token_ids or []) - num_computed_tokens
         return (n, True) if n > 0 else (0, False)

@@ -217,3 +217,89 @@ def test_unknown_transfer_reports_load_errors():
     finally:
         p_work.shutdown()
         d_work.shutdown()
+
+
+class FakeHeadJobs(SessionKVConnector):
+    """Like :class:`FakeJobs`, but each session copies only its KV-head
+    range (the copy named by the transfer id) — the GPU jobs bind one
+    runtime per copy to the same head slices."""
+    arena: dict = {}
+
+    def make_encode_job(self, caches):
+        cache = next(iter(caches.values()))
+        copies = dict(self._copies)
+        self._per_chunk = PER_CHUNK
+
+        def enc(session, pull):
+            c = copies[self.copy_key(session.transfer_id)]
+            ids = session.local_block_ids[0][pull.chunk_id * PER_CHUNK:(pull.chunk_id + 1) * PER_CHUNK]
+            FakeHeadJobs.arena[(session.transfer_id, pull.slot_id)] = \
+                cache[:, ids, :, c.src_head:c.src_head + c.heads].clone()
+            return 1, 1
+        return enc
+
+    def make_decode_job(self, caches):
+        cache = next(iter(caches.values()))
+        copies = dict(self._copies)
+        self._per_chunk = PER_CHUNK
+
+        def dec(session, slot, ready):
+            c = copies[self.copy_key(session.transfer_id)]
+            ids = session.block_ids[0][ready.chunk_id * PER_CHUNK:(ready.chunk_id + 1) * PER_CHUNK]
+            cache[:, ids, :, c.dst_head:c.dst_head + c.heads] = FakeHeadJobs.arena[(session.transfer_id,
+                                                                                     slot.slot_id)]
+        return dec, 1 << 20, b""
+
+
+def _tp_config(producer, port, tp, p_tp, d_tp):
+    cfgs = _vllm_config(producer, port)
+    cfgs.parallel_config = NS(tensor_parallel_size=tp)
+    cfgs.kv_transfer_config.kv_connector_extra_config.update(prefill_tp_size=p_tp, decode_tp_size=d_tp,
+                                                             num_kv_heads=4)
+    return cfgs
+
+
+def test_heterogeneous_tp_pulls_each_head_range_from_its_holder():
+    """Prefill TP 1 (4 KV heads) -> decode TP 2 (2 heads per rank): each
+    decode rank opens one session for its half of the heads; the prefill
+    rank serves both and reports the request sent after both end."""
+    port = _port()
+    src = torch.randn(2, NB, BS, 4, 64).to(torch.bfloat16)
+    dst = [torch.zeros(2, NB, BS, 2, 64, dtype=torch.bfloat16) for _ in range(2)]
+    p_sched = FakeHeadJobs(_tp_config(True, port, 1, 1, 2), KVConnectorRole.SCHEDULER)
+    p_work = FakeHeadJobs(_tp_config(True, port, 1, 1, 2), KVConnectorRole.WORKER)
+    d_sched, d_work = [], []
+    for rank in range(2):
+        d_sched.append(FakeHeadJobs(_tp_config(False, port, 2, 1, 2), KVConnectorRole.SCHEDULER))
+        w = FakeHeadJobs(_tp_config(False, port, 2, 1, 2), KVConnectorRole.WORKER)
+        w._tp_rank = rank
+        d_work.append(w)
+    try:
+        p_work.register_kv_caches({"model.layers.0.self_attn.attn": src})
+        for w, d in zip(d_work, dst):
+            w.register_kv_caches({"model.layers.0.self_attn.attn": d})
+        assert [k for k, _ in p_work._copies] == ["0.0", "1.0"]
+        assert [(c.src_rank, c.src_head, c.heads) for _, c in d_work[1]._copies] == [(0, 2, 2)]
+        prompt, p_blocks, d_blocks = 100, list(range(0, 7)), list(range(10, 17))
+        delay, params = _prefill(p_sched, p_work, "p1", "t1", prompt, p_blocks)
+        assert delay and params["remote_tp_size"] == 1
+        for rank in range(2):
+            dreq = _req("d1", prompt, dict(params), status="WAITING_FOR_REMOTE_KVS")
+            assert d_sched[rank].get_num_new_matched_tokens(dreq, 0) == (prompt, True)
+            d_sched[rank].update_state_after_alloc(dreq, Blocks(d_blocks, d_blocks), prompt)
+        for rank in range(2):
+            assert _wait_recv(d_sched[rank], d_work[rank], "d1")
+            assert torch.equal(dst[rank][:, d_blocks], src[:, p_blocks, :, 2 * rank:2 * rank + 2])
+        deadline = time.monotonic() + 10
+        sending = None
+        while time.monotonic() < deadline and not sending:
+            sending, _ = _step(p_sched, p_work)
+            time.sleep(0.01)
+        assert sending == {"p1"}
+        # a decode request from a prefill engine of another TP size is computed locally
+        other = dict(params, remote_tp_size=4, do_remote_prefill=True)
+        assert d_sched[0].get_num_new_matched_tokens(_req("d9", prompt, other), 0) == (0, False)
+    finally:
+        p_work.shutdown()
+        for w in d_work:
+            w.shutdown()
