@@ -208,6 +208,55 @@ class ServiceThread(threading.Thread):
             self.join(timeout)
 
 
+class _HelperProxy:
+    """The service methods the connector calls, forwarded to a session helper
+    process (:mod:`kvserve_b200.session.process`).  Send events stay in this
+    process, keyed by transfer id."""
+
+    def __init__(self, proc, events: dict):
+        self.proc, self.events = proc, events
+        self.finished: list = []
+
+    def add_send(self, transfer_id, local_block_ids, num_tokens, send_meta=None):
+        from ..session.process import AddSend
+        if send_meta is not None:
+            self.events[transfer_id] = send_meta
+        self.proc.request(AddSend(transfer_id, local_block_ids, num_tokens, None))
+
+    def open(self, endpoint, transfer_id, d_req_id, block_ids, num_tokens, block_size=16,
+             logical_blocks_per_chunk=1):
+        from ..session.process import Open
+        self.proc.request(Open(endpoint, transfer_id, d_req_id, block_ids, num_tokens, block_size,
+                               logical_blocks_per_chunk))
+
+    def cancel(self, transfer_id, reason):
+        from ..session.process import Abort
+        self.proc.request(Abort(transfer_id, reason))
+
+    abort = cancel
+
+    def poll(self, timeout_ms: int = 0) -> int:
+        """Run the helper's pending GPU jobs here and collect ended sessions
+        (as objects shaped like the services' sessions)."""
+        from types import SimpleNamespace
+
+        from ..session.state import SessionState
+        n = self.proc.serve_jobs(timeout_ms / 1000.0)
+        if self.proc.done:
+            for d in self.proc.done:
+                self.events.pop(d.transfer_id, None)
+                self.finished.append(SimpleNamespace(transfer_id=d.transfer_id, state=SessionState[d.state],
+                                                     error=d.error, completed_chunks=d.completed_chunks,
+                                                     total_chunks=d.total_chunks))
+            self.proc.done.clear()
+        if not self.proc.proc.is_alive():
+            raise RuntimeError("the session helper process exited")
+        return n
+
+    def close(self) -> None:
+        self.proc.stop()
+
+
 class SessionKVConnector(KVConnectorBase_V1):
     def __init__(self, vllm_config, role, kv_cache_config=None):
         super().__init__(vllm_config, role, kv_cache_config)
@@ -247,6 +296,8 @@ class SessionKVConnector(KVConnectorBase_V1):
         self._thread: Optional[ServiceThread] = None
         self._closers: list[Callable[[], None]] = []
         self._per_chunk = 1
+        self._use_helper = bool(extra.get("session_process", os.environ.get("KVSERVE_SESSION_PROCESS", "0")
+                                          .strip().lower() in {"1", "true", "yes", "on"}))
         self._device: Optional[torch.device] = None
         self._sends_this_step: list[SendReq] = []
         # scheduler: remote-decode requests -> (transfer id, prompt length,
@@ -339,17 +390,65 @@ class SessionKVConnector(KVConnectorBase_V1):
         if self.is_producer:
             job = self.make_encode_job(caches)
             endpoint = f"tcp://*:{self._port + self._tp_rank}"
-            self._thread = ServiceThread(lambda: ProducerService(endpoint, job, self._open_timeout_s), dev,
-                                         self._collect_sends)
+            if self._use_helper:
+                make = lambda: self._helper("producer", {"endpoint": endpoint,  # noqa: E731
+                                                         "open_timeout_s": self._open_timeout_s}, job)
+            else:
+                make = lambda: ProducerService(endpoint, job, self._open_timeout_s)  # noqa: E731
+            self._thread = ServiceThread(make, dev, self._collect_sends)
         else:
             job, slot_bytes, handle = self.make_decode_job(caches)
             name = f"kvs-d{self._tp_rank}-{os.getpid()}"
-            self._thread = ServiceThread(
-                lambda: ConsumerService(name, self._num_slots, slot_bytes, job, self._on_recv_done,
-                                        self._session_timeout_s, arena_ipc_handle=handle), dev,
-                lambda svc: svc.finished.clear())
+            if self._use_helper:
+                def make():
+                    proxy = self._helper("consumer", {"name": name, "num_slots": self._num_slots,
+                                                      "slot_bytes": slot_bytes,
+                                                      "session_timeout_s": self._session_timeout_s,
+                                                      "arena_ipc_handle": handle}, job)
+                    return proxy
+                after = self._collect_recvs
+            else:
+                def make():
+                    return ConsumerService(name, self._num_slots, slot_bytes, job, self._on_recv_done,
+                                           self._session_timeout_s, arena_ipc_handle=handle)
+                after = lambda svc: svc.finished.clear()  # noqa: E731
+            self._thread = ServiceThread(make, dev, after)
         self._thread.start()
         self._thread.wait_ready()
+
+    def _helper(self, role: str, cfg: dict, job) -> _HelperProxy:
+        """Start the session helper process; its GPU jobs run ``job`` on the
+        service thread of this process."""
+        from types import SimpleNamespace
+
+        from ..session.process import DecodeChunkJob, DrainSlotsJob, EncodeChunkJob, SessionProcess
+        events: dict = {}
+
+        def encode(j):
+            sess = SimpleNamespace(transfer_id=j.transfer_id, remote_meta=j.remote_meta,
+                                   send_meta=events.get(j.transfer_id), local_block_ids=j.local_block_ids,
+                                   valid_tokens_by_group=j.valid_tokens_by_group)
+            pull = SimpleNamespace(chunk_id=j.chunk_id, slot_id=j.slot_id, slot_offset=j.slot_offset,
+                                   flag_index=j.flag_index, transfer_id=j.transfer_id)
+            return job(sess, pull)
+
+        def decode(j):
+            sess = SimpleNamespace(transfer_id=j.transfer_id, block_ids=j.block_ids,
+                                   valid_tokens_by_group=j.valid_tokens_by_group)
+            slot = SimpleNamespace(slot_id=j.slot_id, offset=j.slot_offset)
+            ready = SimpleNamespace(chunk_id=j.chunk_id, payload_bytes=j.payload_bytes)
+            return job(sess, slot, ready)
+
+        handlers = {DrainSlotsJob: lambda j: None}
+        handlers[EncodeChunkJob if role == "producer" else DecodeChunkJob] = encode if role == "producer" \
+            else decode
+        return _HelperProxy(SessionProcess(role, cfg, handlers), events)
+
+    def _collect_recvs(self, proxy) -> None:
+        """Consumer with a helper process: ended sessions arrive as reports."""
+        ended, proxy.finished[:] = list(proxy.finished), []
+        for s in ended:
+            self._on_recv_done(s)
 
     def make_encode_job(self, caches: dict):
         """The producer's ``encode_job``: per KV-head copy, the compression

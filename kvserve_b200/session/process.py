@@ -12,8 +12,14 @@ When a service needs a kernel run it sends a short job over a
 * ``DrainSlotsJob`` (either side, at shutdown) -> ``None``.
 
 Control requests from the engine (``AddSend``, ``Open``, ``Abort``,
-``Stop``) travel the other way on a second pipe.  ``KVSERVE_SESSION_PROCESS``
-(default on) selects the helper; off runs the same service in-process.
+``Stop``) travel the other way on a second pipe, and ``SessionDone`` reports
+ended sessions back.  The session connector runs its service in this helper
+with ``KVSERVE_SESSION_PROCESS=1`` (or ``session_process`` in its extra
+config); otherwise the same service runs on a thread of the engine process.
+Jobs carry everything a GPU job needs that lives in the helper (the
+consumer's metadata with its arena handle, the valid token counts after
+suffix trimming); objects that cannot cross a pipe (CUDA events) stay in the
+engine process, keyed by transfer id.
 """
 from __future__ import annotations
 
@@ -26,7 +32,7 @@ from .service import ConsumerService, ProducerService
 
 
 def session_process_enabled() -> bool:
-    return os.environ.get("KVSERVE_SESSION_PROCESS", "1").strip().lower() not in {"0", "false", "no", "off"}
+    return os.environ.get("KVSERVE_SESSION_PROCESS", "0").strip().lower() in {"1", "true", "yes", "on"}
 
 
 # ----------------------------------------------------------------- messages
@@ -40,6 +46,8 @@ class EncodeChunkJob:
     local_block_ids: Any
     remote_block_ids: Any
     send_meta: Any
+    remote_meta: Any = None             # the consumer's XferMetadata (arena handle, slot size)
+    valid_tokens_by_group: Any = None
 
 
 @dataclass(frozen=True)
@@ -51,6 +59,7 @@ class DecodeChunkJob:
     slot_offset: int
     block_ids: Any
     payload_bytes: int
+    valid_tokens_by_group: Any = None
 
 
 @dataclass(frozen=True)
@@ -94,6 +103,7 @@ class SessionDone:
     state: str
     error: Optional[str]
     completed_chunks: int
+    total_chunks: int = 0
 
 
 # ------------------------------------------------------------ helper side
@@ -108,14 +118,15 @@ def _helper_main(role: str, cfg: dict, ctl, jobs) -> None:
     if role == "producer":
         svc = ProducerService(cfg["endpoint"], lambda s, m: run_job(EncodeChunkJob(
             s.transfer_id, m.chunk_id, m.slot_id, m.slot_offset, m.flag_index, s.local_block_ids,
-            s.remote_block_ids, s.send_meta)), cfg.get("open_timeout_s", 30.0))
+            s.remote_block_ids, s.send_meta, s.remote_meta, dict(s.valid_tokens_by_group))),
+            cfg.get("open_timeout_s", 30.0))
     else:
         def done(s):
-            ctl.send(SessionDone(s.transfer_id, s.state.name, s.error, s.completed_chunks))
+            ctl.send(SessionDone(s.transfer_id, s.state.name, s.error, s.completed_chunks, s.total_chunks))
         svc = ConsumerService(cfg["name"], cfg["num_slots"], cfg["slot_bytes"], lambda s, slot, m: run_job(
             DecodeChunkJob(s.transfer_id, s.d_req_id, m.chunk_id, slot.slot_id, slot.offset, s.block_ids,
-                           m.payload_bytes)), done, cfg.get("session_timeout_s", 60.0),
-            cfg.get("arena_ipc_handle", b""), cfg.get("flags_ipc_handle", b""))
+                           m.payload_bytes, dict(s.valid_tokens_by_group))), done,
+            cfg.get("session_timeout_s", 60.0), cfg.get("arena_ipc_handle", b""), cfg.get("flags_ipc_handle", b""))
     ctl.send("ready")
     try:
         while True:
@@ -130,11 +141,14 @@ def _helper_main(role: str, cfg: dict, ctl, jobs) -> None:
                     svc.open(req.endpoint, req.transfer_id, req.d_req_id, req.block_ids, req.num_tokens,
                              req.block_size, req.logical_blocks_per_chunk)
                 elif isinstance(req, Abort):
-                    svc.abort(req.transfer_id, req.reason)
+                    # a producer withdraws its registered send; a consumer aborts its session
+                    (svc.cancel if role == "producer" else svc.abort)(req.transfer_id, req.reason)
             svc.poll(5)
             if role == "producer":
                 for s in svc.finished:
-                    ctl.send(SessionDone(s.transfer_id, s.state.name, s.error, s.completed_chunks))
+                    ctl.send(SessionDone(s.transfer_id, s.state.name, s.error, s.completed_chunks, s.total_chunks))
+                svc.finished.clear()
+            else:
                 svc.finished.clear()
     finally:
         svc.close()

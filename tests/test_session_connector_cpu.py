@@ -14,6 +14,7 @@ import socket
 import time
 from types import SimpleNamespace as NS
 
+import pytest
 import torch
 
 from kvserve_b200.connector.session_kv_connector import (KVConnectorRole, SessionConnectorMetadata,
@@ -30,13 +31,14 @@ def _port():
     return p
 
 
-def _vllm_config(producer: bool, port: int):
+def _vllm_config(producer: bool, port: int, helper: bool = False):
     comp = {"enable-compression-pipeline": True, "pipeline": ["transformer", "quantizer"],
             "logical_blocks_per_chunk": PER_CHUNK}
     return NS(kv_transfer_config=NS(is_kv_producer=producer, kv_ip="127.0.0.1",
                                     kv_connector_extra_config={"session_port": port, "num_slots": 2,
                                                                "compression": comp, "open_timeout_s": 5.0,
-                                                               "session_timeout_s": 10.0}),
+                                                               "session_timeout_s": 10.0,
+                                                               "session_process": helper}),
               cache_config=NS(block_size=BS), parallel_config=NS(tensor_parallel_size=1),
               model_config=NS(use_mla=False))
 
@@ -85,13 +87,13 @@ def _req(rid, prompt_len, params, status="FINISHED_LENGTH_CAPPED"):
               status=NS(name=status))
 
 
-def _pair(port):
+def _pair(port, helper=False):
     src = torch.randn(2, NB, BS, 2, 64).to(torch.bfloat16)
     dst = torch.zeros_like(src)
     p_sched = FakeJobs(_vllm_config(True, port), KVConnectorRole.SCHEDULER)
     d_sched = FakeJobs(_vllm_config(False, port), KVConnectorRole.SCHEDULER)
-    p_work = FakeJobs(_vllm_config(True, port), KVConnectorRole.WORKER)
-    d_work = FakeJobs(_vllm_config(False, port), KVConnectorRole.WORKER)
+    p_work = FakeJobs(_vllm_config(True, port, helper), KVConnectorRole.WORKER)
+    d_work = FakeJobs(_vllm_config(False, port, helper), KVConnectorRole.WORKER)
     p_work.register_kv_caches({"model.layers.0.self_attn.attn": src})
     d_work.register_kv_caches({"model.layers.0.self_attn.attn": dst})
     return src, dst, p_sched, d_sched, p_work, d_work
@@ -145,10 +147,16 @@ def test_helpers_parse_vllm_names_and_layouts():
     assert k.shape == (3, 16, 2, 8) and k.stride() == v.stride()
 
 
-def test_pull_moves_every_chunk_and_both_sides_report():
+@pytest.mark.parametrize("helper", [False, True], ids=["service-thread", "helper-process"])
+def test_pull_moves_every_chunk_and_both_sides_report(helper):
+    """Also with the session services in helper processes (the GPU jobs
+    still run in the engine processes, fed over pipes)."""
     FakeJobs.seen.clear()
-    src, dst, p_sched, d_sched, p_work, d_work = _pair(_port())
+    src, dst, p_sched, d_sched, p_work, d_work = _pair(_port(), helper)
     try:
+        from kvserve_b200.connector.session_kv_connector import _HelperProxy
+        assert isinstance(p_work._thread.service, _HelperProxy) == helper
+        assert isinstance(d_work._thread.service, _HelperProxy) == helper
         prompt, p_blocks, d_blocks = 100, list(range(0, 7)), list(range(20, 27))
         delay, params = _prefill(p_sched, p_work, "p1", "t1", prompt, p_blocks)
         assert delay and params["do_remote_prefill"] and params["transfer_id"] == "t1"
@@ -191,8 +199,9 @@ def test_cached_prefix_pulls_only_the_suffix():
         d_work.shutdown()
 
 
-def test_unknown_transfer_reports_load_errors():
-    src, dst, p_sched, d_sched, p_work, d_work = _pair(_port())
+@pytest.mark.parametrize("helper", [False, True], ids=["service-thread", "helper-process"])
+def test_unknown_transfer_reports_load_errors(helper):
+    src, dst, p_sched, d_sched, p_work, d_work = _pair(_port(), helper)
     try:
         params = {"do_remote_prefill": True, "transfer_id": "nope", "remote_host": "127.0.0.1",
                   "remote_port": p_sched._port}
