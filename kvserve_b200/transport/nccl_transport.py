@@ -284,8 +284,10 @@ class _IpcPlane:
             self._tickets[ticket] = threading.Event()
         return tensors, {"pool": self.pool_handle, "grants": grants, "ticket": ticket}
 
-    def alloc(self, shape, dtype) -> torch.Tensor:   # unused: grant() places tensors
-        raise NotImplementedError
+    def alloc(self, shape, dtype) -> torch.Tensor:
+        # the other planes allocate receive tensors here; this one places
+        # them inside the exported pool with grant()
+        raise RuntimeError("the IPC data plane places received tensors with grant(), not alloc()")
 
     def recv(self, tensors: list, ticket: int = -1):
         return (time.perf_counter(), self._tickets[ticket], ticket)
