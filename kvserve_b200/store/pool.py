@@ -4,7 +4,14 @@ byte budget the least recently used values move down one tier (a device to
 host copy, or a host tensor written to disk); ``get`` promotes the value
 back to the device tier.  A background thread performs disk writes so a put
 never waits on the filesystem.  Counters are exported as Prometheus metrics
-in a private registry (``pool.registry``)."""
+in a private registry (``pool.registry``).
+
+``shared=True`` (needs ``disk_dir``) makes the directory the store that
+several processes share — the engines of one node, or a scheduler process
+that only looks keys up: every put is also written through to its file, and
+``contains`` / ``get`` consult the directory for keys this process never
+held.  Files are written under a temporary name and renamed, so a reader
+sees a whole value or none."""
 from __future__ import annotations
 
 import os
@@ -17,7 +24,11 @@ import torch
 
 
 class TieredKVPool:
-    def __init__(self, device_bytes: int, host_bytes: int, disk_dir: Optional[str] = None, device=None):
+    def __init__(self, device_bytes: int, host_bytes: int, disk_dir: Optional[str] = None, device=None,
+                 shared: bool = False):
+        if shared and not disk_dir:
+            raise ValueError("a shared pool needs disk_dir")
+        self.shared = shared
         self.device = torch.device(device) if device is not None else (
             torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu"))
         self.budget = {"device": int(device_bytes), "host": int(host_bytes)}
@@ -73,7 +84,9 @@ class TieredKVPool:
                 return
             key, value = item
             path = self._path(key)
-            torch.save(value, path)
+            tmp = f"{path}.{os.getpid()}.{threading.get_ident()}.tmp"
+            torch.save(self._to(value, torch.device("cpu")), tmp)
+            os.replace(tmp, path)
             with self._lock:
                 if self._pending_disk.get(key) is value:
                     self._pending_disk.pop(key)
@@ -95,7 +108,7 @@ class TieredKVPool:
             self.m_evict.labels(tier).inc()
             if tier == "device":
                 self._insert("host", key, self._to(value, torch.device("cpu"), pin=True))
-            elif self.disk_dir:
+            elif self.disk_dir and not (self.shared and key in self.on_disk):
                 self._pending_disk[key] = value
                 self._disk_q.put((key, value))
         for name in ("device", "host"):
@@ -105,7 +118,11 @@ class TieredKVPool:
     def put(self, key: str, value: Any) -> None:
         with self._lock:
             self._drop(key)
-            self._insert("device", key, self._to(value, self.device))
+            dev = self._to(value, self.device)
+            self._insert("device", key, dev)
+            if self.shared and key not in self._pending_disk:
+                self._pending_disk[key] = dev      # write through: other processes read the file
+                self._disk_q.put((key, dev))
 
     def _drop(self, key: str) -> None:
         for tier in ("device", "host"):
@@ -119,7 +136,9 @@ class TieredKVPool:
 
     def contains(self, key: str) -> bool:
         with self._lock:
-            return any(key in t for t in self.tiers.values()) or key in self._pending_disk or key in self.on_disk
+            if any(key in t for t in self.tiers.values()) or key in self._pending_disk or key in self.on_disk:
+                return True
+        return self.shared and os.path.exists(self._path(key))
 
     def tier_of(self, key: str) -> Optional[str]:
         with self._lock:
@@ -148,11 +167,15 @@ class TieredKVPool:
             value = self._pending_disk.get(key)
             if value is None and key in self.on_disk:
                 value = torch.load(self.on_disk[key], weights_only=True)
+            elif value is None and self.shared and os.path.exists(self._path(key)):
+                value = torch.load(self._path(key), weights_only=True)   # written by another process
+                self.on_disk[key] = self._path(key)
             if value is None:
                 self.m_miss.inc()
                 return None
             self.m_hits.labels("disk").inc()
-            self._drop(key)
+            if not self.shared:
+                self._drop(key)
             dev = self._to(value, self.device)
             self._insert("device", key, dev)
             return dev
