@@ -136,6 +136,23 @@ class ModelAccuracyEvaluator:
         return self.last["avg_score"]
 
 
+@torch.no_grad()
+def capture_kv(model: torch.nn.Module, prompts: Sequence[torch.Tensor], dtype=torch.bfloat16) -> torch.Tensor:
+    """The prefill KV a causal LM produces for ``prompts`` (equal lengths), as
+    the ``[L, 2, B, S, H, D]`` sample the offline search and the evaluators
+    take (role of the reference's KV fixture capture,
+    scripts/capture_kv_fixture.py)."""
+    from transformers import DynamicCache
+    ids = torch.stack([p.reshape(-1).long() for p in prompts])
+    cache = DynamicCache()
+    model(input_ids=ids, past_key_values=cache, use_cache=True)
+    layers = []
+    for layer in cache.layers:
+        k, v = layer.keys, layer.values                 # [B, H, S, D]
+        layers.append(torch.stack([k, v]).permute(0, 1, 3, 2, 4))
+    return torch.stack(layers).to(dtype)
+
+
 def synthetic_prompts(count: int, length: int, vocab: int, seed: int = 0) -> list[torch.Tensor]:
     g = torch.Generator().manual_seed(seed)
     return [torch.randint(0, vocab, (length,), generator=g) for _ in range(count)]
@@ -148,14 +165,18 @@ def main() -> None:
     ap.add_argument("--prompts", type=int, default=4)
     ap.add_argument("--prompt-len", type=int, default=256)
     ap.add_argument("--new-tokens", type=int, default=16)
+    ap.add_argument("--capture", default=None,
+                    help="also save the prompts' prefill KV [L, 2, B, S, H, D] here (for search --kv)")
     args = ap.parse_args()
     if args.model:
         from transformers import AutoModelForCausalLM
         model = AutoModelForCausalLM.from_pretrained(args.model, torch_dtype=torch.float32).eval()
     else:
         model = tiny_llama()
-    ev = ModelAccuracyEvaluator(model, synthetic_prompts(args.prompts, args.prompt_len, model.config.vocab_size),
-                                new_tokens=args.new_tokens)
+    prompts = synthetic_prompts(args.prompts, args.prompt_len, model.config.vocab_size)
+    if args.capture:
+        torch.save(capture_kv(model, prompts), args.capture)
+    ev = ModelAccuracyEvaluator(model, prompts, new_tokens=args.new_tokens)
     for path in args.profiles:
         with open(path) as f:
             prof = json.load(f)

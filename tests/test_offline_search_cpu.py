@@ -122,3 +122,15 @@ def test_search_runs_on_the_model_evaluator(tmp_path):
     out = run(str(tmp_path), kv, tolerances=(50.0,), budget=4, levels=(16, 4), ratios=(0.0,),
               model_accuracy=ev.evaluate)
     assert 0.0 <= out["results"]["baseline"]["accuracy"] <= 1.0
+
+
+def test_captured_model_kv_feeds_the_search(tmp_path):
+    """KV captured from a language model's prefill ([L, 2, B, S, H, D]) is
+    the sample the search and its evaluators take."""
+    import torch
+    from kvserve_b200.offline_search.model_eval import capture_kv, synthetic_prompts, tiny_llama
+    lm = tiny_llama(layers=2, hidden=128, heads=2, kv_heads=1, vocab=256)
+    kv = capture_kv(lm, synthetic_prompts(2, 64, 256))
+    assert kv.shape == (2, 2, 2, 64, 1, 64) and kv.dtype == torch.bfloat16
+    out = run(str(tmp_path), kv, tolerances=(5.0,), budget=4, levels=(16, 4), ratios=(0.0,))
+    assert out["results"]["5.0"]["evaluated"] >= 1
