@@ -138,29 +138,29 @@ def _bf16(x: torch.Tensor) -> torch.Tensor:
 
 
 def _pack_bits(sym: np.ndarray, bits: int) -> bytes:
-    """LSB-first packing of uint8 symbols (BitPack stream, no header)."""
-    sym = sym.astype(np.uint64).reshape(-1)
-    n = sym.size
-    nbytes = (n * bits + 7) // 8
-    out = np.zeros(nbytes + 8, dtype=np.uint8)
-    bitpos = np.arange(n, dtype=np.uint64) * np.uint64(bits)
-    for b in range(bits):
-        bit = (sym >> np.uint64(b)) & np.uint64(1)
-        pos = bitpos + np.uint64(b)
-        np.bitwise_or.at(out, (pos >> np.uint64(3)).astype(np.int64),
-                         (bit << (pos & np.uint64(7))).astype(np.uint8))
-    return out[:nbytes].tobytes()
+    """LSB-first packing of uint8 symbols (BitPack stream, no header): bit
+    ``b`` of symbol ``i`` is bit ``i * bits + b`` of the stream, and stream
+    bit ``j`` is bit ``j % 8`` of byte ``j // 8``."""
+    sym = np.ascontiguousarray(sym, dtype=np.uint8).reshape(-1)
+    if bits in (1, 2, 4, 8):              # whole symbols per byte: shift and add
+        per = 8 // bits
+        pad = (-sym.size) % per
+        grp = np.concatenate([sym, np.zeros(pad, dtype=np.uint8)]).reshape(-1, per)
+        shifts = (np.arange(per, dtype=np.uint8) * bits)
+        return np.bitwise_or.reduce(grp << shifts, axis=1).astype(np.uint8).tobytes()
+    planes = np.unpackbits(sym.reshape(-1, 1), axis=1, bitorder="little")[:, :bits]   # [n, bits]
+    return np.packbits(planes.reshape(-1), bitorder="little").tobytes()
 
 
 def _unpack_bits(buf: bytes, bits: int, n: int) -> np.ndarray:
     arr = np.frombuffer(buf, dtype=np.uint8)
-    bitpos = np.arange(n, dtype=np.int64) * bits
-    out = np.zeros(n, dtype=np.uint8)
-    for b in range(bits):
-        pos = bitpos + b
-        bit = (arr[pos >> 3] >> (pos & 7).astype(np.uint8)) & 1
-        out |= (bit << b).astype(np.uint8)
-    return out
+    if bits in (1, 2, 4, 8):
+        per = 8 // bits
+        shifts = (np.arange(per, dtype=np.uint8) * bits)
+        return ((arr[:, None] >> shifts) & np.uint8((1 << bits) - 1)).reshape(-1)[:n].astype(np.uint8)
+    stream = np.unpackbits(arr, bitorder="little", count=n * bits).reshape(n, bits)
+    weights = (1 << np.arange(bits, dtype=np.uint8)).astype(np.uint8)
+    return (stream * weights).sum(axis=1, dtype=np.uint8)
 
 
 def bitpack_header(bits: int, count: int) -> bytes:
