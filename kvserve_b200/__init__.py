@@ -10,6 +10,8 @@ __version__ = "0.1.0"
 
 _LAZY = {
     "CompressedKVConnector": "kvserve_b200.connector.compressed_kv_connector",
+    "SessionKVConnector": "kvserve_b200.connector.session_kv_connector",
+    "StoreKVConnector": "kvserve_b200.connector.store_kv_connector",
     "KVCompressionAdapter": "kvserve_b200.compression.adapter",
     "CompressionManager": "kvserve_b200.compression.manager",
     "PDEngine": "kvserve_b200.engine.pd",
