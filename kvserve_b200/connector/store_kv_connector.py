@@ -12,7 +12,7 @@ Load it into vLLM with::
                      kv_role="kv_both",
                      kv_connector_extra_config={"store": {"dir": "/dev/shm/kvs-store",
                                                           "device_bytes": 8 << 30, "host_bytes": 32 << 30,
-                                                          "blocks_per_chunk": 16},
+                                                          "disk_bytes": 256 << 30, "blocks_per_chunk": 16},
                                                 "compression": None | <modular profile>})
 
 The store is a :class:`~kvserve_b200.store.pool.TieredKVPool` in shared mode:
@@ -87,6 +87,7 @@ class StoreKVConnector(KVConnectorBase_V1):
             raise ValueError("StoreKVConnector needs kv_connector_extra_config['store']['dir']")
         self._device_bytes = int(st.get("device_bytes", 1 << 30))
         self._host_bytes = int(st.get("host_bytes", 4 << 30))
+        self._disk_bytes = int(st["disk_bytes"]) if st.get("disk_bytes") else None
         self._bpc = int(st.get("blocks_per_chunk", 16))
         self._block_size = vllm_config.cache_config.block_size
         self._compression = extra.get("compression")
@@ -118,7 +119,8 @@ class StoreKVConnector(KVConnectorBase_V1):
         from ..store.connector import KVStoreConnector
         from ..store.layout import RankLocalLayout
         from ..store.pool import TieredKVPool
-        pool = TieredKVPool(pool_bytes[0], pool_bytes[1], disk_dir=self._dir, device=device, shared=True)
+        pool = TieredKVPool(pool_bytes[0], pool_bytes[1], disk_dir=self._dir, device=device, shared=True,
+                            disk_bytes=self._disk_bytes)
         return KVStoreConnector(pool, self._block_size, self._bpc, RankLocalLayout(self._model, rank, self._tp_size),
                                 compression, heads, head_size, layers, self._salt)
 

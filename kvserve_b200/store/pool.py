@@ -25,10 +25,14 @@ import torch
 
 class TieredKVPool:
     def __init__(self, device_bytes: int, host_bytes: int, disk_dir: Optional[str] = None, device=None,
-                 shared: bool = False):
+                 shared: bool = False, disk_bytes: Optional[int] = None):
         if shared and not disk_dir:
             raise ValueError("a shared pool needs disk_dir")
         self.shared = shared
+        # byte budget of the directory (None: unbounded); the oldest files go
+        # first, whichever process wrote them
+        self.disk_budget = None if disk_bytes is None else int(disk_bytes)
+        self._disk_estimate = 0
         self.device = torch.device(device) if device is not None else (
             torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu"))
         self.budget = {"device": int(device_bytes), "host": int(host_bytes)}
@@ -40,6 +44,7 @@ class TieredKVPool:
         self.on_disk: dict[str, str] = {}
         self._lock = threading.RLock()
         self._disk_q: "queue.Queue[Optional[tuple[str, Any]]]" = queue.Queue()
+        self._disk_inflight = 0
         self._pending_disk: dict[str, Any] = {}
         self._writer = threading.Thread(target=self._disk_loop, daemon=True, name="kvs-store-disk")
         self._writer.start()
@@ -77,20 +82,64 @@ class TieredKVPool:
     def _path(self, key: str) -> str:
         return os.path.join(self.disk_dir, key.replace("/", "__") + ".pt")
 
+    def _enqueue_disk(self, key: str, value: Any) -> None:
+        with self._lock:
+            self._pending_disk[key] = value
+            self._disk_inflight += 1
+        self._disk_q.put((key, value))
+
     def _disk_loop(self) -> None:
         while True:
             item = self._disk_q.get()
             if item is None:
                 return
-            key, value = item
-            path = self._path(key)
-            tmp = f"{path}.{os.getpid()}.{threading.get_ident()}.tmp"
-            torch.save(self._to(value, torch.device("cpu")), tmp)
-            os.replace(tmp, path)
+            try:
+                self._write_disk(*item)
+            finally:
+                with self._lock:
+                    self._disk_inflight -= 1
+
+    def _write_disk(self, key: str, value: Any) -> None:
+        path = self._path(key)
+        tmp = f"{path}.{os.getpid()}.{threading.get_ident()}.tmp"
+        torch.save(self._to(value, torch.device("cpu")), tmp)
+        size = os.path.getsize(tmp)
+        os.replace(tmp, path)
+        with self._lock:
+            if self._pending_disk.get(key) is value:
+                self._pending_disk.pop(key)
+                self.on_disk[key] = path
+        if self.disk_budget is not None:
+            self._disk_estimate += size
+            if self._disk_estimate > self.disk_budget:
+                self._prune_disk()
+
+    def _prune_disk(self) -> None:
+        """Delete the oldest value files until the directory holds at most
+        90 % of its budget (files of other processes sharing it included)."""
+        files = []
+        for e in os.scandir(self.disk_dir):
+            if e.name.endswith(".pt"):
+                try:
+                    st = e.stat()
+                except FileNotFoundError:      # removed by another process meanwhile
+                    continue
+                files.append((st.st_mtime, st.st_size, e.path))
+        total = sum(f[1] for f in files)
+        target = int(0.9 * self.disk_budget)
+        for _, size, path in sorted(files):
+            if total <= target:
+                break
+            try:
+                os.remove(path)
+            except FileNotFoundError:
+                pass
+            total -= size
             with self._lock:
-                if self._pending_disk.get(key) is value:
-                    self._pending_disk.pop(key)
-                    self.on_disk[key] = path
+                for key in [k for k, p in self.on_disk.items() if p == path]:
+                    self.on_disk.pop(key)
+                self.m_evict.labels("disk").inc()
+        self._disk_estimate = total
 
     def _insert(self, tier: str, key: str, value: Any) -> None:
         t = self.tiers[tier]
@@ -109,8 +158,7 @@ class TieredKVPool:
             if tier == "device":
                 self._insert("host", key, self._to(value, torch.device("cpu"), pin=True))
             elif self.disk_dir and not (self.shared and key in self.on_disk):
-                self._pending_disk[key] = value
-                self._disk_q.put((key, value))
+                self._enqueue_disk(key, value)
         for name in ("device", "host"):
             self.m_bytes.labels(name).set(self.used[name])
 
@@ -121,8 +169,7 @@ class TieredKVPool:
             dev = self._to(value, self.device)
             self._insert("device", key, dev)
             if self.shared and key not in self._pending_disk:
-                self._pending_disk[key] = dev      # write through: other processes read the file
-                self._disk_q.put((key, dev))
+                self._enqueue_disk(key, dev)       # write through: other processes read the file
 
     def _drop(self, key: str) -> None:
         for tier in ("device", "host"):
@@ -185,7 +232,7 @@ class TieredKVPool:
         done = threading.Event()
         while True:
             with self._lock:
-                if not self._pending_disk:
+                if not self._pending_disk and self._disk_inflight == 0:
                     return
             done.wait(0.01)
 

@@ -66,3 +66,24 @@ def test_tp_sharded_layout_maps_head_ranges():
     with pytest.raises(ValueError):
         TPShardedLayout("m", tp_rank=0, tp_size=4, num_kv_heads=8, store_tp_size=2)
     assert RankLocalLayout("m", 1, 2).shards() == ["tp1of2"]
+
+
+def test_shared_pool_directory_is_seen_by_another_pool_and_pruned_oldest_first(tmp_path):
+    """Two pools on one directory (two processes in production): a value
+    put by one is found and read by the other; the directory's byte budget
+    removes the oldest files first."""
+    import time
+    a = TieredKVPool(1 << 20, 1 << 20, disk_dir=str(tmp_path), device="cpu", shared=True, disk_bytes=3 * 6000)
+    b = TieredKVPool(0, 0, disk_dir=str(tmp_path), device="cpu", shared=True)
+    try:
+        vals = {f"k{i}": torch.full((1024,), float(i)) for i in range(5)}   # ~5 KB files
+        for k, v in vals.items():
+            a.put(k, v)
+            a.flush()
+            time.sleep(0.02)
+        assert b.contains("k4") and torch.equal(b.get("k4"), vals["k4"])
+        assert not b.contains("k0") and not b.contains("k1")     # pruned, oldest first
+        assert a.tier_of("k0") == "device"                        # still held in memory by its writer
+    finally:
+        a.close()
+        b.close()
