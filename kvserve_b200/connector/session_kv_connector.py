@@ -208,6 +208,54 @@ class ServiceThread(threading.Thread):
             self.join(timeout)
 
 
+try:
+    from vllm.distributed.kv_transfer.kv_connector.v1.metrics import KVConnectorStats
+except Exception:  # pragma: no cover - vLLM missing
+    @dataclass
+    class KVConnectorStats:  # type: ignore[no-redef]
+        data: dict = field(default_factory=dict)
+
+
+@dataclass
+class SessionTransferStats(KVConnectorStats):
+    """Transfer telemetry of the session connector for vLLM's metrics
+    logger (role of MooncakeKVConnectorStats,
+    kvsfuse-vllm0.30.0/mooncake/stats.py:20-146): per interval, loads
+    completed and failed, chunks, payload and raw bytes, load durations."""
+
+    def __post_init__(self):
+        for k in ("loads", "failed", "chunks", "payload_bytes", "data_bytes"):
+            self.data.setdefault(k, 0)
+        self.data.setdefault("load_ms", [])
+
+    def reset(self):
+        self.data = {}
+        self.__post_init__()
+
+    def aggregate(self, other: "KVConnectorStats") -> "KVConnectorStats":
+        for k, v in other.data.items():
+            if k == "load_ms":
+                self.data["load_ms"] = list(self.data.get("load_ms", [])) + list(v)
+            else:
+                self.data[k] = self.data.get(k, 0) + v
+        return self
+
+    def reduce(self) -> dict:
+        ms = sorted(self.data.get("load_ms", []))
+        out = {k: self.data.get(k, 0) for k in ("loads", "failed", "chunks")}
+        out["payload_MB"] = round(self.data.get("payload_bytes", 0) / 1e6, 3)
+        if self.data.get("payload_bytes"):
+            out["compression_ratio"] = round(self.data.get("data_bytes", 0) / self.data["payload_bytes"], 3)
+        if ms:
+            out["load_ms_avg"] = round(sum(ms) / len(ms), 3)
+            out["load_ms_p50"] = round(ms[len(ms) // 2], 3)
+            out["load_ms_max"] = round(ms[-1], 3)
+        return out
+
+    def is_empty(self) -> bool:
+        return not (self.data.get("loads") or self.data.get("failed") or self.data.get("chunks"))
+
+
 class _HelperProxy:
     """The service methods the connector calls, forwarded to a session helper
     process (:mod:`kvserve_b200.session.process`).  Send events stay in this
@@ -289,6 +337,9 @@ class SessionKVConnector(KVConnectorBase_V1):
         self._send_pending: dict[str, set] = {}      # prefill request id -> copy sessions not ended
         self._recv: dict[str, RecvReq] = {}          # copy transfer id -> load
         self._recv_pending: dict[str, set] = {}      # decode request id -> copy sessions not ended
+        self._recv_started: dict[str, float] = {}
+        self._stats = SessionTransferStats()
+        self._svc_seen: dict[str, int] = {}
         self._done_sending: set[str] = set()
         self._done_recving: set[str] = set()
         self._finished_seen: set[str] = set()
@@ -495,6 +546,7 @@ class SessionKVConnector(KVConnectorBase_V1):
         self._sends_this_step = list(meta.sends)
         for r in meta.recvs:
             with self._lock:
+                self._recv_started[r.request_id] = time.monotonic()
                 self._recv_pending[r.request_id] = {self.copy_tid(r.transfer_id, k) for k, _ in self._copies}
                 for key, _ in self._copies:
                     self._recv[self.copy_tid(r.transfer_id, key)] = r
@@ -555,12 +607,18 @@ class SessionKVConnector(KVConnectorBase_V1):
                 return
             if s.state is not SessionState.COMPLETE:
                 self._load_errors.update(r.block_ids)
+                self._stats.data["failed"] += 1
+            self._stats.data["chunks"] += int(s.completed_chunks or 0)
             pending = self._recv_pending.get(r.request_id)
             if pending is not None:
                 pending.discard(s.transfer_id)
                 if not pending:
                     del self._recv_pending[r.request_id]
                     self._done_recving.add(r.request_id)
+                    self._stats.data["loads"] += 1
+                    t0 = self._recv_started.pop(r.request_id, None)
+                    if t0 is not None:
+                        self._stats.data["load_ms"].append(1e3 * (time.monotonic() - t0))
         write_session_stats({"direction": "recv", "transfer_id": s.transfer_id, "request_id": r.request_id,
                              "state": s.state.name, "chunks": s.completed_chunks, "total_chunks": s.total_chunks,
                              "error": s.error})
@@ -570,6 +628,23 @@ class SessionKVConnector(KVConnectorBase_V1):
 
     def save_kv_layer(self, layer_name: str, kv_layer: torch.Tensor, attn_metadata, **kwargs) -> None:
         return
+
+    def get_kv_connector_stats(self):
+        """This interval's transfer telemetry (consumer side), then reset."""
+        svc = self._thread.service if self._thread is not None else None
+        with self._lock:
+            st = self._stats
+            if svc is not None and isinstance(getattr(svc, "stats", None), dict):
+                for k in ("payload_bytes", "data_bytes"):
+                    now = int(svc.stats.get(k, 0))
+                    st.data[k] += now - self._svc_seen.get(k, 0)
+                    self._svc_seen[k] = now
+            self._stats = SessionTransferStats()
+        return None if st.is_empty() else st
+
+    @classmethod
+    def build_kv_connector_stats(cls, data=None):
+        return SessionTransferStats(data=dict(data or {}))
 
     def get_finished(self, finished_req_ids: set):
         if self._thread is not None and self._thread.error is not None:

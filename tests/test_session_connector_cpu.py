@@ -167,6 +167,14 @@ def test_pull_moves_every_chunk_and_both_sides_report(helper):
         assert _wait_recv(d_sched, d_work, "d1")
         assert torch.equal(dst[:, d_blocks], src[:, p_blocks])
         assert not d_work.get_block_ids_with_load_errors()
+        st = d_work.get_kv_connector_stats()          # vLLM's per-interval transfer telemetry
+        red = st.reduce()
+        assert red["loads"] == 1 and red["chunks"] == 4 and red["failed"] == 0 and red["load_ms_max"] > 0
+        if not helper:
+            assert red["payload_MB"] > 0
+        assert d_work.get_kv_connector_stats() is None     # reset after each interval
+        agg = SessionKVConnector.build_kv_connector_stats(st.data).aggregate(st)
+        assert agg.reduce()["loads"] == 2
         deadline = time.monotonic() + 10
         sending = None
         while time.monotonic() < deadline and not sending:
