@@ -152,3 +152,15 @@ def test_stagewise_bf16_fwht_matches_reference_runtime(n):
     ref_out = torch.empty_like(x)
     RefPipeline._hadamard_transform(x.clone(), ref_out, n)
     assert torch.equal(fwht_bf16_stagewise(x), ref_out)
+
+
+@pytest.mark.parametrize("kind", ["dct", "haar"])
+@pytest.mark.parametrize("dim,seed,layer", [(64, 0x3333, 0), (128, 3237919422, 5), (96, 7, 31)])
+def test_orthogonal_bases_and_signs_equal(kind, dim, seed, layer):
+    """The DCT-II / Haar bases and the per-head signs both peers rebuild from
+    the seed (kvserve_v1/compression/transformer/orthogonal.py:13-42)."""
+    pytest.importorskip("triton")      # the reference module imports it at load time
+    from kvserve_v1.compression.transformer import orthogonal as ref
+    from kvserve_b200.compression.transformer.orthogonal import orthogonal_basis, orthogonal_signs
+    assert torch.equal(orthogonal_basis(kind, dim, seed, layer), ref._base(kind, dim, seed, layer))
+    assert torch.equal(orthogonal_signs(kind, dim, 4, seed, layer), ref._signs(kind, dim, 4, seed, layer))
