@@ -164,3 +164,18 @@ def test_orthogonal_bases_and_signs_equal(kind, dim, seed, layer):
     from kvserve_b200.compression.transformer.orthogonal import orthogonal_basis, orthogonal_signs
     assert torch.equal(orthogonal_basis(kind, dim, seed, layer), ref._base(kind, dim, seed, layer))
     assert torch.equal(orthogonal_signs(kind, dim, 4, seed, layer), ref._signs(kind, dim, 4, seed, layer))
+
+
+@pytest.mark.parametrize("bits", [1, 2, 3, 4])
+def test_codebook_centroids_match(bits):
+    """The centred codebook's Lloyd-Max levels for a standard normal
+    (kvserve_v1/compression/quantizer/centered_codebook.py:14-26): both
+    sides must hold the same table to read each other's symbols."""
+    pytest.importorskip("triton")
+    from kvserve_v1.compression.quantizer import centered_codebook as ref
+    from kvserve_b200.compression.quantizer.centered_codebook import lloyd_max_gaussian
+    ours, theirs = lloyd_max_gaussian(bits), ref._centroids(bits)
+    assert len(ours) == len(theirs) == 1 << bits
+    assert max(abs(a - b) for a, b in zip(ours, theirs)) < 1e-6
+    # the bf16 / fp32 tables the kernels use are identical
+    assert torch.equal(torch.tensor(ours, dtype=torch.float32), torch.tensor(theirs, dtype=torch.float32))
