@@ -179,3 +179,32 @@ def test_codebook_centroids_match(bits):
     assert max(abs(a - b) for a, b in zip(ours, theirs)) < 1e-6
     # the bf16 / fp32 tables the kernels use are identical
     assert torch.equal(torch.tensor(ours, dtype=torch.float32), torch.tensor(theirs, dtype=torch.float32))
+
+
+def test_profile_library_and_controller_decisions_interoperate(tmp_path):
+    """A profile library written by this framework's offline search loads in
+    the reference's ProfileLibrary, and the two online controllers (this one
+    with the reference's analytical model, no exploration) make the same
+    choice for the same request (kvserve_v1/compression/controller/
+    profile_library.py:27-206, online_controller.py:62-211)."""
+    from kvserve_v1.compression.controller.online_controller import OnlineController as RefController
+    from kvserve_v1.compression.controller.profile_library import ProfileLibrary as RefLibrary
+    from kvserve_b200.compression.controller import OnlineController, ProfileLibrary
+    from kvserve_b200.offline_search.search import run, synthetic_kv
+    run(str(tmp_path), synthetic_kv(layers=2, tokens=128, heads=4), tolerances=(1.0, 5.0), budget=8,
+        levels=(16, 8, 4), ratios=(0.0, 1.0))
+    path = str(tmp_path / "profile_library.json")
+    ours, theirs = ProfileLibrary(path), RefLibrary(path)
+    assert ours.get_num_profiles() == theirs.get_num_profiles() > 0
+    assert ours.get_num_buckets() == theirs.get_num_buckets()
+    c_ours = OnlineController(ours, epsilon=0.0, transfer_model="reference")
+    c_ref = RefController(theirs, epsilon=0.0)
+    chosen = set()
+    for acc in (0.5, 0.9, 0.97, 0.99):
+        for mbps in (5.0, 50.0, 400.0, 3000.0, 50000.0):
+            for slo in (50.0, 1e9):
+                a, _ = c_ours.select_profile(512e6, mbps, 20.0, slo, acc)
+                b, _ = c_ref.select_profile(512e6, mbps, 20.0, slo, acc)
+                assert (a.profile_id if a else None) == (b.profile_id if b else None), (acc, mbps, slo)
+                chosen.add(a.profile_id if a else None)
+    assert len(chosen - {None}) >= 1       # some requests do get a profile
