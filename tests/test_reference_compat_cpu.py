@@ -208,3 +208,25 @@ def test_profile_library_and_controller_decisions_interoperate(tmp_path):
                 assert (a.profile_id if a else None) == (b.profile_id if b else None), (acc, mbps, slo)
                 chosen.add(a.profile_id if a else None)
     assert len(chosen - {None}) >= 1       # some requests do get a profile
+
+
+def test_bandit_state_files_interoperate(tmp_path):
+    """Saved bandit state (EWMA residuals per bucket, interval, profile) reads
+    back on the other side (kvserve_v1/compression/controller/
+    bandit_state.py:57-156)."""
+    from kvserve_v1.compression.controller.bandit_state import BanditStateManager as RefBandit
+    from kvserve_b200.compression.controller.bandit import BanditStateManager
+    ours, theirs = BanditStateManager(alpha=0.3), RefBandit(alpha=0.3)
+    for b, i, p, d in [(0, 1, "hadamard_k4v2", 3.5), (0, 1, "hadamard_k4v2", -1.0), (2, 0, "dct_x_y", 0.25)]:
+        ours.update(b, i, p, d)
+        theirs.update(b, i, p, d)
+    ours.save(str(tmp_path / "ours.json"))
+    theirs.save(str(tmp_path / "theirs.json"))
+    back_ref, back_ours = RefBandit(), BanditStateManager()
+    back_ref.load(str(tmp_path / "ours.json"))
+    back_ours.load(str(tmp_path / "theirs.json"))
+    for b, i, p in [(0, 1, "hadamard_k4v2"), (2, 0, "dct_x_y"), (5, 5, "none")]:
+        assert back_ref.get_usage_count(b, i, p) == ours.get_usage_count(b, i, p)
+        assert back_ref.get_residual(b, i, p) == pytest.approx(ours.get_residual(b, i, p))
+        assert back_ours.get_usage_count(b, i, p) == theirs.get_usage_count(b, i, p)
+        assert back_ours.get_residual(b, i, p) == pytest.approx(theirs.get_residual(b, i, p))
