@@ -230,3 +230,41 @@ def test_bandit_state_files_interoperate(tmp_path):
         assert back_ref.get_residual(b, i, p) == pytest.approx(ours.get_residual(b, i, p))
         assert back_ours.get_usage_count(b, i, p) == theirs.get_usage_count(b, i, p)
         assert back_ours.get_residual(b, i, p) == pytest.approx(theirs.get_residual(b, i, p))
+
+
+@pytest.mark.parametrize("direction", ["reference-to-here", "here-to-reference"])
+def test_controller_mode_payloads_interoperate(tmp_path, direction):
+    """Controller mode: the sender's online controller picks a profile from
+    the library and embeds it in the payload (``ctrl_profile_cfg``); the
+    receiver rebuilds that pipeline from the metadata alone
+    (kvserve_v1/compression/manager.py:241-340)."""
+    from kvserve_v1.compression.manager import KVCompressionAdapter as RefAdapter
+    from kvserve_v1.compression.wire import CompressedWire as RefWire, build_wire as ref_build
+    from kvserve_v1.compression.wire import restore_from_wire as ref_restore
+    from kvserve_b200.compression.adapter import KVCompressionAdapter
+    from kvserve_b200.compression.controller.profile import Profile
+    from kvserve_b200.compression.wire import CompressedWire, build_wire, restore_from_wire
+    from kvserve_b200.offline_search.library_builder import build_library, save_library
+    prof = Profile("quant_only", {"model_name": "Llama-3.1-8B-Instruct"}, QUANT_ONLY,
+                   {"compression_ratio": 3.0, "harmonic_speed_mbps": 1e6}, {"accuracy": 1.0})
+    path = str(tmp_path / "library.json")
+    save_library(build_library([prof], [0.0, 0.9, 1.01], model_name="Llama-3.1-8B-Instruct"), path)
+    spec = {"mode": "controller", "library_path": path, "epsilon": 0.0,
+            "service_config": {"bandwidth_mbps": 100.0, "accuracy_requirement": 0.95}}
+    kv = _kv()
+    if direction == "reference-to-here":
+        sender = RefAdapter(spec, 8, 128)
+        c = sender.compress(kv, "req-ref")
+        assert c is not None and c.metadata.get("ctrl_profile_cfg")
+        w = ref_build(c, 1 << 12)
+        out = KVCompressionAdapter(spec, 8, 128, num_layers=32).decompress(
+            restore_from_wire(CompressedWire(w.meta, w.body_chunks, w.aux_tensors)))
+        assert torch.equal(out, sender.decompress(c))
+    else:
+        sender = KVCompressionAdapter(spec, 8, 128, num_layers=32)
+        c = sender.compress(kv, "req-ours")
+        assert c is not None and c.metadata.get("ctrl_profile_cfg")
+        w = build_wire(c, 1 << 12)
+        out = RefAdapter(spec, 8, 128).decompress(ref_restore(RefWire(meta=w.meta, body_chunks=w.body_chunks,
+                                                                       aux_tensors=w.aux_tensors)))
+        assert torch.equal(out, sender.decompress(c))
