@@ -268,3 +268,27 @@ def test_controller_mode_payloads_interoperate(tmp_path, direction):
         out = RefAdapter(spec, 8, 128).decompress(ref_restore(RefWire(meta=w.meta, body_chunks=w.body_chunks,
                                                                        aux_tensors=w.aux_tensors)))
         assert torch.equal(out, sender.decompress(c))
+
+
+def test_analytical_model_reference_mode_matches():
+    """``AnalyticalModel("reference")`` reproduces the reference's latency
+    model, including its transfer term ``V * cr / B``
+    (kvserve_v1/compression/controller/analytical_model.py:27-136); the
+    default model divides by the ratio instead."""
+    from kvserve_v1.compression.controller.analytical_model import AnalyticalModel as RefModel
+    from kvserve_v1.compression.controller.profile import Profile as RefProfile
+    from kvserve_b200.compression.controller.analytical import AnalyticalModel
+    from kvserve_b200.compression.controller.profile import Profile
+    rec = {"profile_id": "p", "metadata": {}, "compression_config": {},
+           "performance_metrics": {"compression_ratio": 4.0, "harmonic_speed_mbps": 2000.0},
+           "quality_metrics": {"accuracy": 0.98}}
+    ours, theirs = Profile.from_dict(rec), RefProfile.from_dict(rec)
+    model = AnalyticalModel("reference")
+    for V, B, T in [(512e6, 100.0, 20.0), (64e6, 5000.0, 3.0), (2e9, 25.0, 150.0)]:
+        assert model.predict_latency(ours, V, B, T) == pytest.approx(RefModel.predict_latency(theirs, V, B, T))
+        assert model.predict_baseline_latency(V, B, T) == pytest.approx(RefModel.predict_baseline_latency(V, B, T))
+        assert model.compute_speedup(ours, V, B, T) == pytest.approx(RefModel.compute_speedup(theirs, V, B, T))
+        assert AnalyticalModel.check_benefit(ours, B) == RefModel.check_benefit(theirs, B)
+    # the corrected default: the transfer term shrinks with the ratio
+    assert AnalyticalModel().predict_latency(ours, 512e6, 100.0, 20.0) < model.predict_latency(ours, 512e6, 100.0,
+                                                                                                20.0)
