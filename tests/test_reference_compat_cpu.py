@@ -292,3 +292,75 @@ def test_analytical_model_reference_mode_matches():
     # the corrected default: the transfer term shrinks with the ratio
     assert AnalyticalModel().predict_latency(ours, 512e6, 100.0, 20.0) < model.predict_latency(ours, 512e6, 100.0,
                                                                                                 20.0)
+
+
+def _fake_vllm_config(producer: bool):
+    from types import SimpleNamespace as NS
+    return NS(kv_transfer_config=NS(is_kv_producer=producer, kv_buffer_size=1 << 20, kv_ip="127.0.0.1",
+                                    kv_port=0, kv_connector_extra_config={"compression": None}),
+              cache_config=NS(block_size=16), parallel_config=NS(tensor_parallel_size=1),
+              model_config=NS(get_num_kv_heads=lambda pc: 8, get_head_size=lambda: 128, model="/m/Llama",
+                              get_num_layers=lambda pc: 32, use_mla=False))
+
+
+def _meta_rows(meta):
+    return [(r.request_id, r.transfer_id, list(r.token_ids), list(r.block_ids), r.slot_mapping.tolist())
+            for r in meta.requests]
+
+
+def test_push_connector_scheduling_matches_reference():
+    """The push connector's scheduler half makes the same decisions as the
+    reference's on the same call sequence (kvserve_v1/connector/
+    compressed_kv_connector.py:499-605): the consumer claims ``prompt - 1 -
+    computed`` tokens and lists new and resumed loads; the producer defers a
+    chunked prefill until the prompt is complete; transfer ids come from the
+    router parameters."""
+    from types import SimpleNamespace as NS
+    from kvserve_v1.connector.compressed_kv_connector import CompressedKVConnector as Ref
+    from vllm.distributed.kv_transfer.kv_connector.v1.base import KVConnectorRole
+    from kvserve_b200.connector.compressed_kv_connector import CompressedKVConnector as Ours
+
+    def req(rid, n, tid=None):
+        return NS(request_id=rid, prompt_token_ids=list(range(100, 100 + n)), all_token_ids=list(range(100, 100 + n)),
+                  kv_transfer_params={"transfer_id": tid} if tid else None)
+
+    class Blocks:
+        def __init__(self, ids):
+            self.ids = ids
+
+        def get_block_ids(self):
+            return (self.ids,)
+
+    def so(new=(), cached=(), sched=None):
+        return NS(scheduled_new_reqs=[NS(req_id=r, prompt_token_ids=p, block_ids=(b,), num_computed_tokens=c)
+                                      for r, p, b, c in new],
+                  num_scheduled_tokens=sched or {},
+                  scheduled_cached_reqs=NS(req_ids=[c[0] for c in cached],
+                                           new_block_ids=[c[1] for c in cached],
+                                           num_computed_tokens=[c[2] for c in cached],
+                                           resumed_req_ids={c[0] for c in cached if c[3]}))
+
+    # consumer
+    outs = []
+    for cls in (Ref, Ours):
+        c = cls(_fake_vllm_config(False), KVConnectorRole.SCHEDULER)
+        r1, r2 = req("d1", 70, "t-1"), req("d2", 40)
+        claims = [c.get_num_new_matched_tokens(r1, 0), c.get_num_new_matched_tokens(r2, 16),
+                  c.get_num_new_matched_tokens(req("d3", 1), 0)]
+        c.update_state_after_alloc(r1, Blocks([4, 5, 6, 7, 8]), 69)
+        c.update_state_after_alloc(r2, Blocks([9, 10, 11]), 23)
+        m1 = c.build_connector_meta(so(new=[("d1", r1.prompt_token_ids, [4, 5, 6, 7, 8], 0)]))
+        m2 = c.build_connector_meta(so(cached=[("d2", ([12, 13, 14],), 16, True)]))
+        outs.append((claims, _meta_rows(m1), _meta_rows(m2)))
+    assert outs[0] == outs[1]
+    # producer with a chunked prefill
+    outs = []
+    for cls in (Ref, Ours):
+        c = cls(_fake_vllm_config(True), KVConnectorRole.SCHEDULER)
+        r = req("p1", 100, "t-9")
+        c.update_state_after_alloc(r, Blocks([0, 1, 2, 3]), 0)
+        m1 = c.build_connector_meta(so(new=[("p1", r.prompt_token_ids, [0, 1, 2, 3], 0)], sched={"p1": 64}))
+        m2 = c.build_connector_meta(so(cached=[("p1", ([4, 5, 6],), 64, False)], sched={"p1": 36}))
+        outs.append((c.get_num_new_matched_tokens(r, 0), _meta_rows(m1), _meta_rows(m2)))
+    assert outs[0] == outs[1]
+    assert outs[0][1] == [] and outs[0][2][0][3] == [0, 1, 2, 3, 4, 5, 6]
