@@ -364,3 +364,31 @@ def test_push_connector_scheduling_matches_reference():
         outs.append((c.get_num_new_matched_tokens(r, 0), _meta_rows(m1), _meta_rows(m2)))
     assert outs[0] == outs[1]
     assert outs[0][1] == [] and outs[0][2][0][3] == [0, 1, 2, 3, 4, 5, 6]
+
+
+@pytest.mark.parametrize("blocks_first", [False, True])
+def test_kv_block_utils_match_reference(blocks_first):
+    """Slot mappings and block gather/scatter on both vLLM cache layouts, with
+    producer/consumer block counts that differ in the tail
+    (kvserve_v1/utils/kv_utils.py:6-119)."""
+    from kvserve_v1.utils import kv_utils as ref
+    from kvserve_b200.utils import kv_utils as ours
+    g = torch.Generator().manual_seed(3)
+    shape = (12, 2, 16, 4, 8) if blocks_first else (2, 12, 16, 4, 8)
+    cache = torch.randn(shape, generator=g).to(torch.bfloat16)
+    toks, blocks = list(range(37)), [7, 2, 9]
+    assert torch.equal(ours.make_slot_mapping(toks, blocks, 16), ref.make_slot_mapping(toks, blocks, 16))
+    a = ours.extract_kv_from_layer_by_blocks(cache, blocks)
+    b = ref.extract_kv_from_layer_by_blocks(cache, blocks)
+    assert torch.equal(a, b)
+    for dst_blocks in ([1, 3, 5], [1, 3, 5, 6]):
+        c1, c2 = torch.zeros_like(cache), torch.zeros_like(cache)
+        ours.inject_kv_into_layer_by_blocks(c1, a, dst_blocks, "r")
+        ref.inject_kv_into_layer_by_blocks(c2, b, dst_blocks, "r")
+        assert torch.equal(c1, c2), dst_blocks
+    # fewer destination blocks than sent: the reference raises although its
+    # docstring promises the overlap; this side writes the overlap
+    c1 = torch.zeros_like(cache)
+    ours.inject_kv_into_layer_by_blocks(c1, a, [1, 3], "r")
+    assert torch.equal(ours.extract_kv_from_layer_by_blocks(c1, [1, 3]),
+                       ours.extract_kv_from_layer_by_blocks(cache, [7, 2]))
