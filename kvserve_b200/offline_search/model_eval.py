@@ -111,8 +111,19 @@ class ModelAccuracyEvaluator:
             return rec.to(kv.dtype), ratio
         return lambda: simulated_cache(bf16_sim, self.L)
 
+    def sim_cache(self, sim):
+        """Caches that apply any simulator of :mod:`.cache_sim` (KIVI,
+        CacheGen, ...) to the bf16 prefill KV, like :meth:`make_cache` does
+        for a profile."""
+        def bf16_sim(kv):
+            rec, ratio = sim(kv.to(torch.bfloat16))
+            return rec.to(kv.dtype), ratio
+        return lambda: simulated_cache(bf16_sim, self.L)
+
     def task_breakdown(self, profile: dict) -> dict:
-        make = self.make_cache(profile)
+        return self._breakdown(self.make_cache(profile))
+
+    def _breakdown(self, make) -> dict:
         agree, like, ratios = [], [], []
         for p, (toks, _, lps) in zip(self.prompts, self._ref):
             cache = make()
@@ -130,7 +141,14 @@ class ModelAccuracyEvaluator:
                 "compression_ratio": (sum(ratios) / len(ratios)) if ratios else 1.0}
 
     def evaluate(self, profile: dict) -> float:
-        b = self.task_breakdown(profile)
+        return self._score(self.task_breakdown(profile))
+
+    def evaluate_sim(self, sim) -> float:
+        """The same score for a baseline method's simulator (the reference's
+        method comparison, e.g. scripts/run_hotpotqa_4way.sh, on these tasks)."""
+        return self._score(self._breakdown(self.sim_cache(sim)))
+
+    def _score(self, b: dict) -> float:
         rel = [b["scores"][k] / b["defaults"][k] for k in b["scores"] if b["defaults"].get(k)]
         self.last = dict(b, avg_score=round(100.0 * sum(rel) / len(rel), 2))
         return self.last["avg_score"]
@@ -160,7 +178,9 @@ def synthetic_prompts(count: int, length: int, vocab: int, seed: int = 0) -> lis
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
-    ap.add_argument("profiles", nargs="+", help="compression profile JSON files")
+    ap.add_argument("profiles", nargs="*", help="compression profile JSON files")
+    ap.add_argument("--baselines", default="",
+                    help="comma-separated baseline methods to score too: kivi2, kivi4, cachegen")
     ap.add_argument("--model", default=None, help="local Hugging Face checkpoint (default: random-init tiny Llama)")
     ap.add_argument("--prompts", type=int, default=4)
     ap.add_argument("--prompt-len", type=int, default=256)
@@ -182,6 +202,12 @@ def main() -> None:
             prof = json.load(f)
         score = ev.evaluate(prof)
         print(json.dumps({"profile": path, "avg_score": score, "scores": ev.last["scores"],
+                          "compression_ratio": round(ev.last["compression_ratio"], 3)}))
+    from .cache_sim import CacheGenSim, KIVISim
+    methods = {"kivi2": lambda: KIVISim(bits=2), "kivi4": lambda: KIVISim(bits=4), "cachegen": CacheGenSim}
+    for name in filter(None, (x.strip() for x in args.baselines.split(","))):
+        score = ev.evaluate_sim(methods[name]())
+        print(json.dumps({"method": name, "avg_score": score, "scores": ev.last["scores"],
                           "compression_ratio": round(ev.last["compression_ratio"], 3)}))
 
 

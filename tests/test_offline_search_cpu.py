@@ -134,3 +134,15 @@ def test_captured_model_kv_feeds_the_search(tmp_path):
     assert kv.shape == (2, 2, 2, 64, 1, 64) and kv.dtype == torch.bfloat16
     out = run(str(tmp_path), kv, tolerances=(5.0,), budget=4, levels=(16, 4), ratios=(0.0,))
     assert out["results"]["5.0"]["evaluated"] >= 1
+
+
+def test_model_evaluator_scores_baseline_methods():
+    """Baseline methods (KIVI, CacheGen restatements) go through the same
+    language-model tasks as the profiles."""
+    from kvserve_b200.offline_search.cache_sim import CacheGenSim, KIVISim
+    from kvserve_b200.offline_search.model_eval import ModelAccuracyEvaluator, synthetic_prompts, tiny_llama
+    lm = tiny_llama(layers=2, hidden=128, heads=2, kv_heads=1, vocab=256)
+    ev = ModelAccuracyEvaluator(lm, synthetic_prompts(1, 96, 256), new_tokens=4)
+    for sim in (KIVISim(bits=2, residual=16), CacheGenSim()):
+        score = ev.evaluate_sim(sim)
+        assert 0.0 <= score <= 100.0 and ev.last["compression_ratio"] > 1.5
