@@ -5,6 +5,8 @@ from __future__ import annotations
 
 import os
 
+import torch
+
 from .config import CompressionConfig
 from .memory import CompressionMemoryPlan, build_memory_plan
 from .spec import CacheSpec
@@ -16,7 +18,8 @@ def create_runtime(plan: CompressionMemoryPlan, kv_cache_layout: str = "HND", bl
                    device=None, backend: str = "auto", **kwargs):
     """Create the runtime for ``plan``.  ``backend`` is accepted for API
     compatibility: every backend name runs the sm_100a fused frame kernels
-    (there is one implementation, no dispatch)."""
+    on a GPU; a CPU ``device`` gets the same API on the frame format's CPU
+    reference encoder and decoder (:mod:`.cpu_runtime`)."""
     if backend == "auto":
         # the reference's selector variable (auto / python / cpp) is accepted;
         # every choice runs the same kernels
@@ -25,8 +28,11 @@ def create_runtime(plan: CompressionMemoryPlan, kv_cache_layout: str = "HND", bl
             raise ValueError(f"KVSERVE_COMPRESSION_BACKEND must be auto, python or cpp, got {env!r}")
     if backend not in ("auto", "fused", "standard"):
         raise ValueError("backend must be auto, fused or standard")
-    from .manager import CompressionRuntime
     kwargs.pop("standard_backend", None)
+    if device is not None and torch.device(device).type == "cpu":
+        from .cpu_runtime import CpuCompressionRuntime
+        return CpuCompressionRuntime(plan, kv_cache_layout, blocks_per_logical, device, **kwargs)
+    from .manager import CompressionRuntime
     return CompressionRuntime(plan, kv_cache_layout, blocks_per_logical, device, **kwargs)
 
 

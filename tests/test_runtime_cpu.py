@@ -53,3 +53,67 @@ def test_memory_plan_is_bounded_and_layer_split():
     assert lows == [0, 0, 0, 0, 2, 2]   # split_type="layer": last round(0.33 * 6) layers low
     with pytest.raises(ValueError):
         build_memory_plan(cfg, {"x": CacheSpec(0, 16, 2, 128, torch.float16)})
+
+
+def _cpu_runtimes(pipeline, layout="NHD", per_chunk=4, levels=None):
+    from kvserve_b200.compression.runtime import create_runtime
+    comp = {"enable-compression-pipeline": True, "pipeline": pipeline, "logical_blocks_per_chunk": per_chunk}
+    comp.update(levels or {})
+    cfg = CompressionConfig.from_extra_config({"compression": comp})
+    specs = {f"l{i}": CacheSpec(i, 16, 4, 128, torch.bfloat16) for i in range(3)}
+    plan = build_memory_plan(cfg, specs, num_layers=3, device="cpu")
+    return (create_runtime(plan, layout, 1, "cpu", execution="encode"),
+            create_runtime(plan, layout, 1, "cpu", execution="decode"))
+
+
+def _cpu_caches(layout, fill, seed=5):
+    g = torch.Generator().manual_seed(seed)
+    shape = (2, 24, 16, 4, 128) if layout == "NHD" else (2, 24, 4, 16, 128)
+    mk = (lambda: torch.randn(shape, generator=g)) if fill else (lambda: torch.zeros(shape))
+    return {f"l{i}": mk().to(torch.bfloat16) for i in range(3)}
+
+
+@pytest.mark.parametrize("layout", ["NHD", "HND"])
+@pytest.mark.parametrize("pipeline", [["transformer", "quantizer"], ["transformer", "quantizer", "codec"]])
+def test_cpu_runtime_round_trip_through_the_slot_api(layout, pipeline):
+    """The runtime API on the CPU: encode a chunk of paged blocks (K and V
+    parts) into a slot, move the payload into the peer's receive buffer,
+    decode into other blocks; the result is the frame format's
+    reconstruction (relative error of 4-bit symbols) and only the target
+    blocks change."""
+    enc, dec = _cpu_runtimes(pipeline, layout, levels={"high_key_num_levels": 16, "low_key_num_levels": 16,
+                                                       "high_value_num_levels": 16, "low_value_num_levels": 16})
+    src, dst = _cpu_caches(layout, True), _cpu_caches(layout, False)
+    enc.bind_kv_caches(src)
+    dec.bind_kv_caches(dst)
+    assert enc.wire_profile == dec.wire_profile
+    sb, db, valid = [3, 4, 5, 6], [10, 11, 12, 13], 4 * 16 - 5
+    for part in (0, 1):
+        r = enc.encode(0, {0: sb}, part, valid_tokens_by_group={0: valid})
+        r.event.synchronize()
+        n = r.codec_bytes
+        dec.receive_buffer(1)[:n].copy_(r.payload[:n])
+        dec.decode(1, {0: db}, part, codec_bytes=n, valid_tokens_by_group={0: valid}).synchronize()
+    for name in src:
+        s, d = src[name].float(), dst[name].float()
+        tok = (lambda t, b: t[:, b].reshape(2, -1, 4, 128)) if layout == "NHD" else \
+            (lambda t, b: t[:, b].permute(0, 1, 3, 2, 4).reshape(2, -1, 4, 128))
+        a, b = tok(s, sb)[:, :valid], tok(d, db)[:, :valid]
+        assert ((a - b).norm() / a.norm()) < 0.15
+        assert tok(d, db)[:, valid:].abs().sum() == 0            # tail rows of the last block untouched
+        others = [i for i in range(24) if i not in db]
+        assert d[:, others].abs().sum() == 0
+
+
+def test_cpu_runtime_frames_match_the_gpu_layout():
+    """Each layer's frame sits at the same slot offset the GPU runtime uses
+    and starts with the frame header (magic, layer, tokens)."""
+    import struct
+    from kvserve_b200.ops.kv_codec import FRAME_MAGIC
+    enc, _ = _cpu_runtimes(["transformer", "quantizer"])
+    enc.bind_kv_caches(_cpu_caches("NHD", True))
+    enc.encode(0, {0: [0, 1]}, 0, valid_tokens_by_group={0: 32})
+    arena = enc.slots[0].arena.numpy()
+    for i in range(3):
+        magic, _, layer, tokens = struct.unpack_from("<4I", arena, i * enc.layout.frame_stride)
+        assert (magic, layer, tokens) == (FRAME_MAGIC, i, 32)
