@@ -44,9 +44,10 @@ runs the reference without compression (``compression=None``).
 
 Topology under ``torchrun`` with N ranks (N even): rank 0 drives the producer
 engine on GPUs [0, N/2) (TP N/2) and rank N/2 the consumer engine on GPUs
-[N/2, N); the other ranks only take part in the host barriers.  N = 1 is not
-available: the reference's transport is NCCL between two engines, and NCCL
-refuses two ranks on one device.
+[N/2, N); the other ranks only take part in the host barriers.  N = 1 cannot
+run the pair (the reference's transport is NCCL between two engines, and NCCL
+refuses two ranks on one device); it reports the labelled composite of
+:func:`run_single_gpu` instead.
 
 Timing (host clock; vLLM's internals are not instrumented so that the stock
 path runs as shipped): every request starts after a barrier of all ranks at a
@@ -110,13 +111,17 @@ K4V2_PROFILE = {
 }
 
 
+NCCL_ONE_GPU = ("the reference's PD path is two vLLM engines joined by NCCL, which refuses two ranks on one "
+                "device")
+
+
 def unavailable_reason(world_size: int = 1) -> Optional[str]:
-    """Why the arm can not run with ``world_size`` ranks here (None: it can)."""
+    """Why the arm can not run with ``world_size`` ranks here (None: it can;
+    one GPU runs the composite of :func:`run_single_gpu`)."""
     if not os.path.isdir(os.path.join(REF_DIR, "kvserve_v1")):
         return "reference not installed in baseline/_ref (pip install --target baseline/_ref failed)"
-    if world_size < 2 or world_size % 2:
-        return ("the reference's PD path is two vLLM engines joined by NCCL; it needs an even number of GPUs "
-                ">= 2 (NCCL refuses two ranks on one device), so 1 GPU has no reference number")
+    if world_size > 1 and world_size % 2:
+        return f"{NCCL_ONE_GPU}; it needs an even number of GPUs"
     try:
         import vllm  # noqa: F401
     except Exception as exc:  # pragma: no cover - environment dependent
@@ -240,6 +245,12 @@ def run(args, emit) -> None:
         if rank == 0:
             emit({"impl": "reference", "unavailable": why})
         return
+    if world == 1:
+        if getattr(args, "ref_engine", "vllm") != "vllm":
+            emit({"impl": "reference", "unavailable": NCCL_ONE_GPU})
+            return
+        emit(run_single_gpu(args))
+        return
     addr, port = os.environ.get("MASTER_ADDR", "127.0.0.1"), int(os.environ["MASTER_PORT"])
     bar = _Barrier(addr, port, rank, world)
     tp = world // 2
@@ -284,6 +295,128 @@ def run(args, emit) -> None:
             out = {"impl": "reference", "unavailable": f"reference run failed: {bar.failed()}",
                    "stock_path": out.get("stock_path")}
         emit(out)
+
+
+def _local_handoff(args, n_req: int) -> dict:
+    """The reference connector's data path for one request's KV on one GPU:
+    ``compress`` of the stacked ``[L, 2, blocks, block_size, H, D]`` KV,
+    ``build_wire``, the payload tensors copied as the transport would land
+    them, ``restore_from_wire``, ``decompress`` and
+    ``inject_kv_into_layer_by_blocks`` into a paged cache (all 8 KV heads,
+    TP 1).  Host clock after device synchronisation; the median."""
+    import torch
+    from kvserve_v1.compression.manager import KVCompressionAdapter
+    from kvserve_v1.compression.wire import CompressedWire, build_wire, restore_from_wire
+    from kvserve_v1.connector.compressed_kv_connector import _max_nccl_chunk_bytes
+    from kvserve_v1.utils.kv_utils import inject_kv_into_layer_by_blocks
+    L, H, D, bs = LLAMA_8B_CONFIG["num_hidden_layers"], LLAMA_8B_CONFIG["num_key_value_heads"], 128, 16
+    nblk = (args.prompt_len - 1 + bs - 1) // bs
+    profile = reference_profile(args.profile)
+    g = torch.Generator(device="cuda").manual_seed(1234)
+    stacked = torch.randn((L, 2, nblk, bs, H, D), generator=g, device="cuda").to(torch.bfloat16)
+    cache = torch.empty((L, 2, nblk + 64, bs, H, D), dtype=torch.bfloat16, device="cuda")
+    block_ids = list(range(7, 7 + nblk))
+    ad = KVCompressionAdapter(profile, H, D) if profile is not None else None
+    times, nbytes = [], stacked.numel() * 2
+    for i in range(n_req):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        if ad is not None:
+            c = ad.compress(stacked, f"kvs-ref-local-{i}")
+            w = build_wire(c, _max_nccl_chunk_bytes())
+            landed = CompressedWire(meta=w.meta, body_chunks=[b.clone() for b in w.body_chunks],
+                                    aux_tensors=[a.clone() for a in w.aux_tensors])
+            kv = ad.decompress(restore_from_wire(landed))
+            nbytes = w.nbytes
+        else:
+            kv = stacked.clone()
+        for li in range(L):
+            inject_kv_into_layer_by_blocks(cache[li], kv[li], block_ids, f"kvs-ref-local-{i}")
+        torch.cuda.synchronize()
+        times.append(1e3 * (time.perf_counter() - t0))
+    del stacked, cache
+    torch.cuda.empty_cache()
+    kept = times[args.warmup:] or times
+    return {"handoff_ms_p50": round(statistics.median(kept), 3), "payload_bytes": int(nbytes),
+            "raw_bytes": 2 * L * nblk * bs * H * D * 2}
+
+
+def run_single_gpu(args) -> dict:
+    """One GPU: the reference cannot run its PD pair here (its transport is
+    an NCCL communicator between two engines).  The arm reports a composite
+    built only from reference code on the same request: the TTFT of vLLM (the
+    reference's engine) prefilling the prompt on this GPU, plus the
+    reference connector's KV data path for that request without the network
+    (:func:`_local_handoff`), plus one decode step (the decode engine
+    recomputes the last prompt token before it samples).  Labelled
+    ``composite``; a failure prints ``unavailable`` with its reason."""
+    out = {"impl": "reference", "metric": args.metric, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup}
+    import torch
+    if not torch.cuda.is_available():
+        return {"impl": "reference", "unavailable": f"{NCCL_ONE_GPU}; no GPU visible for the one-GPU composite"}
+    llm = None
+    try:
+        os.environ["CUDA_VISIBLE_DEVICES"] = os.environ.get("CUDA_VISIBLE_DEVICES", "0")
+        for pth in (REF_DIR, REPO_ROOT):
+            if pth not in sys.path:
+                sys.path.insert(0, pth)
+        from vllm import LLM
+        n_req = args.warmup + args.steps
+        max_len = args.prompt_len + args.max_new
+        llm = LLM(model=write_model_dir(LLAMA_8B_CONFIG), load_format="dummy", skip_tokenizer_init=True,
+                  dtype="bfloat16", max_model_len=max_len, max_num_batched_tokens=max_len,
+                  enable_chunked_prefill=False, enable_prefix_caching=False, gpu_memory_utilization=0.6,
+                  enforce_eager=not getattr(args, "ref_cuda_graphs", False), disable_log_stats=False, seed=0,
+                  attention_backend=REF_ATTENTION_BACKEND)
+        import random
+        rng = random.Random(1234)
+        ttft, step = [], []
+        for i in range(n_req):
+            prompt = [rng.randrange(LLAMA_8B_CONFIG["vocab_size"]) for _ in range(args.prompt_len)]
+            t0 = time.time()
+            o = _generate(llm, prompt, 2, f"kvs-ref-1gpu-{i}", want_output=True)
+            t1 = time.time()
+            m = o.metrics
+            first = (m.arrival_time + m.first_token_latency) if m is not None and m.first_token_latency else None
+            if first is None:
+                raise RuntimeError("vLLM reported no first-token time")
+            if i >= args.warmup:
+                ttft.append(1e3 * (first - t0))
+                step.append(1e3 * (t1 - first))
+        _shutdown(llm)
+        llm = None
+        import gc
+        gc.collect()
+        ho = _local_handoff(args, n_req)
+        prefill, dstep = statistics.median(ttft), statistics.median(step)
+        value = prefill + ho["handoff_ms_p50"] + dstep
+        out.update({
+            "value": round(value, 3), "unit": "ms (TTFT p50, composite)", "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "composite": True, "same_config": True,
+            "composite_parts": {"vllm_prefill_ttft_ms_p50": round(prefill, 3),
+                                "reference_kv_data_path_ms_p50": ho["handoff_ms_p50"],
+                                "decode_step_ms_p50": round(dstep, 3)},
+            "kv_transfer_ms_p50": ho["handoff_ms_p50"],
+            "compression_ratio": round(ho["raw_bytes"] / ho["payload_bytes"], 3),
+            "data": "synthetic (vLLM dummy random-init weights of the named architecture, uniform-random prompt "
+                    "token ids; N(0,1) KV for the data path)",
+            "config": {"model": "llama-3.1-8b", "layers": LLAMA_8B_CONFIG["num_hidden_layers"], "global_batch": 1,
+                       "seq_len": args.prompt_len, "max_new_tokens": args.max_new,
+                       "parallelism": "colocated-1gpu (composite of reference parts)", "profile": args.profile,
+                       "engine": f"vLLM 0.22 V1 (attention {REF_ATTENTION_BACKEND}) + kvserve_v1 connector data "
+                                 f"path (KVCompressionAdapter, CompressedWire, kv_utils) without its NCCL transport"},
+            "why_composite": NCCL_ONE_GPU,
+            "timing": "host clock (vLLM first-token metrics; device-synchronised data path)",
+            "gpu_launches": None,
+            "recon": _reference_recon(args),
+        })
+        return out
+    except BaseException as exc:  # noqa: BLE001 - the arm always prints one line
+        return {"impl": "reference", "unavailable": f"{NCCL_ONE_GPU}; the one-GPU composite failed: "
+                                                    f"{type(exc).__name__}: {str(exc)[:300]}"}
+    finally:
+        if llm is not None:
+            _shutdown(llm)
 
 
 def _tiny_model_dir() -> str:
