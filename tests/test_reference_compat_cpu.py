@@ -10,6 +10,7 @@ heads (kvserve_v1/compression/runtime/scores.py:45-112), and the
 CompressedWire in both directions (kvserve_v1/compression/wire.py:33-136):
 a payload built by one side restores and decompresses on the other.
 """
+import json
 import os
 import sys
 import types
@@ -392,3 +393,45 @@ def test_kv_block_utils_match_reference(blocks_first):
     ours.inject_kv_into_layer_by_blocks(c1, a, [1, 3], "r")
     assert torch.equal(ours.extract_kv_from_layer_by_blocks(c1, [1, 3]),
                        ours.extract_kv_from_layer_by_blocks(cache, [7, 2]))
+
+
+_RUNTIME_EXTRAS = [
+    {},
+    {"compression": {"enable-compression-pipeline": False}},
+    {"compression": {"enable-compression-pipeline": True}},
+    {"compression": {"enable-compression-pipeline": True, "pipeline": ["transformer", "quantizer"],
+                     "high_key_num_levels": 16, "low_value_num_levels": 4, "hybrid_ratio": 0.5,
+                     "split_type": "head", "logical_blocks_per_chunk": 8, "slot_count": 3}},
+    {"compression": {"enable-compression-pipeline": True, "pipeline": ["quantizer", "codec"]}},
+    {"compression": {"enable-compression-pipeline": True, "high_key_num_levels": 1}},        # out of range
+    {"compression": {"enable-compression-pipeline": True, "pipeline": ["codec", "quantizer"]}},  # order
+    {"compression": {"enable-compression-pipeline": True, "axis_key": "diagonal"}},
+    {"compression": {"enable-compression-pipeline": True, "no_such_key": 1}},
+    {"raw_aggregate": True},
+    {"raw_agg": {"slot_count": 4, "logical_blocks_per_chunk": 32}},
+    {"raw_aggregate": {"slot_count": 0}},
+    {"raw_aggregate": False, "compression": {"enable-compression-pipeline": True}},
+]
+
+
+@pytest.mark.parametrize("extra", _RUNTIME_EXTRAS, ids=[str(i) for i in range(len(_RUNTIME_EXTRAS))])
+def test_runtime_config_accepts_and_rejects_what_the_reference_does(extra):
+    """The runtime's public keys (``enable-compression-pipeline``, the level
+    and axis fields, ``raw_aggregate`` / ``raw_agg``) parse to the same
+    configuration, and the same inputs are refused
+    (kvserve_v1/compression/runtime/config.py:17-221); the parser here is
+    this framework's own schema table."""
+    from kvserve_v1.compression.runtime.config import CompressionConfig as Ref
+    from kvserve_b200.compression.runtime import CompressionConfig as Ours
+    outcomes = []
+    for cls in (Ref, Ours):
+        try:
+            c = cls.from_extra_config(json.loads(json.dumps(extra)))
+            outcomes.append(("ok", c.enabled, c.transport, tuple(c.pipeline), c.uses_transformer, c.uses_quantizer,
+                             c.uses_codec, c.high_key_num_levels, c.low_value_num_levels, c.hybrid_ratio,
+                             c.split_type, c.slot_count, c.logical_blocks_per_chunk, c.seed))
+        except (ValueError, TypeError) as exc:
+            outcomes.append(("error", type(exc).__name__))
+    assert outcomes[0][0] == outcomes[1][0], outcomes
+    if outcomes[0][0] == "ok":
+        assert outcomes[0] == outcomes[1]
