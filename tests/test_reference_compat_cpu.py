@@ -435,3 +435,25 @@ def test_runtime_config_accepts_and_rejects_what_the_reference_does(extra):
     assert outcomes[0][0] == outcomes[1][0], outcomes
     if outcomes[0][0] == "ok":
         assert outcomes[0] == outcomes[1]
+
+
+@pytest.mark.parametrize("params", [{}, {"transform_type": "dct"}, {"transform_type": "haar", "seed": 9},
+                                    {"transform_type": "hadamard", "seed": 77}, {"transform_type": "walsh"},
+                                    {"seed": "12"}, {"seed": True}, {"transform_type": "dct", "seed": 1.5}],
+                         ids=lambda p: json.dumps(p))
+def test_transform_stage_accepts_what_the_reference_does(params):
+    """The transform stage takes the same profile parameters (kind, integer
+    seed, defaults hadamard / 0x3333) and refuses the same ones
+    (kvserve_v1/compression/transformer/kvserve_transformer.py:7-51); the
+    dispatch here is this framework's own registry."""
+    pytest.importorskip("triton")
+    from kvserve_v1.compression.transformer.kvserve_transformer import KVServeTransformer as Ref
+    from kvserve_b200.compression.transformer.kvserve_transformer import KVServeTransformer as Ours
+    got = []
+    for cls in (Ref, Ours):
+        try:
+            t = cls(**params)
+            got.append(("ok", t.transform_type, t.seed))
+        except ValueError:
+            got.append(("error",))
+    assert got[0] == got[1], got
