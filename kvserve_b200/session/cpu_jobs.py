@@ -12,6 +12,10 @@ the protocol with real compressed frames).
 * :class:`CpuDecodeJob` (consumer) decodes the slot into the session's
   paged blocks.
 
+A consumer on another node exports no segment (``arena=None`` and an empty
+handle): the producer's job then returns the slot's bytes, the service sends
+them inline in ``ChunkReady``, and the decode job reads them from there.
+
 Payloads in the segment are laid out exactly as on the GPU path (K at the
 slot offset, V half a slot further, each part ``part_bytes`` long).
 """
@@ -59,23 +63,31 @@ class CpuEncodeJob:
             self._mapped[handle] = m
         return m[1]
 
-    def __call__(self, session, pull) -> tuple[int, int]:
+    def __call__(self, session, pull):
         meta = session.remote_meta
-        if meta is None or not meta.arena_ipc_handle:
-            raise RuntimeError("the consumer sent no receive arena")
+        if meta is None:
+            raise RuntimeError("no consumer metadata")
         if meta.slot_bytes < 2 * self.part:
             raise RuntimeError(f"consumer slots of {meta.slot_bytes} bytes can not hold 2 x {self.part}")
-        arena = self._arena(meta.arena_ipc_handle)
+        # an exported arena is written in place; without one (a consumer on
+        # another node) the slot's bytes go back inline in the reply
+        arena = self._arena(meta.arena_ipc_handle) if meta.arena_ipc_handle else None
+        staged = torch.zeros(2 * self.part, dtype=torch.uint8) if arena is None else None
         blocks = _chunk(session.local_block_ids[0], pull.chunk_id, self.per_chunk)
         valid = _valid(session.valid_tokens_by_group[0], pull.chunk_id, self.per_chunk, self.block_size)
         payload = 0
         for part in (0, 1):
             res = self.rt.encode(0, {0: blocks}, part, valid_tokens_by_group={0: valid})
             n = res.codec_bytes
-            off = pull.slot_offset + part * self.part
-            arena[off:off + n].copy_(res.payload[:n])
+            if arena is not None:
+                off = pull.slot_offset + part * self.part
+                arena[off:off + n].copy_(res.payload[:n])
+            else:
+                staged[part * self.part:part * self.part + n].copy_(res.payload[:n])
             payload += n
         data = 2 * valid * sum(e.heads * e.head_size for e in self.rt.layout.layers) * 2
+        if staged is not None:
+            return data, payload, staged.numpy().tobytes()
         return data, payload
 
     def close(self) -> None:
@@ -97,7 +109,12 @@ class CpuDecodeJob:
         valid = _valid(session.valid_tokens_by_group[0], ready.chunk_id, self.per_chunk, self.block_size)
         buf = self.rt.receive_buffer(0)
         n = min(self.part, buf.numel())
+        inline = getattr(ready, "inline", b"")
+        src = torch.frombuffer(bytearray(inline), dtype=torch.uint8) if inline else None
         for part in (0, 1):
-            off = slot.offset + part * self.part
-            buf[:n].copy_(self.arena.view[off:off + n])
+            if src is not None:          # the payload came in the reply
+                buf[:n].copy_(src[part * self.part:part * self.part + n])
+            else:
+                off = slot.offset + part * self.part
+                buf[:n].copy_(self.arena.view[off:off + n])
             self.rt.decode(0, {0: blocks}, part, codec_bytes=n, valid_tokens_by_group={0: valid})

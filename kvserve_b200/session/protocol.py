@@ -10,7 +10,9 @@ Differences from the reference, which addresses RDMA-registered memory:
 the consumer's metadata carries CUDA IPC handles of its frame arena and of
 its publish flags, and a pull names ``slot_id`` plus ``slot_offset`` inside
 that arena; ``flag_index`` is the u32 publish flag the producer's kernel
-release-stores when the chunk's frames have landed.
+release-stores when the chunk's frames have landed.  A consumer that
+exports no arena (a peer on another node) receives each chunk's payload
+inline in its ``ChunkReady``.
 """
 from __future__ import annotations
 
@@ -70,6 +72,9 @@ class ChunkReady(msgspec.Struct, tag=True, frozen=True):
     payload_bytes: int   # bytes written into the slot
     aux_bytes: int = 0
     error: Optional[str] = None
+    # the payload itself, when the consumer exported no arena the producer
+    # can write (peers on different nodes): the reply carries the slot's bytes
+    inline: bytes = b""
 
 
 class SessionAbort(msgspec.Struct, tag=True, frozen=True):

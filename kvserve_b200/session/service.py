@@ -11,7 +11,9 @@ stay transport- and device-agnostic:
 * producer ``encode_job(session, pull) -> (data_bytes, payload_bytes)``:
   encode chunk ``pull.chunk_id`` of ``session`` into the consumer's slot
   (on a node: the fused encode kernel storing through the IPC-mapped
-  arena and release-storing flag ``pull.flag_index``);
+  arena and release-storing flag ``pull.flag_index``); a job that returns
+  ``(data_bytes, payload_bytes, payload)`` sends the payload inline in the
+  reply instead (a consumer on another node, which exported no arena);
 * consumer ``decode_job(session, slot, ready)``: decode the slot into the
   session's paged blocks; ``done_cb(session)`` fires when a session ends.
 
@@ -111,8 +113,12 @@ class ProducerService:
             self._reply(ident, tid, ChunkReady(m.chunk_id, 0, 0, error="no active session"))
             return
         s.inflight_chunks += 1
+        inline = b""
         try:
-            data_bytes, payload_bytes = self.encode_job(s, m)
+            res = self.encode_job(s, m)
+            data_bytes, payload_bytes = res[0], res[1]
+            if len(res) > 2:             # no arena to write: the payload rides in the reply
+                inline = bytes(res[2])
         except Exception as exc:  # the job's failure ends the session, never the service
             s.inflight_chunks -= 1
             s.error = f"encode failed: {exc}"
@@ -123,7 +129,7 @@ class ProducerService:
         s.completed_chunks += 1
         self.stats["payload_bytes"] += int(payload_bytes)
         self.stats["data_bytes"] += int(data_bytes)
-        self._reply(ident, tid, ChunkReady(m.chunk_id, int(data_bytes), int(payload_bytes)))
+        self._reply(ident, tid, ChunkReady(m.chunk_id, int(data_bytes), int(payload_bytes), inline=inline))
         if s.completed_chunks >= s.total_chunks:
             self._finish(s, SessionState.COMPLETE)
 

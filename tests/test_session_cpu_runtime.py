@@ -1,9 +1,10 @@
 """The chunked session protocol end to end on CPUs with real compressed
 frames: a producer process pulls chunks of its paged cache through the CPU
 runtime (Hadamard + 4-bit min-max, with and without the lossless codec)
-into the consumer process's shared-memory receive arena, and the consumer
-decodes them into its blocks.  The result must equal the same runtime round
-trip done in one process, bit for bit."""
+into the consumer process's shared-memory receive arena — or, for a
+consumer that exports no arena (another node), inline in the replies — and
+the consumer decodes them into its blocks.  The result must equal the same
+runtime round trip done in one process, bit for bit."""
 import socket
 import time
 
@@ -62,7 +63,7 @@ def _producer(port, pipeline, q):
     q.put(("producer", out))
 
 
-def _consumer(port, pipeline, q):
+def _consumer(port, pipeline, q, inline=False):
     from kvserve_b200.session.cpu_jobs import CpuDecodeJob, SharedArena
     from kvserve_b200.session.gpu_jobs import part_bytes
     from kvserve_b200.session.service import ConsumerService
@@ -72,10 +73,14 @@ def _consumer(port, pipeline, q):
         rt = _runtime(pipeline, "decode")
         dst = _caches(False)
         rt.bind_kv_caches(dst)
-        arena = SharedArena(2, 2 * part_bytes(rt))
         done = []
-        cons = ConsumerService("d0", 2, arena.slot_bytes, CpuDecodeJob(rt, arena, BS, PER_CHUNK), done.append,
-                               arena_ipc_handle=arena.handle)
+        if inline:
+            slot = (2 * part_bytes(rt) + 255) // 256 * 256
+            cons = ConsumerService("d0", 2, slot, CpuDecodeJob(rt, None, BS, PER_CHUNK), done.append)
+        else:
+            arena = SharedArena(2, 2 * part_bytes(rt))
+            cons = ConsumerService("d0", 2, arena.slot_bytes, CpuDecodeJob(rt, arena, BS, PER_CHUNK), done.append,
+                                   arena_ipc_handle=arena.handle)
         cons.open(f"tcp://127.0.0.1:{port}", "t1", "r1", [DST], TOKENS, block_size=BS,
                   logical_blocks_per_chunk=PER_CHUNK)
         deadline = time.monotonic() + 120
@@ -113,12 +118,13 @@ def _consumer(port, pipeline, q):
     q.put(("consumer", out))
 
 
+@pytest.mark.parametrize("inline", [False, True], ids=["shared-arena", "inline"])
 @pytest.mark.parametrize("pipeline", [["transformer", "quantizer"], ["transformer", "quantizer", "codec"]])
-def test_session_moves_compressed_chunks_between_cpu_processes(pipeline):
+def test_session_moves_compressed_chunks_between_cpu_processes(pipeline, inline):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_consumer, args=(port, pipeline, q)),
+    procs = [ctx.Process(target=_consumer, args=(port, pipeline, q, inline)),
              ctx.Process(target=_producer, args=(port, pipeline, q))]
     for p in procs:
         p.start()
