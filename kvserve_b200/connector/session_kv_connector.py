@@ -58,6 +58,9 @@ head>``) whose runtimes on both sides are bound to that head range of the
 caches; a request is loaded (or sent) once all its copies have ended.  Equal
 TP sizes are the one-copy case.
 Finished sessions append a JSONL row to ``KVSERVE_SESSION_STATS_PATH``.
+Engines on different nodes set ``inline_payloads``: the decode side exports
+no CUDA IPC arena and each chunk's payload travels inside the protocol's
+reply over the ZeroMQ connection.
 """
 from __future__ import annotations
 
@@ -315,6 +318,8 @@ class SessionKVConnector(KVConnectorBase_V1):
         self._host = str(extra.get("session_host") or cfg.kv_ip or "127.0.0.1")
         self._port = int(extra.get("session_port", DEFAULT_SESSION_PORT))
         self._num_slots = int(extra.get("num_slots", 4))
+        # peers on different nodes: no CUDA IPC arena, payloads inline in the replies
+        self._inline = bool(extra.get("inline_payloads", False))
         self._open_timeout_s = float(extra.get("open_timeout_s", 120.0))
         self._session_timeout_s = float(extra.get("session_timeout_s", 120.0))
         self._extra = extra
@@ -449,6 +454,8 @@ class SessionKVConnector(KVConnectorBase_V1):
             self._thread = ServiceThread(make, dev, self._collect_sends)
         else:
             job, slot_bytes, handle = self.make_decode_job(caches)
+            if self._inline:
+                handle = b""
             name = f"kvs-d{self._tp_rank}-{os.getpid()}"
             if self._use_helper:
                 def make():

@@ -15,6 +15,11 @@ messages; these callables are their ``encode_job`` / ``decode_job``:
 * :class:`RuntimeDecodeJob` (decode GPU) decodes the slot straight into the
   session's paged blocks with the fused decode kernels.
 
+Between nodes (no CUDA IPC), the consumer exports no arena: the encode job
+then encodes into its runtime's own slot and returns the bytes, the service
+sends them inline in ``ChunkReady``, and the decode job stages them in its
+runtime's receive buffer before decoding.
+
 This is the transfer the reference's Mooncake connector performs with its
 RDMA engine and session helper process
 (kvsfuse-vllm0.30.0/mooncake/mooncake_connector.py:2201-2232, 2251-2383,
@@ -79,25 +84,36 @@ class RuntimeEncodeJob:
             self._mapped[handle] = base
         return base
 
-    def __call__(self, session, pull) -> tuple[int, int]:
+    def __call__(self, session, pull):
         meta = session.remote_meta
-        if meta is None or not meta.arena_ipc_handle:
-            raise RuntimeError("the consumer sent no receive arena")
+        if meta is None:
+            raise RuntimeError("no consumer metadata")
         if meta.slot_bytes < 2 * self.part:
             raise RuntimeError(f"consumer slots of {meta.slot_bytes} bytes can not hold 2 x {self.part}")
         ready = session.send_meta
         if isinstance(ready, torch.cuda.Event):
             ready.synchronize()    # the forward that wrote these blocks has finished
-        dest = self._arena(meta.arena_ipc_handle) + pull.slot_offset
         blocks = _chunk(session.local_block_ids[0], pull.chunk_id, self.per_chunk)
         valid = _valid(session.valid_tokens_by_group[0], pull.chunk_id, self.per_chunk, self.block_size)
+        data = 2 * valid * sum(e.heads * e.head_size for e in self.rt.layout.layers) * 2
         payload = 0
+        if not meta.arena_ipc_handle:
+            # a consumer on another node: encode into this runtime's slot and
+            # return the bytes, which the service sends inline in its reply
+            staged = bytearray(2 * self.part)
+            for part in (0, 1):
+                res = self.rt.encode(0, {0: blocks}, part, valid_tokens_by_group={0: valid})
+                res.event.synchronize()
+                n = res.codec_bytes
+                staged[part * self.part:part * self.part + n] = res.payload[:n].cpu().numpy().tobytes()
+                payload += n
+            return data, payload, bytes(staged)
+        dest = self._arena(meta.arena_ipc_handle) + pull.slot_offset
         for part in (0, 1):
             res = self.rt.encode(0, {0: blocks}, part, valid_tokens_by_group={0: valid},
                                  dest_ptr=dest + part * self.part)
             res.event.synchronize()
             payload += res.codec_bytes
-        data = 2 * valid * sum(e.heads * e.head_size for e in self.rt.layout.layers) * 2
         return data, payload
 
     def close(self) -> None:
@@ -116,9 +132,21 @@ class RuntimeDecodeJob:
         self.part = part_bytes(runtime)
 
     def __call__(self, session, slot, ready) -> None:
-        src = self.arena.base + slot.offset
         blocks = _chunk(session.block_ids[0], ready.chunk_id, self.per_chunk)
         valid = _valid(session.valid_tokens_by_group[0], ready.chunk_id, self.per_chunk, self.block_size)
+        inline = getattr(ready, "inline", b"")
+        if inline:
+            # the payload came in the reply: stage it in the runtime's own
+            # receive buffer and decode from there
+            buf = self.rt.receive_buffer(0)
+            n = min(self.part, buf.numel())
+            host = torch.frombuffer(bytearray(inline), dtype=torch.uint8)
+            for part in (0, 1):
+                buf[:n].copy_(host[part * self.part:part * self.part + n])
+                self.rt.decode(0, {0: blocks}, part, codec_bytes=n, valid_tokens_by_group={0: valid}).synchronize()
+            self.rt.check_status()
+            return
+        src = self.arena.base + slot.offset
         for part in (0, 1):
             ev = self.rt.decode(0, {0: blocks}, part, codec_bytes=self.part, valid_tokens_by_group={0: valid},
                                 src_ptr=src + part * self.part)
