@@ -513,12 +513,14 @@ class SessionKVConnector(KVConnectorBase_V1):
         runtime bound to those heads of vLLM's paged cache, encoding each
         pulled chunk into the consumer's IPC-mapped slot; a session's copy
         is named by its transfer id."""
+        from ..session.cpu_jobs import CpuEncodeJob
         from ..session.gpu_jobs import RuntimeEncodeJob
         jobs = {}
         for key, c in self._copies:
             rt, cfg = self._build_runtime(caches, "encode", c)
             self._per_chunk = cfg.logical_blocks_per_chunk
-            jobs[key] = RuntimeEncodeJob(rt, self._block_size, cfg.logical_blocks_per_chunk)
+            job_cls = CpuEncodeJob if rt.device.type == "cpu" else RuntimeEncodeJob   # CPU engines: CPU runtime
+            jobs[key] = job_cls(rt, self._block_size, cfg.logical_blocks_per_chunk)
             self._closers.append(jobs[key].close)
         return lambda session, pull: jobs[self.copy_key(session.transfer_id)](session, pull)
 
@@ -526,13 +528,17 @@ class SessionKVConnector(KVConnectorBase_V1):
         """The consumer's ``decode_job`` (per KV-head copy, the runtime bound
         to those heads of its cache, reading one shared receive arena) plus
         the arena's slot size and CUDA-IPC handle."""
+        from ..session.cpu_jobs import CpuDecodeJob, SharedArena
         from ..session.gpu_jobs import ReceiveArena, RuntimeDecodeJob, part_bytes
         built = [(key, *self._build_runtime(caches, "decode", c)) for key, c in self._copies]
         self._per_chunk = built[0][2].logical_blocks_per_chunk
-        arena = ReceiveArena(self._num_slots, 2 * max(part_bytes(rt) for _, rt, _ in built), built[0][1].device)
+        slot = 2 * max(part_bytes(rt) for _, rt, _ in built)
+        cpu = built[0][1].device.type == "cpu"
+        # CPU engines: a shared-memory arena and the CPU runtime's jobs
+        arena = SharedArena(self._num_slots, slot) if cpu else ReceiveArena(self._num_slots, slot, built[0][1].device)
         self._closers.append(arena.close)
-        jobs = {key: RuntimeDecodeJob(rt, arena, self._block_size, cfg.logical_blocks_per_chunk)
-                for key, rt, cfg in built}
+        job_cls = CpuDecodeJob if cpu else RuntimeDecodeJob
+        jobs = {key: job_cls(rt, arena, self._block_size, cfg.logical_blocks_per_chunk) for key, rt, cfg in built}
         return (lambda session, slot, ready: jobs[self.copy_key(session.transfer_id)](session, slot, ready)), \
             arena.slot_bytes, arena.handle
 

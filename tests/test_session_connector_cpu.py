@@ -320,3 +320,44 @@ def test_heterogeneous_tp_pulls_each_head_range_from_its_holder():
         p_work.shutdown()
         for w in d_work:
             w.shutdown()
+
+
+@pytest.mark.parametrize("inline", [False, True], ids=["shared-arena", "inline"])
+def test_real_runtime_pull_on_cpu_engines(inline):
+    """The connector with its own jobs (no fakes) on CPU caches: the CPU
+    runtime encodes each pulled chunk (Hadamard + 4-bit) into the consumer's
+    shared-memory slot (or inline in the reply) and decodes it into the
+    request's blocks; the loaded KV is the compressed reconstruction."""
+    port = _port()
+    comp = {"enable-compression-pipeline": True, "pipeline": ["transformer", "quantizer"],
+            "logical_blocks_per_chunk": PER_CHUNK, "high_key_num_levels": 16, "low_key_num_levels": 16,
+            "high_value_num_levels": 16, "low_value_num_levels": 16}
+
+    def cfg(producer):
+        c = _vllm_config(producer, port)
+        c.kv_transfer_config.kv_connector_extra_config.update(compression=comp, inline_payloads=inline)
+        return c
+    g = torch.Generator().manual_seed(4)
+    src = torch.randn(2, NB, BS, 2, 128, generator=g).to(torch.bfloat16)
+    dst = torch.zeros_like(src)
+    p_sched, p_work = SessionKVConnector(cfg(True), KVConnectorRole.SCHEDULER), \
+        SessionKVConnector(cfg(True), KVConnectorRole.WORKER)
+    d_sched, d_work = SessionKVConnector(cfg(False), KVConnectorRole.SCHEDULER), \
+        SessionKVConnector(cfg(False), KVConnectorRole.WORKER)
+    try:
+        p_work.register_kv_caches({"model.layers.0.self_attn.attn": src})
+        d_work.register_kv_caches({"model.layers.0.self_attn.attn": dst})
+        prompt, p_blocks, d_blocks = 100, list(range(0, 7)), list(range(20, 27))
+        _, params = _prefill(p_sched, p_work, "p1", "t1", prompt, p_blocks)
+        dreq = _req("d1", prompt, dict(params), status="WAITING_FOR_REMOTE_KVS")
+        assert d_sched.get_num_new_matched_tokens(dreq, 0) == (prompt, True)
+        d_sched.update_state_after_alloc(dreq, Blocks(d_blocks, d_blocks), prompt)
+        assert _wait_recv(d_sched, d_work, "d1")
+        assert not d_work.get_block_ids_with_load_errors()
+        a = src[:, p_blocks].float().reshape(2, -1, 2, 128)[:, :prompt]
+        b = dst[:, d_blocks].float().reshape(2, -1, 2, 128)[:, :prompt]
+        assert ((a - b).norm() / a.norm()) < 0.15
+        assert dst[:, d_blocks].float().reshape(2, -1, 2, 128)[:, prompt:].abs().sum() == 0
+    finally:
+        p_work.shutdown()
+        d_work.shutdown()
