@@ -117,3 +117,28 @@ def test_cpu_runtime_frames_match_the_gpu_layout():
     for i in range(3):
         magic, _, layer, tokens = struct.unpack_from("<4I", arena, i * enc.layout.frame_stride)
         assert (magic, layer, tokens) == (FRAME_MAGIC, i, 32)
+
+
+def test_cpu_runtime_slot_safety():
+    """Slot bookkeeping of the runtime API: every encode bumps the slot's
+    generation, a chunk larger than the plan is refused before any work,
+    execution roles are enforced, and the wire profile names the layout."""
+    enc, dec = _cpu_runtimes(["transformer", "quantizer"], per_chunk=2)
+    enc.bind_kv_caches(_cpu_caches("NHD", True))
+    dec.bind_kv_caches(_cpu_caches("NHD", False))
+    g0 = enc.slots[0].generation
+    enc.encode(0, {0: [0, 1]}, "key")
+    enc.encode(0, {0: [0, 1]}, "value")
+    assert enc.slots[0].generation == g0 + 2
+    with pytest.raises(ValueError, match="more blocks"):
+        enc.encode(0, {0: [0, 1, 2]}, 0)
+    with pytest.raises(RuntimeError, match="encode only"):
+        enc.decode(0, {0: [0, 1]}, 0)
+    with pytest.raises(RuntimeError, match="decode only"):
+        dec.encode(0, {0: [0, 1]}, 0)
+    with pytest.raises(ValueError):
+        enc.encode(0, {0: [0, 1]}, "both")
+    assert enc.wire_profile.startswith("kvs-b200-frame-v1:") and enc.wire_profile == dec.wire_profile
+    other, _ = _cpu_runtimes(["transformer", "quantizer"], per_chunk=4)
+    other.bind_kv_caches(_cpu_caches("NHD", True))
+    assert other.wire_profile != enc.wire_profile          # a different chunk geometry is another profile
