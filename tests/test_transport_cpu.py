@@ -268,3 +268,24 @@ def test_slot_guards_detect_an_overrun_into_the_next_slot():
     buf[2 * (payload + guard) - 3] = GUARD_PATTERN ^ 1   # slot 1 wrote 253 bytes past its end
     assert damaged_slots(buf, slots, payload + guard, payload) == [1]
     assert damaged_slots(buf, slots, payload, payload) == []   # no guards configured
+
+
+def test_stats_rows_of_a_real_exchange_summarize(tmp_path):
+    """Rows written by both transport ends during a gloo exchange reduce to
+    per-direction counts, bytes and timing percentiles."""
+    from kvserve_b200.transport.stats_summary import read_rows, summarize
+    path = tmp_path / "stats.jsonl"
+    os.environ["KVSERVE_TRANSPORT_STATS_PATH"] = str(path)
+    try:
+        res, ok = _run()
+    finally:
+        os.environ.pop("KVSERVE_TRANSPORT_STATS_PATH", None)
+    assert ok
+    with open(path, "a") as f:
+        f.write('{"direction": "send", "trunc')                 # a row cut by a crashed writer is skipped
+    s = summarize(read_rows([str(path)]))
+    d = s["directions"]
+    assert d["send"]["count"] == 4 and d["recv"]["count"] == 4
+    assert d["send"]["payload_bytes"] == d["recv"]["payload_bytes"] > 0
+    assert d["send"]["total_s"]["p50_ms"] <= d["send"]["total_s"]["p95_ms"] <= d["send"]["total_s"]["max_ms"]
+    assert "recv_credit" in d and s["credit_retries"] >= 0
