@@ -50,7 +50,8 @@ from typing import Optional
 
 import torch
 
-from .session_kv_connector import KVConnectorBase_V1, KVConnectorMetadata, KVConnectorRole, layer_index
+from .session_kv_connector import (KVConnectorBase_V1, KVConnectorMetadata, KVConnectorRole, KVConnectorStats,
+                                   layer_index)
 
 log = logging.getLogger("kvserve_b200.store_connector")
 
@@ -69,6 +70,31 @@ class StoreSave:
     request_id: str
     token_ids: list
     block_ids: list
+
+
+@dataclass
+class StoreStats(KVConnectorStats):
+    """Per-interval store telemetry for vLLM's metrics logger: prefix tokens
+    loaded, chunks saved, chunks that had vanished at load time."""
+
+    def __post_init__(self):
+        for k in ("loaded_tokens", "saved_chunks", "load_errors"):
+            self.data.setdefault(k, 0)
+
+    def reset(self):
+        self.data = {}
+        self.__post_init__()
+
+    def aggregate(self, other: "KVConnectorStats") -> "KVConnectorStats":
+        for k, v in other.data.items():
+            self.data[k] = self.data.get(k, 0) + v
+        return self
+
+    def reduce(self) -> dict:
+        return {k: self.data.get(k, 0) for k in ("loaded_tokens", "saved_chunks", "load_errors")}
+
+    def is_empty(self) -> bool:
+        return not any(self.data.get(k) for k in ("loaded_tokens", "saved_chunks", "load_errors"))
 
 
 @dataclass
@@ -105,6 +131,8 @@ class StoreKVConnector(KVConnectorBase_V1):
         self._pending_saves: list[StoreSave] = []
         self._local_hit: dict[str, int] = {}
         self._load_errors: set = set()
+        self._errors_total = 0
+        self._stats_seen: dict = {}
         self.stats = {"lookups": 0, "hit_tokens": 0, "loaded_tokens": 0, "saved_chunks": 0}
         if role == KVConnectorRole.WORKER:
             try:
@@ -214,6 +242,7 @@ class StoreKVConnector(KVConnectorBase_V1):
                 first_missing = got // self._block_size
                 last = -(-ld.num_tokens // self._block_size)
                 self._load_errors.update(ld.block_ids[max(first_missing, ld.first_block):last])
+                self._errors_total += 1
                 log.warning("store: request %s loaded %d of %d prefix tokens", ld.request_id, got, ld.num_tokens)
 
     def wait_for_layer_load(self, layer_name: str) -> None:
@@ -240,6 +269,19 @@ class StoreKVConnector(KVConnectorBase_V1):
 
     def get_finished(self, finished_req_ids: set):
         return None, None
+
+    def get_kv_connector_stats(self):
+        """This interval's store telemetry, then reset."""
+        cur = {"loaded_tokens": self.stats["loaded_tokens"], "saved_chunks": self.stats["saved_chunks"],
+               "load_errors": self._errors_total}
+        delta = {k: v - self._stats_seen.get(k, 0) for k, v in cur.items()}
+        self._stats_seen = cur
+        st = StoreStats(data=delta)
+        return None if st.is_empty() else st
+
+    @classmethod
+    def build_kv_connector_stats(cls, data=None):
+        return StoreStats(data=dict(data or {}))
 
     def get_block_ids_with_load_errors(self) -> set:
         out, self._load_errors = self._load_errors, set()

@@ -96,6 +96,10 @@ def test_second_engine_loads_the_stored_prefix(tmp_path, compressed):
         b_sched.update_state_after_alloc(req, Blocks(b_blocks), 96)
         _step(b_sched, b_work, _so([("b1", prompt_b, b_blocks, 96, 14)]))
         assert b_work.stats["loaded_tokens"] == 96 and not b_work.get_block_ids_with_load_errors()
+        st = b_work.get_kv_connector_stats()            # vLLM's per-interval telemetry
+        assert st.reduce() == {"loaded_tokens": 96, "saved_chunks": 0, "load_errors": 0}
+        assert b_work.get_kv_connector_stats() is None
+        assert a_work.get_kv_connector_stats().reduce()["saved_chunks"] == 3
         got, want = _stack(b_kv, b_blocks[:6]), _stack(a_kv, a_blocks[:6])
         if compressed:
             assert ((got - want).norm() / want.norm()) < 0.2
