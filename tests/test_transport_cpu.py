@@ -289,3 +289,21 @@ def test_stats_rows_of_a_real_exchange_summarize(tmp_path):
     assert d["send"]["payload_bytes"] == d["recv"]["payload_bytes"] > 0
     assert d["send"]["total_s"]["p50_ms"] <= d["send"]["total_s"]["p95_ms"] <= d["send"]["total_s"]["max_ms"]
     assert "recv_credit" in d and s["credit_retries"] >= 0
+
+
+def test_llm_facade_resolves_profiles_and_is_exported():
+    """The package root's ``LLM`` entry resolves transfer profiles by name,
+    by connector-style profile dict or JSON file, or passes one through."""
+    import kvserve_b200
+    from kvserve_b200.engine.api import LLM, resolve_profile
+    from kvserve_b200.engine.transfer import TransferProfile
+    assert kvserve_b200.LLM is LLM
+    assert resolve_profile("raw").compressed is False and resolve_profile(None).compressed is False
+    k4v2 = resolve_profile("k4v2")
+    assert k4v2.compressed and tuple(k4v2.value_levels) == (4, 4)
+    from_file = resolve_profile("configs/compression/hadamard_k4v2_bitpack.json")
+    assert from_file.compressed
+    p = TransferProfile.raw()
+    assert resolve_profile(p) is p
+    with pytest.raises(ValueError):
+        resolve_profile(3.14)
