@@ -457,3 +457,23 @@ def test_transform_stage_accepts_what_the_reference_does(params):
         except ValueError:
             got.append(("error",))
     assert got[0] == got[1], got
+
+
+@pytest.mark.parametrize("split", ["head", "layer"])
+@pytest.mark.parametrize("layer", [0, 13, 30])
+def test_hybrid_quantizer_round_trip_equals_reference(split, layer):
+    """The hybrid min-max quantizer (low-precision heads by DuoAttention
+    score or the last third of the layers, per-channel keys and per-token
+    values) restores exactly what the reference's restores
+    (kvserve_v1/compression/quantizer/kvserve_quantizer.py:22-260)."""
+    from kvserve_v1.compression.quantizer.kvserve_quantizer import KVServeQuantizer as Ref
+    from kvserve_b200.compression.quantizer.kvserve_quantizer import KVServeQuantizer as Ours
+    params = dict(model_name="Llama-3.1-8B-Instruct", hybrid_ratio=0.5, high_key_max_value=16,
+                  high_value_max_value=8, low_key_max_value=6, low_value_max_value=4, axis_key="channel",
+                  axis_value="token", split_type=split)
+    g = torch.Generator().manual_seed(layer)
+    x = (torch.randn((2, 3, 16, 8, 128), generator=g) * 2).to(torch.bfloat16)
+    ref, ours = Ref(**params), Ours(**params)
+    rq, rmeta = ref.quantize(layer, x)
+    oq, ometa = ours.quantize(layer, x)
+    assert torch.equal(ref.dequantize(layer, rq, rmeta), ours.dequantize(layer, oq, ometa))
