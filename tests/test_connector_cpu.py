@@ -209,3 +209,29 @@ def test_inject_on_vllm_022_caches_both_layouts():
     assert torch.equal(fa[:, [3, 1]], stacked[0])
     assert torch.equal(fi[[3, 1]], stacked[1].transpose(0, 1))
     assert torch.equal(old[:, [3, 1]], stacked[2])
+
+
+def test_example_configs_build_and_name_real_connectors():
+    """The examples' vLLM configurations build and point at importable
+    connector classes."""
+    import importlib
+    import os
+    import sys
+    pytest.importorskip("vllm")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "examples"))
+    try:
+        ex = importlib.import_module("vllm_connectors")
+        cfgs = [ex.push_config("kv_producer"), ex.push_config("kv_consumer", data_plane="ipc"),
+                ex.pull_config("kv_producer"), ex.pull_config("kv_consumer", prefill_tp=1, decode_tp=2),
+                ex.store_config("/tmp/kvs-store-example", disk_bytes=1 << 30)]
+        for c in cfgs:
+            cls = getattr(importlib.import_module(c.kv_connector_module_path), c.kv_connector)
+            assert cls.__name__ == c.kv_connector
+        assert cfgs[3].kv_connector_extra_config["decode_tp_size"] == 2
+        p = ex.pull_prefill_params("t-1")
+        assert p.max_tokens == 1 and p.extra_args["kv_transfer_params"]["do_remote_decode"]
+        with pytest.raises(ValueError):
+            ex.push_config("kv_both")
+    finally:
+        sys.path.remove(os.path.join(root, "examples"))
