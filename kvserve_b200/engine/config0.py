@@ -20,6 +20,7 @@ from __future__ import annotations
 
 import json
 import multiprocessing as mp
+import os
 import socket
 import time
 
@@ -52,7 +53,19 @@ def _adapter():
     return KVCompressionAdapter(PROFILE, num_kv_heads=HEADS, head_size=DIM, num_layers=LAYERS)
 
 
-def _producer(port: int, q) -> None:
+def _finish(q, role: str, out: dict, done=None) -> None:
+    """Report, then leave without closing the transport: its control thread
+    may still be inside a ZeroMQ call, and closing the socket under it aborts
+    the process before the report is out."""
+    q.put((role, out))
+    if done is not None:
+        done.wait(60)            # the consumer may still be returning credits
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def _producer(port: int, q, done) -> None:
     from ..compression.adapter import add_sentinel
     from ..compression.wire import build_wire
     from ..transport.nccl_transport import NcclTransport
@@ -73,15 +86,13 @@ def _producer(port: int, q) -> None:
                       w.aux_tensors)
         out["sent"] = bool(t.wait_for_sent(timeout=120))
         out["send_ms"] = 1e3 * (time.perf_counter() - t0)
-        time.sleep(0.5)
-        t.close()
     except Exception:  # noqa: BLE001 - reported to the parent
         import traceback
         out["error"] = traceback.format_exc()
-    q.put(("producer", out))
+    _finish(q, "producer", out, done)
 
 
-def _consumer(port: int, q) -> None:
+def _consumer(port: int, q, done) -> None:
     from ..compression.adapter import is_compressed_layer_names
     from ..compression.wire import CompressedWire, restore_from_wire
     from ..transport.nccl_transport import NcclTransport
@@ -113,12 +124,10 @@ def _consumer(port: int, q) -> None:
         out["mse_values"] = float(err[:, 1].pow(2).mean())
         out["relative_error"] = float(err.norm() / kv.norm())
         out["signal_power"] = float(kv.pow(2).mean())
-        time.sleep(0.5)
-        t.close()
     except Exception:  # noqa: BLE001 - reported to the parent
         import traceback
         out["error"] = traceback.format_exc()
-    q.put(("consumer", out))
+    _finish(q, "consumer", out)
 
 
 def _free_port() -> int:
@@ -132,10 +141,10 @@ def _free_port() -> int:
 def run(timeout_s: float = 180.0) -> dict:
     """Run both processes; returns the merged report (``error`` set on failure)."""
     ctx = mp.get_context("spawn")
-    q = ctx.Queue()
+    q, done = ctx.Queue(), ctx.Event()
     port = _free_port()
-    cons = ctx.Process(target=_consumer, args=(port, q))
-    prod = ctx.Process(target=_producer, args=(port, q))
+    cons = ctx.Process(target=_consumer, args=(port, q, done))
+    prod = ctx.Process(target=_producer, args=(port, q, done))
     cons.start()
     time.sleep(0.5)
     prod.start()
@@ -144,7 +153,12 @@ def run(timeout_s: float = 180.0) -> dict:
         for _ in range(2):
             role, out = q.get(timeout=timeout_s)
             res[role] = out
+            if role == "consumer":
+                done.set()
+    except Exception as e:  # noqa: BLE001 - a child that never reported
+        res.setdefault("consumer", {"error": f"no report: {type(e).__name__}"})
     finally:
+        done.set()
         for p in (prod, cons):
             p.join(30)
             if p.is_alive():

@@ -58,7 +58,19 @@ def _caches(fill):
     return {f"model.layers.{i}.self_attn.attn": mk().to(torch.bfloat16) for i in range(L)}
 
 
-def _producer(port, compression, q):
+def _finish(q, role, out, done=None):
+    """Report and leave without tearing the transport down: its control
+    thread may still be inside a ZeroMQ call, and closing the socket under it
+    aborts the process."""
+    q.put((role, out))
+    if done is not None:
+        done.wait(60)          # the consumer may still need this side's replies
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def _producer(port, compression, q, done):
     out = {"error": None}
     try:
         c = _connector(True, port, compression)
@@ -66,16 +78,13 @@ def _producer(port, compression, q):
             c.save_kv_layer(name, kv, None)
         c.wait_for_save()
         c.shutdown()
-        import time
-        time.sleep(0.5)
-        c._transport.close()
     except Exception:  # noqa: BLE001
         import traceback
         out["error"] = traceback.format_exc()
-    q.put(("producer", out))
+    _finish(q, "producer", out, done)
 
 
-def _consumer(port, compression, q):
+def _consumer(port, compression, q, done):
     out = {"error": None}
     try:
         c = _connector(False, port, compression)
@@ -92,29 +101,36 @@ def _consumer(port, compression, q):
         out["max_rel_err"] = max(errs)
         out["others_zero"] = all(float(caches[n].index_select(1, torch.tensor([0, 5, 11])).abs().sum()) == 0
                                  for n in caches)
-        c._transport.close()
     except Exception:  # noqa: BLE001
         import traceback
         out["error"] = traceback.format_exc()
-    q.put(("consumer", out))
+    _finish(q, "consumer", out)
 
 
 @pytest.mark.parametrize("compression", [None, PROFILE], ids=["raw", "k4v4"])
 def test_push_connector_moves_a_request_over_gloo(compression):
     ctx = mp.get_context("spawn")
-    q = ctx.Queue()
+    q, done = ctx.Queue(), ctx.Event()
     port = _port()
-    procs = [ctx.Process(target=_consumer, args=(port, compression, q)),
-             ctx.Process(target=_producer, args=(port, compression, q))]
+    procs = [ctx.Process(target=_consumer, args=(port, compression, q, done)),
+             ctx.Process(target=_producer, args=(port, compression, q, done))]
     procs[0].start()
     import time
     time.sleep(0.5)
     procs[1].start()
-    res = dict(q.get(timeout=240) for _ in procs)
-    for p in procs:
-        p.join(30)
-        if p.is_alive():
-            p.kill()
+    try:
+        res = {}
+        for _ in procs:
+            role, out = q.get(timeout=120)
+            res[role] = out
+            if role == "consumer":
+                done.set()
+    finally:
+        done.set()
+        for p in procs:
+            p.join(30)
+            if p.is_alive():
+                p.kill()
     for r in res.values():
         assert r["error"] is None, r["error"]
     c = res["consumer"]

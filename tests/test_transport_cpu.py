@@ -42,6 +42,8 @@ def _consumer(port, q, capacity, faults_env, expect):
         else:
             out[rid] = ("raw", names, payload.sum().item(), list(payload.shape))
     q.put(out)
+    q.close()
+    q.join_thread()            # the report is out before the transport is torn down
     time.sleep(0.5)
     t.close()
 
@@ -55,6 +57,8 @@ def _producer(port, q, n_raw):
                   [torch.arange(4, dtype=torch.int16)])
     ok = t.wait_for_sent(timeout=60)
     q.put(ok)
+    q.close()
+    q.join_thread()
     time.sleep(1.0)
     t.close()
 
