@@ -333,6 +333,7 @@ class SessionKVConnector(KVConnectorBase_V1):
         total = getattr(getattr(vllm_config, "model_config", None), "get_total_num_kv_heads", None)
         self._num_kv_heads = int(extra.get("num_kv_heads") or (total() if callable(total) else 0))
         self._copies: list = []
+        self._window_blocks = self.sliding_window_blocks(kv_cache_config)
         # scheduler state
         self._pending_sends: list[SendReq] = []
         self._pending_recvs: list[RecvReq] = []
@@ -369,6 +370,31 @@ class SessionKVConnector(KVConnectorBase_V1):
                 self._tp_rank = 0
 
     # ------------------------------------------------------------ helpers
+    @staticmethod
+    def sliding_window_blocks(kv_cache_config) -> int:
+        """How many trailing blocks of a request carry KV that attention
+        still reads, for a sliding-window KV-cache group (0: full attention,
+        every block).  vLLM swaps blocks that fell out of the window for its
+        null block, so only the last ``ceil(window / block_size) + 1`` blocks
+        are sent (the window's first token may sit inside a block, which adds
+        one).  The role of the reference's sliding-window clip,
+        kvsfuse-vllm0.30.0/mooncake/mooncake_connector.py:833-862.  The
+        connector moves one KV-cache group; a hybrid layout with several
+        groups is refused rather than half-transferred."""
+        groups = list(getattr(kv_cache_config, "kv_cache_groups", None) or [])
+        if len(groups) > 1:
+            raise ValueError(f"SessionKVConnector transfers one KV-cache group, this model has {len(groups)}; "
+                             "run vLLM with the hybrid KV-cache manager disabled")
+        if not groups:
+            return 0
+        spec = getattr(groups[0], "kv_cache_spec", None)
+        window = getattr(spec, "sliding_window", None)
+        # a FullAttentionSpec may carry a window too (hybrid manager off): then
+        # every block stays allocated, and possibly prefix-cached, so all move
+        if type(spec).__name__ != "SlidingWindowSpec" or not window:
+            return 0
+        return -(-int(window) // int(spec.block_size)) + 1
+
     def runtime_config(self):
         from ..compression.runtime import CompressionConfig
         comp = self._extra.get("compression")
@@ -722,6 +748,8 @@ class SessionKVConnector(KVConnectorBase_V1):
             return
         get = getattr(blocks, "get_unhashed_block_ids_all_groups", None)
         ids = get()[0] if get is not None else blocks.get_block_ids()[0]
+        if self._window_blocks and len(ids) > self._window_blocks:
+            ids = ids[-self._window_blocks:]      # the rest fell out of the sliding window
         prompt = len(request.prompt_token_ids or [])
         full = -(-prompt // self._block_size)
         # the prompt's last `len(ids)` blocks are loaded; tokens from their start

@@ -207,6 +207,52 @@ def test_cached_prefix_pulls_only_the_suffix():
         d_work.shutdown()
 
 
+class SlidingWindowSpec:          # the name vLLM's sliding-window KV-cache spec has
+    def __init__(self, window):
+        self.sliding_window, self.block_size = window, BS
+
+
+class FullAttentionSpec(SlidingWindowSpec):
+    pass
+
+
+def _groups(*specs):
+    return NS(kv_cache_groups=[NS(kv_cache_spec=s) for s in specs])
+
+
+def test_sliding_window_pulls_only_the_blocks_in_the_window():
+    FakeJobs.seen.clear()
+    port = _port()
+    src, dst, p_sched, _, p_work, d_work = _pair(port)
+    # a 40-token window over 16-token blocks: the last ceil(40/16) + 1 = 4 blocks
+    d_sched = FakeJobs(_vllm_config(False, port), KVConnectorRole.SCHEDULER, _groups(SlidingWindowSpec(40)))
+    try:
+        prompt, p_blocks, d_blocks = 100, list(range(0, 7)), list(range(30, 37))
+        _, params = _prefill(p_sched, p_work, "p5", "t5", prompt, p_blocks)
+        dreq = _req("d5", prompt, dict(params), status="WAITING_FOR_REMOTE_KVS")
+        assert d_sched.get_num_new_matched_tokens(dreq, 0) == (prompt, True)
+        d_sched.update_state_after_alloc(dreq, Blocks(d_blocks, d_blocks), prompt)
+        assert _wait_recv(d_sched, d_work, "d5")
+        assert torch.equal(dst[:, d_blocks[3:]], src[:, p_blocks[3:]])
+        assert dst[:, d_blocks[:3]].abs().sum() == 0            # out of the window: not sent
+        assert [ids for ids, _ in FakeJobs.seen] == [(3, 4), (5, 6)]
+        assert all(v == prompt - 3 * BS for _, v in FakeJobs.seen)
+    finally:
+        p_work.shutdown()
+        d_work.shutdown()
+
+
+def test_window_and_group_rules():
+    blocks = SessionKVConnector.sliding_window_blocks
+    assert blocks(None) == 0 and blocks(_groups()) == 0
+    assert blocks(_groups(SlidingWindowSpec(4096))) == 257
+    assert blocks(_groups(SlidingWindowSpec(48))) == 4
+    # a full-attention spec that carries a window keeps every block
+    assert blocks(_groups(FullAttentionSpec(4096))) == 0
+    with pytest.raises(ValueError, match="one KV-cache group"):
+        blocks(_groups(FullAttentionSpec(None), SlidingWindowSpec(4096)))
+
+
 @pytest.mark.parametrize("helper", [False, True], ids=["service-thread", "helper-process"])
 def test_unknown_transfer_reports_load_errors(helper):
     src, dst, p_sched, d_sched, p_work, d_work = _pair(_port(), helper)
