@@ -67,7 +67,8 @@ class PDEngine:
     def __init__(self, cfg: ModelConfig, ctx: ParallelContext, profile: TransferProfile, max_prompt: int = 8192,
                  max_new_tokens: int = 128, block_size: int = 16, seed: int = 0, link_gbps: float = 0.0,
                  use_graphs: bool = True, ingest_timeout_s: float = 30.0, encode_ctas: int = 222,
-                 profiles: Optional[dict] = None, num_slots: int = 2, max_batch: int = 1):
+                 profiles: Optional[dict] = None, num_slots: int = 2, max_batch: int = 1,
+                 checkpoint: Optional[str] = None):
         self.cfg, self.ctx, self.profile = cfg, ctx, profile
         self.device = torch.device("cuda", torch.cuda.current_device())
         self.max_prompt, self.max_new, self.block_size = max_prompt, max_new_tokens, block_size
@@ -80,6 +81,8 @@ class PDEngine:
         self.model = LlamaShard(cfg, ctx.tp_rank, ctx.tp_size, self.device, seed, ctx.tp_group,
                                 max_position=max_prompt + max_new_tokens + block_size)
         m = self.model
+        if checkpoint:          # weights saved by LlamaShard.save, one file per TP shard
+            m.load(checkpoint)
         # prefill ranks reduce their row-parallel projections inside the GEMM
         m.tp_ar = create_tp_allreduce(ctx, max_prompt, cfg.hidden, self.device, participate=ctx.is_prefill)
         # decode ranks fuse their per-step collectives into the projections

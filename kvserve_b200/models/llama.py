@@ -7,13 +7,15 @@ down row-parallel followed by an NCCL all-reduce over NVLink; the LM head is
 vocab-parallel with a distributed greedy argmax.  KV heads are replicated when
 ``tp_size > num_kv_heads``.  Weights are random-initialised per shard from a
 deterministic seed, so the prefill and decode ranks of one TP index hold
-identical shards without any checkpoint.
+identical shards without any checkpoint; ``save`` / ``load`` write and read
+one safetensors file per shard for runs that want the weights on disk.
 """
 from __future__ import annotations
 
 import hashlib
 import math
-from dataclasses import dataclass
+import os
+from dataclasses import dataclass, fields
 from typing import Callable, Optional
 
 import torch
@@ -106,6 +108,64 @@ class LlamaShard:
         t = torch.empty(shape, dtype=torch.bfloat16, device=self.device)
         t.normal_(0.0, self.init_std if std is None else std, generator=g)
         return t
+
+    # ----------------------------------------------------------- checkpoint
+    CHECKPOINT_FORMAT = "kvserve_b200-llama-shard-v1"
+
+    def state_dict(self) -> dict:
+        """This shard's weights by name (views, not copies): ``embed``,
+        ``lm_head``, ``final_norm`` and ``layers.<l>.<field>`` in the layout
+        the kernels read (gate/up rows interleaved in GATE_UP_BLOCK blocks)."""
+        sd = {"embed": self.embed, "lm_head": self.lm_head, "final_norm": self.final_norm}
+        for l, lw in enumerate(self.layers):
+            for f in fields(LayerWeights):
+                t = getattr(lw, f.name)
+                if t is not None:
+                    sd[f"layers.{l}.{f.name}"] = t
+        return sd
+
+    def load_state_dict(self, sd: dict) -> None:
+        """Copy ``sd`` into the shard's tensors in place, so CUDA graphs and
+        the collective workspaces that hold their addresses stay valid; the
+        names, shapes and dtypes must match exactly."""
+        own = self.state_dict()
+        missing, unexpected = sorted(own.keys() - sd.keys()), sorted(sd.keys() - own.keys())
+        if missing or unexpected:
+            raise KeyError(f"checkpoint does not match the shard: missing {missing[:4]}, unexpected {unexpected[:4]}")
+        for name, t in own.items():
+            src = sd[name]
+            if tuple(src.shape) != tuple(t.shape) or src.dtype != t.dtype:
+                raise ValueError(f"{name}: checkpoint {tuple(src.shape)} {src.dtype}, shard {tuple(t.shape)} {t.dtype}")
+            t.copy_(src)
+
+    @staticmethod
+    def shard_path(prefix: str, tp_rank: int, tp_size: int) -> str:
+        return f"{prefix}.tp{tp_rank}of{tp_size}.safetensors"
+
+    def save(self, prefix: str) -> str:
+        """Write this shard to ``<prefix>.tp<rank>of<size>.safetensors``
+        (atomically: ranks of two engines that hold the same shard may write
+        it at once) and return the path."""
+        from safetensors.torch import save_file
+        path = self.shard_path(prefix, self.tp_rank, self.tp_size)
+        tmp = f"{path}.{os.getpid()}.tmp"
+        meta = {"format": self.CHECKPOINT_FORMAT, "model": self.cfg.name, "seed": str(self.seed),
+                "tp_rank": str(self.tp_rank), "tp_size": str(self.tp_size)}
+        save_file({k: v.contiguous() for k, v in self.state_dict().items()}, tmp, metadata=meta)
+        os.replace(tmp, path)
+        return path
+
+    def load(self, prefix: str) -> None:
+        """Load the shard this rank holds from ``save``'s file of the same TP
+        geometry."""
+        from safetensors import safe_open
+        path = self.shard_path(prefix, self.tp_rank, self.tp_size)
+        with safe_open(path, framework="pt", device=str(self.device)) as f:
+            meta = f.metadata() or {}
+            if meta.get("format") != self.CHECKPOINT_FORMAT or meta.get("model") != self.cfg.name:
+                raise ValueError(f"{path} holds {meta.get('model')!r} in format {meta.get('format')!r}, "
+                                 f"not {self.cfg.name!r}")
+            self.load_state_dict({k: f.get_tensor(k) for k in f.keys()})
 
     def weight_bytes(self) -> int:
         n = sum(t.numel() for lw in self.layers for t in (lw.qkv, lw.o, lw.gate_up, lw.down))
