@@ -116,6 +116,8 @@ class CompressedKVConnectorMetadata(KVConnectorMetadata):
 class CompressedKVConnector(KVConnectorBase_V1):
     def __init__(self, vllm_config, role, kv_cache_config=None):
         super().__init__(vllm_config, role, kv_cache_config)
+        from .kv_groups import sliding_window_blocks
+        sliding_window_blocks(kv_cache_config, "CompressedKVConnector")   # refuses several KV-cache groups
         cfg = vllm_config.kv_transfer_config
         self.is_producer = cfg.is_kv_producer
         self._block_size = vllm_config.cache_config.block_size

@@ -372,28 +372,10 @@ class SessionKVConnector(KVConnectorBase_V1):
     # ------------------------------------------------------------ helpers
     @staticmethod
     def sliding_window_blocks(kv_cache_config) -> int:
-        """How many trailing blocks of a request carry KV that attention
-        still reads, for a sliding-window KV-cache group (0: full attention,
-        every block).  vLLM swaps blocks that fell out of the window for its
-        null block, so only the last ``ceil(window / block_size) + 1`` blocks
-        are sent (the window's first token may sit inside a block, which adds
-        one).  The role of the reference's sliding-window clip,
-        kvsfuse-vllm0.30.0/mooncake/mooncake_connector.py:833-862.  The
-        connector moves one KV-cache group; a hybrid layout with several
-        groups is refused rather than half-transferred."""
-        groups = list(getattr(kv_cache_config, "kv_cache_groups", None) or [])
-        if len(groups) > 1:
-            raise ValueError(f"SessionKVConnector transfers one KV-cache group, this model has {len(groups)}; "
-                             "run vLLM with the hybrid KV-cache manager disabled")
-        if not groups:
-            return 0
-        spec = getattr(groups[0], "kv_cache_spec", None)
-        window = getattr(spec, "sliding_window", None)
-        # a FullAttentionSpec may carry a window too (hybrid manager off): then
-        # every block stays allocated, and possibly prefix-cached, so all move
-        if type(spec).__name__ != "SlidingWindowSpec" or not window:
-            return 0
-        return -(-int(window) // int(spec.block_size)) + 1
+        """Trailing blocks of a request worth sending (0: all of them);
+        see :func:`~kvserve_b200.connector.kv_groups.sliding_window_blocks`."""
+        from .kv_groups import sliding_window_blocks
+        return sliding_window_blocks(kv_cache_config, "SessionKVConnector")
 
     def runtime_config(self):
         from ..compression.runtime import CompressionConfig

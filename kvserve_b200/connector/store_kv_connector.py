@@ -106,6 +106,12 @@ class StoreConnectorMetadata(KVConnectorMetadata):
 class StoreKVConnector(KVConnectorBase_V1):
     def __init__(self, vllm_config, role, kv_cache_config=None):
         super().__init__(vllm_config, role, kv_cache_config)
+        from .kv_groups import sliding_window_blocks
+        if sliding_window_blocks(kv_cache_config, "StoreKVConnector"):
+            # stored chunks are whole prompt prefixes, but blocks that left the
+            # window hold stale KV: a shorter request reusing them would read it
+            raise ValueError("StoreKVConnector keeps whole prompt prefixes; sliding-window KV-cache groups "
+                             "free blocks outside the window, so their chunks can not be stored")
         extra = dict(vllm_config.kv_transfer_config.kv_connector_extra_config or {})
         st = dict(extra.get("store") or {})
         self._dir = st.get("dir")

@@ -149,3 +149,20 @@ def test_chunk_missing_at_load_time_is_reported(tmp_path):
         a_work.shutdown()
         b_work.shutdown()
         b_sched.shutdown()
+
+
+def test_sliding_window_and_hybrid_layouts_are_refused(tmp_path):
+    class SlidingWindowSpec:                 # the name of vLLM's sliding-window spec
+        sliding_window, block_size = 4096, BS
+
+    class FullAttentionSpec:
+        sliding_window, block_size = None, BS
+
+    def groups(*specs):
+        return NS(kv_cache_groups=[NS(kv_cache_spec=s()) for s in specs])
+
+    with pytest.raises(ValueError, match="sliding-window"):
+        StoreKVConnector(_cfg(str(tmp_path)), KVConnectorRole.SCHEDULER, groups(SlidingWindowSpec))
+    with pytest.raises(ValueError, match="one KV-cache group"):
+        StoreKVConnector(_cfg(str(tmp_path)), KVConnectorRole.SCHEDULER, groups(FullAttentionSpec, SlidingWindowSpec))
+    StoreKVConnector(_cfg(str(tmp_path)), KVConnectorRole.SCHEDULER, groups(FullAttentionSpec)).shutdown()
