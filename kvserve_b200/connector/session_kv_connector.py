@@ -21,8 +21,15 @@ pull-based connectors:
 
 * prefill request: ``{"do_remote_decode": True, "transfer_id": T}``; the
   prefill engine's output carries ``{"do_remote_prefill": True,
-  "transfer_id": T, "remote_host": h, "remote_port": p, "remote_tp_size": n}``;
+  "transfer_id": T, "remote_host": h, "remote_port": p, "remote_tp_size": n,
+  "remote_engine_id": e}``;
 * decode request: that dict unchanged.
+
+With ``bootstrap_url`` in the extra config (the service of
+:mod:`kvserve_b200.session.bootstrap`), prefill workers register their
+session endpoints under the engine id and decode workers look the prefill
+rank up there; without it, or when the service does not know the engine,
+the endpoint is ``remote_host`` and ``remote_port`` + rank.
 
 Flow:
 
@@ -112,6 +119,7 @@ class RecvReq:
     port: int
     block_ids: list
     num_tokens: int
+    engine_id: str = ""          # the prefill engine, for a bootstrap lookup
 
 
 @dataclass
@@ -323,6 +331,12 @@ class SessionKVConnector(KVConnectorBase_V1):
         self._open_timeout_s = float(extra.get("open_timeout_s", 120.0))
         self._session_timeout_s = float(extra.get("session_timeout_s", 120.0))
         self._extra = extra
+        # optional registry of session endpoints: prefill workers register,
+        # decode workers look up the producer's rank instead of host:port+rank
+        self._bootstrap_url = str(extra.get("bootstrap_url") or "")
+        self._engine_id = str(extra.get("engine_id") or getattr(cfg, "engine_id", None) or
+                              f"{self._host}:{self._port}")
+        self._endpoints: dict[tuple[str, int], str] = {}
         self._tp_size = int(getattr(vllm_config.parallel_config, "tensor_parallel_size", 1) or 1)
         self._tp_rank = 0
         # TP sizes of the two engines (heterogeneous TP: KV-head copies)
@@ -481,6 +495,10 @@ class SessionKVConnector(KVConnectorBase_V1):
             self._thread = ServiceThread(make, dev, after)
         self._thread.start()
         self._thread.wait_ready()
+        if self.is_producer and self._bootstrap_url:
+            from ..session.bootstrap import BootstrapClient
+            BootstrapClient(self._bootstrap_url).register(
+                self._engine_id, self._tp_rank, f"tcp://{self._host}:{self._port + self._tp_rank}", self._tp_size)
 
     def _helper(self, role: str, cfg: dict, job) -> _HelperProxy:
         """Start the session helper process; its GPU jobs run ``job`` on the
@@ -572,11 +590,31 @@ class SessionKVConnector(KVConnectorBase_V1):
                 for key, _ in self._copies:
                     self._recv[self.copy_tid(r.transfer_id, key)] = r
             for key, c in self._copies:
-                endpoint = f"tcp://{r.host}:{r.port + c.src_rank}"
-                self._thread.submit(lambda svc, r=r, ep=endpoint, ct=self.copy_tid(r.transfer_id, key),
+                # the endpoint is looked up on the service thread: a bootstrap
+                # query never stalls the model runner
+                self._thread.submit(lambda svc, r=r, rank=c.src_rank, ct=self.copy_tid(r.transfer_id, key),
                                     pc=self._per_chunk: svc.open(
-                    ep, ct, r.request_id, [list(r.block_ids)], r.num_tokens, block_size=self._block_size,
-                    logical_blocks_per_chunk=pc))
+                    self._endpoint(r, rank), ct, r.request_id, [list(r.block_ids)], r.num_tokens,
+                    block_size=self._block_size, logical_blocks_per_chunk=pc))
+
+    def _endpoint(self, r: RecvReq, src_rank: int) -> str:
+        """The session endpoint of prefill rank ``src_rank`` of ``r``'s
+        engine: from the bootstrap service when one is configured and knows
+        the engine (cached), else the request's host and port + rank."""
+        if self._bootstrap_url and r.engine_id:
+            key = (r.engine_id, src_rank)
+            ep = self._endpoints.get(key)
+            if ep is None:
+                from ..session.bootstrap import BootstrapClient
+                try:
+                    ep = BootstrapClient(self._bootstrap_url).endpoint(r.engine_id, src_rank)
+                except Exception as e:  # noqa: BLE001 - an unreachable registry: the direct address
+                    log.warning("bootstrap lookup of %s failed: %s", key, e)
+                if ep is not None:
+                    self._endpoints[key] = ep
+            if ep is not None:
+                return ep
+        return f"tcp://{r.host}:{r.port + src_rank}"
 
     def wait_for_save(self) -> None:
         """After the forward that completes the sends' prompt KV has been
@@ -686,6 +724,12 @@ class SessionKVConnector(KVConnectorBase_V1):
         return out
 
     def shutdown(self) -> None:
+        if self.is_producer and self._bootstrap_url and self._thread is not None and self._tp_rank == 0:
+            from ..session.bootstrap import BootstrapClient
+            try:
+                BootstrapClient(self._bootstrap_url).unregister(self._engine_id)
+            except Exception as e:  # noqa: BLE001 - the registry may be gone first
+                log.warning("bootstrap unregister of %s failed: %s", self._engine_id, e)
         if self._thread is not None:
             self._thread.stop()
             self._thread = None
@@ -738,7 +782,7 @@ class SessionKVConnector(KVConnectorBase_V1):
         suffix = prompt - (full - len(ids)) * self._block_size
         self._pending_recvs.append(RecvReq(request.request_id, str(params["transfer_id"]),
                                            str(params.get("remote_host", self._host)), int(params["remote_port"]),
-                                           list(ids), suffix))
+                                           list(ids), suffix, str(params.get("remote_engine_id", ""))))
 
     def build_connector_meta(self, scheduler_output):
         if self.is_producer and scheduler_output is not None:
@@ -792,4 +836,4 @@ class SessionKVConnector(KVConnectorBase_V1):
         self._registered.discard(tid)
         return True, {"do_remote_prefill": True, "do_remote_decode": False, "transfer_id": tid,
                       "remote_host": self._host, "remote_port": self._port, "remote_tp_size": self._tp_size,
-                      "remote_num_tokens": entry[1]}
+                      "remote_num_tokens": entry[1], "remote_engine_id": self._engine_id}

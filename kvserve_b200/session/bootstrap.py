@@ -2,8 +2,9 @@
 kvsfuse-vllm0.30.0/mooncake/mooncake_utils.py:19-126 and stats.py:20-146).
 
 Prefill workers register ``(engine_id, tp_rank) -> session endpoint`` with a
-small FastAPI app; decode workers query it to find the producer of a
-request.  :class:`TransferStats` aggregates per-transfer durations, bytes,
+small FastAPI app (:func:`serve`, or ``python -m kvserve_b200.session.bootstrap``);
+decode workers query it through :class:`BootstrapClient` to find the
+producer of a request.  :class:`TransferStats` aggregates per-transfer durations, bytes,
 chunk counts and failures the way the reference's connector stats do.
 """
 from __future__ import annotations
@@ -69,6 +70,56 @@ def make_app(registry: Optional[Registry] = None):
     return app
 
 
+class BootstrapClient:
+    """HTTP client of :func:`make_app`'s service (prefill workers register,
+    decode workers look up the session endpoint of a rank)."""
+
+    def __init__(self, url: str, timeout_s: float = 5.0):
+        self.url, self.timeout_s = url.rstrip("/"), timeout_s
+
+    def register(self, engine_id: str, tp_rank: int, endpoint: str, tp_size: int = 1) -> None:
+        import requests
+        r = requests.post(f"{self.url}/register", json={"engine_id": engine_id, "tp_rank": int(tp_rank),
+                                                        "endpoint": endpoint, "tp_size": int(tp_size)},
+                          timeout=self.timeout_s)
+        r.raise_for_status()
+
+    def endpoint(self, engine_id: str, tp_rank: int) -> Optional[str]:
+        """The registered endpoint of ``(engine_id, tp_rank)``; None when
+        the service does not know it."""
+        import requests
+        r = requests.get(f"{self.url}/query", params={"engine_id": engine_id, "tp_rank": int(tp_rank)},
+                         timeout=self.timeout_s)
+        if r.status_code == 404:
+            return None
+        r.raise_for_status()
+        return str(r.json()["endpoint"])
+
+    def unregister(self, engine_id: str) -> int:
+        import requests
+        r = requests.delete(f"{self.url}/engine/{engine_id}", timeout=self.timeout_s)
+        r.raise_for_status()
+        return int(r.json()["removed"])
+
+
+def serve(host: str = "127.0.0.1", port: int = 8998, registry: Optional[Registry] = None,
+          timeout_s: float = 10.0):
+    """Run the bootstrap service on a background thread; returns the
+    uvicorn server (``server.should_exit = True`` stops it) and the thread."""
+    import time
+
+    import uvicorn
+    server = uvicorn.Server(uvicorn.Config(make_app(registry), host=host, port=port, log_level="warning"))
+    thread = threading.Thread(target=server.run, name="kvs-bootstrap", daemon=True)
+    thread.start()
+    deadline = time.monotonic() + timeout_s
+    while not server.started:
+        if not thread.is_alive() or time.monotonic() > deadline:
+            raise RuntimeError(f"bootstrap service did not start on {host}:{port}")
+        time.sleep(0.01)
+    return server, thread
+
+
 @dataclass
 class TransferStats:
     durations_s: list = field(default_factory=list)
@@ -99,3 +150,19 @@ class TransferStats:
                 "total_mb": total_b / 2 ** 20, "avg_mb_per_transfer": total_b / n / 2 ** 20,
                 "throughput_gbps": 8 * total_b / total_t / 1e9 if total_t > 0 else 0.0,
                 "avg_chunks": sum(self.chunks) / n}
+
+
+def main(argv=None) -> None:
+    """``python -m kvserve_b200.session.bootstrap --host 0.0.0.0 --port 8998``"""
+    import argparse
+
+    import uvicorn
+    ap = argparse.ArgumentParser(description="session endpoint registry for prefill and decode workers")
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8998)
+    a = ap.parse_args(argv)
+    uvicorn.run(make_app(), host=a.host, port=a.port, log_level="warning")
+
+
+if __name__ == "__main__":
+    main()

@@ -242,6 +242,44 @@ def test_sliding_window_pulls_only_the_blocks_in_the_window():
         d_work.shutdown()
 
 
+def test_decode_finds_the_producer_through_the_bootstrap_service():
+    from kvserve_b200.session.bootstrap import BootstrapClient, Registry, serve
+    FakeJobs.seen.clear()
+    reg = Registry()
+    server, thread = serve("127.0.0.1", _port(), reg)
+    url = f"http://127.0.0.1:{server.config.port}"
+    port = _port()
+
+    def cfg(producer):
+        c = _vllm_config(producer, port)
+        c.kv_transfer_config.kv_connector_extra_config.update(bootstrap_url=url, engine_id="prefill-A")
+        return c
+    src = torch.randn(2, NB, BS, 2, 64).to(torch.bfloat16)
+    dst = torch.zeros_like(src)
+    p_sched, d_sched = FakeJobs(cfg(True), KVConnectorRole.SCHEDULER), FakeJobs(cfg(False), KVConnectorRole.SCHEDULER)
+    p_work, d_work = FakeJobs(cfg(True), KVConnectorRole.WORKER), FakeJobs(cfg(False), KVConnectorRole.WORKER)
+    p_work.register_kv_caches({"model.layers.0.self_attn.attn": src})
+    d_work.register_kv_caches({"model.layers.0.self_attn.attn": dst})
+    try:
+        assert reg.query("prefill-A", 0)["endpoint"] == f"tcp://127.0.0.1:{port}"
+        prompt, p_blocks, d_blocks = 40, [1, 2, 3], [20, 21, 22]
+        _, params = _prefill(p_sched, p_work, "p6", "t6", prompt, p_blocks)
+        assert params["remote_engine_id"] == "prefill-A"
+        params = dict(params, remote_port=1)          # a wrong direct address: only the registry finds P
+        dreq = _req("d6", prompt, params, status="WAITING_FOR_REMOTE_KVS")
+        assert d_sched.get_num_new_matched_tokens(dreq, 0) == (prompt, True)
+        d_sched.update_state_after_alloc(dreq, Blocks(d_blocks, d_blocks), prompt)
+        assert _wait_recv(d_sched, d_work, "d6")
+        assert torch.equal(dst[:, d_blocks], src[:, p_blocks])
+        p_work.shutdown()                               # rank 0 of the engine leaves the registry
+        assert BootstrapClient(url).endpoint("prefill-A", 0) is None
+    finally:
+        p_work.shutdown()
+        d_work.shutdown()
+        server.should_exit = True
+        thread.join(10)
+
+
 def test_window_and_group_rules():
     blocks = SessionKVConnector.sliding_window_blocks
     assert blocks(None) == 0 and blocks(_groups()) == 0
