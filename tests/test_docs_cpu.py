@@ -1,6 +1,6 @@
 """The documentation points at things that exist: every repository path in
-README.md and DESIGN.md (files, ``{a,b}`` groups, package-relative module
-paths) and every ``tests/…py::test`` it cites."""
+the documents listed in ``DOCS`` (files, ``{a,b}`` groups, package-relative
+module paths) and every ``tests/…py::test`` they cite."""
 import os
 import re
 
