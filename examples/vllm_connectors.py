@@ -52,10 +52,13 @@ def push_params(transfer_id: str, max_tokens: int = 32, **sampling):
 
 def pull_config(role: str, prefill_host: str = "127.0.0.1", session_port: int = 26100,
                 compression: Optional[dict] = None, prefill_tp: Optional[int] = None,
-                decode_tp: Optional[int] = None, inline_payloads: bool = False):
+                decode_tp: Optional[int] = None, inline_payloads: bool = False,
+                bootstrap_url: Optional[str] = None, engine_id: Optional[str] = None):
     """The pull connector; ``compression`` uses the runtime's keys
     (default :data:`RUNTIME_K4V4`); give both TP sizes when they differ;
-    ``inline_payloads`` for engines on different nodes."""
+    ``inline_payloads`` for engines on different nodes; ``bootstrap_url``
+    (``python -m kvserve_b200.session.bootstrap``) lets decode workers find
+    prefill ranks by ``engine_id`` instead of host and port."""
     from vllm.config import KVTransferConfig
     extra: dict = {"session_port": session_port, "compression": compression or RUNTIME_K4V4,
                    "inline_payloads": inline_payloads}
@@ -63,6 +66,10 @@ def pull_config(role: str, prefill_host: str = "127.0.0.1", session_port: int = 
         extra["prefill_tp_size"] = prefill_tp
     if decode_tp is not None:
         extra["decode_tp_size"] = decode_tp
+    if bootstrap_url:
+        extra["bootstrap_url"] = bootstrap_url
+    if engine_id:
+        extra["engine_id"] = engine_id
     return KVTransferConfig(kv_connector="SessionKVConnector", kv_connector_module_path=PULL_MODULE, kv_role=role,
                             kv_ip=prefill_host, kv_connector_extra_config=extra)
 

@@ -229,6 +229,9 @@ def test_example_configs_build_and_name_real_connectors():
             cls = getattr(importlib.import_module(c.kv_connector_module_path), c.kv_connector)
             assert cls.__name__ == c.kv_connector
         assert cfgs[3].kv_connector_extra_config["decode_tp_size"] == 2
+        boot = ex.pull_config("kv_producer", bootstrap_url="http://127.0.0.1:8998", engine_id="prefill-0")
+        assert boot.kv_connector_extra_config["bootstrap_url"] == "http://127.0.0.1:8998"
+        assert boot.kv_connector_extra_config["engine_id"] == "prefill-0"
         p = ex.pull_prefill_params("t-1")
         assert p.max_tokens == 1 and p.extra_args["kv_transfer_params"]["do_remote_decode"]
         with pytest.raises(ValueError):
