@@ -336,6 +336,12 @@ class SessionKVConnector(KVConnectorBase_V1):
         self._bootstrap_url = str(extra.get("bootstrap_url") or "")
         self._engine_id = str(extra.get("engine_id") or getattr(cfg, "engine_id", None) or
                               f"{self._host}:{self._port}")
+        par = getattr(vllm_config, "parallel_config", None)
+        if int(getattr(par, "data_parallel_size", 1) or 1) > 1:
+            # data-parallel replicas share the engine id: each registers and
+            # is named as its own replica (the role of the reference's
+            # bootstrap by dp_rank, mooncake_connector.py:191-231)
+            self._engine_id += f"/dp{int(getattr(par, 'data_parallel_rank', 0) or 0)}"
         self._endpoints: dict[tuple[str, int], str] = {}
         self._tp_size = int(getattr(vllm_config.parallel_config, "tensor_parallel_size", 1) or 1)
         self._tp_rank = 0

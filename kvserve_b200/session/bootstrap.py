@@ -62,7 +62,7 @@ def make_app(registry: Optional[Registry] = None):
             raise HTTPException(404, f"no worker for {engine_id}")
         return out if tp_rank is not None else {str(k): v for k, v in out.items()}
 
-    @app.delete("/engine/{engine_id}")
+    @app.delete("/engine/{engine_id:path}")
     def drop(engine_id: str):
         return {"removed": reg.unregister(engine_id)}
 

@@ -280,6 +280,24 @@ def test_decode_finds_the_producer_through_the_bootstrap_service():
         thread.join(10)
 
 
+def test_data_parallel_replicas_register_as_their_own_engines():
+    c = _vllm_config(True, _port())
+    c.kv_transfer_config.kv_connector_extra_config["engine_id"] = "prefill-A"
+    assert FakeJobs(c, KVConnectorRole.SCHEDULER)._engine_id == "prefill-A"
+    c.parallel_config = NS(tensor_parallel_size=1, data_parallel_size=2, data_parallel_rank=1)
+    assert FakeJobs(c, KVConnectorRole.SCHEDULER)._engine_id == "prefill-A/dp1"
+    from kvserve_b200.session.bootstrap import BootstrapClient, serve
+    server, thread = serve("127.0.0.1", _port())
+    try:
+        cl = BootstrapClient(f"http://127.0.0.1:{server.config.port}")
+        cl.register("prefill-A/dp1", 1, "tcp://h:2", 2)
+        assert cl.endpoint("prefill-A/dp1", 1) == "tcp://h:2" and cl.endpoint("prefill-A/dp0", 1) is None
+        assert cl.unregister("prefill-A/dp1") == 1 and cl.endpoint("prefill-A/dp1", 1) is None
+    finally:
+        server.should_exit = True
+        thread.join(10)
+
+
 def test_window_and_group_rules():
     blocks = SessionKVConnector.sliding_window_blocks
     assert blocks(None) == 0 and blocks(_groups()) == 0
